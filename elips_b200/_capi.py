@@ -1,0 +1,104 @@
+"""ctypes binding of include/elips_b200.h.
+
+Loads the in-tree libelips_b200.so. There is no fallback: if the library is
+missing or fails to load, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libelips_b200.so"
+
+OK = 0
+DEVICE_NOT_FOUND = 1
+INSUFFICIENT_MEMORY = 2
+KERNEL_LAUNCH_FAILED = 3
+TRANSFER_FAILED = 4
+INDEX_BUILD_FAILED = 5
+UNSUPPORTED_METRIC = 6
+INITIALIZATION_FAILED = 7
+BACKEND_UNAVAILABLE = 8
+DIMENSION_MISMATCH = 9
+INVALID_ARGUMENT = 10
+DEVICE_TIMEOUT = 11
+
+METRIC_COSINE = 0
+METRIC_EUCLIDEAN = 1
+METRIC_DOT_PRODUCT = 2
+
+PRECISION_FP32 = 0
+PRECISION_FP16 = 1
+PRECISION_INT8 = 2
+PRECISION_AUTO = 3
+PRECISION_BF16 = 4
+
+# (name, restype, argtypes) for every entry point in include/elips_b200.h.
+SIGNATURES = [
+    ("elips_b200_status_string", c_char_p, [c_int]),
+    ("elips_b200_device_count", c_int, [POINTER(c_int)]),
+    ("elips_b200_device_error", c_int, [c_int, POINTER(c_int)]),
+    ("elips_b200_exact_create", c_int, [c_int, c_int, c_int, c_uint32, POINTER(c_void_p)]),
+    ("elips_b200_exact_add", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("elips_b200_exact_size", c_int, [c_void_p, POINTER(c_size_t)]),
+    ("elips_b200_exact_destroy", c_int, [c_void_p]),
+    ("elips_b200_exact_search", c_int,
+     [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_exact_search_device", c_int,
+     [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_exact_search_candidates_device", c_int,
+     [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_uint32, c_void_p, c_void_p]),
+    ("elips_b200_merge_candidates_device", c_int,
+     [c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_void_p, c_void_p, c_void_p]),
+]
+
+
+class ElipsB200Error(RuntimeError):
+    """A non-zero status from the C ABI. `status` is the ELIPS_B200_* code."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        super().__init__(f"{where}: {status_name(status)} ({status})")
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is not built; run `python elips_b200/build.py` "
+            "(the search path has no CPU fallback)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, restype, argtypes in SIGNATURES:
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    return lib
+
+
+LIB = _load()
+
+
+def status_name(status: int) -> str:
+    return LIB.elips_b200_status_string(int(status)).decode()
+
+
+def check(status: int, where: str) -> None:
+    if status != OK:
+        raise ElipsB200Error(status, where)
+
+
+def device_count() -> int:
+    n = c_int(0)
+    status = LIB.elips_b200_device_count(ctypes.byref(n))
+    if status not in (OK, DEVICE_NOT_FOUND, BACKEND_UNAVAILABLE):
+        check(status, "elips_b200_device_count")
+    return n.value
+
+
+def device_error(device: int) -> int:
+    code = c_int(0)
+    check(LIB.elips_b200_device_error(device, ctypes.byref(code)), "elips_b200_device_error")
+    return code.value
+
+
+__all__ = [n for n in dir() if not n.startswith("_")]

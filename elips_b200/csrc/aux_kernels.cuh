@@ -1,0 +1,208 @@
+// Operand preparation and final top-k merge kernels for the exact search.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace eb {
+
+// Rounds fp32 to tf32 (round to nearest, ties away) in an fp32 container.
+__device__ __forceinline__ float to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// One warp per row: converts fp32 rows [rows x d] to the tensor-core operand
+// layout [rows x d_pad] (zero padded to a whole number of 128-byte K blocks)
+// and writes the squared norm of the stored (rounded) row when norms != null.
+//   kind 0: fp16, 1: bf16, 2: tf32 split (hi to out, x - hi to out_lo).
+__global__ void prep_rows_f32_kernel(const float* __restrict__ in, uint64_t rows, uint32_t d,
+                                     uint32_t d_pad, int kind, void* __restrict__ out,
+                                     float* __restrict__ out_lo, float* __restrict__ norms) {
+    const uint64_t row = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31u;
+    if (row >= rows) return;
+    const float* src = in + row * d;
+    float acc = 0.0f;
+    for (uint32_t j = lane; j < d_pad; j += 32) {
+        const float x = j < d ? src[j] : 0.0f;
+        float stored;
+        if (kind == 0) {
+            const __half h = __float2half_rn(x);
+            reinterpret_cast<__half*>(out)[row * d_pad + j] = h;
+            stored = __half2float(h);
+        } else if (kind == 1) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(x);
+            reinterpret_cast<__nv_bfloat16*>(out)[row * d_pad + j] = h;
+            stored = __bfloat162float(h);
+        } else {
+            const float hi = to_tf32(x);
+            reinterpret_cast<float*>(out)[row * d_pad + j] = hi;
+            out_lo[row * d_pad + j] = x - hi;
+            stored = x;
+        }
+        acc = fmaf(stored, stored, acc);
+    }
+    if (norms != nullptr) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) norms[row] = acc;
+    }
+}
+
+// int8 rows [rows x d] -> [rows x d_pad], zero padded.
+__global__ void prep_rows_i8_kernel(const int8_t* __restrict__ in, uint64_t rows, uint32_t d,
+                                    uint32_t d_pad, int8_t* __restrict__ out) {
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= rows * d_pad) return;
+    const uint64_t r = i / d_pad;
+    const uint32_t j = static_cast<uint32_t>(i % d_pad);
+    out[i] = j < d ? in[r * d + j] : int8_t(0);
+}
+
+// Final top-k per query: one warp selects the k smallest (key, row) pairs
+// among `lists` candidate lists of length k and writes them sorted.
+// List l of query q starts at cand + q*stride_q + l*stride_l (entries).
+// Composite 64-bit keys (ordered key << 32 | row) are unique, so an 8-pass
+// radix select finds the exact k-th and a bitonic sort orders the survivors.
+// Dynamic smem per warp: 256 words of histogram + kpow2 u64 sort buffer.
+__global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, uint32_t lists,
+                                  uint32_t k, uint64_t stride_q, uint64_t stride_l, uint32_t kpow2,
+                                  int metric, float* __restrict__ out_dist,
+                                  int64_t* __restrict__ out_rows, uint2* __restrict__ out_cand) {
+    extern __shared__ uint8_t smem[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t warps = blockDim.x >> 5;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + warp * 256u;
+    unsigned long long* buf =
+        reinterpret_cast<unsigned long long*>(smem + warps * 1024u) + static_cast<size_t>(warp) * kpow2;
+    const uint32_t q = blockIdx.x * warps + warp;
+    if (q >= nq) return;
+    const uint32_t count = lists * k;
+    auto composite = [&](uint32_t idx) -> unsigned long long {
+        const uint32_t l = idx / k, i = idx - l * k;
+        const uint2 e = cand[q * stride_q + l * stride_l + i];
+        return (static_cast<unsigned long long>(ordered_key(__uint_as_float(e.x))) << 32) | e.y;
+    };
+    const uint32_t take = min(k, count);
+    if (take == 0) {
+        for (uint32_t i = lane; i < k; i += 32) {
+            if (out_dist != nullptr) {
+                out_dist[static_cast<size_t>(q) * k + i] = __int_as_float(0x7f800000);
+                out_rows[static_cast<size_t>(q) * k + i] = -1;
+            }
+            if (out_cand != nullptr) out_cand[static_cast<size_t>(q) * k + i] = make_uint2(0x7f800000u, 0xFFFFFFFFu);
+        }
+        return;
+    }
+    // radix select the take-th smallest composite
+    unsigned long long prefix = 0, pmask = 0;
+    uint32_t rank = take;
+#pragma unroll 1
+    for (int pass = 0; pass < 8; ++pass) {
+        const uint32_t shift = 56u - 8u * static_cast<uint32_t>(pass);
+        for (uint32_t b = lane; b < 256; b += 32) hist[b] = 0;
+        __syncwarp();
+        for (uint32_t j = lane; j < count; j += 32) {
+            const unsigned long long c = composite(j);
+            if ((c & pmask) == prefix) atomicAdd(&hist[(c >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        uint32_t bins[8], local = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            bins[i] = hist[lane * 8 + i];
+            local += bins[i];
+        }
+        uint32_t incl = local;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= static_cast<uint32_t>(off)) incl += t;
+        }
+        const uint32_t excl = incl - local;
+        const bool mine = excl < rank && rank <= incl;
+        uint32_t digit = 0, before = excl;
+        if (mine) {
+            uint32_t acc = excl;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (acc + bins[i] >= rank) {
+                    digit = lane * 8 + i;
+                    before = acc;
+                    break;
+                }
+                acc += bins[i];
+            }
+        }
+        const uint32_t owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+        digit = __shfl_sync(0xffffffffu, digit, owner);
+        before = __shfl_sync(0xffffffffu, before, owner);
+        rank -= before;
+        prefix |= static_cast<unsigned long long>(digit) << shift;
+        pmask |= 255ull << shift;
+        __syncwarp();
+    }
+    // Gather the survivors: every composite below the take-th, then copies of
+    // the take-th itself up to `take` in total (only the padding composite
+    // can repeat, so the surplus copies are interchangeable).
+    const uint32_t lt = lanemask_lt();
+    uint32_t w = 0;
+    for (uint32_t j0 = 0; j0 < count; j0 += 32) {
+        const uint32_t j = j0 + lane;
+        const unsigned long long c = j < count ? composite(j) : ~0ull;
+        const bool keep = j < count && c < prefix;
+        const uint32_t m = __ballot_sync(0xffffffffu, keep);
+        if (keep) buf[w + __popc(m & lt)] = c;
+        w += __popc(m);
+    }
+    for (uint32_t j0 = 0; j0 < count && w < take; j0 += 32) {
+        const uint32_t j = j0 + lane;
+        const unsigned long long c = j < count ? composite(j) : ~0ull;
+        const bool eq = j < count && c == prefix;
+        const uint32_t m = __ballot_sync(0xffffffffu, eq);
+        const uint32_t pos = w + __popc(m & lt);
+        if (eq && pos < take) buf[pos] = c;
+        w = min(take, w + __popc(m));
+    }
+    for (uint32_t i = w + lane; i < kpow2; i += 32) buf[i] = ~0ull;
+    __syncwarp();
+    for (uint32_t size = 2; size <= kpow2; size <<= 1) {
+        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+            for (uint32_t i = lane; i < kpow2; i += 32) {
+                const uint32_t j = i ^ stride;
+                if (j > i) {
+                    const unsigned long long a = buf[i], b = buf[j];
+                    const bool up = (i & size) == 0;
+                    if ((a > b) == up) {
+                        buf[i] = b;
+                        buf[j] = a;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+    for (uint32_t i = lane; i < k; i += 32) {
+        const unsigned long long c = i < take ? buf[i] : ~0ull;
+        const uint32_t row = static_cast<uint32_t>(c & 0xFFFFFFFFull);
+        const float key = key_to_float(static_cast<uint32_t>(c >> 32));
+        const bool valid = row != 0xFFFFFFFFu;
+        if (out_dist != nullptr) {
+            float dist = key;
+            if (metric == 1) dist = sqrtf(fmaxf(key, 0.0f));
+            out_dist[static_cast<size_t>(q) * k + i] = valid ? dist : __int_as_float(0x7f800000);
+            out_rows[static_cast<size_t>(q) * k + i] = valid ? static_cast<int64_t>(row) : -1;
+        }
+        if (out_cand != nullptr) {
+            out_cand[static_cast<size_t>(q) * k + i] =
+                valid ? make_uint2(__float_as_uint(key), row) : make_uint2(0x7f800000u, 0xFFFFFFFFu);
+        }
+    }
+}
+
+}  // namespace eb

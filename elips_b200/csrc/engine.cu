@@ -1,0 +1,427 @@
+// Host engine for the exact search path: device set-up, buffers, TMA
+// descriptors, launch planning, and the ExactIndex implementation.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/elips_b200.h"
+#include "aux_kernels.cuh"
+#include "engine.cuh"
+#include "exact_topk.cuh"
+
+namespace eb {
+
+void fail(int code, const std::string& what) { throw Error{code, what}; }
+
+void check_cuda(cudaError_t e, int code, const char* what) {
+    if (e == cudaSuccess) return;
+    if (e == cudaErrorMemoryAllocation) code = ELIPS_B200_INSUFFICIENT_MEMORY;
+    fail(code, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+DeviceGuard::DeviceGuard(int device) {
+    check_cuda(cudaGetDevice(&prev_), ELIPS_B200_DEVICE_NOT_FOUND, "cudaGetDevice");
+    if (prev_ != device) check_cuda(cudaSetDevice(device), ELIPS_B200_DEVICE_NOT_FOUND, "cudaSetDevice");
+}
+
+DeviceGuard::~DeviceGuard() {
+    int cur = -1;
+    if (cudaGetDevice(&cur) == cudaSuccess && cur != prev_ && prev_ >= 0) cudaSetDevice(prev_);
+}
+
+namespace {
+
+std::mutex g_props_mu;
+std::vector<DeviceProps> g_props;
+std::vector<bool> g_props_ready;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    std::lock_guard<std::mutex> lock(g_props_mu);
+    if (g_encode == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q),
+                   ELIPS_B200_INITIALIZATION_FAILED, "cudaGetDriverEntryPoint");
+        if (fn == nullptr || q != cudaDriverEntryPointSuccess)
+            fail(ELIPS_B200_INITIALIZATION_FAILED, "cuTensorMapEncodeTiled unavailable");
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    return g_encode;
+}
+
+}  // namespace
+
+const DeviceProps& device_props(int device) {
+    std::lock_guard<std::mutex> lock(g_props_mu);
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count)
+        fail(ELIPS_B200_DEVICE_NOT_FOUND, "no such CUDA device");
+    if (g_props.size() < static_cast<size_t>(count)) {
+        g_props.resize(count);
+        g_props_ready.resize(count, false);
+    }
+    if (!g_props_ready[device]) {
+        cudaDeviceProp prop{};
+        check_cuda(cudaGetDeviceProperties(&prop, device), ELIPS_B200_DEVICE_NOT_FOUND,
+                   "cudaGetDeviceProperties");
+        if (prop.major != 10 || prop.minor != 0)
+            fail(ELIPS_B200_BACKEND_UNAVAILABLE, "device is not sm_100 (B200)");
+        DeviceProps p;
+        p.num_sms = prop.multiProcessorCount;
+        p.cc_major = prop.major;
+        p.cc_minor = prop.minor;
+        p.max_smem_optin = prop.sharedMemPerBlockOptin;
+        // Keep freed stream-ordered scratch cached in the pool between calls.
+        cudaMemPool_t pool;
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+            uint64_t threshold = UINT64_MAX;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold);
+        }
+        if (prev >= 0) cudaSetDevice(prev);
+        g_props[device] = p;
+        g_props_ready[device] = true;
+    }
+    return g_props[device];
+}
+
+DeviceBuffer::DeviceBuffer(int device, size_t bytes) : device_(device), bytes_(bytes) {
+    if (bytes == 0) return;
+    DeviceGuard g(device);
+    check_cuda(cudaMalloc(&ptr_, bytes), ELIPS_B200_INSUFFICIENT_MEMORY, "cudaMalloc");
+}
+
+DeviceBuffer::~DeviceBuffer() { reset(); }
+
+DeviceBuffer& DeviceBuffer::operator=(DeviceBuffer&& o) noexcept {
+    if (this != &o) {
+        reset();
+        device_ = o.device_;
+        ptr_ = o.ptr_;
+        bytes_ = o.bytes_;
+        o.ptr_ = nullptr;
+        o.bytes_ = 0;
+    }
+    return *this;
+}
+
+void DeviceBuffer::reset() {
+    if (ptr_ != nullptr) {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        if (prev != device_) cudaSetDevice(device_);
+        cudaFree(ptr_);
+        if (prev != device_ && prev >= 0) cudaSetDevice(prev);
+    }
+    ptr_ = nullptr;
+    bytes_ = 0;
+}
+
+StreamScratch::StreamScratch(size_t bytes, cudaStream_t stream) : stream_(stream) {
+    check_cuda(cudaMallocAsync(&ptr_, std::max<size_t>(bytes, 256), stream),
+               ELIPS_B200_INSUFFICIENT_MEMORY, "cudaMallocAsync");
+}
+
+StreamScratch::~StreamScratch() {
+    if (ptr_ != nullptr) cudaFreeAsync(ptr_, stream_);
+}
+
+CUtensorMap make_operand_map(const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
+                             uint64_t cols, uint64_t rows, uint32_t box_rows) {
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof(map));
+    const cuuint64_t dims[2] = {cols, std::max<uint64_t>(rows, 1)};
+    const cuuint64_t strides[1] = {cols * elem_bytes};
+    const cuuint32_t box[2] = {128u / elem_bytes, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(
+        &map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(ELIPS_B200_KERNEL_LAUNCH_FAILED, "cuTensorMapEncodeTiled failed");
+    return map;
+}
+
+ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int num_sms) {
+    ExactPlan p;
+    p.bn = bn;
+    p.n_qt = (nq + kTileM - 1) / kTileM;
+    p.n_bt = (n + bn - 1) / bn;
+    // Pick the smallest number of base splits whose (query tile, split)
+    // units fill the SMs in whole waves; each split keeps >= 4 base tiles.
+    uint32_t best_s = 1;
+    double best_eff = -1.0;
+    const uint32_t max_s = std::max<uint32_t>(1, std::min<uint32_t>(256, p.n_bt / 4));
+    for (uint32_t s = 1; s <= max_s; ++s) {
+        const uint64_t units = static_cast<uint64_t>(p.n_qt) * s;
+        const uint64_t waves = (units + num_sms - 1) / num_sms;
+        const double eff = static_cast<double>(units) / static_cast<double>(waves * num_sms);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best_s = s;
+        }
+        if (eff >= 0.97) break;
+    }
+    p.splits = best_s;
+    const uint64_t units = static_cast<uint64_t>(p.n_qt) * p.splits;
+    p.grid = static_cast<uint32_t>(std::min<uint64_t>(units, static_cast<uint64_t>(num_sms)));
+    p.cap = std::max<uint32_t>(256u, ((2u * k + 32u) + 31u) / 32u * 32u);
+    return p;
+}
+
+namespace {
+
+constexpr uint32_t kMaxK = 1024;
+
+uint32_t elem_bytes_of(OperandKind k) {
+    switch (k) {
+        case OperandKind::F16:
+        case OperandKind::BF16: return 2;
+        case OperandKind::TF32X3: return 4;
+        case OperandKind::I8: return 1;
+    }
+    return 2;
+}
+
+CUtensorMapDataType tma_dtype_of(OperandKind k) {
+    switch (k) {
+        case OperandKind::F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        case OperandKind::BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        case OperandKind::TF32X3: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        case OperandKind::I8: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    }
+    return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// Converts `rows` device rows (fp32 or int8) into operand layout at `dst_row`.
+void prep_operands(OperandKind kind, const void* src, size_t rows, uint32_t dim, uint32_t d_pad,
+                   void* ops, void* ops_lo, float* norms, cudaStream_t stream) {
+    if (rows == 0) return;
+    if (kind == OperandKind::I8) {
+        const uint64_t total = static_cast<uint64_t>(rows) * d_pad;
+        const uint32_t blocks = static_cast<uint32_t>((total + 255) / 256);
+        prep_rows_i8_kernel<<<blocks, 256, 0, stream>>>(static_cast<const int8_t*>(src), rows, dim,
+                                                        d_pad, static_cast<int8_t*>(ops));
+    } else {
+        const int k = kind == OperandKind::F16 ? 0 : (kind == OperandKind::BF16 ? 1 : 2);
+        const uint64_t threads = static_cast<uint64_t>(rows) * 32;
+        const uint32_t blocks = static_cast<uint32_t>((threads + 255) / 256);
+        prep_rows_f32_kernel<<<blocks, 256, 0, stream>>>(static_cast<const float*>(src), rows, dim,
+                                                         d_pad, k, ops, static_cast<float*>(ops_lo),
+                                                         norms);
+    }
+    check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "prep kernel launch");
+}
+
+template <OperandKind KIND, int BN, int STAGES>
+void launch_exact_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& alo,
+                         const CUtensorMap& blo, const ExactParams& params, uint32_t grid,
+                         cudaStream_t stream) {
+    using Cfg = ExactConfig<KIND, BN, STAGES>;
+    auto kernel = exact_topk_kernel<KIND, BN, STAGES>;
+    check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(Cfg::kSmemBytes)),
+               ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+    kernel<<<grid, kExactThreads, Cfg::kSmemBytes, stream>>>(a, b, alo, blo, params);
+    check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "exact kernel launch");
+}
+
+uint32_t bn_of(OperandKind k) { return k == OperandKind::TF32X3 ? 128u : 256u; }
+
+}  // namespace
+
+ExactIndex::ExactIndex(int device, int metric, int precision, uint32_t dim)
+    : device_(device), metric_(metric), precision_(precision), dim_(dim) {
+    if (dim == 0 || dim > 65535) fail(ELIPS_B200_INVALID_ARGUMENT, "dimension must be in [1, 65535]");
+    if (metric < 0 || metric > 2) fail(ELIPS_B200_UNSUPPORTED_METRIC, "unknown metric");
+    switch (precision) {
+        case ELIPS_B200_PRECISION_FP32: kind_ = OperandKind::TF32X3; break;
+        case ELIPS_B200_PRECISION_FP16:
+        case ELIPS_B200_PRECISION_AUTO: kind_ = OperandKind::F16; break;
+        case ELIPS_B200_PRECISION_BF16: kind_ = OperandKind::BF16; break;
+        case ELIPS_B200_PRECISION_INT8: kind_ = OperandKind::I8; break;
+        default: fail(ELIPS_B200_INVALID_ARGUMENT, "unknown precision");
+    }
+    if (kind_ == OperandKind::I8 && metric != kDot)
+        fail(ELIPS_B200_UNSUPPORTED_METRIC, "the int8 codec scores inner product only");
+    device_props(device);
+    elem_bytes_ = elem_bytes_of(kind_);
+    const uint32_t per_block = 128u / elem_bytes_;
+    d_pad_ = (dim + per_block - 1) / per_block * per_block;
+}
+
+void ExactIndex::reserve(size_t rows) {
+    if (rows <= capacity_) return;
+    const size_t cap = std::max<size_t>(rows, capacity_ + capacity_ / 2);
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    DeviceBuffer ops(device_, cap * row_bytes);
+    DeviceBuffer lo(device_, kind_ == OperandKind::TF32X3 ? cap * row_bytes : 0);
+    DeviceBuffer norms(device_, metric_ == kEuclidean ? cap * sizeof(float) : 0);
+    if (n_ > 0) {
+        check_cuda(cudaMemcpy(ops.get(), ops_.get(), n_ * row_bytes, cudaMemcpyDeviceToDevice),
+                   ELIPS_B200_TRANSFER_FAILED, "grow copy");
+        if (lo.get() != nullptr)
+            check_cuda(cudaMemcpy(lo.get(), ops_lo_.get(), n_ * row_bytes, cudaMemcpyDeviceToDevice),
+                       ELIPS_B200_TRANSFER_FAILED, "grow copy");
+        if (norms.get() != nullptr)
+            check_cuda(cudaMemcpy(norms.get(), norms_.get(), n_ * sizeof(float), cudaMemcpyDeviceToDevice),
+                       ELIPS_B200_TRANSFER_FAILED, "grow copy");
+    }
+    ops_ = std::move(ops);
+    ops_lo_ = std::move(lo);
+    norms_ = std::move(norms);
+    capacity_ = cap;
+}
+
+void ExactIndex::add(const void* rows_host, size_t n) {
+    if (n == 0) return;
+    if (rows_host == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "rows is null");
+    if (n_ + n >= 0xFFFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "index limited to 2^32-2 rows");
+    DeviceGuard g(device_);
+    reserve(n_ + n);
+    const size_t in_elem = kind_ == OperandKind::I8 ? 1 : 4;
+    const size_t in_row = static_cast<size_t>(dim_) * in_elem;
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    // Stage through a bounded device buffer: 64 MiB of input rows at a time.
+    const size_t chunk = std::max<size_t>(1, (64ull << 20) / in_row);
+    cudaStream_t stream = nullptr;
+    check_cuda(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), ELIPS_B200_INITIALIZATION_FAILED,
+               "cudaStreamCreate");
+    try {
+        DeviceBuffer staging(device_, std::min(chunk, n) * in_row);
+        for (size_t r0 = 0; r0 < n; r0 += chunk) {
+            const size_t rows = std::min(chunk, n - r0);
+            check_cuda(cudaMemcpyAsync(staging.get(), static_cast<const uint8_t*>(rows_host) + r0 * in_row,
+                                       rows * in_row, cudaMemcpyHostToDevice, stream),
+                       ELIPS_B200_TRANSFER_FAILED, "row upload");
+            const size_t dst = n_ + r0;
+            prep_operands(kind_, staging.get(), rows, dim_, d_pad_,
+                          static_cast<uint8_t*>(ops_.get()) + dst * row_bytes,
+                          ops_lo_.get() ? static_cast<uint8_t*>(ops_lo_.get()) + dst * row_bytes : nullptr,
+                          norms_.get() ? static_cast<float*>(norms_.get()) + dst : nullptr, stream);
+            check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "row prep");
+        }
+    } catch (...) {
+        cudaStreamDestroy(stream);
+        throw;
+    }
+    cudaStreamDestroy(stream);
+    n_ += n;
+}
+
+void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const uint32_t* mask,
+                               uint32_t row_offset, float* out_dist, int64_t* out_rows,
+                               uint2* out_cand, cudaStream_t stream) const {
+    if (nq == 0 || k == 0) return;
+    if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
+    if (nq > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "too many queries in one call");
+    if (queries == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "queries is null");
+    DeviceGuard g(device_);
+    const DeviceProps& props = device_props(device_);
+    if (n_ == 0) {
+        // Nothing to search: every slot is empty.
+        merge_candidates(device_, nullptr, static_cast<uint32_t>(nq), 0, static_cast<uint32_t>(k), 0, 0,
+                         metric_, out_dist, out_rows, out_cand, stream);
+        return;
+    }
+    const uint32_t n = static_cast<uint32_t>(n_);
+    const ExactPlan plan = plan_exact(static_cast<uint32_t>(nq), n, static_cast<uint32_t>(k),
+                                      bn_of(kind_), props.num_sms);
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    auto align = [](size_t x) { return (x + 255) / 256 * 256; };
+    const size_t q_ops = align(nq * row_bytes);
+    const size_t q_lo = kind_ == OperandKind::TF32X3 ? q_ops : 0;
+    const size_t q_norm = metric_ == kEuclidean ? align(nq * sizeof(float)) : 0;
+    const size_t cand = align(static_cast<size_t>(plan.grid) * kTileM * plan.cap * sizeof(uint2));
+    const size_t partial = align(nq * plan.splits * k * sizeof(uint2));
+    StreamScratch scratch(q_ops + q_lo + q_norm + cand + partial, stream);
+    uint8_t* s = scratch.get();
+    void* qa = s;
+    void* qlo = q_lo ? s + q_ops : nullptr;
+    float* qn = q_norm ? reinterpret_cast<float*>(s + q_ops + q_lo) : nullptr;
+    uint2* cand_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm);
+    uint2* part_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand);
+    prep_operands(kind_, queries, nq, dim_, d_pad_, qa, qlo, qn, stream);
+
+    const CUtensorMapDataType dt = tma_dtype_of(kind_);
+    const CUtensorMap ma = make_operand_map(qa, dt, elem_bytes_, d_pad_, nq, kTileM);
+    const CUtensorMap mb = make_operand_map(ops_.get(), dt, elem_bytes_, d_pad_, n, plan.bn);
+    CUtensorMap malo = ma, mblo = mb;
+    if (kind_ == OperandKind::TF32X3) {
+        malo = make_operand_map(qlo, dt, elem_bytes_, d_pad_, nq, kTileM);
+        mblo = make_operand_map(ops_lo_.get(), dt, elem_bytes_, d_pad_, n, plan.bn);
+    }
+    ExactParams prm{};
+    prm.base_norms = static_cast<const float*>(norms_.get());
+    prm.query_norms = qn;
+    prm.mask = mask;
+    prm.cand = cand_buf;
+    prm.partial = part_buf;
+    prm.n = n;
+    prm.nq = static_cast<uint32_t>(nq);
+    prm.k = static_cast<uint32_t>(k);
+    prm.cap = plan.cap;
+    prm.splits = plan.splits;
+    prm.n_qt = plan.n_qt;
+    prm.n_bt = plan.n_bt;
+    prm.num_units = plan.n_qt * plan.splits;
+    prm.kblocks = d_pad_ * elem_bytes_ / kKBlockBytes;
+    prm.row_offset = row_offset;
+    prm.metric = metric_;
+    switch (kind_) {
+        case OperandKind::F16:
+            launch_exact_kernel<OperandKind::F16, 256, 4>(ma, mb, malo, mblo, prm, plan.grid, stream);
+            break;
+        case OperandKind::BF16:
+            launch_exact_kernel<OperandKind::BF16, 256, 4>(ma, mb, malo, mblo, prm, plan.grid, stream);
+            break;
+        case OperandKind::TF32X3:
+            launch_exact_kernel<OperandKind::TF32X3, 128, 3>(ma, mb, malo, mblo, prm, plan.grid, stream);
+            break;
+        case OperandKind::I8:
+            launch_exact_kernel<OperandKind::I8, 256, 4>(ma, mb, malo, mblo, prm, plan.grid, stream);
+            break;
+    }
+    merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits, static_cast<uint32_t>(k),
+                     static_cast<uint64_t>(plan.splits) * k, k, metric_, out_dist, out_rows, out_cand,
+                     stream);
+}
+
+void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,
+                      uint64_t stride_q, uint64_t stride_l, int metric, float* out_dist,
+                      int64_t* out_rows, uint2* out_cand, cudaStream_t stream) {
+    if (nq == 0 || k == 0) return;
+    if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
+    (void)device;
+    uint32_t kpow2 = 1;
+    while (kpow2 < k) kpow2 <<= 1;
+    constexpr uint32_t warps = 4;
+    const size_t smem = warps * (1024 + static_cast<size_t>(kpow2) * 8);
+    check_cuda(cudaFuncSetAttribute(merge_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(smem)),
+               ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+    const uint32_t blocks = (nq + warps - 1) / warps;
+    merge_topk_kernel<<<blocks, warps * 32, smem, stream>>>(cand, nq, lists, k, stride_q, stride_l, kpow2,
+                                                           metric, out_dist, out_rows, out_cand);
+    check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "merge kernel launch");
+}
+
+int read_and_clear_device_error(int device) {
+    DeviceGuard g(device);
+    check_cuda(cudaDeviceSynchronize(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaDeviceSynchronize");
+    int code = 0;
+    check_cuda(cudaMemcpyFromSymbol(&code, g_device_error, sizeof(int)), ELIPS_B200_TRANSFER_FAILED,
+               "read device error");
+    const int zero = 0;
+    check_cuda(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)), ELIPS_B200_TRANSFER_FAILED,
+               "clear device error");
+    return code;
+}
+
+}  // namespace eb

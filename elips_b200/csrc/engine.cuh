@@ -1,0 +1,130 @@
+// Host-side engine: device contexts, device buffers, and the exact index.
+// Everything here is C++; the C ABI in capi.cu wraps it and turns exceptions
+// into status codes.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <utility>
+
+#include "exact_topk.cuh"
+
+namespace eb {
+
+// Error carried from the engine to the C ABI. `code` is an ELIPS_B200_* value.
+struct Error {
+    int code;
+    std::string what;
+};
+
+[[noreturn]] void fail(int code, const std::string& what);
+void check_cuda(cudaError_t e, int code, const char* what);
+
+// Makes `device` current for the lifetime of the guard.
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int device);
+    ~DeviceGuard();
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+private:
+    int prev_ = -1;
+};
+
+struct DeviceProps {
+    int num_sms = 0;
+    int cc_major = 0, cc_minor = 0;
+    size_t max_smem_optin = 0;
+};
+
+// Validates the device (sm_100), returns its properties; initialises the
+// stream-ordered memory pool on first use.
+const DeviceProps& device_props(int device);
+
+// Owning device allocation (cudaMalloc / cudaFree).
+class DeviceBuffer {
+public:
+    DeviceBuffer() = default;
+    DeviceBuffer(int device, size_t bytes);
+    ~DeviceBuffer();
+    DeviceBuffer(DeviceBuffer&& o) noexcept { *this = std::move(o); }
+    DeviceBuffer& operator=(DeviceBuffer&& o) noexcept;
+    DeviceBuffer(const DeviceBuffer&) = delete;
+    DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+    void* get() const { return ptr_; }
+    size_t bytes() const { return bytes_; }
+
+private:
+    void reset();
+    int device_ = -1;
+    void* ptr_ = nullptr;
+    size_t bytes_ = 0;
+};
+
+// Stream-ordered scratch (cudaMallocAsync / cudaFreeAsync on `stream`).
+class StreamScratch {
+public:
+    StreamScratch(size_t bytes, cudaStream_t stream);
+    ~StreamScratch();
+    StreamScratch(const StreamScratch&) = delete;
+    StreamScratch& operator=(const StreamScratch&) = delete;
+    uint8_t* get() const { return static_cast<uint8_t*>(ptr_); }
+
+private:
+    void* ptr_ = nullptr;
+    cudaStream_t stream_;
+};
+
+// Builds a 2-D tiled TMA descriptor over a row-major [rows x cols] matrix
+// with 128-byte swizzle and a {128 bytes, box_rows} box.
+CUtensorMap make_operand_map(const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
+                             uint64_t cols, uint64_t rows, uint32_t box_rows);
+
+// Partitioning of one exact search launch.
+struct ExactPlan {
+    uint32_t n_qt = 0, n_bt = 0, splits = 0, grid = 0, cap = 0, bn = 0;
+};
+ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int num_sms);
+
+// Device-resident brute-force index over one base shard.
+class ExactIndex {
+public:
+    ExactIndex(int device, int metric, int precision, uint32_t dim);
+
+    void add(const void* rows_host, size_t n);
+    size_t size() const { return n_; }
+    int device() const { return device_; }
+    int metric() const { return metric_; }
+    uint32_t dim() const { return dim_; }
+    OperandKind kind() const { return kind_; }
+
+    // queries: device, nq x dim (fp32, int8 for INT8). Exactly one of
+    // (out_dist, out_rows) or out_cand is used.
+    void search_device(const void* queries, size_t nq, size_t k, const uint32_t* mask,
+                       uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
+                       cudaStream_t stream) const;
+
+private:
+    void reserve(size_t rows);
+
+    int device_;
+    int metric_;
+    int precision_;
+    OperandKind kind_;
+    uint32_t dim_, d_pad_, elem_bytes_;
+    size_t n_ = 0, capacity_ = 0;
+    DeviceBuffer ops_, ops_lo_, norms_;
+};
+
+// Final merge over candidate lists (see merge_topk_kernel).
+void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,
+                      uint64_t stride_q, uint64_t stride_l, int metric, float* out_dist,
+                      int64_t* out_rows, uint2* out_cand, cudaStream_t stream);
+
+int read_and_clear_device_error(int device);
+
+}  // namespace eb

@@ -1,0 +1,373 @@
+// Fused exact k-NN search: query-tile x base-tile distance GEMM on the
+// tcgen05 tensor cores with the accumulator in TMEM, and a per-query top-k
+// filter fused into the TMEM read-back, so the Q x N distance matrix never
+// reaches HBM.
+//
+// Replaces the reference's exhaustive scan ExactIndex::search
+// (src/ExactIndex.cpp:55-87) and the GpuPort::compute_distances_batch +
+// top_k pair that GpuBruteForceIndex::search_batch chains through a host
+// Q x N matrix (src/gpu_engine/GpuSearchPipeline.cpp:10-41).
+//
+// Work decomposition. Queries are tiled by 128 (one TMEM lane each), base rows
+// by BN. The base is cut into S contiguous splits; a work unit is one
+// (query tile, split) pair and writes that split's k best candidates per
+// query to `partial[q][s][0..k)`. Units are ordered split-major so the CTAs
+// resident at any time share the same base region, which then streams from
+// HBM once and is re-read from L2 by every query tile.
+//
+// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator and
+// MMA issuer, warps 2-5 = epilogue (thread = one query = one TMEM lane).
+#pragma once
+
+#include <cstdint>
+
+#include "ptx.cuh"
+#include "select.cuh"
+
+namespace eb {
+
+enum class OperandKind : int { F16 = 0, BF16 = 1, TF32X3 = 2, I8 = 3 };
+
+enum MetricId : int { kCosine = 0, kEuclidean = 1, kDot = 2 };  // elips::Metric order
+
+constexpr int kTileM = 128;           // queries per tile = TMEM lanes
+constexpr int kKBlockBytes = 128;     // K bytes per pipeline stage (one swizzle atom)
+constexpr int kExactThreads = 192;
+
+struct ExactParams {
+    const float* base_norms;   // [n] squared norms (euclidean only)
+    const float* query_norms;  // [nq] squared norms (euclidean only)
+    const uint32_t* mask;      // [ceil(n/32)] eligibility bits, or null
+    uint2* cand;               // [gridDim.x][128][cap] per-query candidate lists
+    uint2* partial;            // [nq][splits][k]
+    uint32_t n, nq, k, cap, splits, n_qt, n_bt, num_units, kblocks;
+    uint32_t row_offset;       // added to every emitted row (shard base)
+    int metric;
+};
+
+template <OperandKind KIND>
+struct KindTraits;
+template <>
+struct KindTraits<OperandKind::F16> {
+    static constexpr MmaKind mma = MmaKind::F16;
+    static constexpr uint32_t idesc_fmt = 0, c_fmt = 1, elem_bytes = 2;
+    static constexpr bool x3 = false, integer = false;
+};
+template <>
+struct KindTraits<OperandKind::BF16> {
+    static constexpr MmaKind mma = MmaKind::F16;
+    static constexpr uint32_t idesc_fmt = 1, c_fmt = 1, elem_bytes = 2;
+    static constexpr bool x3 = false, integer = false;
+};
+template <>
+struct KindTraits<OperandKind::TF32X3> {
+    static constexpr MmaKind mma = MmaKind::TF32;
+    static constexpr uint32_t idesc_fmt = 2, c_fmt = 1, elem_bytes = 4;
+    static constexpr bool x3 = true, integer = false;
+};
+template <>
+struct KindTraits<OperandKind::I8> {
+    static constexpr MmaKind mma = MmaKind::I8;
+    static constexpr uint32_t idesc_fmt = 1, c_fmt = 2, elem_bytes = 1;
+    static constexpr bool x3 = false, integer = true;
+};
+
+template <OperandKind KIND, int BN, int STAGES>
+struct ExactConfig {
+    using T = KindTraits<KIND>;
+    static constexpr uint32_t kABytes = kTileM * kKBlockBytes;
+    static constexpr uint32_t kBBytes = BN * kKBlockBytes;
+    static constexpr uint32_t kOperands = T::x3 ? 2 : 1;
+    static constexpr uint32_t kStageBytes = (kABytes + kBBytes) * kOperands;
+    static constexpr uint32_t kTmemCols = 2 * BN;
+    static constexpr uint32_t kElemsPerKBlock = kKBlockBytes / T::elem_bytes;
+    // barriers: full[S], empty[S], tfull[2], tempty[2], mma_done
+    static constexpr uint32_t kBarBytes = 8 * (2 * STAGES + 5);
+    static constexpr uint32_t kMiscOffset = STAGES * kStageBytes;
+    static constexpr uint32_t kHistOffset = kMiscOffset + 256;
+    static constexpr uint32_t kSmemBytes = 1024 /* alignment slack */ + kHistOffset + 4 * 1024;
+    static_assert(kBarBytes + 16 <= 256, "barrier area");
+    static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
+};
+
+__device__ __forceinline__ bool drain_wait(uint32_t bar, uint32_t parity) {
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - start > kWaitTimeoutCycles) {
+            record_device_error(kDevErrWaitTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+template <OperandKind KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(kExactThreads, 1)
+    exact_topk_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                      const __grid_constant__ CUtensorMap tm_a_lo,
+                      const __grid_constant__ CUtensorMap tm_b_lo, const __grid_constant__ ExactParams p) {
+    using Cfg = ExactConfig<KIND, BN, STAGES>;
+    using Tr = KindTraits<KIND>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (sbase - raw);
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31u;
+
+    const uint32_t bar0 = sbase + Cfg::kMiscOffset;
+    auto full_bar = [&](uint32_t s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](uint32_t a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](uint32_t a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    const uint32_t mma_done_bar = bar0 + 8u * (2 * STAGES + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOffset + Cfg::kBarBytes);
+    volatile int* abort_flag =
+        reinterpret_cast<volatile int*>(smem + Cfg::kMiscOffset + Cfg::kBarBytes + 8);
+
+    // stage s: A at s*stage, B after A (then A_lo, B_lo for the 3xTF32 split)
+    auto a_addr = [&](uint32_t s) { return sbase + s * Cfg::kStageBytes; };
+    auto b_addr = [&](uint32_t s) { return a_addr(s) + Cfg::kABytes; };
+    auto alo_addr = [&](uint32_t s) { return b_addr(s) + Cfg::kBBytes; };
+    auto blo_addr = [&](uint32_t s) { return alo_addr(s) + Cfg::kABytes; };
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (uint32_t a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 4);
+        }
+        mbar_init(mma_done_bar, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const uint32_t num_units = p.num_units;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (elect_one_sync()) {
+            tma_prefetch_desc(&tm_a);
+            tma_prefetch_desc(&tm_b);
+            if constexpr (Tr::x3) {
+                tma_prefetch_desc(&tm_a_lo);
+                tma_prefetch_desc(&tm_b_lo);
+            }
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_mask = 0, issued_parity = 0;
+            bool ok = true;
+            for (uint32_t unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+                const uint32_t qt = unit % p.n_qt, sp = unit / p.n_qt;
+                const uint32_t bt0 = static_cast<uint32_t>((uint64_t)sp * p.n_bt / p.splits);
+                const uint32_t bt1 = static_cast<uint32_t>((uint64_t)(sp + 1) * p.n_bt / p.splits);
+                for (uint32_t bt = bt0; ok && bt < bt1; ++bt) {
+                    for (uint32_t kb = 0; kb < p.kblocks; ++kb) {
+                        if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
+                        const int32_t x = static_cast<int32_t>(kb * Cfg::kElemsPerKBlock);
+                        tma_load_2d(a_addr(stage), &tm_a, full_bar(stage), x,
+                                    static_cast<int32_t>(qt * kTileM));
+                        tma_load_2d(b_addr(stage), &tm_b, full_bar(stage), x,
+                                    static_cast<int32_t>(bt * BN));
+                        if constexpr (Tr::x3) {
+                            tma_load_2d(alo_addr(stage), &tm_a_lo, full_bar(stage), x,
+                                        static_cast<int32_t>(qt * kTileM));
+                            tma_load_2d(blo_addr(stage), &tm_b_lo, full_bar(stage), x,
+                                        static_cast<int32_t>(bt * BN));
+                        }
+                        issued_mask |= 1u << stage;
+                        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                }
+            }
+            // Every load this thread issued must land before the CTA exits.
+            for (uint32_t s = 0; s < STAGES; ++s) {
+                if (issued_mask & (1u << s)) drain_wait(full_bar(s), (issued_parity >> s) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (elect_one_sync()) {
+            constexpr uint32_t idesc = make_idesc(Tr::c_fmt, Tr::idesc_fmt, kTileM, BN);
+            uint32_t stage = 0, phase = 0, tile_iter = 0;
+            bool ok = true;
+            for (uint32_t unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+                const uint32_t sp = unit / p.n_qt;
+                const uint32_t bt0 = static_cast<uint32_t>((uint64_t)sp * p.n_bt / p.splits);
+                const uint32_t bt1 = static_cast<uint32_t>((uint64_t)(sp + 1) * p.n_bt / p.splits);
+                for (uint32_t bt = bt0; ok && bt < bt1; ++bt, ++tile_iter) {
+                    const uint32_t acc = tile_iter & 1u;
+                    const uint32_t acc_phase = (tile_iter >> 1) & 1u;
+                    if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + acc * BN;
+                    for (uint32_t kb = 0; kb < p.kblocks; ++kb) {
+                        if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+#pragma unroll
+                        for (uint32_t k = 0; k < 4; ++k) {
+                            const uint32_t first = (kb == 0 && k == 0) ? 0u : 1u;
+                            const uint64_t ad = smem_desc_k128(a_addr(stage) + 32u * k);
+                            const uint64_t bd = smem_desc_k128(b_addr(stage) + 32u * k);
+                            if constexpr (Tr::x3) {
+                                const uint64_t adl = smem_desc_k128(alo_addr(stage) + 32u * k);
+                                const uint64_t bdl = smem_desc_k128(blo_addr(stage) + 32u * k);
+                                tc_mma<Tr::mma>(d_tmem, adl, bd, idesc, first);
+                                tc_mma<Tr::mma>(d_tmem, ad, bdl, idesc, 1u);
+                                tc_mma<Tr::mma>(d_tmem, ad, bd, idesc, 1u);
+                            } else {
+                                tc_mma<Tr::mma>(d_tmem, ad, bd, idesc, first);
+                            }
+                        }
+                        tc_commit(empty_bar(stage));
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    tc_commit(tfull_bar(acc));
+                }
+            }
+            // All MMAs this thread issued must finish before TMEM is freed.
+            tc_commit(mma_done_bar);
+            drain_wait(mma_done_bar, 0);
+        }
+    } else {
+        // ------------------------------------------------ epilogue
+        const uint32_t quad = warp & 3u;              // TMEM lane quadrant of this warp
+        const uint32_t lane_row = quad * 32u + lane;  // query row within the tile
+        uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Cfg::kHistOffset) + (warp - 2u) * 256u;
+        uint2* my_list = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + lane_row) * p.cap;
+        const uint32_t lane_base = (quad * 32u) << 16;
+        uint32_t tile_iter = 0;
+        bool ok = true;
+        for (uint32_t unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+            const uint32_t qt = unit % p.n_qt, sp = unit / p.n_qt;
+            const uint32_t bt0 = static_cast<uint32_t>((uint64_t)sp * p.n_bt / p.splits);
+            const uint32_t bt1 = static_cast<uint32_t>((uint64_t)(sp + 1) * p.n_bt / p.splits);
+            const uint32_t q = qt * kTileM + lane_row;
+            const bool qvalid = q < p.nq;
+            float qn = 0.0f;
+            if (p.metric == kEuclidean && qvalid) qn = p.query_norms[q];
+            float tau = __int_as_float(0x7f800000);  // +inf
+            uint32_t cnt = 0;
+            for (uint32_t bt = bt0; bt < bt1; ++bt, ++tile_iter) {
+                const uint32_t acc = tile_iter & 1u;
+                const uint32_t acc_phase = (tile_iter >> 1) & 1u;
+                ok = mbar_wait(tfull_bar(acc), acc_phase, abort_flag);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t row_tile = bt * BN;
+#pragma unroll 1
+                for (uint32_t c = 0; c < BN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + c * 32u, v);
+                    tmem_wait_ld();
+                    if (c == BN / 32 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(tempty_bar(acc));
+                    }
+                    const uint32_t row0 = row_tile + c * 32u;
+                    if (row0 >= p.n) continue;
+                    const uint32_t valid_rows = min(32u, p.n - row0);
+                    uint32_t mword = valid_rows == 32u ? 0xFFFFFFFFu : ((1u << valid_rows) - 1u);
+                    if (p.mask != nullptr) mword &= __ldg(p.mask + (row0 >> 5));
+                    float xn = 0.0f;
+                    if (p.metric == kEuclidean && lane < valid_rows) xn = __ldg(p.base_norms + row0 + lane);
+                    if (!qvalid) mword = 0;
+#pragma unroll
+                    for (uint32_t i = 0; i < 32; ++i) {
+                        float key;
+                        if constexpr (Tr::integer) {
+                            key = -static_cast<float>(static_cast<int32_t>(v[i]));
+                        } else {
+                            const float a = __uint_as_float(v[i]);
+                            if (p.metric == kCosine) {
+                                key = 1.0f - a;
+                            } else if (p.metric == kDot) {
+                                key = -a;
+                            } else {
+                                const float xi = __shfl_sync(0xffffffffu, xn, i);
+                                key = fmaf(-2.0f, a, qn + xi);
+                            }
+                        }
+                        if (((mword >> i) & 1u) && key < tau) {
+                            my_list[cnt] = make_uint2(__float_as_uint(key), p.row_offset + row0 + i);
+                            ++cnt;
+                        }
+                    }
+                    // Keep room for one more chunk: compact any list that could overflow.
+                    __syncwarp();
+                    uint32_t need = __ballot_sync(0xffffffffu, cnt + 32u > p.cap);
+                    while (need) {
+                        const uint32_t L = __ffs(need) - 1;
+                        const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
+                        uint2* list_l = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + quad * 32u + L) * p.cap;
+                        const float th = warp_compact_list(list_l, cnt_l, p.k, hist);
+                        if (lane == L) {
+                            tau = th;
+                            cnt = p.k;
+                        }
+                        need &= need - 1;
+                    }
+                }
+            }
+            if (!ok) break;
+            // End of unit: reduce every list to its k best, then publish.
+            __syncwarp();
+            uint32_t need = __ballot_sync(0xffffffffu, cnt > p.k);
+            while (need) {
+                const uint32_t L = __ffs(need) - 1;
+                const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
+                uint2* list_l = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + quad * 32u + L) * p.cap;
+                warp_compact_list(list_l, cnt_l, p.k, hist);
+                if (lane == L) cnt = p.k;
+                need &= need - 1;
+            }
+            if (qvalid) {
+                uint2* out = p.partial + (static_cast<size_t>(q) * p.splits + sp) * p.k;
+                for (uint32_t i = 0; i < p.k; ++i) {
+                    out[i] = i < cnt ? my_list[i] : make_uint2(0x7f800000u, 0xFFFFFFFFu);
+                }
+            }
+            __syncwarp();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+}  // namespace eb

@@ -1,0 +1,106 @@
+// Warp-cooperative k-selection over candidate lists held in global memory.
+//
+// A candidate is a uint2 {float key bits, row}. Lists are kept in ascending
+// row order (candidates are appended in scan order and every compaction below
+// is stable), so "ascending (key, row)" order equals "ascending key, earlier
+// position first" and a 32-bit radix select on the key plus a stable
+// tie-break by position reproduces the (key, row) order exactly.
+#pragma once
+
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace eb {
+
+// Finds the k-th smallest ordered key (1-based rank k) among list[0, count)
+// with a 4-pass, 8-bit radix select. hist is a 256-word shared-memory scratch
+// owned by this warp. On return *kth_key is the ordered key of rank k and
+// *need_eq is how many entries equal to it belong to the k smallest.
+// Requires 1 <= k <= count. Must be called by the whole warp.
+__device__ __forceinline__ void warp_radix_select(const uint2* list, uint32_t count, uint32_t k,
+                                                  uint32_t* hist, uint32_t* kth_key,
+                                                  uint32_t* need_eq) {
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t prefix = 0, prefix_mask = 0, rank = k;
+#pragma unroll 1
+    for (int pass = 0; pass < 4; ++pass) {
+        const uint32_t shift = 24u - 8u * static_cast<uint32_t>(pass);
+        for (uint32_t b = lane; b < 256; b += 32) hist[b] = 0;
+        __syncwarp();
+        for (uint32_t j = lane; j < count; j += 32) {
+            const uint32_t u = ordered_key(__uint_as_float(list[j].x));
+            if ((u & prefix_mask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        // lane owns bins [8*lane, 8*lane + 8)
+        uint32_t bins[8];
+        uint32_t local = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            bins[i] = hist[lane * 8 + i];
+            local += bins[i];
+        }
+        uint32_t incl = local;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= static_cast<uint32_t>(off)) incl += t;
+        }
+        const uint32_t excl = incl - local;
+        const bool mine = excl < rank && rank <= incl;
+        uint32_t digit = 0, before = excl;
+        if (mine) {
+            uint32_t acc = excl;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (acc + bins[i] >= rank) {
+                    digit = lane * 8 + i;
+                    before = acc;
+                    break;
+                }
+                acc += bins[i];
+            }
+        }
+        const uint32_t owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+        digit = __shfl_sync(0xffffffffu, digit, owner);
+        before = __shfl_sync(0xffffffffu, before, owner);
+        rank -= before;
+        prefix |= digit << shift;
+        prefix_mask |= 255u << shift;
+        __syncwarp();
+    }
+    *kth_key = prefix;
+    *need_eq = rank;
+}
+
+// Stable in-place compaction of list[0, count) down to its k smallest
+// (key, position) entries. Returns the float key of rank k (the new admission
+// threshold: later candidates need key < threshold). Whole warp.
+__device__ __forceinline__ float warp_compact_list(uint2* list, uint32_t count, uint32_t k,
+                                                   uint32_t* hist) {
+    uint32_t kth, need_eq;
+    warp_radix_select(list, count, k, hist, &kth, &need_eq);
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t lt_mask = lanemask_lt();
+    uint32_t w = 0, eq_taken = 0;
+    for (uint32_t j0 = 0; j0 < count; j0 += 32) {
+        const uint32_t j = j0 + lane;
+        uint2 e = make_uint2(0u, 0u);
+        if (j < count) e = list[j];
+        const uint32_t u = ordered_key(__uint_as_float(e.x));
+        const bool lt = j < count && u < kth;
+        const bool eq = j < count && u == kth;
+        const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
+        const uint32_t eq_rank = eq_taken + __popc(eq_mask & lt_mask);
+        const bool keep = lt || (eq && eq_rank < need_eq);
+        const uint32_t keep_mask = __ballot_sync(0xffffffffu, keep);
+        if (keep) list[w + __popc(keep_mask & lt_mask)] = e;
+        w += __popc(keep_mask);
+        eq_taken += __popc(eq_mask);
+    }
+    __syncwarp();
+    return key_to_float(kth);
+}
+
+}  // namespace eb

@@ -1,0 +1,160 @@
+"""Exact (brute-force) k-NN index on one B200.
+
+Mirrors the reference's exhaustive index interface: ExactIndex
+(include/elips/index_engine/ExactIndex.hpp:26-66; search at
+src/ExactIndex.cpp:55-87) and GpuBruteForceIndex::search_batch
+(src/gpu_engine/GpuBruteForceIndex.cpp:152-170). Rows are identified by their
+insertion slot (0, 1, 2, ...); the caller keeps the slot -> RecordID map, as
+GpuBruteForceIndex keeps `ids_`.
+
+Distances follow src/Metrics.cpp:104-115 (cosine = 1 - dot on pre-normalised
+vectors, euclidean = sqrt of the squared L2, dot_product = -dot); results are
+ascending by (distance, slot).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _capi as capi
+
+METRICS = {"cosine": capi.METRIC_COSINE, "euclidean": capi.METRIC_EUCLIDEAN,
+           "dot_product": capi.METRIC_DOT_PRODUCT}
+PRECISIONS = {"fp32": capi.PRECISION_FP32, "fp16": capi.PRECISION_FP16,
+              "int8": capi.PRECISION_INT8, "auto": capi.PRECISION_AUTO,
+              "bf16": capi.PRECISION_BF16}
+
+
+class DimensionMismatch(ValueError):
+    """Raised where the reference throws elips::DimensionMismatch
+    (src/ExactIndex.cpp:14-20)."""
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class ExactIndex:
+    """Device-resident exhaustive index searched by the fused tensor-core kernel.
+
+    precision: "fp32" (3xTF32, fp32-exact ranking), "fp16", "bf16", or "int8"
+    (symmetric int8 codec: int8 rows and queries, dot_product only, exact int32
+    scores).
+    """
+
+    def __init__(self, metric: str, dimension: int, precision: str = "fp32", device: int = 0):
+        if metric not in METRICS:
+            raise ValueError(f"unknown metric {metric!r}")
+        if precision not in PRECISIONS:
+            raise ValueError(f"unknown precision {precision!r}")
+        self.metric = metric
+        self.dimension = int(dimension)
+        self.precision = precision
+        self.device = int(device)
+        self._in_dtype = np.int8 if precision == "int8" else np.float32
+        handle = ctypes.c_void_p()
+        capi.check(capi.LIB.elips_b200_exact_create(self.device, METRICS[metric], PRECISIONS[precision],
+                                                    self.dimension, ctypes.byref(handle)),
+                   "elips_b200_exact_create")
+        self._h = handle
+
+    # -- IndexPort ---------------------------------------------------------
+    def add(self, rows: np.ndarray) -> None:
+        """Appends rows (n x dimension) to the next slots."""
+        rows = np.ascontiguousarray(rows, dtype=self._in_dtype)
+        if rows.ndim != 2 or rows.shape[1] != self.dimension:
+            raise DimensionMismatch("vector dimension does not match index")
+        capi.check(capi.LIB.elips_b200_exact_add(self._h, _ptr(rows), rows.shape[0]),
+                   "elips_b200_exact_add")
+
+    def insert(self, vector: np.ndarray) -> None:
+        self.add(np.asarray(vector, dtype=self._in_dtype).reshape(1, -1))
+
+    def size(self) -> int:
+        n = ctypes.c_size_t(0)
+        capi.check(capi.LIB.elips_b200_exact_size(self._h, ctypes.byref(n)), "elips_b200_exact_size")
+        return n.value
+
+    def search(self, query: np.ndarray, k: int) -> list[tuple[int, float]]:
+        """IndexPort::search for one query: up to k (slot, distance) pairs."""
+        d, r = self.search_batch(np.asarray(query).reshape(1, -1), k)
+        return [(int(r[0, i]), float(d[0, i])) for i in range(d.shape[1]) if r[0, i] >= 0]
+
+    def search_batch(self, queries: np.ndarray, k: int,
+                     mask: Optional[np.ndarray] = None) -> tuple[np.ndarray, np.ndarray]:
+        """Host arrays in, host arrays out: (distances [nq, k] fp32, slots [nq, k] int64).
+        Unfilled slots hold (+inf, -1). mask: uint32 words, bit i = slot i eligible."""
+        q = np.ascontiguousarray(queries, dtype=self._in_dtype)
+        if q.ndim != 2 or q.shape[1] != self.dimension:
+            raise DimensionMismatch("query dimension does not match index")
+        nq = q.shape[0]
+        dist = np.empty((nq, k), dtype=np.float32)
+        rows = np.empty((nq, k), dtype=np.int64)
+        m = None
+        if mask is not None:
+            m = np.ascontiguousarray(mask, dtype=np.uint32)
+            if m.size < (self.size() + 31) // 32:
+                raise ValueError("mask has fewer words than ceil(size / 32)")
+        capi.check(capi.LIB.elips_b200_exact_search(self._h, _ptr(q), nq, k,
+                                                    _ptr(m) if m is not None else None,
+                                                    _ptr(dist), _ptr(rows)),
+                   "elips_b200_exact_search")
+        return dist, rows
+
+    # -- device-pointer entry points (torch tensors as plumbing) -----------
+    def search_device(self, queries, k: int, mask=None, out_dist=None, out_rows=None, stream=None):
+        """queries: CUDA tensor [nq, dimension] (float32, int8 for int8). Asynchronous on
+        `stream` (default: torch's current stream). Returns (dist, rows) CUDA tensors."""
+        import torch
+        nq = queries.shape[0]
+        if queries.shape[1] != self.dimension:
+            raise DimensionMismatch("query dimension does not match index")
+        if out_dist is None:
+            out_dist = torch.empty((nq, k), dtype=torch.float32, device=queries.device)
+        if out_rows is None:
+            out_rows = torch.empty((nq, k), dtype=torch.int64, device=queries.device)
+        s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_exact_search_device(
+            self._h, queries.data_ptr(), nq, k, mask.data_ptr() if mask is not None else None,
+            out_dist.data_ptr(), out_rows.data_ptr(), s), "elips_b200_exact_search_device")
+        return out_dist, out_rows
+
+    def search_candidates_device(self, queries, k: int, row_offset: int, out_cand, mask=None, stream=None):
+        """Shard-level search: writes [nq, k, 2] uint32-as-int32 candidate pairs to out_cand."""
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_exact_search_candidates_device(
+            self._h, queries.data_ptr(), queries.shape[0], k,
+            mask.data_ptr() if mask is not None else None, row_offset, out_cand.data_ptr(), s),
+            "elips_b200_exact_search_candidates_device")
+        return out_cand
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            capi.LIB.elips_b200_exact_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def merge_candidates_device(cand, lists: int, k: int, metric: str, out_dist=None, out_rows=None,
+                            stream=None):
+    """Final top-k over `lists` blocks of [nq, k] candidate pairs (block-major)."""
+    import torch
+    nq = cand.numel() // (2 * lists * k) if lists else 0
+    dev = cand.device
+    if out_dist is None:
+        out_dist = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    if out_rows is None:
+        out_rows = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    capi.check(capi.LIB.elips_b200_merge_candidates_device(
+        dev.index, cand.data_ptr(), nq, lists, k, METRICS[metric], out_dist.data_ptr(),
+        out_rows.data_ptr(), s), "elips_b200_merge_candidates_device")
+    return out_dist, out_rows

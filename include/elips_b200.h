@@ -1,0 +1,143 @@
+/*
+ * elips_b200.h -- C ABI of the B200 k-NN search backend for ELIPS.
+ *
+ * Plain C types only: no C++ exceptions, no torch types, no CUDA headers.
+ * Every function returns an int status (ELIPS_B200_OK = 0). Streams are
+ * passed as `void*` holding a cudaStream_t (NULL = the legacy default stream).
+ *
+ * Each entry point names the reference interface it replaces (paths relative
+ * to the axiomchronicles/elips source tree).
+ */
+#ifndef ELIPS_B200_H
+#define ELIPS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ELIPS_B200_API __attribute__((visibility("default")))
+#else
+#define ELIPS_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. 1..8 are elips::gpu::GpuError (include/elips/gpu_engine/
+ * GpuPort.hpp:15-24) as (int)GpuError + 1, so a CudaBackend maps them 1:1. */
+enum {
+    ELIPS_B200_OK = 0,
+    ELIPS_B200_DEVICE_NOT_FOUND = 1,
+    ELIPS_B200_INSUFFICIENT_MEMORY = 2,
+    ELIPS_B200_KERNEL_LAUNCH_FAILED = 3,
+    ELIPS_B200_TRANSFER_FAILED = 4,
+    ELIPS_B200_INDEX_BUILD_FAILED = 5,
+    ELIPS_B200_UNSUPPORTED_METRIC = 6,
+    ELIPS_B200_INITIALIZATION_FAILED = 7,
+    ELIPS_B200_BACKEND_UNAVAILABLE = 8,
+    /* IndexPort::search throws DimensionMismatch on a bad query width
+     * (src/ExactIndex.cpp:14-20); across a C ABI that becomes this code. */
+    ELIPS_B200_DIMENSION_MISMATCH = 9,
+    ELIPS_B200_INVALID_ARGUMENT = 10,
+    /* A bounded device-side wait expired; the kernel returned early. */
+    ELIPS_B200_DEVICE_TIMEOUT = 11
+};
+
+/* elips::Metric (include/elips/Config.hpp:27). Distances are the reference's
+ * ordering-normalised ones (src/Metrics.cpp:104-115): cosine = 1 - dot,
+ * euclidean = sqrt(sum (a-b)^2), dot_product = -dot; smaller is closer. */
+enum {
+    ELIPS_B200_METRIC_COSINE = 0,
+    ELIPS_B200_METRIC_EUCLIDEAN = 1,
+    ELIPS_B200_METRIC_DOT_PRODUCT = 2
+};
+
+/* elips::gpu::GpuPrecision (include/elips/gpu_engine/GpuConfig.hpp:34) with
+ * BF16 appended. FP32 runs as 3xTF32 on the tensor cores; INT8 is the
+ * symmetric int8 codec (rows and queries are int8, score = -sum q_i*x_i in
+ * exact int32, dot_product metric only). */
+enum {
+    ELIPS_B200_PRECISION_FP32 = 0,
+    ELIPS_B200_PRECISION_FP16 = 1,
+    ELIPS_B200_PRECISION_INT8 = 2,
+    ELIPS_B200_PRECISION_AUTO = 3,
+    ELIPS_B200_PRECISION_BF16 = 4
+};
+
+/* ------------------------------------------------------------- utilities */
+
+/* Human-readable name of a status code (static storage). */
+ELIPS_B200_API const char* elips_b200_status_string(int status);
+
+/* Number of CUDA devices visible (GpuDeviceManager::probe_all_devices,
+ * src/gpu_engine/GpuDeviceManager.cpp:68-132). */
+ELIPS_B200_API int elips_b200_device_count(int* count_out);
+
+/* Reads and clears the device-side error word of `device` that bounded waits
+ * write on timeout (0 = none). Synchronises the device. */
+ELIPS_B200_API int elips_b200_device_error(int device, int* code_out);
+
+/* ------------------------------------------------ exact brute-force index */
+/* Replaces ExactIndex (include/elips/index_engine/ExactIndex.hpp:26-66) and
+ * GpuBruteForceIndex (src/gpu_engine/GpuBruteForceIndex.cpp:77-170): a
+ * device-resident base set searched by the fused tensor-core kernel. */
+
+typedef struct elips_b200_exact elips_b200_exact;
+
+/* GpuBruteForceIndex(backend, metric, dimension, config) with
+ * config.search_precision = precision. */
+ELIPS_B200_API int elips_b200_exact_create(int device, int metric, int precision, uint32_t dimension,
+                            elips_b200_exact** out);
+
+/* IndexPort::insert for n rows at once (ExactIndex.cpp:24-35; row i of the
+ * call gets the next slot). rows: HOST memory, n x dimension, fp32 (int8 for
+ * PRECISION_INT8). */
+ELIPS_B200_API int elips_b200_exact_add(elips_b200_exact* index, const void* rows, size_t n);
+
+/* IndexPort::size. */
+ELIPS_B200_API int elips_b200_exact_size(const elips_b200_exact* index, size_t* n_out);
+
+ELIPS_B200_API int elips_b200_exact_destroy(elips_b200_exact* index);
+
+/* GpuIndexPort::search_batch (GpuIndexPort.hpp:120-124) / ExactIndex::search
+ * (ExactIndex.cpp:55-87) for nq queries. HOST pointers; synchronous.
+ * queries: nq x dimension fp32 (int8 for PRECISION_INT8). mask: optional
+ * eligibility bitmask over slots (bit i&31 of word i>>5), the dense form of
+ * MetadataIndex::exact_candidates (src/MetadataIndex.cpp:66-99), or NULL.
+ * Output nq x k, ascending by (distance, slot); slots past the number of
+ * eligible rows hold distance +inf and slot -1. */
+ELIPS_B200_API int elips_b200_exact_search(const elips_b200_exact* index, const void* queries, size_t nq,
+                            size_t k, const uint32_t* mask, float* out_dist, int64_t* out_rows);
+
+/* Same search with DEVICE pointers, asynchronous on `stream`. */
+ELIPS_B200_API int elips_b200_exact_search_device(const elips_b200_exact* index, const void* queries,
+                                   size_t nq, size_t k, const uint32_t* mask, float* out_dist,
+                                   int64_t* out_rows, void* stream);
+
+/* Shard-level search for row-sharded multi-GPU search
+ * (GpuDistributedIndex::search_batch, src/gpu_engine/GpuDistributedIndex.cpp:
+ * 155-207): DEVICE pointers; writes nq x k candidates as pairs of uint32
+ * {ordering key bits, row_offset + slot} to out_cand (2*nq*k words), unsorted,
+ * padded with {+inf, 0xFFFFFFFF}. The key is the distance before the final
+ * square root for euclidean. */
+ELIPS_B200_API int elips_b200_exact_search_candidates_device(const elips_b200_exact* index,
+                                              const void* queries, size_t nq, size_t k,
+                                              const uint32_t* mask, uint32_t row_offset,
+                                              uint32_t* out_cand, void* stream);
+
+/* Final top-k over candidate lists (GpuDistributedIndex::merge_hits,
+ * src/gpu_engine/GpuDistributedIndex.cpp:68-83): cand holds `lists` blocks of
+ * nq x k pairs as written above, block-major (block l = one shard's output for
+ * every query, e.g. an all-gather over `lists` ranks); 2*lists*nq*k words,
+ * DEVICE. Writes the k best per query ascending by (distance, row), applying
+ * the metric's final transform (square root for euclidean). */
+ELIPS_B200_API int elips_b200_merge_candidates_device(int device, const uint32_t* cand, size_t nq,
+                                       size_t lists, size_t k, int metric, float* out_dist,
+                                       int64_t* out_rows, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ELIPS_B200_H */

@@ -1,0 +1,337 @@
+"""CPU checkers for the parity tests. TEST INFRASTRUCTURE ONLY.
+
+Two libraries, both built by oracle/Makefile:
+  * liboracle.so             -- oracle.c, a C restatement of the reference's
+                                search arithmetic (each function cites the
+                                reference file:line it follows);
+  * _ref/libelips_ref.so     -- the reference's own sources compiled in place
+                                plus ref_driver.cpp, used to pin the
+                                restatement and as the timed CPU baseline.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+legs may import this package; the product path (elips_b200/) never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import POINTER, c_float, c_int, c_int64, c_size_t, c_uint8, c_uint32, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "liboracle.so"
+REF_SO = HERE / "_ref" / "libelips_ref.so"
+REF_ROOT = Path(os.environ.get("ELIPS_REF_ROOT", "/root/reference"))
+
+METRIC = {"cosine": 0, "euclidean": 1, "dot_product": 2}
+
+
+def build(ref: bool = True) -> None:
+    """Builds liboracle.so and, when the reference sources are present, _ref."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    if ref and REF_ROOT.exists():
+        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref", f"REF_ROOT={REF_ROOT}"], check=True)
+
+
+_orc = None
+_ref = None
+
+
+def orc() -> ctypes.CDLL:
+    global _orc
+    if _orc is None:
+        if not ORACLE_SO.exists():
+            build(ref=False)
+        _orc = ctypes.CDLL(str(ORACLE_SO))
+        _orc.orc_distance.restype = c_float
+        _orc.orc_distance.argtypes = [c_int, c_void_p, c_void_p, c_size_t]
+        _orc.orc_sq8_lut_distance.restype = c_float
+        _orc.orc_pq_lut_distance.restype = c_float
+        _orc.orc_nearest_centroid.restype = c_uint8
+    return _orc
+
+
+def ref_available() -> bool:
+    return REF_SO.exists() or REF_ROOT.exists()
+
+
+def ref() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        if not REF_SO.exists():
+            build(ref=True)
+        _ref = ctypes.CDLL(str(REF_SO))
+        _ref.ref_distance.restype = c_float
+        _ref.ref_distance.argtypes = [c_int, c_void_p, c_void_p, c_size_t]
+        for name in ("ref_exact_create", "ref_sq8_exact_create", "ref_pq_exact_create", "ref_ivfpq_create"):
+            getattr(_ref, name).restype = c_void_p
+    return _ref
+
+
+def _p(a: np.ndarray):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _threads(n):
+    return int(n) if n else (os.cpu_count() or 1)
+
+
+# ------------------------------------------------------------- restatement
+
+def distance(metric: str, a, b) -> float:
+    a, b = _f32(a), _f32(b)
+    return float(orc().orc_distance(METRIC[metric], _p(a), _p(b), a.size))
+
+
+def exact_search(metric, base, queries, k, nthreads=None, mask=None):
+    base, queries = _f32(base), _f32(queries)
+    n, d = base.shape
+    nq = queries.shape[0]
+    dist = np.empty((nq, k), np.float32)
+    rows = np.empty((nq, k), np.int64)
+    if mask is None:
+        orc().orc_exact_search(METRIC[metric], _p(base), c_size_t(n), c_size_t(d), _p(queries),
+                               c_size_t(nq), c_size_t(k), c_int(_threads(nthreads)), _p(dist), _p(rows))
+    else:
+        m = np.ascontiguousarray(mask, np.uint32)
+        orc().orc_exact_search_masked(METRIC[metric], _p(base), c_size_t(n), c_size_t(d), _p(m),
+                                      _p(queries), c_size_t(nq), c_size_t(k), c_int(_threads(nthreads)),
+                                      _p(dist), _p(rows))
+    return dist, rows
+
+
+def int8_ip_search(base, queries, k, nthreads=None):
+    base = np.ascontiguousarray(base, np.int8)
+    queries = np.ascontiguousarray(queries, np.int8)
+    n, d = base.shape
+    nq = queries.shape[0]
+    dist = np.empty((nq, k), np.float32)
+    rows = np.empty((nq, k), np.int64)
+    orc().orc_int8_ip_search(_p(base), c_size_t(n), c_size_t(d), _p(queries), c_size_t(nq), c_size_t(k),
+                             c_int(_threads(nthreads)), _p(dist), _p(rows))
+    return dist, rows
+
+
+def sq8_train(rows):
+    rows = _f32(rows)
+    n, d = rows.shape
+    mins = np.empty(d, np.float32)
+    scales = np.empty(d, np.float32)
+    orc().orc_sq8_train(c_size_t(d), _p(rows), c_size_t(n), _p(mins), _p(scales))
+    return mins, scales
+
+
+def sq8_encode(mins, scales, rows):
+    rows = _f32(rows)
+    n, d = rows.shape
+    codes = np.empty((n, d), np.uint8)
+    orc().orc_sq8_encode(c_size_t(d), _p(_f32(mins)), _p(_f32(scales)), _p(rows), c_size_t(n), _p(codes))
+    return codes
+
+
+def sq8_search(metric, mins, scales, codes, queries, k, nthreads=None):
+    codes = np.ascontiguousarray(codes, np.uint8)
+    queries = _f32(queries)
+    n, d = codes.shape
+    nq = queries.shape[0]
+    dist = np.empty((nq, k), np.float32)
+    rows = np.empty((nq, k), np.int64)
+    orc().orc_sq8_search(METRIC[metric], c_size_t(d), _p(_f32(mins)), _p(_f32(scales)), _p(codes),
+                         c_size_t(n), _p(queries), c_size_t(nq), c_size_t(k), c_int(_threads(nthreads)),
+                         _p(dist), _p(rows))
+    return dist, rows
+
+
+def pq_search(metric, codebook, codes, queries, k, nthreads=None):
+    codebook = _f32(codebook)
+    m, ksub, sub = codebook.shape
+    codes = np.ascontiguousarray(codes, np.uint8)
+    queries = _f32(queries)
+    n = codes.shape[0]
+    nq, d = queries.shape
+    dist = np.empty((nq, k), np.float32)
+    rows = np.empty((nq, k), np.int64)
+    orc().orc_pq_search(METRIC[metric], c_size_t(d), c_size_t(m), c_size_t(ksub), _p(codebook), _p(codes),
+                        c_size_t(n), _p(queries), c_size_t(nq), c_size_t(k), c_int(_threads(nthreads)),
+                        _p(dist), _p(rows))
+    return dist, rows
+
+
+def encode_pq(codebook, rows):
+    codebook = _f32(codebook)
+    m, ksub, sub = codebook.shape
+    rows = _f32(rows)
+    n, d = rows.shape
+    codes = np.empty((n, m), np.uint8)
+    orc().orc_encode_pq(_p(rows), _p(codebook), c_size_t(n), c_size_t(d), c_size_t(m), c_size_t(ksub),
+                        _p(codes))
+    return codes
+
+
+def kmeans(rows, k, iters):
+    rows = _f32(rows)
+    n, d = rows.shape
+    cent = np.empty((k, d), np.float32)
+    orc().orc_kmeans(_p(rows), c_size_t(n), c_size_t(d), c_size_t(k), c_size_t(iters), _p(cent))
+    return cent
+
+
+def ivf_assign(metric, rows, centroids):
+    rows, centroids = _f32(rows), _f32(centroids)
+    out = np.empty(rows.shape[0], np.uint32)
+    orc().orc_ivf_assign(METRIC[metric], _p(rows), c_size_t(rows.shape[0]), c_size_t(rows.shape[1]),
+                         _p(centroids), c_size_t(centroids.shape[0]), _p(out))
+    return out
+
+
+def lists_csr(assignments, nlist):
+    """Members of each list in ascending row order (IvfIndexState.cpp:75-83)."""
+    assignments = np.asarray(assignments, np.uint32)
+    order = np.argsort(assignments, kind="stable").astype(np.uint32)
+    counts = np.bincount(assignments, minlength=nlist)
+    offsets = np.zeros(nlist + 1, np.uint32)
+    offsets[1:] = np.cumsum(counts)
+    return offsets, order
+
+
+def ivfpq_search(metric, centroids, codebook, codes, vectors, assignments, queries, nprobe, k, nthreads=None):
+    centroids, codebook, vectors, queries = _f32(centroids), _f32(codebook), _f32(vectors), _f32(queries)
+    nlist, d = centroids.shape
+    m, ksub, sub = codebook.shape
+    offsets, order = lists_csr(assignments, nlist)
+    codes = np.ascontiguousarray(codes, np.uint8)
+    nq = queries.shape[0]
+    dist = np.empty((nq, k), np.float32)
+    rows = np.empty((nq, k), np.int64)
+    orc().orc_ivfpq_search(METRIC[metric], c_size_t(d), c_size_t(m), c_size_t(ksub), c_size_t(nlist),
+                           c_size_t(nprobe), _p(centroids), _p(codebook), _p(codes), _p(vectors), _p(offsets),
+                           _p(order), _p(queries), c_size_t(nq), c_size_t(k), c_int(_threads(nthreads)),
+                           _p(dist), _p(rows))
+    return dist, rows
+
+
+# --------------------------------------------------- reference, compiled
+
+class RefExactIndex:
+    """The reference's ExactIndex (optionally with its sq8 or PQ codec)."""
+
+    def __init__(self, metric, base, codec=None, mins=None, scales=None, codebook=None, pq_bits=8):
+        base = _f32(base)
+        self.dim = base.shape[1]
+        lib = ref()
+        if codec is None:
+            self.h = lib.ref_exact_create(METRIC[metric], c_uint32(self.dim), _p(base), c_size_t(base.shape[0]))
+        elif codec == "sq8":
+            self.h = lib.ref_sq8_exact_create(METRIC[metric], c_uint32(self.dim), _p(_f32(mins)),
+                                              _p(_f32(scales)), _p(base), c_size_t(base.shape[0]))
+        elif codec == "pq":
+            cb = _f32(codebook)
+            self.h = lib.ref_pq_exact_create(METRIC[metric], c_uint32(self.dim), c_uint32(cb.shape[0]),
+                                             c_uint32(pq_bits), _p(cb), _p(base), c_size_t(base.shape[0]))
+        else:
+            raise ValueError(codec)
+        self.h = c_void_p(self.h)
+
+    def search(self, queries, k, nthreads=None):
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        dist = np.empty((nq, k), np.float32)
+        rows = np.empty((nq, k), np.int64)
+        ref().ref_exact_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+                               c_int(_threads(nthreads)), _p(dist), _p(rows))
+        return dist, rows
+
+    def __del__(self):
+        try:
+            ref().ref_exact_destroy(self.h)
+        except Exception:
+            pass
+
+
+class RefIvfPqIndex:
+    """The reference's GpuIVFPQIndex on a CPU GpuPort, loaded via import_snapshot."""
+
+    def __init__(self, metric, centroids, assignments, codebook, codes, vectors, nprobe, pq_bits=8):
+        centroids, codebook, vectors = _f32(centroids), _f32(codebook), _f32(vectors)
+        assignments = np.ascontiguousarray(assignments, np.uint32)
+        codes = np.ascontiguousarray(codes, np.uint8)
+        self.dim = vectors.shape[1]
+        h = ref().ref_ivfpq_create(METRIC[metric], c_uint32(self.dim), c_size_t(centroids.shape[0]),
+                                   c_size_t(nprobe), c_uint32(codebook.shape[0]), c_uint32(pq_bits),
+                                   _p(centroids), _p(assignments), _p(codebook), _p(codes), _p(vectors),
+                                   c_size_t(vectors.shape[0]))
+        if not h:
+            raise RuntimeError("reference IVF-PQ import_snapshot failed")
+        self.h = c_void_p(h)
+
+    def search(self, queries, k, nthreads=None):
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        dist = np.empty((nq, k), np.float32)
+        rows = np.empty((nq, k), np.int64)
+        ref().ref_ivfpq_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+                               c_int(_threads(nthreads)), _p(dist), _p(rows))
+        return dist, rows
+
+    def __del__(self):
+        try:
+            ref().ref_ivfpq_destroy(self.h)
+        except Exception:
+            pass
+
+
+def ref_distance(metric, a, b):
+    a, b = _f32(a), _f32(b)
+    return float(ref().ref_distance(METRIC[metric], _p(a), _p(b), a.size))
+
+
+def ref_sq8_train(metric, rows):
+    rows = _f32(rows)
+    n, d = rows.shape
+    mins = np.empty(d, np.float32)
+    scales = np.empty(d, np.float32)
+    ref().ref_sq8_train(METRIC[metric], c_uint32(d), _p(rows), c_size_t(n), _p(mins), _p(scales))
+    return mins, scales
+
+
+def ref_sq8_encode(metric, mins, scales, rows):
+    rows = _f32(rows)
+    n, d = rows.shape
+    codes = np.empty((n, d), np.uint8)
+    ref().ref_sq8_encode(METRIC[metric], c_uint32(d), _p(_f32(mins)), _p(_f32(scales)), _p(rows),
+                         c_size_t(n), _p(codes))
+    return codes
+
+
+def ref_train_pq_codebook(rows, m, ksub, iters):
+    rows = _f32(rows)
+    n, d = rows.shape
+    cb = np.empty((m, ksub, d // m), np.float32)
+    ref().ref_train_pq_codebook(_p(rows), c_size_t(n), c_size_t(d), c_size_t(m), c_size_t(ksub),
+                                c_size_t(iters), _p(cb))
+    return cb
+
+
+def ref_encode_pq(codebook, rows):
+    codebook, rows = _f32(codebook), _f32(rows)
+    m, ksub, sub = codebook.shape
+    n, d = rows.shape
+    codes = np.empty((n, m), np.uint8)
+    ref().ref_encode_pq(_p(rows), _p(codebook), c_size_t(n), c_size_t(d), c_size_t(m), c_size_t(ksub),
+                        _p(codes))
+    return codes
+
+
+def ref_kmeans(rows, k, iters):
+    rows = _f32(rows)
+    n, d = rows.shape
+    cent = np.empty((k, d), np.float32)
+    ref().ref_kmeans(_p(rows), c_size_t(n), c_size_t(d), c_size_t(k), c_size_t(iters), _p(cent))
+    return cent

@@ -1,0 +1,341 @@
+// Test infrastructure only: a C-ABI driver over the reference's own compiled
+// classes (ExactIndex, ScalarQuantizer, ProductQuantizer, quant::detail
+// k-means, GpuIVFPQIndex on a CPU GpuPort). It is linked with the reference
+// sources by oracle/Makefile into oracle/_ref/libelips_ref.so, and is used by
+// the tests to pin the C restatement in oracle/oracle.c, to generate golden
+// fixtures, and by bench.py's CPU baseline / reference arm. Nothing in the
+// product path loads it.
+//
+// Row identity: every row i is given RecordID(bytes) whose last eight bytes are
+// i in big-endian order, so search results map back to row indexes
+// deterministically (RecordID.hpp:18 takes raw bytes).
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <span>
+#include <thread>
+#include <vector>
+
+#include "elips/Config.hpp"
+#include "elips/domain/RecordID.hpp"
+#include "elips/gpu_engine/GpuIVFPQIndex.hpp"
+#include "elips/gpu_engine/GpuPort.hpp"
+#include "elips/index_engine/ExactIndex.hpp"
+#include "elips/index_engine/IndexSnapshot.hpp"
+#include "elips/quant_engine/ProductQuantizer.hpp"
+#include "elips/quant_engine/ScalarQuantizer.hpp"
+#include "elips/quant_engine/detail/KMeans.hpp"
+#include "elips/vector_engine/Metrics.hpp"
+
+namespace {
+
+using elips::Metric;
+using elips::RecordID;
+
+RecordID row_id(std::uint64_t row) {
+    RecordID::Bytes b{};
+    for (int i = 0; i < 8; ++i) {
+        b[15 - i] = static_cast<std::uint8_t>(row >> (8 * i));
+    }
+    return RecordID{b};
+}
+
+std::int64_t id_row(const RecordID& id) {
+    std::uint64_t row = 0;
+    for (int i = 8; i < 16; ++i) {
+        row = (row << 8) | id.bytes()[i];
+    }
+    return static_cast<std::int64_t>(row);
+}
+
+// A stateless, thread-safe CPU GpuPort: compute_distances_batch is the
+// reference distance loop and top_k is a partial_sort, the same arithmetic as
+// the reference's own test backend (tests/unit/gpu/TestRecordingBackend.hpp:
+// 75-120). Ties in top_k break by index so repeated runs agree.
+class CpuPort final : public elips::gpu::GpuPort {
+public:
+    std::expected<void, elips::gpu::GpuError> initialize(const elips::gpu::GpuConfig&) override { return {}; }
+    void shutdown() noexcept override {}
+    elips::gpu::GpuDeviceInfo device_info() const noexcept override {
+        elips::gpu::GpuDeviceInfo info;
+        info.name = "cpu-oracle";
+        info.backend = "cpu";
+        info.supports_ivf_pq = true;
+        return info;
+    }
+    bool is_available() const noexcept override { return true; }
+    std::expected<elips::gpu::GpuBuffer, elips::gpu::GpuError> allocate_device(size_t bytes) override {
+        return elips::gpu::GpuBuffer{nullptr, bytes, this};
+    }
+    void free_device(elips::gpu::GpuBuffer) noexcept override {}
+    std::expected<void, elips::gpu::GpuError> upload(const void*, elips::gpu::GpuBuffer&, size_t) override { return {}; }
+    std::expected<void, elips::gpu::GpuError> download(const elips::gpu::GpuBuffer&, void*, size_t) override { return {}; }
+    std::expected<void, elips::gpu::GpuError> compute_distances_batch(
+        std::span<const float> queries, std::span<const float> database,
+        std::span<float> out, size_t nq, size_t nb, size_t dim, Metric metric) override {
+        for (size_t q = 0; q < nq; ++q) {
+            const auto query = queries.subspan(q * dim, dim);
+            for (size_t i = 0; i < nb; ++i) {
+                out[q * nb + i] = elips::distance(metric, query, database.subspan(i * dim, dim));
+            }
+        }
+        return {};
+    }
+    std::expected<void, elips::gpu::GpuError> top_k(
+        std::span<const float> distances, std::span<uint32_t> indices_out,
+        std::span<float> values_out, size_t nq, size_t nb, size_t k) override {
+        for (size_t q = 0; q < nq; ++q) {
+            std::vector<std::pair<float, uint32_t>> ranked(nb);
+            for (size_t i = 0; i < nb; ++i) {
+                ranked[i] = {distances[q * nb + i], static_cast<uint32_t>(i)};
+            }
+            const auto take = std::min(k, nb);
+            std::partial_sort(ranked.begin(), ranked.begin() + static_cast<std::ptrdiff_t>(take),
+                              ranked.end());
+            for (size_t i = 0; i < take; ++i) {
+                indices_out[q * k + i] = ranked[i].second;
+                values_out[q * k + i] = ranked[i].first;
+            }
+        }
+        return {};
+    }
+    void synchronize() override {}
+    bool is_idle() const noexcept override { return true; }
+};
+
+// Runs fn(q) for q in [0, nq) on nthreads std::threads (strided split).
+template <class Fn>
+void parallel_queries(size_t nq, int nthreads, Fn fn) {
+    if (nthreads <= 1 || nq <= 1) {
+        for (size_t q = 0; q < nq; ++q) fn(q);
+        return;
+    }
+    const size_t workers = std::min<size_t>(static_cast<size_t>(nthreads), nq);
+    std::vector<std::thread> pool;
+    pool.reserve(workers);
+    for (size_t w = 0; w < workers; ++w) {
+        pool.emplace_back([&, w] {
+            for (size_t q = w; q < nq; q += workers) fn(q);
+        });
+    }
+    for (auto& t : pool) t.join();
+}
+
+template <class Hit>
+void write_hits(const std::vector<Hit>& hits, size_t k, float* out_dist, std::int64_t* out_rows) {
+    for (size_t i = 0; i < k; ++i) {
+        if (i < hits.size()) {
+            out_dist[i] = hits[i].second;
+            out_rows[i] = id_row(hits[i].first);
+        } else {
+            out_dist[i] = 0.0F;
+            out_rows[i] = -1;
+        }
+    }
+}
+
+struct ExactHandle {
+    std::unique_ptr<elips::ExactIndex> index;
+};
+
+struct IvfPqHandle {
+    CpuPort port;
+    std::unique_ptr<elips::gpu::GpuIVFPQIndex> index;
+};
+
+}  // namespace
+
+extern "C" {
+
+float ref_distance(int metric, const float* a, const float* b, size_t n) {
+    return elips::distance(static_cast<Metric>(metric), std::span<const float>{a, n},
+                           std::span<const float>{b, n});
+}
+
+// ExactIndex over fp32 rows (no quantizer).
+void* ref_exact_create(int metric, uint32_t dim, const float* rows, size_t n) {
+    auto* h = new ExactHandle;
+    h->index = std::make_unique<elips::ExactIndex>(static_cast<Metric>(metric),
+                                                   static_cast<std::uint16_t>(dim));
+    for (size_t i = 0; i < n; ++i) {
+        h->index->insert(row_id(i), std::span<const float>{rows + i * dim, dim});
+    }
+    return h;
+}
+
+// ExactIndex with the reference's sq8 codec built from given mins/scales; the
+// rows are encoded by the reference's own ScalarQuantizer::encode.
+void* ref_sq8_exact_create(int metric, uint32_t dim, const float* mins, const float* scales,
+                           const float* rows, size_t n) {
+    auto q = std::make_shared<elips::quant::ScalarQuantizer>(
+        static_cast<Metric>(metric), static_cast<std::uint16_t>(dim),
+        std::vector<float>(mins, mins + dim), std::vector<float>(scales, scales + dim));
+    auto* h = new ExactHandle;
+    h->index = std::make_unique<elips::ExactIndex>(static_cast<Metric>(metric),
+                                                   static_cast<std::uint16_t>(dim), q);
+    for (size_t i = 0; i < n; ++i) {
+        h->index->insert(row_id(i), std::span<const float>{rows + i * dim, dim});
+    }
+    return h;
+}
+
+// ExactIndex with a plain (non-residual, no rotation) PQ codec built from a
+// given codebook [pq_dim][2^pq_bits][dim/pq_dim].
+void* ref_pq_exact_create(int metric, uint32_t dim, uint32_t pq_dim, uint32_t pq_bits,
+                          const float* codebook, const float* rows, size_t n) {
+    const size_t cb = static_cast<size_t>(pq_dim) * (size_t{1} << pq_bits) * (dim / pq_dim);
+    auto q = std::make_shared<elips::quant::ProductQuantizer>(
+        static_cast<Metric>(metric), static_cast<std::uint16_t>(dim), pq_dim, pq_bits,
+        std::vector<float>(codebook, codebook + cb), std::vector<float>{});
+    auto* h = new ExactHandle;
+    h->index = std::make_unique<elips::ExactIndex>(static_cast<Metric>(metric),
+                                                   static_cast<std::uint16_t>(dim), q);
+    for (size_t i = 0; i < n; ++i) {
+        h->index->insert(row_id(i), std::span<const float>{rows + i * dim, dim});
+    }
+    return h;
+}
+
+int ref_exact_search(void* handle, uint32_t dim, const float* queries, size_t nq, size_t k,
+                     int nthreads, float* out_dist, std::int64_t* out_rows) {
+    auto* h = static_cast<ExactHandle*>(handle);
+    parallel_queries(nq, nthreads, [&](size_t q) {
+        const auto hits = h->index->search(std::span<const float>{queries + q * dim, dim}, k);
+        write_hits(hits, k, out_dist + q * k, out_rows + q * k);
+    });
+    return 0;
+}
+
+void ref_exact_destroy(void* handle) { delete static_cast<ExactHandle*>(handle); }
+
+// ScalarQuantizer::train (ScalarQuantizer.cpp:26-50).
+void ref_sq8_train(int metric, uint32_t dim, const float* rows, size_t n, float* mins_out,
+                   float* scales_out) {
+    auto q = elips::quant::ScalarQuantizer::train(static_cast<Metric>(metric),
+                                                  static_cast<std::uint16_t>(dim),
+                                                  std::span<const float>{rows, n * dim}, n);
+    std::copy(q->mins().begin(), q->mins().end(), mins_out);
+    std::copy(q->scales().begin(), q->scales().end(), scales_out);
+}
+
+// ScalarQuantizer::encode over n rows (ScalarQuantizer.cpp:52-68).
+void ref_sq8_encode(int metric, uint32_t dim, const float* mins, const float* scales,
+                    const float* rows, size_t n, std::uint8_t* codes_out) {
+    elips::quant::ScalarQuantizer q(static_cast<Metric>(metric), static_cast<std::uint16_t>(dim),
+                                    std::vector<float>(mins, mins + dim),
+                                    std::vector<float>(scales, scales + dim));
+    for (size_t i = 0; i < n; ++i) {
+        q.encode(std::span<const float>{rows + i * dim, dim},
+                 std::span<std::uint8_t>{codes_out + i * dim, dim});
+    }
+}
+
+// ScalarQuantizer::make_lut + lut_distance for one query over n codes.
+void ref_sq8_distances(int metric, uint32_t dim, const float* mins, const float* scales,
+                       const float* query, const std::uint8_t* codes, size_t n, float* out) {
+    elips::quant::ScalarQuantizer q(static_cast<Metric>(metric), static_cast<std::uint16_t>(dim),
+                                    std::vector<float>(mins, mins + dim),
+                                    std::vector<float>(scales, scales + dim));
+    const auto lut = q.make_lut(std::span<const float>{query, dim});
+    for (size_t i = 0; i < n; ++i) {
+        out[i] = q.lut_distance(lut, std::span<const std::uint8_t>{codes + i * dim, dim});
+    }
+}
+
+// quant::detail::train_pq_codebook (KMeans.cpp:249-268).
+void ref_train_pq_codebook(const float* rows, size_t n, size_t dim, size_t pq_dim, size_t ksub,
+                           size_t iters, float* codebook_out) {
+    elips::quant::detail::train_pq_codebook(
+        std::span<const float>{rows, n * dim}, n, dim, pq_dim, ksub, iters,
+        std::span<float>{codebook_out, pq_dim * ksub * (dim / pq_dim)});
+}
+
+// quant::detail::encode_pq (KMeans.cpp:270-285).
+void ref_encode_pq(const float* rows, const float* codebook, size_t n, size_t dim, size_t pq_dim,
+                   size_t ksub, std::uint8_t* codes_out) {
+    elips::quant::detail::encode_pq(
+        std::span<const float>{rows, n * dim},
+        std::span<const float>{codebook, pq_dim * ksub * (dim / pq_dim)}, n, dim, pq_dim, ksub,
+        std::span<std::uint8_t>{codes_out, n * pq_dim});
+}
+
+// quant::detail::kmeans (KMeans.cpp:182-247).
+void ref_kmeans(const float* rows, size_t n, size_t dim, size_t k, size_t iters,
+                float* centroids_out) {
+    elips::quant::detail::kmeans(std::span<const float>{rows, n * dim}, n, dim, k, iters,
+                                 std::span<float>{centroids_out, k * dim});
+}
+
+// ProductQuantizer::make_lut + lut_distance for one query over n codes.
+void ref_pq_distances(int metric, uint32_t dim, uint32_t pq_dim, uint32_t pq_bits,
+                      const float* codebook, const float* query, const std::uint8_t* codes,
+                      size_t n, float* out) {
+    const size_t cb = static_cast<size_t>(pq_dim) * (size_t{1} << pq_bits) * (dim / pq_dim);
+    elips::quant::ProductQuantizer q(static_cast<Metric>(metric), static_cast<std::uint16_t>(dim),
+                                     pq_dim, pq_bits, std::vector<float>(codebook, codebook + cb),
+                                     std::vector<float>{});
+    const auto lut = q.make_lut(std::span<const float>{query, dim});
+    for (size_t i = 0; i < n; ++i) {
+        out[i] = q.lut_distance(lut, std::span<const std::uint8_t>{codes + i * pq_dim, pq_dim});
+    }
+}
+
+// GpuIVFPQIndex on the CPU port, loaded through import_snapshot with a model
+// trained elsewhere (GpuIVFPQIndex.cpp:327-348, IvfIndexState.cpp:339-374).
+// codes are the residual PQ codes, one pq_dim-byte row per vector.
+void* ref_ivfpq_create(int metric, uint32_t dim, size_t n_lists, size_t nprobe, uint32_t pq_dim,
+                       uint32_t pq_bits, const float* centroids, const uint32_t* assignments,
+                       const float* codebook, const std::uint8_t* codes, const float* vectors,
+                       size_t n) {
+    auto* h = new IvfPqHandle;
+    elips::gpu::GpuConfig config;
+    config.default_ef_search_gpu = nprobe;
+    config.ivf_pq_params.n_lists = n_lists;
+    config.ivf_pq_params.pq_dim = pq_dim;
+    config.ivf_pq_params.pq_bits = pq_bits;
+    h->index = std::make_unique<elips::gpu::GpuIVFPQIndex>(h->port, static_cast<Metric>(metric),
+                                                           static_cast<std::uint16_t>(dim), config);
+    elips::IndexSnapshot snap;
+    snap.kind = elips::IndexSnapshotKind::gpu_ivf_pq;
+    snap.metric = static_cast<Metric>(metric);
+    snap.dimension = static_cast<std::uint16_t>(dim);
+    snap.ids.reserve(n);
+    for (size_t i = 0; i < n; ++i) snap.ids.push_back(row_id(i));
+    snap.vectors.assign(vectors, vectors + n * dim);
+    elips::IvfSnapshot ivf;
+    ivf.n_lists = n_lists;
+    ivf.n_probe = nprobe;
+    ivf.centroids.assign(centroids, centroids + n_lists * dim);
+    ivf.assignments.assign(assignments, assignments + n);
+    snap.ivf = std::move(ivf);
+    elips::PqSnapshot pq;
+    pq.pq_dim = pq_dim;
+    pq.pq_bits = pq_bits;
+    pq.codebook.assign(codebook,
+                       codebook + static_cast<size_t>(pq_dim) * (size_t{1} << pq_bits) * (dim / pq_dim));
+    pq.codes.assign(codes, codes + n * pq_dim);
+    snap.pq = std::move(pq);
+    auto imported = h->index->import_snapshot(snap);
+    if (!imported.has_value()) {
+        delete h;
+        return nullptr;
+    }
+    return h;
+}
+
+int ref_ivfpq_search(void* handle, uint32_t dim, const float* queries, size_t nq, size_t k,
+                     int nthreads, float* out_dist, std::int64_t* out_rows) {
+    auto* h = static_cast<IvfPqHandle*>(handle);
+    parallel_queries(nq, nthreads, [&](size_t q) {
+        const auto hits = h->index->search(std::span<const float>{queries + q * dim, dim}, k);
+        write_hits(hits, k, out_dist + q * k, out_rows + q * k);
+    });
+    return 0;
+}
+
+void ref_ivfpq_destroy(void* handle) { delete static_cast<IvfPqHandle*>(handle); }
+
+}  // extern "C"
