@@ -1,0 +1,542 @@
+#!/usr/bin/env python3
+"""k-NN search throughput (queries/sec) of the B200 backend, and of the
+reference's CPU path on this host.
+
+Default workload (N=1 and the scaling runs): exact cosine search, fp16 rows,
+base N=2,000,000 x d=768 drawn from a Gaussian mixture (1,024 centroids
+~N(0, I), per-point noise sigma=0.1, L2-normalised), Q=10,000 queries from the
+same mixture, k=100. With N GPUs the base is row-sharded (contiguous ranges,
+as GpuDistributedIndex's split_ids) and the per-rank top-k lists are merged by
+an NCCL all-gather plus the library's merge kernel: total work is fixed, so
+the scaling is strong. One step = one search of all Q queries.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl reference]
+
+Inputs are seeded synthetic data with the configuration's shapes and value
+distributions; the base (>= 2 GB) is larger than L2, so no flush is needed
+between steps for the default workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    "exact_fp16_cosine": dict(
+        workload="exact cosine fp16, N=2,000,000 x d=768 Gaussian mixture (1,024 centroids, sigma=0.1, "
+                 "L2-normalised), Q=10,000, k=100",
+        n=2_000_000, d=768, q=10_000, k=100, metric="cosine", precision="fp16", data="mixture",
+        centroids=1024, sigma=0.1, normalized=True, dtype="f16 (fp32 accumulate)"),
+    "exact_fp32_l2": dict(
+        workload="exact L2 fp32 (3xTF32), N=100,000 x d=128 N(0,1), Q=1,000, k=10",
+        n=100_000, d=128, q=1_000, k=10, metric="euclidean", precision="fp32", data="gaussian",
+        dtype="f32 (3xTF32)"),
+    "int8_ip": dict(
+        workload="int8 inner product, N=5,000,000 x d=1,024 uniform int8 [-127,127], Q=4,096, k=50, int32 accumulate",
+        n=5_000_000, d=1024, q=4096, k=50, metric="dot_product", precision="int8", data="int8",
+        dtype="s8 (int32 accumulate)"),
+    "filtered_bf16_l2": dict(
+        workload="filtered exact L2 bf16, N=1,000,000 x d=384 N(0,1), Bernoulli(0.1) mask, Q=64, k=20",
+        n=1_000_000, d=384, q=64, k=20, metric="euclidean", precision="bf16", data="gaussian",
+        mask_p=0.1, dtype="bf16 (fp32 accumulate)"),
+}
+DEFAULT_CONFIG = "exact_fp16_cosine"
+METRIC_NAME = "k-NN queries/sec (exact d=768 N=2M k=100; IVF-PQ) at 1/2/4/8 B200, % roofline"
+CHUNK = 1 << 16
+SEED = 20261201
+
+
+# ----------------------------------------------------------------- data
+
+def _centroids(cfg, device="cpu"):
+    import torch
+    g = torch.Generator().manual_seed(SEED)
+    return torch.randn(cfg["centroids"], cfg["d"], generator=g).to(device)
+
+
+def _gen_chunk(cfg, c, stream_seed, total, cents, device):
+    import torch
+    g = torch.Generator(device=device).manual_seed(stream_seed * 1_000_003 + c)
+    rows = min(CHUNK, total - c * CHUNK)
+    if cfg["data"] == "mixture":
+        u = torch.randint(0, cents.shape[0], (rows,), generator=g, device=device)
+        x = cents[u] + cfg["sigma"] * torch.randn(rows, cfg["d"], generator=g, device=device)
+        if cfg.get("normalized"):
+            x = x / x.norm(dim=1, keepdim=True)
+    elif cfg["data"] == "gaussian":
+        x = torch.randn(rows, cfg["d"], generator=g, device=device)
+    else:
+        x = torch.randint(-127, 128, (rows, cfg["d"]), generator=g, dtype=torch.int8, device=device)
+    if cfg["precision"] == "fp16":
+        x = x.half().float()
+    elif cfg["precision"] == "bf16":
+        x = x.bfloat16().float()
+    return x
+
+
+def gen_rows(cfg, start: int, count: int, stream_seed: int, total: int, cents=None, device="cpu"):
+    """Rows [start, start+count) of a seeded table of `total` rows, generated in
+    fixed 65,536-row chunks so any rank can produce any range (float32, or int8
+    for the int8 configuration), on `device`. Values are rounded to the
+    configuration's storage precision (fp16 / bf16) and widened back."""
+    import torch
+    from concurrent.futures import ThreadPoolExecutor
+    c0, c1 = start // CHUNK, (start + count - 1) // CHUNK
+    chunks = list(range(c0, c1 + 1))
+    if str(device) == "cpu" and len(chunks) > 1:
+        with ThreadPoolExecutor(max_workers=min(len(chunks), os.cpu_count() or 1)) as ex:
+            parts = list(ex.map(lambda c: _gen_chunk(cfg, c, stream_seed, total, cents, device), chunks))
+    else:
+        parts = [_gen_chunk(cfg, c, stream_seed, total, cents, device) for c in chunks]
+    out = []
+    for c, x in zip(chunks, parts):
+        lo = max(start, c * CHUNK) - c * CHUNK
+        hi = min(start + count, c * CHUNK + x.shape[0]) - c * CHUNK
+        out.append(x[lo:hi])
+    return torch.cat(out).contiguous()
+
+
+def gen_mask_words(cfg, total: int):
+    import torch
+    g = torch.Generator().manual_seed(SEED + 7)
+    bits = (torch.rand(total, generator=g) < cfg["mask_p"]).numpy()
+    words = np.zeros((total + 31) // 32, np.uint32)
+    idx = np.nonzero(bits)[0]
+    np.bitwise_or.at(words, idx >> 5, (np.uint32(1) << (idx & 31).astype(np.uint32)))
+    return words
+
+
+# --------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clock, max clock and clock-event reasons of one GPU through
+    NVML (what nvidia-smi reports) every 100 ms while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, torch_device: int):
+        self.samples = []
+        self.active = False
+        self._stop = threading.Event()
+        self._handle = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(torch_device).uuid)
+            self._handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self._nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # pragma: no cover - depends on the box
+            self.error = f"nvml unavailable: {e}"
+            self.max_mhz = None
+
+    def _run(self):
+        p = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = p.nvmlDeviceGetClockInfo(self._handle, p.NVML_CLOCK_SM)
+                try:
+                    reasons = p.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                except Exception:
+                    reasons = p.nvmlDeviceGetCurrentClocksThrottleReasons(self._handle)
+                self.samples.append((time.perf_counter(), sm, reasons, self.active))
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._handle is not None:
+            self._t.join()
+
+    def summary(self):
+        if self._handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": getattr(self, "error", "")}
+        load = [s for s in self.samples if s[3]] or self.samples
+        mhz = [s[1] for s in load]
+        mask = 0
+        for s in load:
+            mask |= s[2]
+        reasons = sorted(name for bit, name in self.REASONS.items() if mask & bit)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(load)}
+
+
+# ------------------------------------------------------------ helpers
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def load_traffic(config: str, n_shard: int):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary,
+    scaled to this shard's rows when the capture was taken on a smaller case."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text()).get(config)
+    if not d:
+        return None
+    return d["dram_bytes_per_launch"] * n_shard / d["rows"]
+
+
+# ------------------------------------------------------------ b200 arm
+
+def run_b200(args, cfg, world, rank, local):
+    import torch
+    from elips_b200 import ExactIndex, _capi
+    from elips_b200.distributed import ShardedExactIndex, shard_range
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n, d, nq, k = cfg["n"], cfg["d"], cfg["q"], cfg["k"]
+    lo, hi = shard_range(n, rank, world)
+    cents = _centroids(cfg, dev) if cfg["data"] == "mixture" else None
+
+    # ---- build: this rank's shard, generated on the device in chunks
+    t0 = time.perf_counter()
+    index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local)
+    host_base = [] if (world == 1 and not args.no_cpu_baseline) else None
+    step_rows = 1 << 18
+    for r0 in range(lo, hi, step_rows):
+        cnt = min(step_rows, hi - r0)
+        rows = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev)
+        if host_base is not None:
+            host_base.append(rows.cpu().numpy())
+        index.add_device(rows)
+        del rows
+    q_dev = gen_rows(cfg, 0, nq, SEED + 2, nq, cents, device=dev)
+    queries = q_dev.cpu()
+    mask_words = None
+    mask_dev = None
+    if cfg.get("mask_p"):
+        words = gen_mask_words(cfg, n)
+        if world > 1:
+            # each rank's mask covers its own rows, starting at bit 0
+            sub = np.zeros((hi - lo + 31) // 32, np.uint32)
+            idx = np.arange(lo, hi)
+            bits = (words[idx >> 5] >> (idx & 31).astype(np.uint32)) & 1
+            on = np.nonzero(bits)[0]
+            np.bitwise_or.at(sub, on >> 5, (np.uint32(1) << (on & 31).astype(np.uint32)))
+            words = sub
+        mask_words = words
+        mask_dev = torch.from_numpy(words.view(np.int32)).to(dev)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+
+    out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    out_r = torch.empty((nq, k), dtype=torch.int64, device=dev)
+
+    def step():
+        if world == 1:
+            index.local.search_device(q_dev, k, mask=mask_dev, out_dist=out_d, out_rows=out_r)
+        else:
+            index.search_device(q_dev, k, mask=mask_dev)
+
+    # ---- device-resident throughput (value), with the kernel profiler live
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    _capi.profiler_reset()
+    _capi.profiler_enable(True)
+    launches0 = _capi.launch_count()
+    stream = torch.cuda.current_stream(dev)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler:
+        time.sleep(0.25)
+        sampler.active = True
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        sampler.active = False
+    barrier(world)
+    launches = _capi.launch_count() - launches0
+    _capi.profiler_enable(False)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, world)
+    kstats = _capi.profiler_stats("exact_topk")
+    allstats = _capi.profiler_stats(None)
+    ms_per_step = ms_max / args.steps
+    value = nq * args.steps / (ms_max / 1e3)
+
+    # ---- end to end through the public API, host (pinned) buffers
+    q_pin = queries.pin_memory()
+    if world == 1:
+        q_np = q_pin.numpy()
+        od = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+        orr = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+        od_np, or_np = od.numpy(), orr.numpy()
+
+        def e2e_step():
+            index.local.search_batch(q_np, k, mask=mask_words, out_dist=od_np, out_rows=or_np)
+    else:
+        def e2e_step():
+            index.search_batch(q_pin, k)
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier(world)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t, world)
+    barrier(world)
+    in_bytes = queries.numel() * queries.element_size() * world
+    if mask_words is not None:
+        in_bytes += mask_words.nbytes
+    e2e = {"value": round(nq * args.steps / e2e_s, 2), "unit": "queries/s",
+           "h2d_bytes_per_step": int(in_bytes), "d2h_bytes_per_step": int(nq * k * (4 + 8)),
+           "api": "elips_b200_exact_search (host buffers)" if world == 1 else
+                  "ShardedExactIndex.search_batch (host buffers, NCCL all-gather, merge kernel)"}
+
+    # ---- roofline of the dominant kernel (fused GEMM + top-k)
+    peaks, peak_src = load_peaks()
+    n_shard = hi - lo
+    d_pad = (d + 63) // 64 * 64
+    if cfg["precision"] == "int8":
+        flops = 2.0 * nq * n_shard * d
+        peak = 2.0 * peaks["bf16_tflops"]
+        peak_note = f"int8 dense = 2 x {peak_src} bf16 burst"
+    elif cfg["precision"] == "fp32":
+        flops = 2.0 * nq * n_shard * d
+        peak = peaks["bf16_tflops"] / 2.0
+        peak_note = f"tf32 dense = {peak_src} bf16 burst / 2 (3xTF32 issues 3 MMAs per counted flop)"
+    else:
+        flops = 2.0 * nq * n_shard * d
+        long_run = ms_max > 2000
+        peak = peaks["bf16_tflops_sustained"] if long_run else peaks["bf16_tflops"]
+        peak_note = f"{peak_src} bf16 {'sustained' if long_run else 'burst'}"
+    avg_kernel_ms = kstats["total_ms"] / max(1, kstats["launches"])
+    achieved = flops / (avg_kernel_ms / 1e3) / 1e12
+    bytes_alg = n_shard * d * (2 if cfg["precision"] in ("fp16", "bf16") else (1 if cfg["precision"] == "int8" else 4))
+    roofline = {
+        "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+        "frac": round(achieved / peak, 4), "traffic": load_traffic(args.config, n_shard),
+        "kernel": "exact_topk_kernel", "kernel_ms_avg": round(avg_kernel_ms, 4),
+        "kernel_share_of_step": round(kstats["total_ms"] / max(1e-9, allstats["total_ms"]), 4),
+        "algorithmic_flops_per_launch": flops, "algorithmic_bytes_per_launch": bytes_alg,
+        "hbm_time_ms_at_peak": round(bytes_alg / (peaks["hbm_gbs"] * 1e9) * 1e3, 4),
+        "peak_source": peak_note}
+
+    clocks = sampler.summary()
+    result = {
+        "metric": METRIC_NAME, "value": round(value, 2), "unit": "queries/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes and distributions of the configuration)",
+        "config": {"workload": cfg["workload"], "config": args.config, "base_rows": n, "dim": d,
+                   "queries_per_step": nq, "k": k, "metric": cfg["metric"], "precision": cfg["precision"],
+                   "sharding": f"rows split {world} ways (contiguous ranges)" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (base >= 2 GB); no flush"
+                         if n * d * 2 > 126e6 else "L2-resident base; steps back to back"},
+        "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "clocks": clocks,
+        "build_s": round(build_s, 2),
+    }
+    if world == 1 and not args.no_cpu_baseline and rank == 0:
+        result["cpu_baseline"] = cpu_baseline(cfg, np.concatenate(host_base) if host_base else None,
+                                              queries.numpy(), mask_words)
+    return result
+
+
+# ------------------------------------------------------- CPU reference
+
+def _ref_or_port():
+    import oracle
+    try:
+        oracle.ref()
+        return oracle, "reference"
+    except Exception:
+        return oracle, "port"
+
+
+def _cpu_searcher(cfg, base, mask_words):
+    """Returns (search(queries, k, threads), kind, description) for the reference's
+    CPU path on this configuration."""
+    oracle, kind = _ref_or_port()
+    metric = cfg["metric"]
+    if cfg["precision"] == "int8":
+        # No reference int8 codec: time its sq8 ExactIndex path (dot_product) on
+        # the same rows, the nearest codec the reference ships.
+        b = base.astype(np.float32)
+        if kind == "reference":
+            mins, scales = oracle.ref_sq8_train(metric, b)
+            idx = oracle.RefExactIndex(metric, b, codec="sq8", mins=mins, scales=scales)
+            return (lambda q, k, t: idx.search(q.astype(np.float32), k, t)), kind, \
+                "reference ExactIndex + ScalarQuantizer(sq8, dot_product)"
+        mins, scales = oracle.sq8_train(b)
+        codes = oracle.sq8_encode(mins, scales, b)
+        return (lambda q, k, t: oracle.sq8_search(metric, mins, scales, codes, q.astype(np.float32), k, t)), \
+            kind, "C restatement of ExactIndex + sq8"
+    if mask_words is not None:
+        if kind == "reference":
+            bits = ((mask_words[np.arange(base.shape[0]) >> 5] >> (np.arange(base.shape[0]) & 31).astype(np.uint32)) & 1)
+            sel = np.nonzero(bits)[0]
+            idx = oracle.RefExactIndex(metric, base[sel])
+            return (lambda q, k, t: idx.search(q, k, t)), kind, \
+                "reference ExactIndex over the MetadataIndex::exact_candidates subset"
+        return (lambda q, k, t: oracle.exact_search(metric, base, q, k, t, mask=mask_words)), kind, \
+            "C restatement, masked scan"
+    if kind == "reference":
+        idx = oracle.RefExactIndex(metric, base)
+        return (lambda q, k, t: idx.search(q, k, t)), kind, "reference ExactIndex::search (src/ExactIndex.cpp:55-87)"
+    return (lambda q, k, t: oracle.exact_search(metric, base, q, k, t)), kind, "C restatement of ExactIndex::search"
+
+
+def _calibrated_sample(search, cfg, queries, threads, target_s):
+    """Query count (a multiple of the thread count) whose search takes about
+    target_s seconds on this host."""
+    first = min(queries.shape[0], threads)
+    t = time.perf_counter()
+    search(queries[:first], cfg["k"], threads)
+    dt = max(time.perf_counter() - t, 1e-6)
+    rounds = max(1, int(target_s / dt))
+    return min(queries.shape[0], first * rounds)
+
+
+def cpu_baseline(cfg, base, queries, mask_words):
+    threads = os.cpu_count() or 1
+    search, kind, what = _cpu_searcher(cfg, base, mask_words)
+    sample = _calibrated_sample(search, cfg, queries, threads, target_s=10.0)
+    t = time.perf_counter()
+    search(queries[:sample], cfg["k"], threads)
+    dt = time.perf_counter() - t
+    return {"value": round(sample / dt, 3), "unit": "queries/s", "cores": min(threads, sample), "kind": kind,
+            "sample": f"{sample} of the {queries.shape[0]} queries over the full {base.shape[0]}-row base "
+                      f"({what}), {dt:.2f} s wall"}
+
+
+def run_reference(args, cfg):
+    """The reference's CPU implementation of the path, all host threads, one
+    bounded query sample per step."""
+    import torch
+    # Data generation only (untimed): on the GPU when one is visible, else CPU.
+    gdev = "cuda" if torch.cuda.is_available() else "cpu"
+    cents = _centroids(cfg, gdev) if cfg["data"] == "mixture" else None
+    base = np.concatenate([gen_rows(cfg, r0, min(1 << 18, cfg["n"] - r0), SEED + 1, cfg["n"], cents,
+                                    device=gdev).cpu().numpy() for r0 in range(0, cfg["n"], 1 << 18)])
+    queries = gen_rows(cfg, 0, cfg["q"], SEED + 2, cfg["q"], cents, device=gdev).cpu().numpy()
+    if gdev == "cuda":
+        torch.cuda.empty_cache()
+    mask_words = gen_mask_words(cfg, cfg["n"]) if cfg.get("mask_p") else None
+    threads = os.cpu_count() or 1
+    search, kind, what = _cpu_searcher(cfg, base, mask_words)
+    sample = _calibrated_sample(search, cfg, queries, threads, target_s=1.0)
+    for i in range(args.warmup):
+        search(queries[:sample], cfg["k"], threads)
+    t = time.perf_counter()
+    for i in range(args.steps):
+        j = (i * sample) % max(1, queries.shape[0] - sample + 1)
+        search(queries[j:j + sample], cfg["k"], threads)
+    dt = time.perf_counter() - t
+    value = sample * args.steps / dt
+    return {
+        "metric": METRIC_NAME, "value": round(value, 3), "unit": "queries/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; shapes and distributions of the configuration)",
+        "config": {"workload": cfg["workload"], "config": args.config},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 3), "unit": "queries/s", "cores": threads, "kind": kind,
+                         "sample": f"{sample} queries per step over the full {base.shape[0]}-row base ({what})"},
+        "e2e": {"value": round(value, 3), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--base-rows", type=int, default=None,
+                    help="smaller base of the same configuration (profiling captures)")
+    ap.add_argument("--queries", type=int, default=None,
+                    help="smaller query batch of the same configuration (profiling captures)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = dict(CONFIGS[args.config])
+    if args.base_rows:
+        cfg["n"] = args.base_rows
+        cfg["workload"] += f" [reduced: N={args.base_rows:,}]"
+    if args.queries:
+        cfg["q"] = args.queries
+        cfg["workload"] += f" [reduced: Q={args.queries:,}]"
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        print(json.dumps(run_reference(args, cfg)), flush=True)
+        return
+    world, rank, local = dist_setup(args)
+    try:
+        result = run_b200(args, cfg, world, rank, local)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -41,6 +41,7 @@ SIGNATURES = [
     ("elips_b200_device_error", c_int, [c_int, POINTER(c_int)]),
     ("elips_b200_exact_create", c_int, [c_int, c_int, c_int, c_uint32, POINTER(c_void_p)]),
     ("elips_b200_exact_add", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("elips_b200_exact_add_device", c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     ("elips_b200_exact_size", c_int, [c_void_p, POINTER(c_size_t)]),
     ("elips_b200_exact_destroy", c_int, [c_void_p]),
     ("elips_b200_exact_search", c_int,
@@ -51,6 +52,11 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_uint32, c_void_p, c_void_p]),
     ("elips_b200_merge_candidates_device", c_int,
      [c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_profiler_enable", c_int, [c_int]),
+    ("elips_b200_profiler_stats", c_int,
+     [c_char_p, POINTER(ctypes.c_uint64), POINTER(ctypes.c_double), POINTER(ctypes.c_uint64)]),
+    ("elips_b200_profiler_reset", c_int, []),
+    ("elips_b200_launch_count", c_int, [POINTER(ctypes.c_uint64)]),
 ]
 
 
@@ -99,6 +105,28 @@ def device_error(device: int) -> int:
     code = c_int(0)
     check(LIB.elips_b200_device_error(device, ctypes.byref(code)), "elips_b200_device_error")
     return code.value
+
+
+def profiler_enable(on: bool = True) -> None:
+    check(LIB.elips_b200_profiler_enable(1 if on else 0), "elips_b200_profiler_enable")
+
+
+def profiler_reset() -> None:
+    check(LIB.elips_b200_profiler_reset(), "elips_b200_profiler_reset")
+
+
+def profiler_stats(kernel: str | None = None) -> dict:
+    """{'launches', 'total_ms', 'items'} for one kernel (None = all)."""
+    n, ms, it = ctypes.c_uint64(0), ctypes.c_double(0.0), ctypes.c_uint64(0)
+    check(LIB.elips_b200_profiler_stats(kernel.encode() if kernel else None, ctypes.byref(n),
+                                        ctypes.byref(ms), ctypes.byref(it)), "elips_b200_profiler_stats")
+    return {"launches": n.value, "total_ms": ms.value, "items": it.value}
+
+
+def launch_count() -> int:
+    n = ctypes.c_uint64(0)
+    check(LIB.elips_b200_launch_count(ctypes.byref(n)), "elips_b200_launch_count")
+    return n.value
 
 
 __all__ = [n for n in dir() if not n.startswith("_")]

@@ -5,6 +5,7 @@
 
 #include "../../include/elips_b200.h"
 #include "engine.cuh"
+#include "profiler.cuh"
 
 struct elips_b200_exact {
     eb::ExactIndex index;
@@ -82,6 +83,11 @@ int elips_b200_exact_create(int device, int metric, int precision, uint32_t dime
 int elips_b200_exact_add(elips_b200_exact* index, const void* rows, size_t n) {
     if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] { index->index.add(rows, n); });
+}
+
+int elips_b200_exact_add_device(elips_b200_exact* index, const void* rows, size_t n, void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.add_device(rows, n, as_stream(stream)); });
 }
 
 int elips_b200_exact_size(const elips_b200_exact* index, size_t* n_out) {
@@ -182,6 +188,30 @@ int elips_b200_merge_candidates_device(int device, const uint32_t* cand, size_t 
                              static_cast<uint64_t>(nq) * k, metric, out_dist, out_rows, nullptr,
                              as_stream(stream));
     });
+}
+
+int elips_b200_profiler_enable(int enabled) {
+    eb::Profiler::get().set_enabled(enabled != 0);
+    return ELIPS_B200_OK;
+}
+
+int elips_b200_profiler_stats(const char* kernel, uint64_t* launches, double* total_ms, uint64_t* items) {
+    return guarded([&] {
+        const eb::KernelStats s = eb::Profiler::get().query(kernel);
+        if (launches) *launches = s.launches;
+        if (total_ms) *total_ms = s.total_ms;
+        if (items) *items = s.items;
+    });
+}
+
+int elips_b200_profiler_reset(void) {
+    return guarded([&] { eb::Profiler::get().reset(); });
+}
+
+int elips_b200_launch_count(uint64_t* launches) {
+    if (launches == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *launches = eb::Profiler::get().total_launches();
+    return ELIPS_B200_OK;
 }
 
 }  // extern "C"

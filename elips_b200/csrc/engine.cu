@@ -11,6 +11,7 @@
 #include "aux_kernels.cuh"
 #include "engine.cuh"
 #include "exact_topk.cuh"
+#include "profiler.cuh"
 
 namespace eb {
 
@@ -206,12 +207,14 @@ void prep_operands(OperandKind kind, const void* src, size_t rows, uint32_t dim,
     if (kind == OperandKind::I8) {
         const uint64_t total = static_cast<uint64_t>(rows) * d_pad;
         const uint32_t blocks = static_cast<uint32_t>((total + 255) / 256);
+        Profiler::Scope prof("prep_rows", stream, rows);
         prep_rows_i8_kernel<<<blocks, 256, 0, stream>>>(static_cast<const int8_t*>(src), rows, dim,
                                                         d_pad, static_cast<int8_t*>(ops));
     } else {
         const int k = kind == OperandKind::F16 ? 0 : (kind == OperandKind::BF16 ? 1 : 2);
         const uint64_t threads = static_cast<uint64_t>(rows) * 32;
         const uint32_t blocks = static_cast<uint32_t>((threads + 255) / 256);
+        Profiler::Scope prof("prep_rows", stream, rows);
         prep_rows_f32_kernel<<<blocks, 256, 0, stream>>>(static_cast<const float*>(src), rows, dim,
                                                          d_pad, k, ops, static_cast<float*>(ops_lo),
                                                          norms);
@@ -228,6 +231,7 @@ void launch_exact_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUten
     check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(Cfg::kSmemBytes)),
                ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+    Profiler::Scope prof("exact_topk", stream, static_cast<uint64_t>(params.nq) * params.n);
     kernel<<<grid, kExactThreads, Cfg::kSmemBytes, stream>>>(a, b, alo, blo, params);
     check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "exact kernel launch");
 }
@@ -312,6 +316,22 @@ void ExactIndex::add(const void* rows_host, size_t n) {
         throw;
     }
     cudaStreamDestroy(stream);
+    n_ += n;
+}
+
+void ExactIndex::add_device(const void* rows, size_t n, cudaStream_t stream) {
+    if (n == 0) return;
+    if (rows == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "rows is null");
+    if (n_ + n >= 0xFFFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "index limited to 2^32-2 rows");
+    DeviceGuard g(device_);
+    // Growing reallocates; finish work already queued on `stream` first.
+    check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "add_device sync");
+    reserve(n_ + n);
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    prep_operands(kind_, rows, n, dim_, d_pad_, static_cast<uint8_t*>(ops_.get()) + n_ * row_bytes,
+                  ops_lo_.get() ? static_cast<uint8_t*>(ops_lo_.get()) + n_ * row_bytes : nullptr,
+                  norms_.get() ? static_cast<float*>(norms_.get()) + n_ : nullptr, stream);
+    check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "row prep");
     n_ += n;
 }
 
@@ -407,6 +427,7 @@ void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists
                                     static_cast<int>(smem)),
                ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
     const uint32_t blocks = (nq + warps - 1) / warps;
+    Profiler::Scope prof("merge_topk", stream, static_cast<uint64_t>(nq) * lists * k);
     merge_topk_kernel<<<blocks, warps * 32, smem, stream>>>(cand, nq, lists, k, stride_q, stride_l, kpow2,
                                                            metric, out_dist, out_rows, out_cand);
     check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "merge kernel launch");

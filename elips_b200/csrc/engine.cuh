@@ -96,6 +96,8 @@ public:
     ExactIndex(int device, int metric, int precision, uint32_t dim);
 
     void add(const void* rows_host, size_t n);
+    // rows: device memory, same element type as add(); converted on `stream`.
+    void add_device(const void* rows, size_t n, cudaStream_t stream);
     size_t size() const { return n_; }
     int device() const { return device_; }
     int metric() const { return metric_; }

@@ -69,6 +69,16 @@ class ExactIndex:
         capi.check(capi.LIB.elips_b200_exact_add(self._h, _ptr(rows), rows.shape[0]),
                    "elips_b200_exact_add")
 
+    def add_device(self, rows, stream=None) -> None:
+        """Appends rows held in a CUDA tensor [n, dimension] (float32, int8 for int8)."""
+        import torch
+        if rows.dim() != 2 or rows.shape[1] != self.dimension:
+            raise DimensionMismatch("vector dimension does not match index")
+        rows = rows.contiguous()
+        s = stream if stream is not None else torch.cuda.current_stream(rows.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_exact_add_device(self._h, rows.data_ptr(), rows.shape[0], s),
+                   "elips_b200_exact_add_device")
+
     def insert(self, vector: np.ndarray) -> None:
         self.add(np.asarray(vector, dtype=self._in_dtype).reshape(1, -1))
 
@@ -82,16 +92,21 @@ class ExactIndex:
         d, r = self.search_batch(np.asarray(query).reshape(1, -1), k)
         return [(int(r[0, i]), float(d[0, i])) for i in range(d.shape[1]) if r[0, i] >= 0]
 
-    def search_batch(self, queries: np.ndarray, k: int,
-                     mask: Optional[np.ndarray] = None) -> tuple[np.ndarray, np.ndarray]:
+    def search_batch(self, queries: np.ndarray, k: int, mask: Optional[np.ndarray] = None,
+                     out_dist: Optional[np.ndarray] = None,
+                     out_rows: Optional[np.ndarray] = None) -> tuple[np.ndarray, np.ndarray]:
         """Host arrays in, host arrays out: (distances [nq, k] fp32, slots [nq, k] int64).
-        Unfilled slots hold (+inf, -1). mask: uint32 words, bit i = slot i eligible."""
+        Unfilled slots hold (+inf, -1). mask: uint32 words, bit i = slot i eligible.
+        out_dist / out_rows: optional preallocated (e.g. pinned) C-contiguous outputs."""
         q = np.ascontiguousarray(queries, dtype=self._in_dtype)
         if q.ndim != 2 or q.shape[1] != self.dimension:
             raise DimensionMismatch("query dimension does not match index")
         nq = q.shape[0]
-        dist = np.empty((nq, k), dtype=np.float32)
-        rows = np.empty((nq, k), dtype=np.int64)
+        dist = np.empty((nq, k), dtype=np.float32) if out_dist is None else out_dist
+        rows = np.empty((nq, k), dtype=np.int64) if out_rows is None else out_rows
+        if dist.shape != (nq, k) or rows.shape != (nq, k) or dist.dtype != np.float32 \
+                or rows.dtype != np.int64 or not dist.flags.c_contiguous or not rows.flags.c_contiguous:
+            raise ValueError("outputs must be C-contiguous float32 / int64 arrays of shape (nq, k)")
         m = None
         if mask is not None:
             m = np.ascontiguousarray(mask, dtype=np.uint32)

@@ -95,6 +95,11 @@ ELIPS_B200_API int elips_b200_exact_create(int device, int metric, int precision
  * PRECISION_INT8). */
 ELIPS_B200_API int elips_b200_exact_add(elips_b200_exact* index, const void* rows, size_t n);
 
+/* Same as elips_b200_exact_add with rows in DEVICE memory; returns after the
+ * rows are converted (work queued on `stream` completes first). */
+ELIPS_B200_API int elips_b200_exact_add_device(elips_b200_exact* index, const void* rows, size_t n,
+                                               void* stream);
+
 /* IndexPort::size. */
 ELIPS_B200_API int elips_b200_exact_size(const elips_b200_exact* index, size_t* n_out);
 
@@ -135,6 +140,25 @@ ELIPS_B200_API int elips_b200_exact_search_candidates_device(const elips_b200_ex
 ELIPS_B200_API int elips_b200_merge_candidates_device(int device, const uint32_t* cand, size_t nq,
                                        size_t lists, size_t k, int metric, float* out_dist,
                                        int64_t* out_rows, void* stream);
+
+/* ------------------------------------------------------------ profiling */
+/* Device-side counterpart of GpuProfiler (src/gpu_engine/GpuProfiler.cpp:
+ * 5-23) and GpuConfig::enable_profiling (GpuConfig.hpp:83): while enabled,
+ * every kernel this library launches is bracketed by CUDA events on its
+ * launching stream. */
+ELIPS_B200_API int elips_b200_profiler_enable(int enabled);
+
+/* Totals since the last reset for one kernel ("exact_topk", "merge_topk",
+ * "prep_rows", ...; NULL = all): timed launches, summed milliseconds, summed
+ * work items. Waits for the pending events. Any output pointer may be NULL. */
+ELIPS_B200_API int elips_b200_profiler_stats(const char* kernel, uint64_t* launches,
+                                             double* total_ms, uint64_t* items);
+
+ELIPS_B200_API int elips_b200_profiler_reset(void);
+
+/* Kernels launched by this library since it was loaded (always counted,
+ * GpuProfiler::total_launches). */
+ELIPS_B200_API int elips_b200_launch_count(uint64_t* launches);
 
 #ifdef __cplusplus
 }
