@@ -172,7 +172,9 @@ ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int num_s
     p.splits = best_s;
     const uint64_t units = static_cast<uint64_t>(p.n_qt) * p.splits;
     p.grid = static_cast<uint32_t>(std::min<uint64_t>(units, static_cast<uint64_t>(num_sms)));
-    p.cap = std::max<uint32_t>(256u, ((2u * k + 32u) + 31u) / 32u * 32u);
+    // List capacity: room for k survivors plus several hundred admissions
+    // between compactions; lists up to 512 entries are compacted in registers.
+    p.cap = k <= 224 ? 512u : ((2u * k + 32u) + 31u) / 32u * 32u;
     return p;
 }
 
@@ -360,13 +362,17 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     const size_t q_norm = metric_ == kEuclidean ? align(nq * sizeof(float)) : 0;
     const size_t cand = align(static_cast<size_t>(plan.grid) * kTileM * plan.cap * sizeof(uint2));
     const size_t partial = align(nq * plan.splits * k * sizeof(uint2));
-    StreamScratch scratch(q_ops + q_lo + q_norm + cand + partial, stream);
+    const size_t qtau = align(nq * sizeof(uint32_t));
+    StreamScratch scratch(q_ops + q_lo + q_norm + cand + partial + qtau, stream);
     uint8_t* s = scratch.get();
     void* qa = s;
     void* qlo = q_lo ? s + q_ops : nullptr;
     float* qn = q_norm ? reinterpret_cast<float*>(s + q_ops + q_lo) : nullptr;
     uint2* cand_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm);
     uint2* part_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand);
+    uint32_t* qtau_buf = reinterpret_cast<uint32_t*>(s + q_ops + q_lo + q_norm + cand + partial);
+    check_cuda(cudaMemsetAsync(qtau_buf, 0xFF, nq * sizeof(uint32_t), stream), ELIPS_B200_KERNEL_LAUNCH_FAILED,
+               "threshold init");
     prep_operands(kind_, queries, nq, dim_, d_pad_, qa, qlo, qn, stream);
 
     const CUtensorMapDataType dt = tma_dtype_of(kind_);
@@ -383,6 +389,7 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     prm.mask = mask;
     prm.cand = cand_buf;
     prm.partial = part_buf;
+    prm.qtau = qtau_buf;
     prm.n = n;
     prm.nq = static_cast<uint32_t>(nq);
     prm.k = static_cast<uint32_t>(k);

@@ -40,6 +40,7 @@ struct ExactParams {
     const uint32_t* mask;      // [ceil(n/32)] eligibility bits, or null
     uint2* cand;               // [gridDim.x][128][cap] per-query candidate lists
     uint2* partial;            // [nq][splits][k]
+    uint32_t* qtau;            // [nq] shared admission bound per query (ordered key)
     uint32_t n, nq, k, cap, splits, n_qt, n_bt, num_units, kblocks;
     uint32_t row_offset;       // added to every emitted row (shard base)
     int metric;
@@ -99,6 +100,30 @@ __device__ __forceinline__ bool drain_wait(uint32_t bar, uint32_t parity) {
         }
     }
     return true;
+}
+
+// Largest candidate list the register-resident compaction handles (16
+// entries per lane); longer lists take the global-memory path.
+constexpr uint32_t kRegListCap = 512;
+
+// Reduces one query's list to its k best entries (whole warp).
+__device__ __forceinline__ float compact_one(uint2* list, uint32_t count, uint32_t k, uint32_t cap,
+                                             uint32_t* hist) {
+    if (cap <= kRegListCap) return warp_compact_regs<kRegListCap / 32>(list, count, k, hist);
+    return warp_compact_list(list, count, k, hist);
+}
+
+// Effective strict admission threshold: below this unit's own k-th key, and
+// at or below the best k-th key any unit has published for the query (a
+// candidate equal to another unit's bound may still precede that unit's
+// entries in (key, row) order, so the shared bound admits equality).
+__device__ __forceinline__ float admission_threshold(float tau_local, uint32_t shared_bound) {
+    const uint32_t inf_key = 0xFF800000u;  // ordered_key(+inf)
+    uint32_t t = ordered_key(tau_local);
+    const uint32_t g = shared_bound == 0xFFFFFFFFu ? 0xFFFFFFFFu : shared_bound + 1u;
+    t = min(t, g);
+    t = min(t, inf_key);
+    return key_to_float(t);
 }
 
 template <OperandKind KIND, int BN, int STAGES>
@@ -275,11 +300,12 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             const bool qvalid = q < p.nq;
             float qn = 0.0f;
             if (p.metric == kEuclidean && qvalid) qn = p.query_norms[q];
-            float tau = __int_as_float(0x7f800000);  // +inf
+            float tau = __int_as_float(0x7f800000);  // +inf: this unit's own k-th key
             uint32_t cnt = 0;
             for (uint32_t bt = bt0; bt < bt1; ++bt, ++tile_iter) {
                 const uint32_t acc = tile_iter & 1u;
                 const uint32_t acc_phase = (tile_iter >> 1) & 1u;
+                const float thr = admission_threshold(tau, qvalid ? __ldcg(p.qtau + q) : 0xFFFFFFFFu);
                 ok = mbar_wait(tfull_bar(acc), acc_phase, abort_flag);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
@@ -319,7 +345,7 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                                 key = fmaf(-2.0f, a, qn + xi);
                             }
                         }
-                        if (((mword >> i) & 1u) && key < tau) {
+                        if (((mword >> i) & 1u) && key < thr) {
                             my_list[cnt] = make_uint2(__float_as_uint(key), p.row_offset + row0 + i);
                             ++cnt;
                         }
@@ -331,10 +357,11 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                         const uint32_t L = __ffs(need) - 1;
                         const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
                         uint2* list_l = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + quad * 32u + L) * p.cap;
-                        const float th = warp_compact_list(list_l, cnt_l, p.k, hist);
+                        const float th = compact_one(list_l, cnt_l, p.k, p.cap, hist);
                         if (lane == L) {
                             tau = th;
                             cnt = p.k;
+                            atomicMin(p.qtau + q, ordered_key(th));
                         }
                         need &= need - 1;
                     }
@@ -348,8 +375,11 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                 const uint32_t L = __ffs(need) - 1;
                 const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
                 uint2* list_l = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + quad * 32u + L) * p.cap;
-                warp_compact_list(list_l, cnt_l, p.k, hist);
-                if (lane == L) cnt = p.k;
+                const float th = compact_one(list_l, cnt_l, p.k, p.cap, hist);
+                if (lane == L) {
+                    cnt = p.k;
+                    atomicMin(p.qtau + q, ordered_key(th));
+                }
                 need &= need - 1;
             }
             if (qvalid) {

@@ -103,4 +103,90 @@ __device__ __forceinline__ float warp_compact_list(uint2* list, uint32_t count, 
     return key_to_float(kth);
 }
 
+// Same contract as warp_compact_list for count <= 32*E, with the list held in
+// registers for the whole selection: one batch of independent loads, four
+// histogram passes over registers, one stable write-back. Entry j of the list
+// lives in slot j/32 of lane j%32, so the write-back walks positions in order.
+template <int E>
+__device__ __forceinline__ float warp_compact_regs(uint2* list, uint32_t count, uint32_t k,
+                                                   uint32_t* hist) {
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t key[E], row[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const uint32_t j = static_cast<uint32_t>(i) * 32u + lane;
+        uint2 e = make_uint2(0u, 0u);
+        if (j < count) e = list[j];
+        key[i] = ordered_key(__uint_as_float(e.x));
+        row[i] = e.y;
+    }
+    uint32_t prefix = 0, prefix_mask = 0, rank = k;
+#pragma unroll 1
+    for (int pass = 0; pass < 4; ++pass) {
+        const uint32_t shift = 24u - 8u * static_cast<uint32_t>(pass);
+        for (uint32_t b = lane; b < 256; b += 32) hist[b] = 0;
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const uint32_t j = static_cast<uint32_t>(i) * 32u + lane;
+            if (j < count && (key[i] & prefix_mask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        uint32_t bins[8];
+        uint32_t local = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            bins[i] = hist[lane * 8 + i];
+            local += bins[i];
+        }
+        uint32_t incl = local;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= static_cast<uint32_t>(off)) incl += t;
+        }
+        const uint32_t excl = incl - local;
+        const bool mine = excl < rank && rank <= incl;
+        uint32_t digit = 0, before = excl;
+        if (mine) {
+            uint32_t acc = excl;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (acc + bins[i] >= rank) {
+                    digit = lane * 8 + i;
+                    before = acc;
+                    break;
+                }
+                acc += bins[i];
+            }
+        }
+        const uint32_t owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+        digit = __shfl_sync(0xffffffffu, digit, owner);
+        before = __shfl_sync(0xffffffffu, before, owner);
+        rank -= before;
+        prefix |= digit << shift;
+        prefix_mask |= 255u << shift;
+        __syncwarp();
+    }
+    const uint32_t kth = prefix, need_eq = rank;
+    const uint32_t lt_mask = lanemask_lt();
+    uint32_t w = 0, eq_taken = 0;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const uint32_t j = static_cast<uint32_t>(i) * 32u + lane;
+        const bool valid = j < count;
+        const bool lt = valid && key[i] < kth;
+        const bool eq = valid && key[i] == kth;
+        const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
+        const uint32_t eq_rank = eq_taken + __popc(eq_mask & lt_mask);
+        const bool keep = lt || (eq && eq_rank < need_eq);
+        const uint32_t keep_mask = __ballot_sync(0xffffffffu, keep);
+        if (keep) list[w + __popc(keep_mask & lt_mask)] = make_uint2(__float_as_uint(key_to_float(key[i])), row[i]);
+        w += __popc(keep_mask);
+        eq_taken += __popc(eq_mask);
+    }
+    __syncwarp();
+    return key_to_float(kth);
+}
+
 }  // namespace eb
