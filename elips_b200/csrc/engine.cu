@@ -224,12 +224,12 @@ void prep_operands(OperandKind kind, const void* src, size_t rows, uint32_t dim,
     check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "prep kernel launch");
 }
 
-template <OperandKind KIND, int BN, int STAGES>
+template <OperandKind KIND, int BN, int STAGES, int METRIC>
 void launch_exact_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& alo,
                          const CUtensorMap& blo, const ExactParams& params, uint32_t grid,
                          cudaStream_t stream) {
     using Cfg = ExactConfig<KIND, BN, STAGES>;
-    auto kernel = exact_topk_kernel<KIND, BN, STAGES>;
+    auto kernel = exact_topk_kernel<KIND, BN, STAGES, METRIC>;
     check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(Cfg::kSmemBytes)),
                ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
@@ -239,6 +239,27 @@ void launch_exact_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUten
 }
 
 uint32_t bn_of(OperandKind k) { return k == OperandKind::TF32X3 ? 128u : 256u; }
+
+template <OperandKind KIND, int BN, int STAGES>
+void dispatch_metric(int metric, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& alo,
+                     const CUtensorMap& blo, const ExactParams& prm, uint32_t grid, cudaStream_t stream) {
+    switch (metric) {
+        case kCosine: launch_exact_kernel<KIND, BN, STAGES, kCosine>(a, b, alo, blo, prm, grid, stream); break;
+        case kEuclidean: launch_exact_kernel<KIND, BN, STAGES, kEuclidean>(a, b, alo, blo, prm, grid, stream); break;
+        default: launch_exact_kernel<KIND, BN, STAGES, kDot>(a, b, alo, blo, prm, grid, stream); break;
+    }
+}
+
+void dispatch_exact(OperandKind kind, int metric, const CUtensorMap& a, const CUtensorMap& b,
+                    const CUtensorMap& alo, const CUtensorMap& blo, const ExactParams& prm, uint32_t grid,
+                    cudaStream_t stream) {
+    switch (kind) {
+        case OperandKind::F16: dispatch_metric<OperandKind::F16, 256, 4>(metric, a, b, alo, blo, prm, grid, stream); break;
+        case OperandKind::BF16: dispatch_metric<OperandKind::BF16, 256, 4>(metric, a, b, alo, blo, prm, grid, stream); break;
+        case OperandKind::TF32X3: dispatch_metric<OperandKind::TF32X3, 128, 3>(metric, a, b, alo, blo, prm, grid, stream); break;
+        case OperandKind::I8: launch_exact_kernel<OperandKind::I8, 256, 4, kDot>(a, b, alo, blo, prm, grid, stream); break;
+    }
+}
 
 }  // namespace
 
@@ -401,20 +422,7 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     prm.kblocks = d_pad_ * elem_bytes_ / kKBlockBytes;
     prm.row_offset = row_offset;
     prm.metric = metric_;
-    switch (kind_) {
-        case OperandKind::F16:
-            launch_exact_kernel<OperandKind::F16, 256, 4>(ma, mb, malo, mblo, prm, plan.grid, stream);
-            break;
-        case OperandKind::BF16:
-            launch_exact_kernel<OperandKind::BF16, 256, 4>(ma, mb, malo, mblo, prm, plan.grid, stream);
-            break;
-        case OperandKind::TF32X3:
-            launch_exact_kernel<OperandKind::TF32X3, 128, 3>(ma, mb, malo, mblo, prm, plan.grid, stream);
-            break;
-        case OperandKind::I8:
-            launch_exact_kernel<OperandKind::I8, 256, 4>(ma, mb, malo, mblo, prm, plan.grid, stream);
-            break;
-    }
+    dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan.grid, stream);
     merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits, static_cast<uint32_t>(k),
                      static_cast<uint64_t>(plan.splits) * k, k, metric_, out_dist, out_rows, out_cand,
                      stream);

@@ -86,7 +86,8 @@ struct ExactConfig {
     static constexpr uint32_t kBarBytes = 8 * (2 * STAGES + 5);
     static constexpr uint32_t kMiscOffset = STAGES * kStageBytes;
     static constexpr uint32_t kHistOffset = kMiscOffset + 256;
-    static constexpr uint32_t kSmemBytes = 1024 /* alignment slack */ + kHistOffset + 4 * 1024;
+    static constexpr uint32_t kNormOffset = kHistOffset + 4 * 1024;  // per-warp base-norm tile
+    static constexpr uint32_t kSmemBytes = 1024 /* alignment slack */ + kNormOffset + 4 * BN * 4;
     static_assert(kBarBytes + 16 <= 256, "barrier area");
     static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
 };
@@ -126,7 +127,46 @@ __device__ __forceinline__ float admission_threshold(float tau_local, uint32_t s
     return key_to_float(t);
 }
 
-template <OperandKind KIND, int BN, int STAGES>
+// Ordering key of one accumulator word: the distance before the final
+// square root (euclidean), i.e. 1 - dot (cosine), -dot (dot product),
+// (|x|^2 - 2 q.x) + |q|^2 (euclidean), -(int32 dot) for the int8 codec.
+template <OperandKind KIND, int METRIC>
+__device__ __forceinline__ float key_of(uint32_t v, float xn, float qn) {
+    if constexpr (KindTraits<KIND>::integer) {
+        return -static_cast<float>(static_cast<int32_t>(v));
+    } else if constexpr (METRIC == kCosine) {
+        return 1.0f - __uint_as_float(v);
+    } else if constexpr (METRIC == kDot) {
+        return -__uint_as_float(v);
+    } else {
+        return fmaf(-2.0f, __uint_as_float(v), xn) + qn;
+    }
+}
+
+// Smallest key of a 32-column chunk, computed with one min/max per value.
+// Every key_of above is a monotone function of one running extreme, so this
+// equals the minimum of key_of over the chunk exactly.
+template <OperandKind KIND, int METRIC>
+__device__ __forceinline__ float chunk_min_key(const uint32_t (&v)[32], const float* xn, float qn) {
+    if constexpr (KindTraits<KIND>::integer) {
+        int32_t m = static_cast<int32_t>(v[0]);
+#pragma unroll
+        for (int i = 1; i < 32; ++i) m = max(m, static_cast<int32_t>(v[i]));
+        return -static_cast<float>(m);
+    } else if constexpr (METRIC == kEuclidean) {
+        float m = fmaf(-2.0f, __uint_as_float(v[0]), xn[0]);
+#pragma unroll
+        for (int i = 1; i < 32; ++i) m = fminf(m, fmaf(-2.0f, __uint_as_float(v[i]), xn[i]));
+        return m + qn;
+    } else {
+        float m = __uint_as_float(v[0]);
+#pragma unroll
+        for (int i = 1; i < 32; ++i) m = fmaxf(m, __uint_as_float(v[i]));
+        return METRIC == kCosine ? 1.0f - m : -m;
+    }
+}
+
+template <OperandKind KIND, int BN, int STAGES, int METRIC>
 __global__ void __launch_bounds__(kExactThreads, 1)
     exact_topk_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_a_lo,
@@ -288,6 +328,7 @@ __global__ void __launch_bounds__(kExactThreads, 1)
         const uint32_t quad = warp & 3u;              // TMEM lane quadrant of this warp
         const uint32_t lane_row = quad * 32u + lane;  // query row within the tile
         uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Cfg::kHistOffset) + (warp - 2u) * 256u;
+        float* xs = reinterpret_cast<float*>(smem + Cfg::kNormOffset) + (warp - 2u) * BN;
         uint2* my_list = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + lane_row) * p.cap;
         const uint32_t lane_base = (quad * 32u) << 16;
         uint32_t tile_iter = 0;
@@ -299,18 +340,28 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             const uint32_t q = qt * kTileM + lane_row;
             const bool qvalid = q < p.nq;
             float qn = 0.0f;
-            if (p.metric == kEuclidean && qvalid) qn = p.query_norms[q];
+            if constexpr (METRIC == kEuclidean) {
+                if (qvalid) qn = p.query_norms[q];
+            }
             float tau = __int_as_float(0x7f800000);  // +inf: this unit's own k-th key
             uint32_t cnt = 0;
             for (uint32_t bt = bt0; bt < bt1; ++bt, ++tile_iter) {
                 const uint32_t acc = tile_iter & 1u;
                 const uint32_t acc_phase = (tile_iter >> 1) & 1u;
                 const float thr = admission_threshold(tau, qvalid ? __ldcg(p.qtau + q) : 0xFFFFFFFFu);
+                const uint32_t row_tile = bt * BN;
+                if constexpr (METRIC == kEuclidean) {
+                    // stage this tile's base norms (rows past n read as 0)
+                    for (uint32_t j = lane; j < BN; j += 32) {
+                        const uint32_t r = row_tile + j;
+                        xs[j] = r < p.n ? __ldg(p.base_norms + r) : 0.0f;
+                    }
+                    __syncwarp();
+                }
                 ok = mbar_wait(tfull_bar(acc), acc_phase, abort_flag);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t row_tile = bt * BN;
 #pragma unroll 1
                 for (uint32_t c = 0; c < BN / 32; ++c) {
                     uint32_t v[32];
@@ -326,28 +377,17 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                     const uint32_t valid_rows = min(32u, p.n - row0);
                     uint32_t mword = valid_rows == 32u ? 0xFFFFFFFFu : ((1u << valid_rows) - 1u);
                     if (p.mask != nullptr) mword &= __ldg(p.mask + (row0 >> 5));
-                    float xn = 0.0f;
-                    if (p.metric == kEuclidean && lane < valid_rows) xn = __ldg(p.base_norms + row0 + lane);
                     if (!qvalid) mword = 0;
+                    const float* xn = xs + c * 32u;
+                    // Fast reject: most chunks hold nothing below the threshold.
+                    if (mword != 0u && chunk_min_key<KIND, METRIC>(v, xn, qn) < thr) {
 #pragma unroll
-                    for (uint32_t i = 0; i < 32; ++i) {
-                        float key;
-                        if constexpr (Tr::integer) {
-                            key = -static_cast<float>(static_cast<int32_t>(v[i]));
-                        } else {
-                            const float a = __uint_as_float(v[i]);
-                            if (p.metric == kCosine) {
-                                key = 1.0f - a;
-                            } else if (p.metric == kDot) {
-                                key = -a;
-                            } else {
-                                const float xi = __shfl_sync(0xffffffffu, xn, i);
-                                key = fmaf(-2.0f, a, qn + xi);
+                        for (uint32_t i = 0; i < 32; ++i) {
+                            const float key = key_of<KIND, METRIC>(v[i], xn[i], qn);
+                            if (((mword >> i) & 1u) && key < thr) {
+                                my_list[cnt] = make_uint2(__float_as_uint(key), p.row_offset + row0 + i);
+                                ++cnt;
                             }
-                        }
-                        if (((mword >> i) & 1u) && key < thr) {
-                            my_list[cnt] = make_uint2(__float_as_uint(key), p.row_offset + row0 + i);
-                            ++cnt;
                         }
                     }
                     // Keep room for one more chunk: compact any list that could overflow.
@@ -366,6 +406,7 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                         need &= need - 1;
                     }
                 }
+                if constexpr (METRIC == kEuclidean) __syncwarp();
             }
             if (!ok) break;
             // End of unit: reduce every list to its k best, then publish.
