@@ -365,6 +365,8 @@ __global__ void __launch_bounds__(kExactThreads, 1)
 #pragma unroll 1
                 for (uint32_t c = 0; c < BN / 32; ++c) {
                     uint32_t v[32];
+                    // tcgen05.ld is .sync.aligned: the warp must arrive converged.
+                    __syncwarp();
                     tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + c * 32u, v);
                     tmem_wait_ld();
                     if (c == BN / 32 - 1) {

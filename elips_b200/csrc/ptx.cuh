@@ -194,7 +194,9 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t ab_fm
 }
 
 // 32 lanes x 32 columns of 32-bit TMEM words into 32 registers per thread.
-// Thread t of the warp reads lane (lane base of taddr) + t.
+// Thread t of the warp reads lane (lane base of taddr) + t. The instruction is
+// .sync.aligned: every lane of the warp must execute it together, so callers
+// place a __syncwarp() directly before it after any lane-dependent branch.
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32"
