@@ -172,9 +172,10 @@ ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int num_s
     p.splits = best_s;
     const uint64_t units = static_cast<uint64_t>(p.n_qt) * p.splits;
     p.grid = static_cast<uint32_t>(std::min<uint64_t>(units, static_cast<uint64_t>(num_sms)));
-    // List capacity: room for k survivors plus several hundred admissions
-    // between compactions; lists up to 512 entries are compacted in registers.
-    p.cap = k <= 224 ? 512u : ((2u * k + 32u) + 31u) / 32u * 32u;
+    // List capacity: k survivors plus at least one whole half-tile of
+    // admissions (compaction is checked once per tile); lists up to 512
+    // entries are compacted in registers.
+    p.cap = std::max<uint32_t>(512u, (k + bn / 2 + 32u + 31u) / 32u * 32u);
     return p;
 }
 
@@ -381,8 +382,8 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     const size_t q_ops = align(nq * row_bytes);
     const size_t q_lo = kind_ == OperandKind::TF32X3 ? q_ops : 0;
     const size_t q_norm = metric_ == kEuclidean ? align(nq * sizeof(float)) : 0;
-    const size_t cand = align(static_cast<size_t>(plan.grid) * kTileM * plan.cap * sizeof(uint2));
-    const size_t partial = align(nq * plan.splits * k * sizeof(uint2));
+    const size_t cand = align(static_cast<size_t>(plan.grid) * 2 * kTileM * plan.cap * sizeof(uint2));
+    const size_t partial = align(nq * plan.splits * 2 * k * sizeof(uint2));
     const size_t qtau = align(nq * sizeof(uint32_t));
     StreamScratch scratch(q_ops + q_lo + q_norm + cand + partial + qtau, stream);
     uint8_t* s = scratch.get();
@@ -423,8 +424,8 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     prm.row_offset = row_offset;
     prm.metric = metric_;
     dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan.grid, stream);
-    merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits, static_cast<uint32_t>(k),
-                     static_cast<uint64_t>(plan.splits) * k, k, metric_, out_dist, out_rows, out_cand,
+    merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits * 2, static_cast<uint32_t>(k),
+                     static_cast<uint64_t>(plan.splits) * 2 * k, k, metric_, out_dist, out_rows, out_cand,
                      stream);
 }
 

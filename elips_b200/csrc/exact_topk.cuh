@@ -15,8 +15,10 @@
 // resident at any time share the same base region, which then streams from
 // HBM once and is re-read from L2 by every query tile.
 //
-// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator and
-// MMA issuer, warps 2-5 = epilogue (thread = one query = one TMEM lane).
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator and
+// MMA issuer, warps 2-9 = epilogue. Two epilogue warps share each 32-lane
+// TMEM quadrant and split the tile's columns in halves; a thread owns one
+// (query, column half) pair and its own candidate list.
 #pragma once
 
 #include <cstdint>
@@ -32,14 +34,15 @@ enum MetricId : int { kCosine = 0, kEuclidean = 1, kDot = 2 };  // elips::Metric
 
 constexpr int kTileM = 128;           // queries per tile = TMEM lanes
 constexpr int kKBlockBytes = 128;     // K bytes per pipeline stage (one swizzle atom)
-constexpr int kExactThreads = 192;
+constexpr int kEpilogueWarps = 8;
+constexpr int kExactThreads = 32 * (2 + kEpilogueWarps);
 
 struct ExactParams {
     const float* base_norms;   // [n] squared norms (euclidean only)
     const float* query_norms;  // [nq] squared norms (euclidean only)
     const uint32_t* mask;      // [ceil(n/32)] eligibility bits, or null
-    uint2* cand;               // [gridDim.x][128][cap] per-query candidate lists
-    uint2* partial;            // [nq][splits][k]
+    uint2* cand;               // [gridDim.x][2][128][cap] candidate lists per (column half, query)
+    uint2* partial;            // [nq][splits][2][k]
     uint32_t* qtau;            // [nq] shared admission bound per query (ordered key)
     uint32_t n, nq, k, cap, splits, n_qt, n_bt, num_units, kblocks;
     uint32_t row_offset;       // added to every emitted row (shard base)
@@ -86,8 +89,8 @@ struct ExactConfig {
     static constexpr uint32_t kBarBytes = 8 * (2 * STAGES + 5);
     static constexpr uint32_t kMiscOffset = STAGES * kStageBytes;
     static constexpr uint32_t kHistOffset = kMiscOffset + 256;
-    static constexpr uint32_t kNormOffset = kHistOffset + 4 * 1024;  // per-warp base-norm tile
-    static constexpr uint32_t kSmemBytes = 1024 /* alignment slack */ + kNormOffset + 4 * BN * 4;
+    static constexpr uint32_t kNormOffset = kHistOffset + kEpilogueWarps * 1024;  // per-warp norms
+    static constexpr uint32_t kSmemBytes = 1024 /* alignment slack */ + kNormOffset + kEpilogueWarps * (BN / 2) * 4;
     static_assert(kBarBytes + 16 <= 256, "barrier area");
     static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
 };
@@ -148,21 +151,29 @@ __device__ __forceinline__ float key_of(uint32_t v, float xn, float qn) {
 // equals the minimum of key_of over the chunk exactly.
 template <OperandKind KIND, int METRIC>
 __device__ __forceinline__ float chunk_min_key(const uint32_t (&v)[32], const float* xn, float qn) {
+    // Four independent running extremes, then combined: short dependency chains.
     if constexpr (KindTraits<KIND>::integer) {
-        int32_t m = static_cast<int32_t>(v[0]);
+        int32_t m[4];
 #pragma unroll
-        for (int i = 1; i < 32; ++i) m = max(m, static_cast<int32_t>(v[i]));
-        return -static_cast<float>(m);
+        for (int j = 0; j < 4; ++j) m[j] = static_cast<int32_t>(v[j]);
+#pragma unroll
+        for (int i = 4; i < 32; ++i) m[i & 3] = max(m[i & 3], static_cast<int32_t>(v[i]));
+        return -static_cast<float>(max(max(m[0], m[1]), max(m[2], m[3])));
     } else if constexpr (METRIC == kEuclidean) {
-        float m = fmaf(-2.0f, __uint_as_float(v[0]), xn[0]);
+        float m[4];
 #pragma unroll
-        for (int i = 1; i < 32; ++i) m = fminf(m, fmaf(-2.0f, __uint_as_float(v[i]), xn[i]));
-        return m + qn;
+        for (int j = 0; j < 4; ++j) m[j] = fmaf(-2.0f, __uint_as_float(v[j]), xn[j]);
+#pragma unroll
+        for (int i = 4; i < 32; ++i) m[i & 3] = fminf(m[i & 3], fmaf(-2.0f, __uint_as_float(v[i]), xn[i]));
+        return fminf(fminf(m[0], m[1]), fminf(m[2], m[3])) + qn;
     } else {
-        float m = __uint_as_float(v[0]);
+        float m[4];
 #pragma unroll
-        for (int i = 1; i < 32; ++i) m = fmaxf(m, __uint_as_float(v[i]));
-        return METRIC == kCosine ? 1.0f - m : -m;
+        for (int j = 0; j < 4; ++j) m[j] = __uint_as_float(v[j]);
+#pragma unroll
+        for (int i = 4; i < 32; ++i) m[i & 3] = fmaxf(m[i & 3], __uint_as_float(v[i]));
+        const float mx = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+        return METRIC == kCosine ? 1.0f - mx : -mx;
     }
 }
 
@@ -204,7 +215,7 @@ __global__ void __launch_bounds__(kExactThreads, 1)
         }
         for (uint32_t a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 4);
+            mbar_init(tempty_bar(a), kEpilogueWarps);
         }
         mbar_init(mma_done_bar, 1);
         *abort_flag = 0;
@@ -325,11 +336,16 @@ __global__ void __launch_bounds__(kExactThreads, 1)
         }
     } else {
         // ------------------------------------------------ epilogue
+        const uint32_t ew = warp - 2u;                // epilogue warp 0..7
         const uint32_t quad = warp & 3u;              // TMEM lane quadrant of this warp
+        const uint32_t half = ew >> 2;                // column half of the tile
         const uint32_t lane_row = quad * 32u + lane;  // query row within the tile
-        uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Cfg::kHistOffset) + (warp - 2u) * 256u;
-        float* xs = reinterpret_cast<float*>(smem + Cfg::kNormOffset) + (warp - 2u) * BN;
-        uint2* my_list = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + lane_row) * p.cap;
+        constexpr uint32_t kHalfCols = BN / 2;
+        constexpr uint32_t kChunks = kHalfCols / 32;
+        uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Cfg::kHistOffset) + ew * 256u;
+        float* xs = reinterpret_cast<float*>(smem + Cfg::kNormOffset) + ew * kHalfCols;
+        uint2* const lists = p.cand + (static_cast<size_t>(blockIdx.x) * 2u + half) * kTileM * p.cap;
+        uint2* const my_list = lists + static_cast<size_t>(lane_row) * p.cap;
         const uint32_t lane_base = (quad * 32u) << 16;
         uint32_t tile_iter = 0;
         bool ok = true;
@@ -343,17 +359,18 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             if constexpr (METRIC == kEuclidean) {
                 if (qvalid) qn = p.query_norms[q];
             }
-            float tau = __int_as_float(0x7f800000);  // +inf: this unit's own k-th key
+            float tau = __int_as_float(0x7f800000);  // +inf: this list's own k-th key
             uint32_t cnt = 0;
             for (uint32_t bt = bt0; bt < bt1; ++bt, ++tile_iter) {
                 const uint32_t acc = tile_iter & 1u;
                 const uint32_t acc_phase = (tile_iter >> 1) & 1u;
                 const float thr = admission_threshold(tau, qvalid ? __ldcg(p.qtau + q) : 0xFFFFFFFFu);
-                const uint32_t row_tile = bt * BN;
+                const uint32_t col0 = half * kHalfCols;
+                const uint32_t row_half = bt * BN + col0;
                 if constexpr (METRIC == kEuclidean) {
-                    // stage this tile's base norms (rows past n read as 0)
-                    for (uint32_t j = lane; j < BN; j += 32) {
-                        const uint32_t r = row_tile + j;
+                    // stage this half-tile's base norms (rows past n read as 0)
+                    for (uint32_t j = lane; j < kHalfCols; j += 32) {
+                        const uint32_t r = row_half + j;
                         xs[j] = r < p.n ? __ldg(p.base_norms + r) : 0.0f;
                     }
                     __syncwarp();
@@ -363,18 +380,18 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll 1
-                for (uint32_t c = 0; c < BN / 32; ++c) {
+                for (uint32_t c = 0; c < kChunks; ++c) {
                     uint32_t v[32];
                     // tcgen05.ld is .sync.aligned: the warp must arrive converged.
                     __syncwarp();
-                    tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + c * 32u, v);
+                    tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + col0 + c * 32u, v);
                     tmem_wait_ld();
-                    if (c == BN / 32 - 1) {
+                    if (c == kChunks - 1) {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(tempty_bar(acc));
                     }
-                    const uint32_t row0 = row_tile + c * 32u;
+                    const uint32_t row0 = row_half + c * 32u;
                     if (row0 >= p.n) continue;
                     const uint32_t valid_rows = min(32u, p.n - row0);
                     uint32_t mword = valid_rows == 32u ? 0xFFFFFFFFu : ((1u << valid_rows) - 1u);
@@ -382,31 +399,32 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                     if (!qvalid) mword = 0;
                     const float* xn = xs + c * 32u;
                     // Fast reject: most chunks hold nothing below the threshold.
-                    if (mword != 0u && chunk_min_key<KIND, METRIC>(v, xn, qn) < thr) {
+                    const bool slow = mword != 0u && chunk_min_key<KIND, METRIC>(v, xn, qn) < thr;
+                    if (__any_sync(0xffffffffu, slow)) {
+                        // Predicated appends: no per-value branches.
 #pragma unroll
                         for (uint32_t i = 0; i < 32; ++i) {
                             const float key = key_of<KIND, METRIC>(v[i], xn[i], qn);
-                            if (((mword >> i) & 1u) && key < thr) {
-                                my_list[cnt] = make_uint2(__float_as_uint(key), p.row_offset + row0 + i);
-                                ++cnt;
-                            }
+                            const bool take = slow && ((mword >> i) & 1u) && key < thr;
+                            if (take) my_list[cnt] = make_uint2(__float_as_uint(key), p.row_offset + row0 + i);
+                            cnt += take ? 1u : 0u;
                         }
                     }
-                    // Keep room for one more chunk: compact any list that could overflow.
-                    __syncwarp();
-                    uint32_t need = __ballot_sync(0xffffffffu, cnt + 32u > p.cap);
-                    while (need) {
-                        const uint32_t L = __ffs(need) - 1;
-                        const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
-                        uint2* list_l = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + quad * 32u + L) * p.cap;
-                        const float th = compact_one(list_l, cnt_l, p.k, p.cap, hist);
-                        if (lane == L) {
-                            tau = th;
-                            cnt = p.k;
-                            atomicMin(p.qtau + q, ordered_key(th));
-                        }
-                        need &= need - 1;
+                }
+                // Keep room for one more half-tile: compact any list that could overflow.
+                __syncwarp();
+                uint32_t need = __ballot_sync(0xffffffffu, cnt + kHalfCols > p.cap);
+                while (need) {
+                    const uint32_t L = __ffs(need) - 1;
+                    const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
+                    uint2* list_l = lists + static_cast<size_t>(quad * 32u + L) * p.cap;
+                    const float th = compact_one(list_l, cnt_l, p.k, p.cap, hist);
+                    if (lane == L) {
+                        tau = th;
+                        cnt = p.k;
+                        atomicMin(p.qtau + q, ordered_key(th));
                     }
+                    need &= need - 1;
                 }
                 if constexpr (METRIC == kEuclidean) __syncwarp();
             }
@@ -417,7 +435,7 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             while (need) {
                 const uint32_t L = __ffs(need) - 1;
                 const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
-                uint2* list_l = p.cand + (static_cast<size_t>(blockIdx.x) * kTileM + quad * 32u + L) * p.cap;
+                uint2* list_l = lists + static_cast<size_t>(quad * 32u + L) * p.cap;
                 const float th = compact_one(list_l, cnt_l, p.k, p.cap, hist);
                 if (lane == L) {
                     cnt = p.k;
@@ -425,8 +443,9 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                 }
                 need &= need - 1;
             }
+            __syncwarp();
             if (qvalid) {
-                uint2* out = p.partial + (static_cast<size_t>(q) * p.splits + sp) * p.k;
+                uint2* out = p.partial + ((static_cast<size_t>(q) * p.splits + sp) * 2u + half) * p.k;
                 for (uint32_t i = 0; i < p.k; ++i) {
                     out[i] = i < cnt ? my_list[i] : make_uint2(0x7f800000u, 0xFFFFFFFFu);
                 }
