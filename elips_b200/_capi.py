@@ -48,6 +48,8 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
     ("elips_b200_exact_search_device", c_int,
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_exact_search_noalloc", c_int,
+     [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("elips_b200_exact_search_candidates_device", c_int,
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_uint32, c_void_p, c_void_p]),
     ("elips_b200_merge_candidates_device", c_int,

@@ -429,6 +429,82 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
                      stream);
 }
 
+void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t k, const uint32_t* mask,
+                                          float* out_dist, int64_t* out_rows, uint8_t* scratch,
+                                          size_t scratch_bytes, uint32_t max_grid,
+                                          cudaStream_t stream) const {
+    if (nq == 0 || k == 0) return;
+    if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
+    if (nq > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "too many queries in one call");
+    if (queries == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "queries is null");
+    if (scratch == nullptr || max_grid == 0) fail(ELIPS_B200_INVALID_ARGUMENT, "no scratch buffer");
+    DeviceGuard g(device_);
+    const DeviceProps& props = device_props(device_);
+    if (n_ == 0) {
+        merge_candidates(device_, nullptr, static_cast<uint32_t>(nq), 0, static_cast<uint32_t>(k), 0, 0,
+                         metric_, out_dist, out_rows, nullptr, stream);
+        return;
+    }
+    const uint32_t n = static_cast<uint32_t>(n_);
+    const int ctas = static_cast<int>(std::min<uint32_t>(max_grid, static_cast<uint32_t>(props.num_sms)));
+    const ExactPlan plan = plan_exact(static_cast<uint32_t>(nq), n, static_cast<uint32_t>(k), bn_of(kind_), ctas);
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    auto align = [](size_t x) { return (x + 255) / 256 * 256; };
+    const size_t q_ops = align(nq * row_bytes);
+    const size_t q_lo = kind_ == OperandKind::TF32X3 ? q_ops : 0;
+    const size_t q_norm = metric_ == kEuclidean ? align(nq * sizeof(float)) : 0;
+    const size_t cand = align(static_cast<size_t>(plan.grid) * 2 * kTileM * plan.cap * sizeof(uint2));
+    const size_t partial = align(nq * plan.splits * 2 * k * sizeof(uint2));
+    const size_t qtau = align(nq * sizeof(uint32_t));
+    const size_t need = q_ops + q_lo + q_norm + cand + partial + qtau;
+    if (need > scratch_bytes)
+        fail(ELIPS_B200_INVALID_ARGUMENT,
+             "search needs " + std::to_string(need >> 20) + " MiB of scratch, above the " +
+                 std::to_string(scratch_bytes >> 20) + " MiB fixed buffer; split the query batch");
+    uint8_t* s = scratch;
+    void* qa = s;
+    void* qlo = q_lo ? s + q_ops : nullptr;
+    float* qn = q_norm ? reinterpret_cast<float*>(s + q_ops + q_lo) : nullptr;
+    uint2* cand_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm);
+    uint2* part_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand);
+    uint32_t* qtau_buf = reinterpret_cast<uint32_t*>(s + q_ops + q_lo + q_norm + cand + partial);
+    // The buffer keeps the previous call's contents: the shared bounds must
+    // start at "no bound"; the lists and partial outputs are always written
+    // before they are read.
+    check_cuda(cudaMemsetAsync(qtau_buf, 0xFF, nq * sizeof(uint32_t), stream), ELIPS_B200_KERNEL_LAUNCH_FAILED,
+               "threshold init");
+    prep_operands(kind_, queries, nq, dim_, d_pad_, qa, qlo, qn, stream);
+    const CUtensorMapDataType dt = tma_dtype_of(kind_);
+    const CUtensorMap ma = make_operand_map(qa, dt, elem_bytes_, d_pad_, nq, kTileM);
+    const CUtensorMap mb = make_operand_map(ops_.get(), dt, elem_bytes_, d_pad_, n, plan.bn);
+    CUtensorMap malo = ma, mblo = mb;
+    if (kind_ == OperandKind::TF32X3) {
+        malo = make_operand_map(qlo, dt, elem_bytes_, d_pad_, nq, kTileM);
+        mblo = make_operand_map(ops_lo_.get(), dt, elem_bytes_, d_pad_, n, plan.bn);
+    }
+    ExactParams prm{};
+    prm.base_norms = static_cast<const float*>(norms_.get());
+    prm.query_norms = qn;
+    prm.mask = mask;
+    prm.cand = cand_buf;
+    prm.partial = part_buf;
+    prm.qtau = qtau_buf;
+    prm.n = n;
+    prm.nq = static_cast<uint32_t>(nq);
+    prm.k = static_cast<uint32_t>(k);
+    prm.cap = plan.cap;
+    prm.splits = plan.splits;
+    prm.n_qt = plan.n_qt;
+    prm.n_bt = plan.n_bt;
+    prm.num_units = plan.n_qt * plan.splits;
+    prm.kblocks = d_pad_ * elem_bytes_ / kKBlockBytes;
+    prm.row_offset = 0;
+    prm.metric = metric_;
+    dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan.grid, stream);
+    merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits * 2, static_cast<uint32_t>(k),
+                     static_cast<uint64_t>(plan.splits) * 2 * k, k, metric_, out_dist, out_rows, nullptr, stream);
+}
+
 void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,
                       uint64_t stride_q, uint64_t stride_l, int metric, float* out_dist,
                       int64_t* out_rows, uint2* out_cand, cudaStream_t stream) {

@@ -110,6 +110,14 @@ public:
                        uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
                        cudaStream_t stream) const;
 
+    // The same search with all scratch carved from a caller-provided device
+    // buffer of `scratch_bytes` and at most `max_grid` CTAs; performs no
+    // device allocation. Fails with INVALID_ARGUMENT when the call needs more
+    // scratch than the buffer holds.
+    void search_device_in_scratch(const void* queries, size_t nq, size_t k, const uint32_t* mask,
+                                  float* out_dist, int64_t* out_rows, uint8_t* scratch,
+                                  size_t scratch_bytes, uint32_t max_grid, cudaStream_t stream) const;
+
 private:
     void reserve(size_t rows);
 

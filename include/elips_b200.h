@@ -120,6 +120,24 @@ ELIPS_B200_API int elips_b200_exact_search_device(const elips_b200_exact* index,
                                    size_t nq, size_t k, const uint32_t* mask, float* out_dist,
                                    int64_t* out_rows, void* stream);
 
+/* Exact search that allocates no device memory. It has no counterpart in
+ * the reference: it exists for callers that cannot call cudaMalloc at search
+ * time -- a process whose device memory is already fully reserved by another
+ * allocator, or a latency-critical path where an allocation may synchronise
+ * the device. Same arguments and results as elips_b200_exact_search_device
+ * (DEVICE pointers, asynchronous on `stream`, no row offset). Scratch comes
+ * from one fixed 64 MiB device array inside this library, which every GPU that
+ * loads the library holds until the process exits; a call needing more (large
+ * query batches) fails with ELIPS_B200_INVALID_ARGUMENT, and at most 32 SMs
+ * are used. The first call on a device looks up the array's address (no
+ * allocation); make that first call before any stream capture. All calls
+ * share the array and it keeps the last call's contents: calls that overlap
+ * on the GPU (different streams, or unordered host threads) race, so the
+ * caller must serialise them. */
+ELIPS_B200_API int elips_b200_exact_search_noalloc(const elips_b200_exact* index, const void* queries,
+                                                   size_t nq, size_t k, const uint32_t* mask,
+                                                   float* out_dist, int64_t* out_rows, void* stream);
+
 /* Shard-level search for row-sharded multi-GPU search
  * (GpuDistributedIndex::search_batch, src/gpu_engine/GpuDistributedIndex.cpp:
  * 155-207): DEVICE pointers; writes nq x k candidates as pairs of uint32
