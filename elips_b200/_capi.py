@@ -34,6 +34,10 @@ PRECISION_INT8 = 2
 PRECISION_AUTO = 3
 PRECISION_BF16 = 4
 
+CODEC_PQ = 1
+CODEC_OPQ = 2
+CODEC_SQ8 = 3
+
 # (name, restype, argtypes) for every entry point in include/elips_b200.h.
 SIGNATURES = [
     ("elips_b200_status_string", c_char_p, [c_int]),
@@ -54,6 +58,19 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_uint32, c_void_p, c_void_p]),
     ("elips_b200_merge_candidates_device", c_int,
      [c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_compute_distances_batch", c_int,
+     [c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_int, c_void_p]),
+    ("elips_b200_top_k", c_int,
+     [c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_void_p]),
+    ("elips_b200_quant_create", c_int,
+     [c_int, c_int, c_int, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, POINTER(c_void_p)]),
+    ("elips_b200_quant_add", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("elips_b200_quant_add_codes", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("elips_b200_quant_size", c_int, [c_void_p, POINTER(c_size_t)]),
+    ("elips_b200_quant_search", c_int, [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p]),
+    ("elips_b200_quant_search_device", c_int,
+     [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_quant_destroy", c_int, [c_void_p]),
     ("elips_b200_profiler_enable", c_int, [c_int]),
     ("elips_b200_profiler_stats", c_int,
      [c_char_p, POINTER(ctypes.c_uint64), POINTER(ctypes.c_double), POINTER(ctypes.c_uint64)]),

@@ -1,0 +1,444 @@
+// Host side of the bit-exact SIMT paths: GpuPort's distance / top-k
+// primitives and the ExactIndex-with-Quantizer scans (PQ, OPQ, sq8).
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../../include/elips_b200.h"
+#include "engine.cuh"
+#include "profiler.cuh"
+#include "scan_kernels.cuh"
+
+namespace eb {
+namespace {
+
+constexpr uint32_t kMaxK = 1024;
+
+uint32_t pow2_at_least(uint32_t x) {
+    uint32_t p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+uint32_t btk_cap(uint32_t k) { return (k + kScanThreads + 31u) / 32u * 32u; }
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+void launch_check(const char* what) { check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, what); }
+
+// Number of row splits for a scan over n rows with `cta_rows` CTAs per split
+// column: aim for ~4 CTAs per SM, keep >= 1024 rows per split.
+uint32_t scan_splits(uint32_t n, uint32_t ctas_per_split, int num_sms) {
+    const uint32_t want = std::max<uint32_t>(1, (4u * num_sms + ctas_per_split - 1) / ctas_per_split);
+    const uint32_t max_by_rows = std::max<uint32_t>(1, n / 1024u);
+    return std::min<uint32_t>({want, max_by_rows, 4096u});
+}
+
+}  // namespace
+
+void compute_distances_device(int device, const float* q, const float* db, float* out, size_t nq, size_t nb,
+                              size_t d, int metric, cudaStream_t stream) {
+    if (nq == 0 || nb == 0) return;
+    if (metric < 0 || metric > 2) fail(ELIPS_B200_UNSUPPORTED_METRIC, "unknown metric");
+    if (d == 0) fail(ELIPS_B200_INVALID_ARGUMENT, "dimension is zero");
+    if (nb > 0xFFFFFFFFull || nq > 65535ull * kDistQ) fail(ELIPS_B200_INVALID_ARGUMENT, "batch too large");
+    DeviceGuard g(device);
+    device_props(device);
+    const dim3 grid(static_cast<uint32_t>((nb + kDistRows - 1) / kDistRows), static_cast<uint32_t>((nq + kDistQ - 1) / kDistQ));
+    Profiler::Scope prof("distances", stream, static_cast<uint64_t>(nq) * nb);
+    distances_kernel<<<grid, kDistRows, 0, stream>>>(q, db, static_cast<uint32_t>(nq), static_cast<uint32_t>(nb),
+                                                    static_cast<uint32_t>(d), metric, out);
+    launch_check("distances kernel");
+}
+
+void top_k_device(int device, const float* dist, uint32_t* idx, float* val, size_t nq, size_t nb, size_t k,
+                  cudaStream_t stream) {
+    if (nq == 0 || k == 0) return;
+    if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
+    if (nb > 0xFFFFFFFEull || nq > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "batch too large");
+    DeviceGuard g(device);
+    device_props(device);
+    const uint32_t cap = btk_cap(static_cast<uint32_t>(k));
+    const uint32_t kp = pow2_at_least(static_cast<uint32_t>(k));
+    const size_t smem = btk_bytes(cap) + static_cast<size_t>(kp) * 8;
+    check_cuda(cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+               ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+    Profiler::Scope prof("topk_rows", stream, static_cast<uint64_t>(nq) * nb);
+    topk_rows_kernel<<<static_cast<uint32_t>(nq), kScanThreads, smem, stream>>>(
+        dist, static_cast<uint32_t>(nq), static_cast<uint32_t>(nb), static_cast<uint32_t>(k), cap, kp, idx, val);
+    launch_check("top-k kernel");
+}
+
+// ExactIndex with a Quantizer attached, codes resident on the device.
+class QuantIndex {
+public:
+    QuantIndex(int device, int codec, int metric, uint32_t dim, uint32_t pq_dim, uint32_t pq_bits,
+               const float* params, const float* rotation)
+        : device_(device), codec_(codec), metric_(metric), dim_(dim), pq_dim_(pq_dim), pq_bits_(pq_bits) {
+        if (metric < 0 || metric > 2) fail(ELIPS_B200_UNSUPPORTED_METRIC, "unknown metric");
+        if (dim == 0 || dim > 65535) fail(ELIPS_B200_INVALID_ARGUMENT, "dimension must be in [1, 65535]");
+        if (params == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "codec parameters are null");
+        device_props(device);
+        DeviceGuard g(device);
+        if (codec == ELIPS_B200_CODEC_SQ8) {
+            code_bytes_ = dim;
+            params_ = DeviceBuffer(device, 2ull * dim * sizeof(float));
+            check_cuda(cudaMemcpy(params_.get(), params, 2ull * dim * sizeof(float), cudaMemcpyHostToDevice),
+                       ELIPS_B200_TRANSFER_FAILED, "sq8 parameters");
+        } else if (codec == ELIPS_B200_CODEC_PQ || codec == ELIPS_B200_CODEC_OPQ) {
+            if (pq_dim == 0 || dim % pq_dim != 0 || pq_bits < 4 || pq_bits > 8)
+                fail(ELIPS_B200_INVALID_ARGUMENT, "pq_dim must divide the dimension and pq_bits be in [4, 8]");
+            if ((codec == ELIPS_B200_CODEC_OPQ) != (rotation != nullptr))
+                fail(ELIPS_B200_INVALID_ARGUMENT, "OPQ needs a rotation and PQ must not have one");
+            code_bytes_ = pq_dim;
+            ksub_ = 1u << pq_bits;
+            const size_t cb = static_cast<size_t>(pq_dim) * ksub_ * (dim / pq_dim);
+            params_ = DeviceBuffer(device, cb * sizeof(float));
+            check_cuda(cudaMemcpy(params_.get(), params, cb * sizeof(float), cudaMemcpyHostToDevice),
+                       ELIPS_B200_TRANSFER_FAILED, "pq codebook");
+            if (rotation != nullptr) {
+                rotation_ = DeviceBuffer(device, static_cast<size_t>(dim) * dim * sizeof(float));
+                check_cuda(cudaMemcpy(rotation_.get(), rotation, static_cast<size_t>(dim) * dim * sizeof(float),
+                                      cudaMemcpyHostToDevice),
+                           ELIPS_B200_TRANSFER_FAILED, "opq rotation");
+            }
+        } else {
+            fail(ELIPS_B200_INVALID_ARGUMENT, "unknown codec");
+        }
+    }
+
+    int device() const { return device_; }
+    size_t size() const { return n_; }
+    uint32_t dim() const { return dim_; }
+
+    void add_codes_device(const uint8_t* codes, size_t n, cudaStream_t stream) {
+        reserve(n_ + n);
+        check_cuda(cudaMemcpyAsync(static_cast<uint8_t*>(codes_.get()) + n_ * code_bytes_, codes, n * code_bytes_,
+                                   cudaMemcpyDeviceToDevice, stream),
+                   ELIPS_B200_TRANSFER_FAILED, "code copy");
+        check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_TRANSFER_FAILED, "code copy");
+        n_ += n;
+    }
+
+    void add_codes_host(const uint8_t* codes, size_t n) {
+        if (n == 0) return;
+        DeviceGuard g(device_);
+        reserve(n_ + n);
+        check_cuda(cudaMemcpy(static_cast<uint8_t*>(codes_.get()) + n_ * code_bytes_, codes, n * code_bytes_,
+                              cudaMemcpyHostToDevice),
+                   ELIPS_B200_TRANSFER_FAILED, "code upload");
+        n_ += n;
+    }
+
+    // Encodes fp32 rows (device) with the codec's own encode and appends them.
+    void encode_add_device(const float* rows, size_t n, cudaStream_t stream) {
+        if (n == 0) return;
+        DeviceGuard g(device_);
+        reserve(n_ + n);
+        uint8_t* dst = static_cast<uint8_t*>(codes_.get()) + n_ * code_bytes_;
+        const float* src = rows;
+        StreamScratch rot(rotation_.get() ? n * dim_ * sizeof(float) : 0, stream);
+        if (rotation_.get() != nullptr) {
+            const uint64_t total = static_cast<uint64_t>(n) * dim_;
+            Profiler::Scope prof("rotate_rows", stream, n);
+            rotate_rows_kernel<<<static_cast<uint32_t>((total + 255) / 256), 256, 0, stream>>>(
+                static_cast<const float*>(rotation_.get()), rows, n, dim_, reinterpret_cast<float*>(rot.get()));
+            launch_check("rotate kernel");
+            src = reinterpret_cast<const float*>(rot.get());
+        }
+        if (codec_ == ELIPS_B200_CODEC_SQ8) {
+            const uint64_t total = static_cast<uint64_t>(n) * dim_;
+            const float* mins = static_cast<const float*>(params_.get());
+            Profiler::Scope prof("sq8_encode", stream, n);
+            sq8_encode_kernel<<<static_cast<uint32_t>((total + 255) / 256), 256, 0, stream>>>(src, mins, mins + dim_, n,
+                                                                                           dim_, dst);
+        } else {
+            const uint64_t total = static_cast<uint64_t>(n) * pq_dim_;
+            Profiler::Scope prof("pq_encode", stream, n);
+            pq_encode_kernel<<<static_cast<uint32_t>((total + 127) / 128), 128, 0, stream>>>(
+                src, static_cast<const float*>(params_.get()), n, dim_, pq_dim_, ksub_, dst);
+        }
+        launch_check("encode kernel");
+        check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "encode");
+        n_ += n;
+    }
+
+    void search_device(const float* queries, size_t nq, size_t k, float* out_dist, int64_t* out_rows,
+                       cudaStream_t stream) const {
+        if (nq == 0 || k == 0) return;
+        if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
+        if (nq > 65535ull * kPqQueriesPerCta) fail(ELIPS_B200_INVALID_ARGUMENT, "too many queries in one call");
+        DeviceGuard g(device_);
+        const DeviceProps& props = device_props(device_);
+        if (n_ == 0) {
+            merge_candidates(device_, nullptr, static_cast<uint32_t>(nq), 0, static_cast<uint32_t>(k), 0, 0, 0, out_dist,
+                             out_rows, nullptr, stream);
+            return;
+        }
+        const uint32_t n = static_cast<uint32_t>(n_);
+        const uint32_t cap = btk_cap(static_cast<uint32_t>(k));
+        const bool sq8 = codec_ == ELIPS_B200_CODEC_SQ8;
+        const size_t lut_floats = sq8 ? static_cast<size_t>(dim_) * 256 : static_cast<size_t>(pq_dim_) * ksub_;
+        const uint32_t ctas_per_split = sq8 ? static_cast<uint32_t>(nq)
+                                            : static_cast<uint32_t>((nq + kPqQueriesPerCta - 1) / kPqQueriesPerCta);
+        const uint32_t splits = scan_splits(n, ctas_per_split, props.num_sms);
+        const size_t rot_bytes = rotation_.get() ? align256(nq * dim_ * sizeof(float)) : 0;
+        const size_t lut_bytes = align256(nq * lut_floats * sizeof(float));
+        const size_t part_bytes = align256(nq * splits * k * sizeof(uint2));
+        StreamScratch scratch(rot_bytes + lut_bytes + part_bytes, stream);
+        const float* q = queries;
+        if (rot_bytes) {
+            float* rq = reinterpret_cast<float*>(scratch.get());
+            const uint64_t total = static_cast<uint64_t>(nq) * dim_;
+            Profiler::Scope prof("rotate_rows", stream, nq);
+            rotate_rows_kernel<<<static_cast<uint32_t>((total + 255) / 256), 256, 0, stream>>>(
+                static_cast<const float*>(rotation_.get()), queries, nq, dim_, rq);
+            launch_check("rotate kernel");
+            q = rq;
+        }
+        float* lut = reinterpret_cast<float*>(scratch.get() + rot_bytes);
+        uint2* part = reinterpret_cast<uint2*>(scratch.get() + rot_bytes + lut_bytes);
+        const uint64_t lut_total = nq * lut_floats;
+        const uint32_t lut_blocks = static_cast<uint32_t>((lut_total + 255) / 256);
+        if (sq8) {
+            const float* mins = static_cast<const float*>(params_.get());
+            {
+                Profiler::Scope prof("sq8_lut", stream, nq);
+                sq8_lut_kernel<<<lut_blocks, 256, 0, stream>>>(q, mins, mins + dim_, static_cast<uint32_t>(nq), dim_,
+                                                              metric_, lut);
+                launch_check("sq8 lut kernel");
+            }
+            const bool in_smem = dim_ <= 192;
+            const size_t smem = btk_bytes(cap) + (in_smem ? static_cast<size_t>(dim_) * 256 * sizeof(float) : 0);
+            check_cuda(cudaFuncSetAttribute(sq8_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem)),
+                       ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+            Profiler::Scope prof("sq8_scan", stream, static_cast<uint64_t>(nq) * n);
+            sq8_scan_kernel<<<dim3(splits, static_cast<uint32_t>(nq)), kScanThreads, smem, stream>>>(
+                lut, static_cast<const uint8_t*>(codes_.get()), n, dim_, metric_, static_cast<uint32_t>(k), cap, splits,
+                in_smem ? 1 : 0, part);
+            launch_check("sq8 scan kernel");
+        } else {
+            {
+                Profiler::Scope prof("pq_lut", stream, nq);
+                pq_lut_kernel<<<lut_blocks, 256, 0, stream>>>(q, static_cast<const float*>(params_.get()),
+                                                             static_cast<uint32_t>(nq), dim_, pq_dim_, ksub_, metric_, lut);
+                launch_check("pq lut kernel");
+            }
+            const size_t smem = kPqQueriesPerCta * (lut_floats * sizeof(float) + btk_bytes(cap));
+            if (smem > device_props(device_).max_smem_optin)
+                fail(ELIPS_B200_INVALID_ARGUMENT, "pq_dim x 2^pq_bits too large for the scan kernel");
+            check_cuda(cudaFuncSetAttribute(pq_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem)),
+                       ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+            const dim3 grid(splits, static_cast<uint32_t>((nq + kPqQueriesPerCta - 1) / kPqQueriesPerCta));
+            Profiler::Scope prof("pq_scan", stream, static_cast<uint64_t>(nq) * n);
+            pq_scan_kernel<<<grid, kScanThreads, smem, stream>>>(lut, static_cast<const uint8_t*>(codes_.get()), n,
+                                                                 static_cast<uint32_t>(nq), pq_dim_, ksub_, metric_,
+                                                                 static_cast<uint32_t>(k), cap, splits, part);
+            launch_check("pq scan kernel");
+        }
+        // Keys are final lut_distance values: the merge applies no transform (0).
+        merge_candidates(device_, part, static_cast<uint32_t>(nq), splits, static_cast<uint32_t>(k),
+                         static_cast<uint64_t>(splits) * k, k, 0, out_dist, out_rows, nullptr, stream);
+    }
+
+private:
+    void reserve(size_t rows) {
+        if (rows <= capacity_) return;
+        if (rows >= 0xFFFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "index limited to 2^32-2 rows");
+        const size_t cap = std::max<size_t>(rows, capacity_ + capacity_ / 2);
+        DeviceBuffer nb(device_, cap * code_bytes_);
+        if (n_ > 0)
+            check_cuda(cudaMemcpy(nb.get(), codes_.get(), n_ * code_bytes_, cudaMemcpyDeviceToDevice),
+                       ELIPS_B200_TRANSFER_FAILED, "grow copy");
+        codes_ = std::move(nb);
+        capacity_ = cap;
+    }
+
+    int device_, codec_, metric_;
+    uint32_t dim_, pq_dim_, pq_bits_, ksub_ = 256, code_bytes_ = 0;
+    size_t n_ = 0, capacity_ = 0;
+    DeviceBuffer params_, rotation_, codes_;
+};
+
+}  // namespace eb
+
+struct elips_b200_quant {
+    eb::QuantIndex index;
+};
+
+namespace {
+
+template <class Fn>
+int guarded(Fn&& fn) {
+    try {
+        fn();
+        return ELIPS_B200_OK;
+    } catch (const eb::Error& e) {
+        std::fprintf(stderr, "elips_b200: %s\n", e.what.c_str());
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        return ELIPS_B200_INSUFFICIENT_MEMORY;
+    } catch (...) {
+        return ELIPS_B200_KERNEL_LAUNCH_FAILED;
+    }
+}
+
+size_t align_up(size_t x) { return (x + 255) / 256 * 256; }
+
+struct OwnedStream {
+    cudaStream_t s = nullptr;
+    OwnedStream() {
+        eb::check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), ELIPS_B200_INITIALIZATION_FAILED,
+                       "cudaStreamCreate");
+    }
+    ~OwnedStream() { cudaStreamDestroy(s); }
+};
+
+}  // namespace
+
+extern "C" {
+
+int elips_b200_compute_distances_batch(int device, const float* queries, const float* database,
+                                       float* distances_out, size_t nq, size_t nb, size_t dim, int metric,
+                                       int pointers_on_device, void* stream) {
+    if (nq > 0 && nb > 0 && (queries == nullptr || database == nullptr || distances_out == nullptr))
+        return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        if (pointers_on_device) {
+            eb::compute_distances_device(device, queries, database, distances_out, nq, nb, dim, metric,
+                                         static_cast<cudaStream_t>(stream));
+            return;
+        }
+        if (nq == 0 || nb == 0) return;
+        eb::DeviceGuard g(device);
+        OwnedStream st;
+        {
+            eb::StreamScratch s((nq + nb) * dim * 4 + nq * nb * 4 + 512, st.s);
+            float* dq = reinterpret_cast<float*>(s.get());
+            float* ddb = dq + nq * dim;
+            float* dout = ddb + nb * dim;
+            eb::check_cuda(cudaMemcpyAsync(dq, queries, nq * dim * 4, cudaMemcpyHostToDevice, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "query upload");
+            eb::check_cuda(cudaMemcpyAsync(ddb, database, nb * dim * 4, cudaMemcpyHostToDevice, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "database upload");
+            eb::compute_distances_device(device, dq, ddb, dout, nq, nb, dim, metric, st.s);
+            eb::check_cuda(cudaMemcpyAsync(distances_out, dout, nq * nb * 4, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "distance download");
+        }
+        eb::check_cuda(cudaStreamSynchronize(st.s), ELIPS_B200_KERNEL_LAUNCH_FAILED, "distances");
+    });
+}
+
+int elips_b200_top_k(int device, const float* distances, uint32_t* indices_out, float* values_out, size_t nq,
+                     size_t nb, size_t k, int pointers_on_device, void* stream) {
+    if (nq > 0 && k > 0 && (indices_out == nullptr || values_out == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && nb > 0 && distances == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        if (pointers_on_device) {
+            eb::top_k_device(device, distances, indices_out, values_out, nq, nb, k, static_cast<cudaStream_t>(stream));
+            return;
+        }
+        if (nq == 0 || k == 0) return;
+        eb::DeviceGuard g(device);
+        OwnedStream st;
+        {
+            eb::StreamScratch s(nq * nb * 4 + nq * k * 8 + 512, st.s);
+            float* dd = reinterpret_cast<float*>(s.get());
+            uint32_t* di = reinterpret_cast<uint32_t*>(dd + nq * nb);
+            float* dv = reinterpret_cast<float*>(di + nq * k);
+            eb::check_cuda(cudaMemcpyAsync(dd, distances, nq * nb * 4, cudaMemcpyHostToDevice, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "distance upload");
+            eb::top_k_device(device, dd, di, dv, nq, nb, k, st.s);
+            eb::check_cuda(cudaMemcpyAsync(indices_out, di, nq * k * 4, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "index download");
+            eb::check_cuda(cudaMemcpyAsync(values_out, dv, nq * k * 4, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "value download");
+        }
+        eb::check_cuda(cudaStreamSynchronize(st.s), ELIPS_B200_KERNEL_LAUNCH_FAILED, "top_k");
+    });
+}
+
+int elips_b200_quant_create(int device, int codec, int metric, uint32_t dimension, uint32_t pq_dim,
+                            uint32_t pq_bits, const float* params, const float* rotation,
+                            elips_b200_quant** out) {
+    if (out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *out = nullptr;
+    return guarded([&] {
+        *out = new elips_b200_quant{eb::QuantIndex(device, codec, metric, dimension, pq_dim, pq_bits, params, rotation)};
+    });
+}
+
+int elips_b200_quant_add(elips_b200_quant* index, const float* rows, size_t n) {
+    if (index == nullptr || (n > 0 && rows == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        if (n == 0) return;
+        eb::DeviceGuard g(index->index.device());
+        OwnedStream st;
+        const size_t bytes = n * index->index.dim() * sizeof(float);
+        eb::StreamScratch s(bytes, st.s);
+        eb::check_cuda(cudaMemcpyAsync(s.get(), rows, bytes, cudaMemcpyHostToDevice, st.s), ELIPS_B200_TRANSFER_FAILED,
+                       "row upload");
+        index->index.encode_add_device(reinterpret_cast<const float*>(s.get()), n, st.s);
+    });
+}
+
+int elips_b200_quant_add_codes(elips_b200_quant* index, const uint8_t* codes, size_t n) {
+    if (index == nullptr || (n > 0 && codes == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.add_codes_host(codes, n); });
+}
+
+int elips_b200_quant_size(const elips_b200_quant* index, size_t* n_out) {
+    if (index == nullptr || n_out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *n_out = index->index.size();
+    return ELIPS_B200_OK;
+}
+
+int elips_b200_quant_search(const elips_b200_quant* index, const float* queries, size_t nq, size_t k,
+                            float* out_dist, int64_t* out_rows) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (queries == nullptr || out_dist == nullptr || out_rows == nullptr))
+        return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        if (nq == 0 || k == 0) return;
+        const eb::QuantIndex& ix = index->index;
+        eb::DeviceGuard g(ix.device());
+        OwnedStream st;
+        {
+            const size_t qb = nq * ix.dim() * sizeof(float);
+            const size_t ob = nq * k;
+            eb::StreamScratch s(align_up(qb) + ob * 12 + 512, st.s);
+            float* dq = reinterpret_cast<float*>(s.get());
+            float* dd = reinterpret_cast<float*>(s.get() + align_up(qb));
+            int64_t* dr = reinterpret_cast<int64_t*>(s.get() + align_up(qb) + align_up(ob * 4));
+            eb::check_cuda(cudaMemcpyAsync(dq, queries, qb, cudaMemcpyHostToDevice, st.s), ELIPS_B200_TRANSFER_FAILED,
+                           "query upload");
+            ix.search_device(dq, nq, k, dd, dr, st.s);
+            eb::check_cuda(cudaMemcpyAsync(out_dist, dd, ob * 4, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "distance download");
+            eb::check_cuda(cudaMemcpyAsync(out_rows, dr, ob * 8, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "row download");
+        }
+        eb::check_cuda(cudaStreamSynchronize(st.s), ELIPS_B200_KERNEL_LAUNCH_FAILED, "quantized search");
+    });
+}
+
+int elips_b200_quant_search_device(const elips_b200_quant* index, const float* queries, size_t nq, size_t k,
+                                   float* out_dist, int64_t* out_rows, void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (queries == nullptr || out_dist == nullptr || out_rows == nullptr))
+        return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.search_device(queries, nq, k, out_dist, out_rows, static_cast<cudaStream_t>(stream)); });
+}
+
+int elips_b200_quant_destroy(elips_b200_quant* index) {
+    if (index == nullptr) return ELIPS_B200_OK;
+    return guarded([&] {
+        eb::DeviceGuard g(index->index.device());
+        delete index;
+    });
+}
+
+}  // extern "C"

@@ -159,6 +159,71 @@ ELIPS_B200_API int elips_b200_merge_candidates_device(int device, const uint32_t
                                        size_t lists, size_t k, int metric, float* out_dist,
                                        int64_t* out_rows, void* stream);
 
+/* ------------------------------------------------- GpuPort primitives */
+/* GpuPort::compute_distances_batch (include/elips/gpu_engine/GpuPort.hpp:
+ * 65-73): distances_out[q * nb + i] = elips::distance(metric, queries[q],
+ * database[i]) with the reference's arithmetic bit for bit (sequential fp32,
+ * no fused multiply-add, src/Metrics.cpp:20-37,104-115). Row-major fp32
+ * inputs. pointers_on_device = 0: HOST pointers, synchronous (copies in and
+ * out, as a GpuPort must accept host spans); 1: DEVICE pointers, asynchronous
+ * on `stream`. */
+ELIPS_B200_API int elips_b200_compute_distances_batch(int device, const float* queries,
+                                                      const float* database, float* distances_out,
+                                                      size_t nq, size_t nb, size_t dim, int metric,
+                                                      int pointers_on_device, void* stream);
+
+/* GpuPort::top_k (GpuPort.hpp:75-82): per row of an nq x nb distance matrix,
+ * the k smallest values ascending with their column indexes (ties by index);
+ * slots past nb hold index 0xFFFFFFFF and +inf. Pointer modes as above. */
+ELIPS_B200_API int elips_b200_top_k(int device, const float* distances, uint32_t* indices_out,
+                                    float* values_out, size_t nq, size_t nb, size_t k,
+                                    int pointers_on_device, void* stream);
+
+/* ---------------------------------------------- quantized exhaustive index */
+/* ExactIndex with a trained Quantizer attached (include/elips/index_engine/
+ * ExactIndex.hpp:26-66, search at src/ExactIndex.cpp:62-71): codes resident
+ * on the device, each query's lookup table built with make_lut and every row
+ * scored with lut_distance, bit for bit (ProductQuantizer.cpp:118-183,
+ * ScalarQuantizer.cpp:83-128). Codec ids are quant::CodecId
+ * (include/elips/quant_engine/QuantParams.hpp:19-26). */
+enum {
+    ELIPS_B200_CODEC_PQ = 1,
+    ELIPS_B200_CODEC_OPQ = 2,
+    ELIPS_B200_CODEC_SQ8 = 3
+};
+
+typedef struct elips_b200_quant elips_b200_quant;
+
+/* params: PQ/OPQ codebook [pq_dim][2^pq_bits][dimension/pq_dim] (subspace-
+ * major, ProductQuantizer.hpp:102-104); SQ8 mins[dimension] followed by
+ * scales[dimension]. rotation: OPQ only, dimension x dimension row-major
+ * (NULL for PQ and SQ8). HOST pointers, copied. */
+ELIPS_B200_API int elips_b200_quant_create(int device, int codec, int metric, uint32_t dimension,
+                                           uint32_t pq_dim, uint32_t pq_bits, const float* params,
+                                           const float* rotation, elips_b200_quant** out);
+
+/* IndexPort::insert for n fp32 rows (HOST), encoded on the device exactly as
+ * Quantizer::encode does (ScalarQuantizer.cpp:52-68; ProductQuantizer.cpp:
+ * 71-86 with KMeans.cpp:166-180). */
+ELIPS_B200_API int elips_b200_quant_add(elips_b200_quant* index, const float* rows, size_t n);
+
+/* Appends n rows given as codes (HOST, n x code_bytes). */
+ELIPS_B200_API int elips_b200_quant_add_codes(elips_b200_quant* index, const uint8_t* codes, size_t n);
+
+ELIPS_B200_API int elips_b200_quant_size(const elips_b200_quant* index, size_t* n_out);
+
+/* ExactIndex::search over the codes: HOST pointers, synchronous; results as
+ * elips_b200_exact_search (ascending by (distance, slot)). */
+ELIPS_B200_API int elips_b200_quant_search(const elips_b200_quant* index, const float* queries,
+                                           size_t nq, size_t k, float* out_dist, int64_t* out_rows);
+
+/* Same with DEVICE pointers, asynchronous on `stream`. */
+ELIPS_B200_API int elips_b200_quant_search_device(const elips_b200_quant* index, const float* queries,
+                                                  size_t nq, size_t k, float* out_dist,
+                                                  int64_t* out_rows, void* stream);
+
+ELIPS_B200_API int elips_b200_quant_destroy(elips_b200_quant* index);
+
 /* ------------------------------------------------------------ profiling */
 /* Device-side counterpart of GpuProfiler (src/gpu_engine/GpuProfiler.cpp:
  * 5-23) and GpuConfig::enable_profiling (GpuConfig.hpp:83): while enabled,

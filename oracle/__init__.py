@@ -66,7 +66,8 @@ def ref() -> ctypes.CDLL:
         _ref = ctypes.CDLL(str(REF_SO))
         _ref.ref_distance.restype = c_float
         _ref.ref_distance.argtypes = [c_int, c_void_p, c_void_p, c_size_t]
-        for name in ("ref_exact_create", "ref_sq8_exact_create", "ref_pq_exact_create", "ref_ivfpq_create"):
+        for name in ("ref_exact_create", "ref_sq8_exact_create", "ref_pq_exact_create", "ref_opq_exact_create",
+                     "ref_ivfpq_create"):
             getattr(_ref, name).restype = c_void_p
     return _ref
 
@@ -175,6 +176,15 @@ def encode_pq(codebook, rows):
     return codes
 
 
+def rotate_rows(rotation, rows):
+    """apply_matrix on every row (KMeans.cpp:295-305)."""
+    rotation, rows = _f32(rotation), _f32(rows)
+    n, d = rows.shape
+    out = np.empty_like(rows)
+    orc().orc_rotate_rows(_p(rotation), _p(rows), c_size_t(n), c_size_t(d), _p(out))
+    return out
+
+
 def kmeans(rows, k, iters):
     rows = _f32(rows)
     n, d = rows.shape
@@ -222,7 +232,7 @@ def ivfpq_search(metric, centroids, codebook, codes, vectors, assignments, queri
 class RefExactIndex:
     """The reference's ExactIndex (optionally with its sq8 or PQ codec)."""
 
-    def __init__(self, metric, base, codec=None, mins=None, scales=None, codebook=None, pq_bits=8):
+    def __init__(self, metric, base, codec=None, mins=None, scales=None, codebook=None, pq_bits=8, rotation=None):
         base = _f32(base)
         self.dim = base.shape[1]
         lib = ref()
@@ -235,6 +245,11 @@ class RefExactIndex:
             cb = _f32(codebook)
             self.h = lib.ref_pq_exact_create(METRIC[metric], c_uint32(self.dim), c_uint32(cb.shape[0]),
                                              c_uint32(pq_bits), _p(cb), _p(base), c_size_t(base.shape[0]))
+        elif codec == "opq":
+            cb = _f32(codebook)
+            rot = _f32(rotation)
+            self.h = lib.ref_opq_exact_create(METRIC[metric], c_uint32(self.dim), c_uint32(cb.shape[0]),
+                                              c_uint32(pq_bits), _p(cb), _p(rot), _p(base), c_size_t(base.shape[0]))
         else:
             raise ValueError(codec)
         self.h = c_void_p(self.h)

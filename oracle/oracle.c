@@ -462,6 +462,20 @@ void orc_kmeans(const float* rows, size_t n, size_t dim, size_t k, size_t iters,
     free(sums); free(counts);
 }
 
+/* detail::apply_matrix, KMeans.cpp:295-305: out_i = sum_j R[i][j] * v[j],
+ * sequential over j. OPQ rotates rows before encode and queries before
+ * make_lut with it (ProductQuantizer.cpp:41-48, 79-85, 127-133). */
+void orc_rotate_rows(const float* rot, const float* rows, size_t n, size_t d, float* out) {
+    for (size_t r = 0; r < n; ++r) {
+        for (size_t i = 0; i < d; ++i) {
+            const float* m = rot + i * d;
+            float sum = 0.0f;
+            for (size_t j = 0; j < d; ++j) sum += m[j] * rows[r * d + j];
+            out[r * d + i] = sum;
+        }
+    }
+}
+
 /* ------------------------------------------------------------------------ */
 /* IVF coarse assignment and IVF-PQ search                                    */
 /* ------------------------------------------------------------------------ */

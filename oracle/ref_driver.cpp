@@ -199,6 +199,24 @@ void* ref_pq_exact_create(int metric, uint32_t dim, uint32_t pq_dim, uint32_t pq
     return h;
 }
 
+// ExactIndex with an OPQ codec (ProductQuantizer with a rotation) built from
+// a given codebook and dimension x dimension rotation.
+void* ref_opq_exact_create(int metric, uint32_t dim, uint32_t pq_dim, uint32_t pq_bits,
+                           const float* codebook, const float* rotation, const float* rows, size_t n) {
+    const size_t cb = static_cast<size_t>(pq_dim) * (size_t{1} << pq_bits) * (dim / pq_dim);
+    auto q = std::make_shared<elips::quant::ProductQuantizer>(
+        static_cast<Metric>(metric), static_cast<std::uint16_t>(dim), pq_dim, pq_bits,
+        std::vector<float>(codebook, codebook + cb),
+        std::vector<float>(rotation, rotation + static_cast<size_t>(dim) * dim));
+    auto* h = new ExactHandle;
+    h->index = std::make_unique<elips::ExactIndex>(static_cast<Metric>(metric),
+                                                   static_cast<std::uint16_t>(dim), q);
+    for (size_t i = 0; i < n; ++i) {
+        h->index->insert(row_id(i), std::span<const float>{rows + i * dim, dim});
+    }
+    return h;
+}
+
 int ref_exact_search(void* handle, uint32_t dim, const float* queries, size_t nq, size_t k,
                      int nthreads, float* out_dist, std::int64_t* out_rows) {
     auto* h = static_cast<ExactHandle*>(handle);
