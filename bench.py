@@ -50,6 +50,12 @@ CONFIGS = {
         workload="filtered exact L2 bf16, N=1,000,000 x d=384 N(0,1), Bernoulli(0.1) mask, Q=64, k=20",
         n=1_000_000, d=384, q=64, k=20, metric="euclidean", precision="bf16", data="gaussian",
         mask_p=0.1, dtype="bf16 (fp32 accumulate)"),
+    "ivfpq": dict(
+        workload="IVF-PQ, N=10,000,000 x d=128 Gaussian mixture (4,096 centroids, sigma=0.2, fp32), nlist=4,096 "
+                 "(k-means), PQ 16 x 8 bits on residuals, nprobe=32, Q=10,000, k=10",
+        n=10_000_000, d=128, q=10_000, k=10, metric="euclidean", precision="fp32", data="mixture",
+        centroids=4096, sigma=0.2, normalized=False, nlist=4096, pq_dim=16, pq_bits=8, nprobe=32,
+        kmeans_iters=4, pq_train_rows=262_144, pq_iters=6, dtype="f32 (u8 PQ codes)"),
 }
 DEFAULT_CONFIG = "exact_fp16_cosine"
 METRIC_NAME = "k-NN queries/sec (exact d=768 N=2M k=100; IVF-PQ) at 1/2/4/8 B200, % roofline"
@@ -233,7 +239,187 @@ def load_traffic(config: str, n_shard: int):
     return d["dram_bytes_per_launch"] * n_shard / d["rows"]
 
 
+# ------------------------------------------------- IVF-PQ model (setup)
+
+def _nearest(x, c, chunk=131072):
+    """Index of the nearest row of c (squared L2) for every row of x (torch)."""
+    import torch
+    cn = (c * c).sum(1)
+    out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
+    for i in range(0, x.shape[0], chunk):
+        xb = x[i:i + chunk]
+        out[i:i + chunk] = (cn[None, :] - 2.0 * (xb @ c.T)).argmin(1)
+    return out
+
+
+def _nearest_k(x, c, k):
+    cn = (c * c).sum(1)
+    return (cn[None, :] - 2.0 * (x @ c.T)).topk(k, dim=1, largest=False).indices
+
+
+def _lloyd(x, init, iters):
+    import torch
+    c = init.clone()
+    for _ in range(iters):
+        a = _nearest(x, c)
+        sums = torch.zeros_like(c).index_add_(0, a, x)
+        cnt = torch.bincount(a, minlength=c.shape[0]).to(x.dtype)
+        nz = cnt > 0
+        c[nz] = sums[nz] / cnt[nz, None]
+    return c
+
+
+def train_ivfpq_model(cfg, base):
+    """Input preparation for the IVF-PQ workload (not part of the timed search):
+    coarse k-means seeded with strided rows as IvfIndexState::train_centroids
+    (IvfIndexState.cpp:118-127), the final assignment, and a residual PQ
+    codebook trained on a strided sample; torch ops on the base's device.
+    Returns (centroids [nlist, d], assignments int32 [n], codebook [m, ksub, d/m])."""
+    import torch
+    n, d, nlist = base.shape[0], base.shape[1], cfg["nlist"]
+    stride = max(1, n // nlist)
+    seeds = base[torch.arange(nlist, device=base.device) * stride]
+    cent = _lloyd(base, seeds, cfg["kmeans_iters"])
+    assign = _nearest(base, cent)
+    step = max(1, n // cfg["pq_train_rows"])
+    sample = base[::step] - cent[assign[::step]]
+    m, ksub = cfg["pq_dim"], 1 << cfg["pq_bits"]
+    sub = d // m
+    cb = torch.empty((m, ksub, sub), dtype=torch.float32, device=base.device)
+    for j in range(m):
+        xs = sample[:, j * sub:(j + 1) * sub].contiguous()
+        init = xs[torch.arange(ksub, device=base.device) * max(1, xs.shape[0] // ksub)]
+        cb[j] = _lloyd(xs, init, cfg["pq_iters"])
+    return cent.contiguous(), assign.to(torch.int32), cb.contiguous()
+
+
+def scanned_bytes(cfg, centroids, queries, assign):
+    """Algorithmic bytes of one IVF-PQ scan: for every (query, probed list),
+    each member's code (pq_dim bytes) and slot id (4 bytes)."""
+    import torch
+    nprobe = min(cfg["nprobe"], centroids.shape[0])
+    probes = _nearest_k(queries, centroids, nprobe)
+    sizes = torch.bincount(assign.long(), minlength=centroids.shape[0])
+    return int(sizes[probes].sum().item()) * (cfg["pq_dim"] + 4)
+
+
 # ------------------------------------------------------------ b200 arm
+
+def run_b200_ivfpq(args, cfg, world, rank, local):
+    """IVF-PQ on one GPU (the list-sharded multi-GPU path is not built yet)."""
+    import torch
+    from elips_b200 import _capi
+    from elips_b200.ivfpq import IvfPqIndex
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n, d, nq, k = cfg["n"], cfg["d"], cfg["q"], cfg["k"]
+    cents = _centroids(cfg, dev)
+    t0 = time.perf_counter()
+    base = torch.empty((n, d), dtype=torch.float32, device=dev)
+    for r0 in range(0, n, 1 << 20):
+        cnt = min(1 << 20, n - r0)
+        base[r0:r0 + cnt] = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev)
+    q_dev = gen_rows(cfg, 0, nq, SEED + 2, nq, cents, device=dev)
+    centroids, assign, codebook = train_ivfpq_model(cfg, base)
+    index = IvfPqIndex(cfg["metric"], d, centroids.cpu().numpy(), codebook.cpu().numpy(), nprobe=cfg["nprobe"],
+                       pq_bits=cfg["pq_bits"], device=local)
+    for r0 in range(0, n, 1 << 21):
+        index.add_device(base[r0:r0 + (1 << 21)], assign[r0:r0 + (1 << 21)])
+    alg_bytes = scanned_bytes(cfg, centroids, q_dev, assign)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    out_r = torch.empty((nq, k), dtype=torch.int64, device=dev)
+
+    def step():
+        index.search_device(q_dev, k, out_dist=out_d, out_rows=out_r)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _capi.profiler_reset()
+    _capi.profiler_enable(True)
+    launches0 = _capi.launch_count()
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler:
+        time.sleep(0.25)
+        sampler.active = True
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        sampler.active = False
+    launches = _capi.launch_count() - launches0
+    _capi.profiler_enable(False)
+    ms = ev0.elapsed_time(ev1)
+    scan = _capi.profiler_stats("ivfpq_scan")
+    allk = _capi.profiler_stats(None)
+    per_kernel = {name: round(_capi.profiler_stats(name)["total_ms"] / args.steps, 4)
+                  for name in ("distances", "topk_rows", "ivfpq_scan", "merge_topk", "ivfpq_rerank")}
+    value = nq * args.steps / (ms / 1e3)
+
+    q_np = q_dev.cpu().pin_memory().numpy()
+    od = torch.empty((nq, k), dtype=torch.float32).pin_memory().numpy()
+    orr = torch.empty((nq, k), dtype=torch.int64).pin_memory().numpy()
+    for _ in range(max(1, args.warmup)):
+        index.search_batch(q_np, k, out_dist=od, out_rows=orr)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        index.search_batch(q_np, k, out_dist=od, out_rows=orr)
+    e2e_s = time.perf_counter() - t
+    e2e = {"value": round(nq * args.steps / e2e_s, 2), "unit": "queries/s", "h2d_bytes_per_step": int(q_np.nbytes),
+           "d2h_bytes_per_step": int(nq * k * 12), "api": "elips_b200_ivfpq_search (host buffers)"}
+
+    peaks, peak_src = load_peaks()
+    scan_ms = scan["total_ms"] / max(1, scan["launches"])
+    achieved = alg_bytes / (scan_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(peaks["hbm_gbs"], 1), "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(args.config, n),
+                "kernel": "ivfpq_scan_kernel", "kernel_ms_avg": round(scan_ms, 4),
+                "kernel_share_of_step": round(scan["total_ms"] / max(1e-9, allk["total_ms"]), 4),
+                "algorithmic_bytes_per_launch": alg_bytes, "per_kernel_ms_per_step": per_kernel,
+                "peak_source": f"{peak_src} HBM copy bandwidth"}
+    result = {
+        "metric": METRIC_NAME, "value": round(value, 2), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic (seeded; shapes and distributions of the configuration)",
+        "config": {"workload": cfg["workload"], "config": args.config, "base_rows": n, "dim": d,
+                   "queries_per_step": nq, "k": k, "nlist": cfg["nlist"], "nprobe": cfg["nprobe"],
+                   "pq": f"{cfg['pq_dim']}x{cfg['pq_bits']}",
+                   "l2": "inputs larger than L2 (codes 160 MB, vectors 5.1 GB); no flush"},
+        "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "clocks": sampler.summary(),
+        "build_s": round(build_s, 2)}
+    if not args.no_cpu_baseline and rank == 0:
+        import oracle
+        host_base = base.cpu().numpy()
+        codes = index.codes()
+        a_np = assign.cpu().numpy().view(np.uint32)
+        cent_np, cb_np = centroids.cpu().numpy(), codebook.cpu().numpy()
+        threads = os.cpu_count() or 1
+        try:
+            ref = oracle.RefIvfPqIndex(cfg["metric"], cent_np, a_np, cb_np, codes, host_base, cfg["nprobe"],
+                                       pq_bits=cfg["pq_bits"])
+            kind, what = "reference", "reference GpuIVFPQIndex::search on a CPU GpuPort (import_snapshot of this model)"
+            search = lambda qq, kk, tt: ref.search(qq, kk, tt)
+        except Exception:
+            kind, what = "port", "C restatement of GpuIVFPQIndex::search"
+            search = lambda qq, kk, tt: oracle.ivfpq_search(cfg["metric"], cent_np, cb_np, codes, host_base, a_np,
+                                                            qq, cfg["nprobe"], kk, tt)
+        qh = q_dev.cpu().numpy()
+        sample = _calibrated_sample(search, cfg, qh, threads, target_s=10.0)
+        t = time.perf_counter()
+        search(qh[:sample], k, threads)
+        dt = time.perf_counter() - t
+        result["cpu_baseline"] = {"value": round(sample / dt, 3), "unit": "queries/s", "cores": min(threads, sample),
+                                  "kind": kind, "sample": f"{sample} of the {nq} queries over the full {n}-row "
+                                  f"index ({what}), {dt:.2f} s wall"}
+    return result
+
 
 def run_b200(args, cfg, world, rank, local):
     import torch
@@ -529,7 +715,12 @@ def main():
         return
     world, rank, local = dist_setup(args)
     try:
-        result = run_b200(args, cfg, world, rank, local)
+        if args.config == "ivfpq":
+            if world > 1:
+                raise SystemExit("the list-sharded multi-GPU IVF-PQ path is not built yet")
+            result = run_b200_ivfpq(args, cfg, world, rank, local)
+        else:
+            result = run_b200(args, cfg, world, rank, local)
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:

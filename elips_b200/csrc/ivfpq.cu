@@ -1,0 +1,384 @@
+// Host side of the IVF-PQ index: GpuIVFPQIndex (src/gpu_engine/
+// GpuIVFPQIndex.cpp) with its model (centroids, list assignments, residual
+// codebook, codes) imported as GpuIVFPQIndex::import_snapshot does
+// (:327-348), rows resident on the device, codes stored list-major.
+#include <algorithm>
+#include <cstdio>
+#include <vector>
+
+#include "../../include/elips_b200.h"
+#include "engine.cuh"
+#include "ivfpq_kernels.cuh"
+#include "profiler.cuh"
+
+namespace eb {
+
+void compute_distances_device(int device, const float* q, const float* db, float* out, size_t nq, size_t nb,
+                              size_t d, int metric, cudaStream_t stream);
+void top_k_device(int device, const float* dist, uint32_t* idx, float* val, size_t nq, size_t nb, size_t k,
+                  cudaStream_t stream);
+
+namespace {
+
+size_t a256(size_t x) { return (x + 255) / 256 * 256; }
+
+void launch_ok(const char* what) { check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, what); }
+
+}  // namespace
+
+class IvfPqIndex {
+public:
+    IvfPqIndex(int device, int metric, uint32_t dim, uint32_t nlist, uint32_t nprobe, uint32_t pq_dim,
+               uint32_t pq_bits, const float* centroids, const float* codebook)
+        : device_(device), metric_(metric), dim_(dim), nlist_(nlist), nprobe_(std::max<uint32_t>(1, nprobe)),
+          m_(pq_dim) {
+        if (metric < 0 || metric > 2) fail(ELIPS_B200_UNSUPPORTED_METRIC, "unknown metric");
+        if (dim == 0 || dim > 65535 || nlist == 0) fail(ELIPS_B200_INVALID_ARGUMENT, "bad dimension or list count");
+        if (pq_dim == 0 || dim % pq_dim != 0 || pq_bits < 4 || pq_bits > 8)
+            fail(ELIPS_B200_INVALID_ARGUMENT, "pq_dim must divide the dimension and pq_bits be in [4, 8]");
+        if (centroids == nullptr || codebook == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "model is null");
+        device_props(device);
+        DeviceGuard g(device);
+        ksub_ = 1u << pq_bits;
+        centroids_ = DeviceBuffer(device, static_cast<size_t>(nlist) * dim * 4);
+        check_cuda(cudaMemcpy(centroids_.get(), centroids, static_cast<size_t>(nlist) * dim * 4, cudaMemcpyHostToDevice),
+                   ELIPS_B200_TRANSFER_FAILED, "centroids");
+        const size_t cb = static_cast<size_t>(m_) * ksub_ * (dim / m_);
+        codebook_ = DeviceBuffer(device, cb * 4);
+        check_cuda(cudaMemcpy(codebook_.get(), codebook, cb * 4, cudaMemcpyHostToDevice), ELIPS_B200_TRANSFER_FAILED,
+                   "codebook");
+    }
+
+    int device() const { return device_; }
+    uint32_t dim() const { return dim_; }
+    uint32_t pq_dim() const { return m_; }
+    size_t size() const { return n_; }
+    void set_nprobe(uint32_t nprobe) { nprobe_ = std::max<uint32_t>(1, nprobe); }
+
+    // Appends n rows (DEVICE pointers). assign: list of each row; codes may be
+    // null, in which case the residuals are encoded on the device exactly as
+    // rebuild_codes does (fp32 x - centroid, then encode_pq).
+    void add_device(const float* vectors, const uint32_t* assign, const uint8_t* codes, size_t n, cudaStream_t stream) {
+        if (n == 0) return;
+        if (vectors == nullptr || assign == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "vectors and assignments are required");
+        if (n_ + n >= 0xFFFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "index limited to 2^32-2 rows");
+        DeviceGuard g(device_);
+        std::vector<uint32_t> host_assign(n);
+        check_cuda(cudaMemcpyAsync(host_assign.data(), assign, n * 4, cudaMemcpyDeviceToHost, stream),
+                   ELIPS_B200_TRANSFER_FAILED, "assignment copy");
+        check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_TRANSFER_FAILED, "assignment copy");
+        for (uint32_t a : host_assign)
+            if (a >= nlist_) fail(ELIPS_B200_INVALID_ARGUMENT, "assignment names a list past n_lists");
+        reserve(n_ + n);
+        float* vdst = static_cast<float*>(vectors_.get()) + n_ * dim_;
+        uint8_t* cdst = static_cast<uint8_t*>(codes_.get()) + n_ * m_;
+        check_cuda(cudaMemcpyAsync(vdst, vectors, n * dim_ * 4, cudaMemcpyDeviceToDevice, stream),
+                   ELIPS_B200_TRANSFER_FAILED, "vector copy");
+        if (codes != nullptr) {
+            check_cuda(cudaMemcpyAsync(cdst, codes, n * m_, cudaMemcpyDeviceToDevice, stream), ELIPS_B200_TRANSFER_FAILED,
+                       "code copy");
+        } else {
+            StreamScratch res(n * dim_ * 4, stream);
+            const uint64_t total = static_cast<uint64_t>(n) * dim_;
+            {
+                Profiler::Scope prof("residuals", stream, n);
+                residuals_kernel<<<static_cast<uint32_t>((total + 255) / 256), 256, 0, stream>>>(
+                    vectors, assign, static_cast<const float*>(centroids_.get()), n, dim_,
+                    reinterpret_cast<float*>(res.get()));
+                launch_ok("residual kernel");
+            }
+            const uint64_t tc = static_cast<uint64_t>(n) * m_;
+            Profiler::Scope prof("pq_encode", stream, n);
+            pq_encode_kernel<<<static_cast<uint32_t>((tc + 127) / 128), 128, 0, stream>>>(
+                reinterpret_cast<const float*>(res.get()), static_cast<const float*>(codebook_.get()), n, dim_, m_,
+                ksub_, cdst);
+            launch_ok("pq encode kernel");
+        }
+        check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "ivf-pq add");
+        assign_.insert(assign_.end(), host_assign.begin(), host_assign.end());
+        n_ += n;
+        dirty_ = true;
+    }
+
+    // Codes of every row in slot order (DEVICE destination, n x pq_dim).
+    void read_codes(uint8_t* dst, cudaStream_t stream) const {
+        DeviceGuard g(device_);
+        if (n_ == 0) return;
+        check_cuda(cudaMemcpyAsync(dst, codes_.get(), n_ * m_, cudaMemcpyDeviceToDevice, stream),
+                   ELIPS_B200_TRANSFER_FAILED, "code read");
+    }
+
+    void search_device(const float* queries, size_t nq, size_t k, float* out_dist, int64_t* out_rows,
+                       cudaStream_t stream) {
+        if (nq == 0 || k == 0) return;
+        if (k > 256) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 256 is not supported (rerank set is 4k)");
+        if (nq * nprobe_ > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "too many queries in one call");
+        if (queries == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "queries is null");
+        DeviceGuard g(device_);
+        if (n_ == 0) {
+            merge_candidates(device_, nullptr, static_cast<uint32_t>(nq), 0, static_cast<uint32_t>(k), 0, 0, 0, out_dist,
+                             out_rows, nullptr, stream);
+            return;
+        }
+        finalize(stream);
+        const uint32_t nprobe = std::min(nprobe_, nlist_);
+        const uint32_t r = static_cast<uint32_t>(4 * k);
+        const size_t dist_b = a256(nq * nlist_ * 4);
+        const size_t probe_b = a256(nq * nprobe * 4);
+        const size_t pval_b = a256(nq * nprobe * 4);
+        const size_t part_b = a256(nq * nprobe * static_cast<size_t>(r) * 8);
+        const size_t cand_b = a256(nq * static_cast<size_t>(r) * 8);
+        StreamScratch s(dist_b + probe_b + pval_b + part_b + cand_b, stream);
+        float* dist = reinterpret_cast<float*>(s.get());
+        uint32_t* probes = reinterpret_cast<uint32_t*>(s.get() + dist_b);
+        float* pval = reinterpret_cast<float*>(s.get() + dist_b + probe_b);
+        uint2* part = reinterpret_cast<uint2*>(s.get() + dist_b + probe_b + pval_b);
+        uint2* cand = reinterpret_cast<uint2*>(s.get() + dist_b + probe_b + pval_b + part_b);
+        // 1. probe (IvfIndexState::probe_lists): exact distances, then top-nprobe
+        compute_distances_device(device_, queries, static_cast<const float*>(centroids_.get()), dist, nq, nlist_, dim_,
+                                 metric_, stream);
+        top_k_device(device_, dist, probes, pval, nq, nlist_, nprobe, stream);
+        // 2. per (query, probed list) approximate scan, top-R per list
+        IvfPqParams p{};
+        p.queries = queries;
+        p.centroids = static_cast<const float*>(centroids_.get());
+        p.codebook = static_cast<const float*>(codebook_.get());
+        p.list_codes = static_cast<const uint8_t*>(list_codes_.get());
+        p.list_rows = static_cast<const uint32_t*>(list_rows_.get());
+        p.list_off = static_cast<const uint32_t*>(list_off_.get());
+        p.probes = probes;
+        p.partial = part;
+        p.nq = static_cast<uint32_t>(nq);
+        p.d = dim_;
+        p.nlist = nlist_;
+        p.nprobe = nprobe;
+        p.m = m_;
+        p.ksub = ksub_;
+        p.r = r;
+        p.cap = (r + kIvfThreads + 31u) / 32u * 32u;
+        p.metric = metric_;
+        const size_t smem = static_cast<size_t>(m_) * ksub_ * 4 + 2ull * dim_ * 4 + btk_bytes(p.cap);
+        if (smem > device_props(device_).max_smem_optin) fail(ELIPS_B200_INVALID_ARGUMENT, "model too large for the scan");
+        check_cuda(cudaFuncSetAttribute(ivfpq_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+                   ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+        {
+            Profiler::Scope prof("ivfpq_scan", stream, nq * nprobe);
+            ivfpq_scan_kernel<<<static_cast<uint32_t>(nq * nprobe), kIvfThreads, smem, stream>>>(p);
+            launch_ok("ivf-pq scan kernel");
+        }
+        // 3. R best approximate candidates per query across its probed lists
+        //    (keys are final approximate distances: no transform, metric 0)
+        merge_candidates(device_, part, static_cast<uint32_t>(nq), nprobe, r, static_cast<uint64_t>(nprobe) * r, r, 0,
+                         nullptr, nullptr, cand, stream);
+        // 4. exact rerank (exact_rank)
+        uint32_t rp = 1;
+        while (rp < r) rp <<= 1;
+        constexpr uint32_t warps = 4;
+        const size_t rsmem = static_cast<size_t>(warps) * rp * 8;
+        check_cuda(cudaFuncSetAttribute(ivfpq_rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(rsmem)),
+                   ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+        Profiler::Scope prof("ivfpq_rerank", stream, nq * r);
+        ivfpq_rerank_kernel<<<static_cast<uint32_t>((nq + warps - 1) / warps), warps * 32, rsmem, stream>>>(
+            queries, static_cast<const float*>(vectors_.get()), cand, static_cast<uint32_t>(nq), dim_, r,
+            static_cast<uint32_t>(k), rp, metric_, out_dist, out_rows);
+        launch_ok("ivf-pq rerank kernel");
+    }
+
+private:
+    void reserve(size_t rows) {
+        if (rows <= capacity_) return;
+        const size_t cap = std::max<size_t>(rows, capacity_ + capacity_ / 2);
+        DeviceBuffer v(device_, cap * dim_ * 4), c(device_, cap * m_);
+        if (n_ > 0) {
+            check_cuda(cudaMemcpy(v.get(), vectors_.get(), n_ * dim_ * 4, cudaMemcpyDeviceToDevice),
+                       ELIPS_B200_TRANSFER_FAILED, "grow copy");
+            check_cuda(cudaMemcpy(c.get(), codes_.get(), n_ * m_, cudaMemcpyDeviceToDevice), ELIPS_B200_TRANSFER_FAILED,
+                       "grow copy");
+        }
+        vectors_ = std::move(v);
+        codes_ = std::move(c);
+        capacity_ = cap;
+    }
+
+    // Lists in ascending slot order (IvfIndexState::rebuild_list_members,
+    // IvfIndexState.cpp:75-83) and the list-major code copy.
+    void finalize(cudaStream_t stream) {
+        if (!dirty_) return;
+        std::vector<uint32_t> off(nlist_ + 1, 0);
+        for (uint32_t a : assign_) ++off[a + 1];
+        for (uint32_t l = 0; l < nlist_; ++l) off[l + 1] += off[l];
+        std::vector<uint32_t> rows(n_);
+        std::vector<uint32_t> fill(off.begin(), off.end() - 1);
+        for (size_t s = 0; s < n_; ++s) rows[fill[assign_[s]]++] = static_cast<uint32_t>(s);
+        list_off_ = DeviceBuffer(device_, off.size() * 4);
+        list_rows_ = DeviceBuffer(device_, std::max<size_t>(n_, 1) * 4);
+        list_codes_ = DeviceBuffer(device_, std::max<size_t>(n_, 1) * m_);
+        check_cuda(cudaMemcpyAsync(list_off_.get(), off.data(), off.size() * 4, cudaMemcpyHostToDevice, stream),
+                   ELIPS_B200_TRANSFER_FAILED, "list offsets");
+        check_cuda(cudaMemcpyAsync(list_rows_.get(), rows.data(), n_ * 4, cudaMemcpyHostToDevice, stream),
+                   ELIPS_B200_TRANSFER_FAILED, "list rows");
+        const uint64_t total = static_cast<uint64_t>(n_) * m_;
+        {
+            Profiler::Scope prof("gather_codes", stream, n_);
+            gather_codes_kernel<<<static_cast<uint32_t>((total + 255) / 256), 256, 0, stream>>>(
+                static_cast<const uint8_t*>(codes_.get()), static_cast<const uint32_t*>(list_rows_.get()), n_, m_,
+                static_cast<uint8_t*>(list_codes_.get()));
+            launch_ok("gather codes kernel");
+        }
+        check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "list build");
+        dirty_ = false;
+    }
+
+    int device_, metric_;
+    uint32_t dim_, nlist_, nprobe_, m_, ksub_ = 256;
+    size_t n_ = 0, capacity_ = 0;
+    bool dirty_ = false;
+    std::vector<uint32_t> assign_;
+    DeviceBuffer centroids_, codebook_, vectors_, codes_, list_off_, list_rows_, list_codes_;
+};
+
+}  // namespace eb
+
+struct elips_b200_ivfpq {
+    eb::IvfPqIndex index;
+};
+
+namespace {
+
+template <class Fn>
+int guarded(Fn&& fn) {
+    try {
+        fn();
+        return ELIPS_B200_OK;
+    } catch (const eb::Error& e) {
+        std::fprintf(stderr, "elips_b200: %s\n", e.what.c_str());
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        return ELIPS_B200_INSUFFICIENT_MEMORY;
+    } catch (...) {
+        return ELIPS_B200_KERNEL_LAUNCH_FAILED;
+    }
+}
+
+struct OwnedStream {
+    cudaStream_t s = nullptr;
+    OwnedStream() {
+        eb::check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), ELIPS_B200_INITIALIZATION_FAILED,
+                       "cudaStreamCreate");
+    }
+    ~OwnedStream() { cudaStreamDestroy(s); }
+};
+
+size_t up256(size_t x) { return (x + 255) / 256 * 256; }
+
+}  // namespace
+
+extern "C" {
+
+int elips_b200_ivfpq_create(int device, int metric, uint32_t dimension, uint32_t n_lists, uint32_t nprobe,
+                            uint32_t pq_dim, uint32_t pq_bits, const float* centroids, const float* codebook,
+                            elips_b200_ivfpq** out) {
+    if (out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *out = nullptr;
+    return guarded([&] {
+        *out = new elips_b200_ivfpq{
+            eb::IvfPqIndex(device, metric, dimension, n_lists, nprobe, pq_dim, pq_bits, centroids, codebook)};
+    });
+}
+
+int elips_b200_ivfpq_add(elips_b200_ivfpq* index, const float* vectors, const uint32_t* assignments,
+                         const uint8_t* codes, size_t n) {
+    if (index == nullptr || (n > 0 && (vectors == nullptr || assignments == nullptr))) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        if (n == 0) return;
+        eb::IvfPqIndex& ix = index->index;
+        eb::DeviceGuard g(ix.device());
+        OwnedStream st;
+        const size_t vb = up256(n * ix.dim() * 4);
+        const size_t ab = up256(n * 4);
+        const size_t cb = codes ? n * ix.pq_dim() : 0;
+        eb::StreamScratch s(vb + ab + cb + 256, st.s);
+        float* dv = reinterpret_cast<float*>(s.get());
+        uint32_t* da = reinterpret_cast<uint32_t*>(s.get() + vb);
+        uint8_t* dc = codes ? s.get() + vb + ab : nullptr;
+        eb::check_cuda(cudaMemcpyAsync(dv, vectors, n * ix.dim() * 4, cudaMemcpyHostToDevice, st.s),
+                       ELIPS_B200_TRANSFER_FAILED, "vector upload");
+        eb::check_cuda(cudaMemcpyAsync(da, assignments, n * 4, cudaMemcpyHostToDevice, st.s), ELIPS_B200_TRANSFER_FAILED,
+                       "assignment upload");
+        if (codes != nullptr)
+            eb::check_cuda(cudaMemcpyAsync(dc, codes, cb, cudaMemcpyHostToDevice, st.s), ELIPS_B200_TRANSFER_FAILED,
+                           "code upload");
+        ix.add_device(dv, da, dc, n, st.s);
+    });
+}
+
+int elips_b200_ivfpq_add_device(elips_b200_ivfpq* index, const float* vectors, const uint32_t* assignments,
+                                const uint8_t* codes, size_t n, void* stream) {
+    if (index == nullptr || (n > 0 && (vectors == nullptr || assignments == nullptr))) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.add_device(vectors, assignments, codes, n, static_cast<cudaStream_t>(stream)); });
+}
+
+int elips_b200_ivfpq_size(const elips_b200_ivfpq* index, size_t* n_out) {
+    if (index == nullptr || n_out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *n_out = index->index.size();
+    return ELIPS_B200_OK;
+}
+
+int elips_b200_ivfpq_set_nprobe(elips_b200_ivfpq* index, uint32_t nprobe) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    index->index.set_nprobe(nprobe);
+    return ELIPS_B200_OK;
+}
+
+int elips_b200_ivfpq_search(elips_b200_ivfpq* index, const float* queries, size_t nq, size_t k, float* out_dist,
+                            int64_t* out_rows) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (queries == nullptr || out_dist == nullptr || out_rows == nullptr))
+        return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        if (nq == 0 || k == 0) return;
+        eb::IvfPqIndex& ix = index->index;
+        eb::DeviceGuard g(ix.device());
+        OwnedStream st;
+        {
+            const size_t qb = up256(nq * ix.dim() * 4);
+            const size_t db = up256(nq * k * 4);
+            eb::StreamScratch s(qb + db + nq * k * 8 + 256, st.s);
+            float* dq = reinterpret_cast<float*>(s.get());
+            float* dd = reinterpret_cast<float*>(s.get() + qb);
+            int64_t* dr = reinterpret_cast<int64_t*>(s.get() + qb + db);
+            eb::check_cuda(cudaMemcpyAsync(dq, queries, nq * ix.dim() * 4, cudaMemcpyHostToDevice, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "query upload");
+            ix.search_device(dq, nq, k, dd, dr, st.s);
+            eb::check_cuda(cudaMemcpyAsync(out_dist, dd, nq * k * 4, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "distance download");
+            eb::check_cuda(cudaMemcpyAsync(out_rows, dr, nq * k * 8, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "row download");
+        }
+        eb::check_cuda(cudaStreamSynchronize(st.s), ELIPS_B200_KERNEL_LAUNCH_FAILED, "ivf-pq search");
+    });
+}
+
+int elips_b200_ivfpq_search_device(elips_b200_ivfpq* index, const float* queries, size_t nq, size_t k,
+                                   float* out_dist, int64_t* out_rows, void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (queries == nullptr || out_dist == nullptr || out_rows == nullptr))
+        return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.search_device(queries, nq, k, out_dist, out_rows, static_cast<cudaStream_t>(stream)); });
+}
+
+int elips_b200_ivfpq_codes_device(const elips_b200_ivfpq* index, uint8_t* codes_out, void* stream) {
+    if (index == nullptr || codes_out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.read_codes(codes_out, static_cast<cudaStream_t>(stream)); });
+}
+
+int elips_b200_ivfpq_destroy(elips_b200_ivfpq* index) {
+    if (index == nullptr) return ELIPS_B200_OK;
+    return guarded([&] {
+        eb::DeviceGuard g(index->index.device());
+        delete index;
+    });
+}
+
+}  // extern "C"

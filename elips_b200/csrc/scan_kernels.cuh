@@ -36,7 +36,7 @@ constexpr int kDistQ = 8;        // queries per CTA
 constexpr int kDistDims = 32;    // dimensions staged per step
 
 // out[q * nb + r] = elips::distance(metric, queries[q], db[r]) exactly.
-__global__ void __launch_bounds__(kDistRows)
+static __global__ void __launch_bounds__(kDistRows)
     distances_kernel(const float* __restrict__ queries, const float* __restrict__ db, uint32_t nq,
                      uint32_t nb, uint32_t d, int metric, float* __restrict__ out) {
     __shared__ float dbs[kDistRows][kDistDims + 1];
@@ -129,7 +129,7 @@ __host__ __device__ constexpr uint32_t btk_bytes(uint32_t cap) { return cap * 16
 
 // One CTA per query row: the k smallest (value, index) of dist[q][0..nb),
 // ascending, ties by index. indices_out / values_out are [nq][k].
-__global__ void topk_rows_kernel(const float* __restrict__ dist, uint32_t nq, uint32_t nb, uint32_t k,
+static __global__ void topk_rows_kernel(const float* __restrict__ dist, uint32_t nq, uint32_t nb, uint32_t k,
                                  uint32_t cap, uint32_t kpow2, uint32_t* __restrict__ idx_out,
                                  float* __restrict__ val_out) {
     extern __shared__ uint8_t smem[];
@@ -162,7 +162,7 @@ __global__ void topk_rows_kernel(const float* __restrict__ dist, uint32_t nq, ui
 
 // out[r] = R x in[r] with apply_matrix's order: out_i = sum_j R[i][j] * v[j],
 // sequential over j (KMeans.cpp:295-305). One thread per (row, i).
-__global__ void rotate_rows_kernel(const float* __restrict__ rot, const float* __restrict__ in, uint64_t rows,
+static __global__ void rotate_rows_kernel(const float* __restrict__ rot, const float* __restrict__ in, uint64_t rows,
                                    uint32_t d, float* __restrict__ out) {
     const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t >= rows * d) return;
@@ -179,7 +179,7 @@ __global__ void rotate_rows_kernel(const float* __restrict__ rot, const float* _
 
 // lut[q][m][c] per ProductQuantizer::make_lut: -sum q_s*c (cos, dot) or
 // sum (q_s - c)^2 (euclidean), sequential over sub_dim. One thread per entry.
-__global__ void pq_lut_kernel(const float* __restrict__ queries, const float* __restrict__ codebook,
+static __global__ void pq_lut_kernel(const float* __restrict__ queries, const float* __restrict__ codebook,
                               uint32_t nq, uint32_t d, uint32_t m_sub, uint32_t ksub, int metric,
                               float* __restrict__ lut) {
     const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -219,7 +219,7 @@ constexpr int kPqQueriesPerCta = 4;
 // in shared memory, rows [split range) in rounds of 256 (one row per thread),
 // sum over m sequential, one running top-k per query; writes
 // partial[q][split][k].
-__global__ void __launch_bounds__(kScanThreads)
+static __global__ void __launch_bounds__(kScanThreads)
     pq_scan_kernel(const float* __restrict__ lut, const uint8_t* __restrict__ codes, uint32_t n, uint32_t nq,
                    uint32_t m_sub, uint32_t ksub, int metric, uint32_t k, uint32_t cap, uint32_t splits,
                    uint2* __restrict__ partial) {
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kScanThreads)
 
 // lut[q][i][level] per ScalarQuantizer::make_lut: value = min + level*scale;
 // -(q*value) (cos, dot) or (q - value)^2 (euclidean).
-__global__ void sq8_lut_kernel(const float* __restrict__ queries, const float* __restrict__ mins,
+static __global__ void sq8_lut_kernel(const float* __restrict__ queries, const float* __restrict__ mins,
                                const float* __restrict__ scales, uint32_t nq, uint32_t d, int metric,
                                float* __restrict__ lut) {
     const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -295,7 +295,7 @@ __global__ void sq8_lut_kernel(const float* __restrict__ queries, const float* _
 // Exhaustive sq8 ADC scan, one query per CTA: grid = (splits, nq). The
 // query's d x 256 LUT is staged in shared memory when lut_in_smem (d <= 192),
 // else read from global memory. Sum over the d dimensions is sequential.
-__global__ void __launch_bounds__(kScanThreads)
+static __global__ void __launch_bounds__(kScanThreads)
     sq8_scan_kernel(const float* __restrict__ lut, const uint8_t* __restrict__ codes, uint32_t n, uint32_t d,
                     int metric, uint32_t k, uint32_t cap, uint32_t splits, int lut_in_smem,
                     uint2* __restrict__ partial) {
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(kScanThreads)
 
 // ScalarQuantizer::encode: level = (x - min) / scale, clamp to [0, 255],
 // round half away from zero. One thread per element.
-__global__ void sq8_encode_kernel(const float* __restrict__ rows, const float* __restrict__ mins,
+static __global__ void sq8_encode_kernel(const float* __restrict__ rows, const float* __restrict__ mins,
                                   const float* __restrict__ scales, uint64_t n, uint32_t d,
                                   uint8_t* __restrict__ codes) {
     const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -341,7 +341,7 @@ __global__ void sq8_encode_kernel(const float* __restrict__ rows, const float* _
 
 // encode_pq / nearest_centroid: per (row, subspace), the codeword with the
 // smallest sequential squared distance; strict '<' keeps the lowest index.
-__global__ void pq_encode_kernel(const float* __restrict__ rows, const float* __restrict__ codebook, uint64_t n,
+static __global__ void pq_encode_kernel(const float* __restrict__ rows, const float* __restrict__ codebook, uint64_t n,
                                  uint32_t d, uint32_t m_sub, uint32_t ksub, uint8_t* __restrict__ codes) {
     const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t >= n * m_sub) return;

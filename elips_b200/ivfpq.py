@@ -1,0 +1,109 @@
+"""IVF-PQ index on one B200: GpuIVFPQIndex (src/gpu_engine/GpuIVFPQIndex.cpp)
+with its trained model imported as import_snapshot does (:327-348).
+
+Search follows GpuIVFPQIndex::search (:161-237): exact probe of the nprobe
+nearest lists, approximate scoring of their members from the residual codes,
+exact rerank of the best R = max(4k, k) on the raw vectors. Returned
+distances are the exact ones, ascending by (distance, slot).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _capi as capi
+from .exact import METRICS, DimensionMismatch
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class IvfPqIndex:
+    def __init__(self, metric: str, dimension: int, centroids: np.ndarray, codebook: np.ndarray,
+                 nprobe: int, pq_bits: int = 8, device: int = 0):
+        self.metric, self.dimension, self.device = metric, int(dimension), int(device)
+        cent = np.ascontiguousarray(centroids, np.float32)
+        cb = np.ascontiguousarray(codebook, np.float32)
+        if cent.shape[1] != self.dimension:
+            raise DimensionMismatch("centroid dimension does not match index")
+        self.n_lists, self.pq_dim = cent.shape[0], cb.shape[0]
+        h = ctypes.c_void_p()
+        capi.check(capi.LIB.elips_b200_ivfpq_create(self.device, METRICS[metric], self.dimension, self.n_lists,
+                                                    int(nprobe), self.pq_dim, int(pq_bits), _ptr(cent), _ptr(cb),
+                                                    ctypes.byref(h)), "elips_b200_ivfpq_create")
+        self._h = h
+
+    def add(self, vectors: np.ndarray, assignments: np.ndarray, codes: Optional[np.ndarray] = None) -> None:
+        """Host rows, their list ids, and optionally their residual codes."""
+        v = np.ascontiguousarray(vectors, np.float32)
+        a = np.ascontiguousarray(assignments, np.uint32)
+        if v.ndim != 2 or v.shape[1] != self.dimension:
+            raise DimensionMismatch("vector dimension does not match index")
+        c = None if codes is None else np.ascontiguousarray(codes, np.uint8)
+        capi.check(capi.LIB.elips_b200_ivfpq_add(self._h, _ptr(v), _ptr(a), _ptr(c) if c is not None else None,
+                                                 v.shape[0]), "elips_b200_ivfpq_add")
+
+    def add_device(self, vectors, assignments, codes=None, stream=None) -> None:
+        """CUDA tensors: vectors [n, d] float32, assignments [n] int32 (list ids)."""
+        import torch
+        if vectors.shape[1] != self.dimension:
+            raise DimensionMismatch("vector dimension does not match index")
+        vectors, assignments = vectors.contiguous(), assignments.contiguous()
+        s = stream if stream is not None else torch.cuda.current_stream(vectors.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_ivfpq_add_device(self._h, vectors.data_ptr(), assignments.data_ptr(),
+                                                        codes.data_ptr() if codes is not None else None,
+                                                        vectors.shape[0], s), "elips_b200_ivfpq_add_device")
+
+    def size(self) -> int:
+        n = ctypes.c_size_t(0)
+        capi.check(capi.LIB.elips_b200_ivfpq_size(self._h, ctypes.byref(n)), "elips_b200_ivfpq_size")
+        return n.value
+
+    def set_nprobe(self, nprobe: int) -> None:
+        capi.check(capi.LIB.elips_b200_ivfpq_set_nprobe(self._h, int(nprobe)), "elips_b200_ivfpq_set_nprobe")
+
+    def codes(self) -> np.ndarray:
+        """Residual codes of every row in slot order (export_snapshot's pq.codes)."""
+        import torch
+        out = torch.empty((max(self.size(), 1), self.pq_dim), dtype=torch.uint8, device=f"cuda:{self.device}")
+        capi.check(capi.LIB.elips_b200_ivfpq_codes_device(self._h, out.data_ptr(),
+                                                          torch.cuda.current_stream(out.device).cuda_stream),
+                   "elips_b200_ivfpq_codes_device")
+        torch.cuda.synchronize(out.device)
+        return out[:self.size()].cpu().numpy()
+
+    def search_batch(self, queries: np.ndarray, k: int, out_dist=None, out_rows=None):
+        q = np.ascontiguousarray(queries, np.float32)
+        if q.ndim != 2 or q.shape[1] != self.dimension:
+            raise DimensionMismatch("query dimension does not match index")
+        nq = q.shape[0]
+        dist = np.empty((nq, k), np.float32) if out_dist is None else out_dist
+        rows = np.empty((nq, k), np.int64) if out_rows is None else out_rows
+        capi.check(capi.LIB.elips_b200_ivfpq_search(self._h, _ptr(q), nq, k, _ptr(dist), _ptr(rows)),
+                   "elips_b200_ivfpq_search")
+        return dist, rows
+
+    def search_device(self, queries, k: int, out_dist=None, out_rows=None, stream=None):
+        import torch
+        nq = queries.shape[0]
+        if out_dist is None:
+            out_dist = torch.empty((nq, k), dtype=torch.float32, device=queries.device)
+            out_rows = torch.empty((nq, k), dtype=torch.int64, device=queries.device)
+        s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_ivfpq_search_device(self._h, queries.data_ptr(), nq, k, out_dist.data_ptr(),
+                                                           out_rows.data_ptr(), s), "elips_b200_ivfpq_search_device")
+        return out_dist, out_rows
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            capi.LIB.elips_b200_ivfpq_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -224,6 +224,58 @@ ELIPS_B200_API int elips_b200_quant_search_device(const elips_b200_quant* index,
 
 ELIPS_B200_API int elips_b200_quant_destroy(elips_b200_quant* index);
 
+/* ---------------------------------------------------------------- IVF-PQ */
+/* GpuIVFPQIndex (src/gpu_engine/GpuIVFPQIndex.cpp): residual product
+ * quantization over an inverted-file coarse quantizer. Search = probe the
+ * nprobe nearest lists with exact distances (IvfIndexState.cpp:395-423),
+ * score their members approximately from the residual codes, rerank the best
+ * R = max(4k, k) with exact distances on the raw vectors (GpuIVFPQIndex.cpp:
+ * 161-237). The model is imported as GpuIVFPQIndex::import_snapshot does
+ * (:327-348): centroids [n_lists][dimension] and the residual codebook
+ * [pq_dim][2^pq_bits][dimension/pq_dim] (HOST, copied); nprobe plays
+ * GpuConfig::default_ef_search_gpu (IvfIndexState.cpp:45). */
+typedef struct elips_b200_ivfpq elips_b200_ivfpq;
+
+ELIPS_B200_API int elips_b200_ivfpq_create(int device, int metric, uint32_t dimension,
+                                           uint32_t n_lists, uint32_t nprobe, uint32_t pq_dim,
+                                           uint32_t pq_bits, const float* centroids,
+                                           const float* codebook, elips_b200_ivfpq** out);
+
+/* Appends n rows: raw vectors (n x dimension fp32, kept for the exact
+ * rerank), their list assignments (IvfSnapshot::assignments) and optionally
+ * their residual codes (n x pq_dim, IndexSnapshot::pq->codes); with codes =
+ * NULL the residuals x - centroid are encoded on the device exactly as
+ * GpuIVFPQIndex::rebuild_codes does (:88-130). HOST pointers. */
+ELIPS_B200_API int elips_b200_ivfpq_add(elips_b200_ivfpq* index, const float* vectors,
+                                        const uint32_t* assignments, const uint8_t* codes, size_t n);
+
+/* Same with DEVICE pointers, ordered on `stream`. */
+ELIPS_B200_API int elips_b200_ivfpq_add_device(elips_b200_ivfpq* index, const float* vectors,
+                                               const uint32_t* assignments, const uint8_t* codes,
+                                               size_t n, void* stream);
+
+ELIPS_B200_API int elips_b200_ivfpq_size(const elips_b200_ivfpq* index, size_t* n_out);
+
+/* Number of lists probed per query (GpuConfig::default_ef_search_gpu). */
+ELIPS_B200_API int elips_b200_ivfpq_set_nprobe(elips_b200_ivfpq* index, uint32_t nprobe);
+
+/* GpuIndexPort::search_batch: HOST pointers, synchronous; k <= 256. Results
+ * ascending by (exact distance, slot), padded with (+inf, -1). */
+ELIPS_B200_API int elips_b200_ivfpq_search(elips_b200_ivfpq* index, const float* queries, size_t nq,
+                                           size_t k, float* out_dist, int64_t* out_rows);
+
+/* Same with DEVICE pointers, asynchronous on `stream`. */
+ELIPS_B200_API int elips_b200_ivfpq_search_device(elips_b200_ivfpq* index, const float* queries,
+                                                  size_t nq, size_t k, float* out_dist,
+                                                  int64_t* out_rows, void* stream);
+
+/* Copies the residual codes of every row, slot order (n x pq_dim), to DEVICE
+ * memory: the `pq.codes` of GpuIVFPQIndex::export_snapshot (:312-325). */
+ELIPS_B200_API int elips_b200_ivfpq_codes_device(const elips_b200_ivfpq* index, uint8_t* codes_out,
+                                                 void* stream);
+
+ELIPS_B200_API int elips_b200_ivfpq_destroy(elips_b200_ivfpq* index);
+
 /* ------------------------------------------------------------ profiling */
 /* Device-side counterpart of GpuProfiler (src/gpu_engine/GpuProfiler.cpp:
  * 5-23) and GpuConfig::enable_profiling (GpuConfig.hpp:83): while enabled,

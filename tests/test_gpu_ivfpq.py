@@ -1,0 +1,112 @@
+"""IVF-PQ parity (through the C ABI) with the reference's GpuIVFPQIndex::search
+(src/gpu_engine/GpuIVFPQIndex.cpp:161-237), run here from its own compiled
+sources (oracle/_ref) and from the golden fixture it produced.
+
+Returned ids and distances are the exact-reranked ones, so they must be
+identical. The approximate stage groups the same per-dimension terms by
+subspace, which could move a candidate across the rerank boundary
+(rank R = 4k) only on a rounding tie; the tests require identical results on
+every query and report any query that differs."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle as O
+from tests import helpers as H
+
+pytestmark = pytest.mark.gpu
+
+
+def test_ivfpq_golden_fixture():
+    from elips_b200.ivfpq import IvfPqIndex
+    G = np.load(Path(__file__).resolve().parent / "golden" / "reference_outputs.npz")
+    ix = IvfPqIndex("euclidean", 24, G["ivf_centroids"], G["ivf_codebook"], nprobe=3, pq_bits=4)
+    ix.add(G["base"], G["ivf_assignments"])          # residual codes encoded on the device
+    assert np.array_equal(ix.codes(), G["ivf_codes"])
+    d, r = ix.search_batch(G["queries"], 4)
+    assert np.array_equal(r, G["ivf_rows"])
+    assert np.array_equal(d, G["ivf_dist"])
+
+
+@pytest.fixture(scope="module")
+def model():
+    d, nlist = 64, 128
+    cents = H.gaussian(nlist, d, seed=61)
+    base = H.mixture(60_000, d, cents, 0.2, seed=62)
+    queries = H.mixture(200, d, cents, 0.2, seed=63)
+    cent = O.ref_kmeans(base[::10], nlist, 4)
+    asg = O.ivf_assign("euclidean", base, cent)
+    res = base - cent[asg]
+    cb = O.ref_train_pq_codebook(res[::6], 8, 256, 4)
+    codes = O.ref_encode_pq(cb, res)
+    return dict(base=base, queries=queries, cent=cent, asg=asg, cb=cb, codes=codes)
+
+
+@pytest.mark.parametrize("nprobe,k", [(8, 10), (1, 5), (200, 3)])
+def test_ivfpq_matches_reference(model, nprobe, k, nthreads):
+    from elips_b200.ivfpq import IvfPqIndex
+    m = model
+    ix = IvfPqIndex("euclidean", 64, m["cent"], m["cb"], nprobe=nprobe)
+    ix.add(m["base"], m["asg"], m["codes"])
+    d, r = ix.search_batch(m["queries"], k)
+    ref = O.RefIvfPqIndex("euclidean", m["cent"], m["asg"], m["cb"], m["codes"], m["base"], nprobe)
+    d_ref, r_ref = ref.search(m["queries"], k, nthreads)
+    bad = [q for q in range(r.shape[0]) if not (np.array_equal(r[q], r_ref[q]) and np.array_equal(d[q], d_ref[q]))]
+    assert not bad, f"{len(bad)} queries differ from the reference, first {bad[:5]}"
+
+
+def test_ivfpq_device_codes_match_reference_encode(model):
+    from elips_b200.ivfpq import IvfPqIndex
+    m = model
+    ix = IvfPqIndex("euclidean", 64, m["cent"], m["cb"], nprobe=8)
+    ix.add(m["base"][:20_000], m["asg"][:20_000])
+    ix.add(m["base"][20_000:], m["asg"][20_000:])
+    assert np.array_equal(ix.codes(), m["codes"])
+
+
+@pytest.mark.parametrize("metric", ["cosine", "dot_product"])
+def test_ivfpq_inner_product_metrics_match_reference(metric, nthreads):
+    from elips_b200.ivfpq import IvfPqIndex
+    d, nlist = 32, 40
+    base = H.normalize(H.gaussian(8000, d, seed=64))
+    q = H.normalize(H.gaussian(50, d, seed=65))
+    cent = O.ref_kmeans(base, nlist, 4)
+    asg = O.ivf_assign(metric, base, cent)
+    res = base - cent[asg]
+    cb = O.ref_train_pq_codebook(res, 4, 64, 4)
+    codes = O.ref_encode_pq(cb, res)
+    ix = IvfPqIndex(metric, d, cent, cb, nprobe=6, pq_bits=6)
+    ix.add(base, asg, codes)
+    dist, rows = ix.search_batch(q, 7)
+    d_ref, r_ref = O.RefIvfPqIndex(metric, cent, asg, cb, codes, base, 6, pq_bits=6).search(q, 7, nthreads)
+    assert np.array_equal(rows, r_ref) and np.array_equal(dist, d_ref)
+
+
+def test_ivfpq_device_api_and_empty_index(model):
+    import torch
+    from elips_b200.ivfpq import IvfPqIndex
+    m = model
+    empty = IvfPqIndex("euclidean", 64, m["cent"], m["cb"], nprobe=4)
+    d, r = empty.search_batch(m["queries"][:3], 5)
+    assert (r == -1).all()
+    ix = IvfPqIndex("euclidean", 64, m["cent"], m["cb"], nprobe=4)
+    vd = torch.from_numpy(m["base"]).cuda()
+    ad = torch.from_numpy(m["asg"].view(np.int32)).cuda()
+    ix.add_device(vd, ad)
+    d1, r1 = ix.search_batch(m["queries"], 10)
+    d2, r2 = ix.search_device(torch.from_numpy(m["queries"]).cuda(), 10)
+    torch.cuda.synchronize()
+    assert np.array_equal(r1, r2.cpu().numpy()) and np.array_equal(d1, d2.cpu().numpy())
+
+
+def test_ivfpq_rejects_bad_assignment(model):
+    from elips_b200 import ElipsB200Error
+    from elips_b200.ivfpq import IvfPqIndex
+    m = model
+    ix = IvfPqIndex("euclidean", 64, m["cent"], m["cb"], nprobe=4)
+    bad = m["asg"][:10].copy()
+    bad[3] = 128  # one past the last list
+    with pytest.raises(ElipsB200Error):
+        ix.add(m["base"][:10], bad)
+    assert ix.size() == 0
