@@ -293,6 +293,35 @@ def train_ivfpq_model(cfg, base):
     return cent.contiguous(), assign.to(torch.int32), cb.contiguous()
 
 
+def ivfpq_inputs(cfg, dev):
+    """Seeded base rows and queries of the IVF-PQ workload and its trained
+    model, all on `dev`: (base, queries, centroids, assignments, codebook)."""
+    import torch
+    n, d = cfg["n"], cfg["d"]
+    cents = _centroids(cfg, dev)
+    base = torch.empty((n, d), dtype=torch.float32, device=dev)
+    for r0 in range(0, n, 1 << 20):
+        cnt = min(1 << 20, n - r0)
+        base[r0:r0 + cnt] = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev)
+    queries = gen_rows(cfg, 0, cfg["q"], SEED + 2, cfg["q"], cents, device=dev)
+    centroids, assign, codebook = train_ivfpq_model(cfg, base)
+    return base, queries, centroids, assign, codebook
+
+
+def encode_residuals(base, centroids, assign, codebook, chunk=1 << 20):
+    """Residual PQ codes (nearest codeword per subspace) with torch ops: the
+    snapshot codes the reference arm imports (import_snapshot takes codes as
+    given, GpuIVFPQIndex.cpp:327-348)."""
+    import torch
+    m, ksub, sub = codebook.shape
+    codes = torch.empty((base.shape[0], m), dtype=torch.uint8, device=base.device)
+    for i in range(0, base.shape[0], chunk):
+        res = base[i:i + chunk] - centroids[assign[i:i + chunk].long()]
+        for j in range(m):
+            codes[i:i + chunk, j] = _nearest(res[:, j * sub:(j + 1) * sub].contiguous(), codebook[j]).to(torch.uint8)
+    return codes
+
+
 def scanned_bytes(cfg, centroids, queries, assign):
     """Algorithmic bytes of one IVF-PQ scan: for every (query, probed list),
     each member's code (pq_dim bytes) and slot id (4 bytes)."""
@@ -314,14 +343,8 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     n, d, nq, k = cfg["n"], cfg["d"], cfg["q"], cfg["k"]
-    cents = _centroids(cfg, dev)
     t0 = time.perf_counter()
-    base = torch.empty((n, d), dtype=torch.float32, device=dev)
-    for r0 in range(0, n, 1 << 20):
-        cnt = min(1 << 20, n - r0)
-        base[r0:r0 + cnt] = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev)
-    q_dev = gen_rows(cfg, 0, nq, SEED + 2, nq, cents, device=dev)
-    centroids, assign, codebook = train_ivfpq_model(cfg, base)
+    base, q_dev, centroids, assign, codebook = ivfpq_inputs(cfg, dev)
     index = IvfPqIndex(cfg["metric"], d, centroids.cpu().numpy(), codebook.cpu().numpy(), nprobe=cfg["nprobe"],
                        pq_bits=cfg["pq_bits"], device=local)
     for r0 in range(0, n, 1 << 21):
@@ -649,10 +672,38 @@ def cpu_baseline(cfg, base, queries, mask_words):
                       f"({what}), {dt:.2f} s wall"}
 
 
+def _reference_ivfpq(cfg):
+    """(search, kind, description, base rows, queries) for the reference's
+    GpuIVFPQIndex::search on a CPU GpuPort, the trained model imported as a
+    snapshot. Inputs are prepared with torch (on the GPU when one is visible)."""
+    import torch
+    oracle, kind = _ref_or_port()
+    gdev = "cuda" if torch.cuda.is_available() else "cpu"
+    base, q, cent, assign, cb = ivfpq_inputs(cfg, gdev)
+    codes = encode_residuals(base, cent, assign, cb).cpu().numpy()
+    base_np, q_np = base.cpu().numpy(), q.cpu().numpy()
+    cent_np, cb_np, a_np = cent.cpu().numpy(), cb.cpu().numpy(), assign.cpu().numpy().view(np.uint32)
+    del base, q, cent, assign, cb
+    if gdev == "cuda":
+        torch.cuda.empty_cache()
+    if kind == "reference":
+        idx = oracle.RefIvfPqIndex(cfg["metric"], cent_np, a_np, cb_np, codes, base_np, cfg["nprobe"],
+                                   pq_bits=cfg["pq_bits"])
+        return (lambda qq, kk, tt: idx.search(qq, kk, tt)), kind, \
+            "reference GpuIVFPQIndex::search on a CPU GpuPort (import_snapshot of the trained model)", base_np, q_np
+    return (lambda qq, kk, tt: oracle.ivfpq_search(cfg["metric"], cent_np, cb_np, codes, base_np, a_np, qq,
+                                                   cfg["nprobe"], kk, tt)), kind, \
+        "C restatement of GpuIVFPQIndex::search", base_np, q_np
+
+
 def run_reference(args, cfg):
     """The reference's CPU implementation of the path, all host threads, one
     bounded query sample per step."""
     import torch
+    if args.config == "ivfpq":
+        threads = os.cpu_count() or 1
+        search, kind, what, base, queries = _reference_ivfpq(cfg)
+        return _time_reference(args, cfg, search, kind, what, base, queries, threads)
     # Data generation only (untimed): on the GPU when one is visible, else CPU.
     gdev = "cuda" if torch.cuda.is_available() else "cpu"
     cents = _centroids(cfg, gdev) if cfg["data"] == "mixture" else None
@@ -664,6 +715,10 @@ def run_reference(args, cfg):
     mask_words = gen_mask_words(cfg, cfg["n"]) if cfg.get("mask_p") else None
     threads = os.cpu_count() or 1
     search, kind, what = _cpu_searcher(cfg, base, mask_words)
+    return _time_reference(args, cfg, search, kind, what, base, queries, threads)
+
+
+def _time_reference(args, cfg, search, kind, what, base, queries, threads):
     sample = _calibrated_sample(search, cfg, queries, threads, target_s=1.0)
     for i in range(args.warmup):
         search(queries[:sample], cfg["k"], threads)

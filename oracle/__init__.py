@@ -211,20 +211,29 @@ def lists_csr(assignments, nlist):
     return offsets, order
 
 
-def ivfpq_search(metric, centroids, codebook, codes, vectors, assignments, queries, nprobe, k, nthreads=None):
+def ivfpq_search(metric, centroids, codebook, codes, vectors, assignments, queries, nprobe, k, nthreads=None,
+                 order="reference", with_gap=False):
+    """GpuIVFPQIndex::search. order="reference": the reference's own tie order
+    (libstdc++ partial_sort for the rerank set, rerank position for exact
+    ties); order="device": subspace-grouped approximate sums and ties by slot,
+    the device path's documented order. with_gap also returns, per query, the
+    relative gap between the R-th approximate distance and the first one left
+    out (0 = tied at the rerank boundary)."""
     centroids, codebook, vectors, queries = _f32(centroids), _f32(codebook), _f32(vectors), _f32(queries)
     nlist, d = centroids.shape
     m, ksub, sub = codebook.shape
-    offsets, order = lists_csr(assignments, nlist)
+    offsets, order_rows = lists_csr(assignments, nlist)
     codes = np.ascontiguousarray(codes, np.uint8)
     nq = queries.shape[0]
     dist = np.empty((nq, k), np.float32)
     rows = np.empty((nq, k), np.int64)
+    gap = np.empty(nq, np.float32)
+    mode = {"reference": 0, "device": 1}[order]
     orc().orc_ivfpq_search(METRIC[metric], c_size_t(d), c_size_t(m), c_size_t(ksub), c_size_t(nlist),
                            c_size_t(nprobe), _p(centroids), _p(codebook), _p(codes), _p(vectors), _p(offsets),
-                           _p(order), _p(queries), c_size_t(nq), c_size_t(k), c_int(_threads(nthreads)),
-                           _p(dist), _p(rows))
-    return dist, rows
+                           _p(order_rows), _p(queries), c_size_t(nq), c_size_t(k), c_int(mode),
+                           c_int(_threads(nthreads)), _p(dist), _p(rows), _p(gap))
+    return (dist, rows, gap) if with_gap else (dist, rows)
 
 
 # --------------------------------------------------- reference, compiled

@@ -517,27 +517,125 @@ typedef struct {
     int metric; size_t d, m, ksub, nlist, nprobe;
     const float* centroids; const float* codebook; const uint8_t* codes; const float* vectors;
     const uint32_t* list_offsets; const uint32_t* list_rows; /* CSR: members of each list */
-    const float* queries; size_t k; float* out_d; int64_t* out_r;
+    const float* queries; size_t k; int mode; float* out_d; int64_t* out_r; float* out_gap;
 } ivfpq_ctx;
 
-typedef struct { float d; uint64_t pos; uint32_t row; } cand_t;
+typedef struct { float d; uint32_t row; } cand_t;
 
-static int cand_cmp(const void* a, const void* b) {
+/* std::partial_sort(first, middle, last, by distance) as GNU libstdc++
+ * (bits/stl_algo.h, bits/stl_heap.h; GCC 13.3 here, unchanged for many
+ * releases) implements it: heap-select (build a max-heap over [first, middle)
+ * bottom-up, then every later element strictly below the root replaces it by
+ * a pop), then heap-sort of [first, middle). The standard leaves the order of
+ * equal distances unspecified; this restates the one the reference's build
+ * actually produces, so that candidates tied at the rerank boundary are
+ * chosen exactly as the reference chooses them. */
+static int cand_less(const cand_t* a, const cand_t* b) { return a->d < b->d; }
+
+/* Moves the hole at `hole` down to a leaf (always along the larger child,
+ * the right one unless the left is strictly larger), then sifts `v` up from
+ * there, no higher than `top`. */
+static void heap_adjust(cand_t* a, size_t hole, size_t len, cand_t v) {
+    const size_t top = hole;
+    size_t child = hole;
+    while (len > 2 && child < (len - 1) / 2) {
+        child = 2 * (child + 1);
+        if (cand_less(&a[child], &a[child - 1])) --child;
+        a[hole] = a[child];
+        hole = child;
+    }
+    if ((len & 1) == 0 && len >= 2 && child == (len - 2) / 2) {
+        child = 2 * (child + 1);
+        a[hole] = a[child - 1];
+        hole = child - 1;
+    }
+    while (hole > top) {
+        const size_t parent = (hole - 1) / 2;
+        if (!cand_less(&a[parent], &v)) break;
+        a[hole] = a[parent];
+        hole = parent;
+    }
+    a[hole] = v;
+}
+
+static void partial_sort_libstdcxx(cand_t* a, size_t mid, size_t n) {
+    if (mid < 2) {  /* one-element heap: replacement still follows the root test */
+        for (size_t i = mid; mid == 1 && i < n; ++i)
+            if (cand_less(&a[i], &a[0])) { cand_t t = a[0]; a[0] = a[i]; a[i] = t; }
+        return;
+    }
+    for (size_t parent = (mid - 2) / 2;; --parent) {
+        heap_adjust(a, parent, mid, a[parent]);
+        if (parent == 0) break;
+    }
+    for (size_t i = mid; i < n; ++i) {
+        if (cand_less(&a[i], &a[0])) {  /* pop: the root goes to i, a[i] re-enters */
+            const cand_t v = a[i];
+            a[i] = a[0];
+            heap_adjust(a, 0, mid, v);
+        }
+    }
+    for (size_t last = mid; last > 1;) {  /* sort_heap */
+        --last;
+        const cand_t v = a[last];
+        a[last] = a[0];
+        heap_adjust(a, 0, last, v);
+    }
+}
+
+static int cand_slot_cmp(const void* a, const void* b) {
     const cand_t* x = (const cand_t*)a; const cand_t* y = (const cand_t*)b;
     if (x->d < y->d) return -1;
     if (y->d < x->d) return 1;
-    return x->pos < y->pos ? -1 : (x->pos > y->pos);
+    return x->row < y->row ? -1 : (x->row > y->row);
+}
+
+/* Approximate distance of one candidate, decoded as centroid + codeword in
+ * fp32 (decode_candidate_vector, GpuIVFPQIndex.cpp:132-148).
+ * mode 0: elips::distance on the decoded vector, one sequential sum over all
+ *         dimensions (GpuIVFPQIndex.cpp:204);
+ * mode 1: the same per-dimension terms summed per subspace, then the subspace
+ *         sums in order: the lookup-table grouping the device scan uses. */
+static float ivfpq_approx(const ivfpq_ctx* x, const float* qv, const float* cen, const uint8_t* code, float* dec) {
+    const size_t d = x->d, sub = d / x->m;
+    if (x->mode == 0) {
+        for (size_t s = 0; s < x->m; ++s) {
+            const float* cw = x->codebook + (s * x->ksub + code[s]) * sub;
+            for (size_t t = 0; t < sub; ++t) dec[s * sub + t] = cen[s * sub + t] + cw[t];
+        }
+        return orc_distance(x->metric, qv, dec, d);
+    }
+    float total = 0.0f;
+    for (size_t s = 0; s < x->m; ++s) {
+        const float* cw = x->codebook + (s * x->ksub + code[s]) * sub;
+        float acc = 0.0f;
+        for (size_t t = 0; t < sub; ++t) {
+            const size_t i = s * sub + t;
+            const float dv = cen[i] + cw[t];
+            if (x->metric == ORC_EUCLIDEAN) { const float df = qv[i] - dv; acc += df * df; }
+            else acc += qv[i] * dv;
+        }
+        total += acc;
+    }
+    if (x->metric == ORC_EUCLIDEAN) return sqrtf(total);
+    return x->metric == ORC_COSINE ? 1.0f - total : -total;
 }
 
 /* GpuIVFPQIndex::search, GpuIVFPQIndex.cpp:161-237:
  *   probe_lists -> gather_candidates (probe order, then list member order,
- *   IvfIndexState.cpp:466-504) -> decode each candidate as centroid +
- *   codeword in fp32 (decode_candidate_vector, :132-148) -> elips::distance
- *   -> keep R = max(4k, k) smallest (:210-218) -> exact_rank: exact
- *   elips::distance on the raw vectors and top-k (:37-71, :235-236). */
+ *   IvfIndexState.cpp:466-504) -> approximate distance per candidate
+ *   (:190-206) -> keep R = max(4k, k) smallest (:208-218) -> exact_rank:
+ *   exact elips::distance on the raw vectors and top-k (:37-71, :235-236).
+ * mode 0 is the reference's own order: R chosen by libstdc++'s partial_sort,
+ *   exact top-k ties broken by rerank position (GpuPort::top_k order);
+ * mode 1 is the device path's documented order: approximate sums grouped by
+ *   subspace, ties broken by slot in both stages.
+ * out_gap[q] (optional): relative gap between the R-th smallest approximate
+ *   distance and the smallest one left out (0 = tied at the boundary, +inf =
+ *   nothing left out), in this mode's arithmetic. */
 static void ivfpq_one(const void* c, size_t q, hit_t* scratch) {
     const ivfpq_ctx* x = (const ivfpq_ctx*)c;
-    const size_t d = x->d, sub = d / x->m;
+    const size_t d = x->d;
     const float* qv = x->queries + q * d;
     uint32_t* lists = (uint32_t*)malloc(sizeof(uint32_t) * x->nprobe);
     orc_ivf_probe(x->metric, qv, d, x->centroids, x->nlist, x->nprobe, lists, NULL);
@@ -553,27 +651,37 @@ static void ivfpq_one(const void* c, size_t q, hit_t* scratch) {
         const float* cen = x->centroids + (size_t)l * d;
         for (uint32_t j = x->list_offsets[l]; j < x->list_offsets[l + 1]; ++j) {
             const uint32_t row = x->list_rows[j];
-            const uint8_t* code = x->codes + (size_t)row * x->m;
-            for (size_t s = 0; s < x->m; ++s) {
-                const float* cw = x->codebook + (s * x->ksub + code[s]) * sub;
-                for (size_t t = 0; t < sub; ++t) dec[s * sub + t] = cen[s * sub + t] + cw[t];
-            }
-            cands[nc].d = orc_distance(x->metric, qv, dec, d);
-            cands[nc].pos = nc;
+            cands[nc].d = ivfpq_approx(x, qv, cen, x->codes + (size_t)row * x->m, dec);
             cands[nc].row = row;
             ++nc;
         }
     }
     size_t rk = 4 * x->k > x->k ? 4 * x->k : x->k;
     if (rk > nc) rk = nc;
-    qsort(cands, nc, sizeof(cand_t), cand_cmp);
+    if (x->mode == 0) partial_sort_libstdcxx(cands, rk, nc);
+    else qsort(cands, nc, sizeof(cand_t), cand_slot_cmp);
+    if (x->out_gap) {
+        float g = INFINITY;
+        if (rk > 0 && rk < nc) {
+            float lo = cands[rk].d;
+            for (size_t i = rk + 1; i < nc; ++i) if (cands[i].d < lo) lo = cands[i].d;
+            const float hi = cands[rk - 1].d, mag = fmaxf(fabsf(hi), fabsf(lo));
+            g = mag > 0.0f ? (lo - hi) / mag : lo - hi;
+        }
+        x->out_gap[q] = g;
+    }
     heap_t hp = { scratch, 0, x->k };
     for (size_t i = 0; i < rk; ++i) {
         const uint32_t row = cands[i].row;
-        hit_t h = { orc_distance(x->metric, qv, x->vectors + (size_t)row * d, d), (int64_t)row };
+        hit_t h = { orc_distance(x->metric, qv, x->vectors + (size_t)row * d, d),
+                    x->mode == 0 ? (int64_t)i : (int64_t)row };
         heap_push(&hp, h);
     }
-    heap_emit(&hp, x->k, x->out_d + q * x->k, x->out_r + q * x->k);
+    float* od = x->out_d + q * x->k;
+    int64_t* orow = x->out_r + q * x->k;
+    heap_emit(&hp, x->k, od, orow);
+    if (x->mode == 0)
+        for (size_t i = 0; i < x->k; ++i) if (orow[i] >= 0) orow[i] = cands[orow[i]].row;
     free(dec); free(cands); free(lists);
 }
 
@@ -581,8 +689,8 @@ void orc_ivfpq_search(int metric, size_t d, size_t m, size_t ksub, size_t nlist,
                       const float* centroids, const float* codebook, const uint8_t* codes,
                       const float* vectors, const uint32_t* list_offsets,
                       const uint32_t* list_rows, const float* queries, size_t nq, size_t k,
-                      int nthreads, float* out_d, int64_t* out_r) {
+                      int mode, int nthreads, float* out_d, int64_t* out_r, float* out_gap) {
     ivfpq_ctx c = { metric, d, m, ksub, nlist, nprobe, centroids, codebook, codes, vectors,
-                    list_offsets, list_rows, queries, k, out_d, out_r };
+                    list_offsets, list_rows, queries, k, mode, out_d, out_r, out_gap };
     run_queries(&c, ivfpq_one, nq, nthreads, k);
 }

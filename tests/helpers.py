@@ -73,3 +73,22 @@ def assert_ranked_match(dist_gpu, rows_gpu, dist_ref, rows_ref, true_dist, rtol,
     for q in range(rows_gpu.shape[0]):
         r = rows_gpu[q][rows_gpu[q] >= 0]
         assert len(np.unique(r)) == len(r), f"duplicate slots for query {q}"
+
+
+def ivfpq_tie_model():
+    """IVF-PQ model whose lists hold many rows with identical residual codes
+    (12.7k of 60k rows share a code with another row): coarse k-means leaves
+    tight residual clusters, so approximate distances tie exactly at the
+    rerank boundary for about a quarter of the queries. Trained with the
+    reference's own k-means and PQ trainer (oracle/_ref)."""
+    import oracle as O
+    d, nlist = 64, 128
+    cents = gaussian(nlist, d, seed=61)
+    base = mixture(60_000, d, cents, 0.2, seed=62)
+    queries = mixture(200, d, cents, 0.2, seed=63)
+    cent = O.ref_kmeans(base[::10], nlist, 4)
+    asg = O.ivf_assign("euclidean", base, cent)
+    res = base - cent[asg]
+    cb = O.ref_train_pq_codebook(res[::6], 8, 256, 4)
+    codes = O.ref_encode_pq(cb, res)
+    return dict(base=base, queries=queries, cent=cent, asg=asg, cb=cb, codes=codes)

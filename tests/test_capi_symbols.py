@@ -56,5 +56,7 @@ def test_library_links_no_torch():
     """The shipped library depends on the CUDA runtime only (statically)."""
     import subprocess
     from elips_b200 import _capi
-    out = subprocess.run(["ldd", str(_capi.LIB_PATH)], capture_output=True, text=True).stdout
-    assert "torch" not in out and "c10" not in out
+    out = subprocess.run(["readelf", "-d", str(_capi.LIB_PATH)], capture_output=True, text=True, check=True).stdout
+    needed = re.findall(r"\(NEEDED\)\s+Shared library: \[([^\]]+)\]", out)
+    assert needed, out
+    assert not [n for n in needed if "torch" in n or "c10" in n or "cudart" in n], needed

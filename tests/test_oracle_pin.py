@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 
 import oracle as O
+from tests import helpers as H
 
 pytestmark = pytest.mark.skipif(not O.ref_available(), reason="reference sources not present")
 
@@ -89,3 +90,20 @@ def test_ivfpq_search_matches_reference(data):
     d1, r1 = O.ivfpq_search("euclidean", cent, cb, codes, base, asg, q, 5, 10)
     d2, r2 = O.RefIvfPqIndex("euclidean", cent, asg, cb, codes, base, 5, pq_bits=4).search(q, 10)
     assert np.array_equal(d1, d2) and np.array_equal(r1, r2)
+
+
+@pytest.mark.parametrize("nprobe,k", [(8, 10), (1, 5), (200, 3)])
+def test_ivfpq_tie_order_matches_reference(nprobe, k):
+    """Candidates tied at the rerank boundary: the restatement of libstdc++'s
+    partial_sort picks the same ones as the reference on every query, and
+    the device order (ties by slot) differs from it only on tied queries."""
+    m = H.ivfpq_tie_model()
+    args = ("euclidean", m["cent"], m["cb"], m["codes"], m["base"], m["asg"], m["queries"], nprobe, k)
+    d0, r0, gap = O.ivfpq_search(*args, order="reference", with_gap=True)
+    d1, r1 = O.ivfpq_search(*args, order="device")
+    d2, r2 = O.RefIvfPqIndex("euclidean", m["cent"], m["asg"], m["cb"], m["codes"], m["base"], nprobe).search(
+        m["queries"], k)
+    assert np.array_equal(d0, d2) and np.array_equal(r0, r2)
+    assert (gap == 0).sum() >= 20  # the model really exercises boundary ties
+    differ = [q for q in range(len(r1)) if not (np.array_equal(r1[q], r2[q]) and np.array_equal(d1[q], d2[q]))]
+    assert all(gap[q] == 0 for q in differ)
