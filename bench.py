@@ -382,7 +382,7 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
     scan = _capi.profiler_stats("ivfpq_scan")
     allk = _capi.profiler_stats(None)
     per_kernel = {name: round(_capi.profiler_stats(name)["total_ms"] / args.steps, 4)
-                  for name in ("distances", "topk_rows", "ivfpq_scan", "merge_topk", "ivfpq_rerank")}
+                  for name in ("distances", "topk_rows", "ivfpq_plan", "ivfpq_scan", "merge_topk", "ivfpq_rerank")}
     value = nq * args.steps / (ms / 1e3)
 
     q_np = q_dev.cpu().pin_memory().numpy()

@@ -40,6 +40,10 @@ public:
         device_props(device);
         DeviceGuard g(device);
         ksub_ = 1u << pq_bits;
+        pq_bits_ = pq_bits;
+        if (group_layout(1, dim, group_lut_stride(m_, ksub_), group_capacity(1, 4 * 256)).total >
+            device_props(device).max_smem_optin)
+            fail(ELIPS_B200_INVALID_ARGUMENT, "pq_dim x 2^pq_bits lookup table too large for shared memory");
         centroids_ = DeviceBuffer(device, static_cast<size_t>(nlist) * dim * 4);
         check_cuda(cudaMemcpy(centroids_.get(), centroids, static_cast<size_t>(nlist) * dim * 4, cudaMemcpyHostToDevice),
                    ELIPS_B200_TRANSFER_FAILED, "centroids");
@@ -123,49 +127,98 @@ public:
         finalize(stream);
         const uint32_t nprobe = std::min(nprobe_, nlist_);
         const uint32_t r = static_cast<uint32_t>(4 * k);
+        const size_t npairs = nq * nprobe;
         const size_t dist_b = a256(nq * nlist_ * 4);
-        const size_t probe_b = a256(nq * nprobe * 4);
-        const size_t pval_b = a256(nq * nprobe * 4);
-        const size_t part_b = a256(nq * nprobe * static_cast<size_t>(r) * 8);
+        const size_t probe_b = a256(npairs * 4);
+        const size_t pval_b = a256(npairs * 4);
+        const size_t part_b = a256(npairs * static_cast<size_t>(r) * 8);
         const size_t cand_b = a256(nq * static_cast<size_t>(r) * 8);
-        StreamScratch s(dist_b + probe_b + pval_b + part_b + cand_b, stream);
-        float* dist = reinterpret_cast<float*>(s.get());
-        uint32_t* probes = reinterpret_cast<uint32_t*>(s.get() + dist_b);
-        float* pval = reinterpret_cast<float*>(s.get() + dist_b + probe_b);
-        uint2* part = reinterpret_cast<uint2*>(s.get() + dist_b + probe_b + pval_b);
-        uint2* cand = reinterpret_cast<uint2*>(s.get() + dist_b + probe_b + pval_b + part_b);
+        const size_t list_b = a256(static_cast<size_t>(nlist_) * 4);
+        const size_t pairs_b = a256(npairs * 4);
+        const size_t items_b = a256((npairs + nlist_) * 8);
+        StreamScratch s(dist_b + probe_b + pval_b + part_b + cand_b + 3 * list_b + pairs_b + items_b + 256 + a256(nq * 4),
+                        stream);
+        uint8_t* w = s.get();
+        auto carve = [&](size_t bytes) {
+            uint8_t* at = w;
+            w += bytes;
+            return at;
+        };
+        float* dist = reinterpret_cast<float*>(carve(dist_b));
+        uint32_t* probes = reinterpret_cast<uint32_t*>(carve(probe_b));
+        float* pval = reinterpret_cast<float*>(carve(pval_b));
+        uint2* part = reinterpret_cast<uint2*>(carve(part_b));
+        uint2* cand = reinterpret_cast<uint2*>(carve(cand_b));
+        uint32_t* counts = reinterpret_cast<uint32_t*>(carve(list_b));
+        uint32_t* list_start = reinterpret_cast<uint32_t*>(carve(list_b));
+        uint32_t* cursor = reinterpret_cast<uint32_t*>(carve(list_b));
+        uint32_t* pairs = reinterpret_cast<uint32_t*>(carve(pairs_b));
+        uint2* items = reinterpret_cast<uint2*>(carve(items_b));
+        uint32_t* ctrl = reinterpret_cast<uint32_t*>(carve(256));
+        uint32_t* qbound = reinterpret_cast<uint32_t*>(carve(a256(nq * 4)));
         // 1. probe (IvfIndexState::probe_lists): exact distances, then top-nprobe
         compute_distances_device(device_, queries, static_cast<const float*>(centroids_.get()), dist, nq, nlist_, dim_,
                                  metric_, stream);
         top_k_device(device_, dist, probes, pval, nq, nlist_, nprobe, stream);
-        // 2. per (query, probed list) approximate scan, top-R per list
-        IvfPqParams p{};
+        // 2. group the (query, probe) pairs by list
+        const uint32_t G = group_size(npairs, r);
+        const auto& props = device_props(device_);
+        const uint32_t lut_stride = group_lut_stride(m_, ksub_);
+        const uint32_t capq = group_capacity(G, r);
+        const GroupLayout L = group_layout(G, dim_, lut_stride, capq);
+        check_cuda(cudaMemsetAsync(counts, 0, static_cast<size_t>(nlist_) * 4, stream), ELIPS_B200_KERNEL_LAUNCH_FAILED,
+                   "pair counts");
+        check_cuda(cudaMemsetAsync(qbound, 0xFF, nq * 4, stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "query bounds");
+        const uint32_t pblocks = static_cast<uint32_t>((npairs + 255) / 256);
+        {
+            Profiler::Scope prof("ivfpq_plan", stream, npairs);
+            ivf_pair_count_kernel<<<pblocks, 256, 0, stream>>>(probes, static_cast<uint32_t>(npairs), nlist_, counts,
+                                                               part, r);
+            launch_ok("pair count kernel");
+        }
+        {
+            uint32_t npow2 = 1;
+            while (npow2 < nlist_) npow2 <<= 1;
+            const size_t psmem = nlist_ <= kPlanSortMax ? static_cast<size_t>(npow2) * 8 : 0;
+            check_cuda(cudaFuncSetAttribute(ivf_group_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(psmem)),
+                       ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+            Profiler::Scope prof("ivfpq_plan", stream, nlist_);
+            ivf_group_plan_kernel<<<1, kPlanThreads, psmem, stream>>>(
+                counts, static_cast<const uint32_t*>(list_off_.get()), nlist_, G, list_start, cursor, items, ctrl);
+            launch_ok("group plan kernel");
+        }
+        {
+            Profiler::Scope prof("ivfpq_plan", stream, npairs);
+            ivf_pair_scatter_kernel<<<pblocks, 256, 0, stream>>>(probes, static_cast<uint32_t>(npairs), nlist_,
+                                                                 list_start, cursor, pairs);
+            launch_ok("pair scatter kernel");
+        }
+        // 3. per (list, query group) approximate scan, R best per (query, list)
+        IvfGroupParams p{};
         p.queries = queries;
         p.centroids = static_cast<const float*>(centroids_.get());
         p.codebook = static_cast<const float*>(codebook_.get());
         p.list_codes = static_cast<const uint8_t*>(list_codes_.get());
         p.list_rows = static_cast<const uint32_t*>(list_rows_.get());
         p.list_off = static_cast<const uint32_t*>(list_off_.get());
-        p.probes = probes;
+        p.counts = counts;
+        p.list_start = list_start;
+        p.pairs = pairs;
+        p.items = items;
+        p.ctrl = ctrl;
         p.partial = part;
-        p.nq = static_cast<uint32_t>(nq);
+        p.qbound = qbound;
         p.d = dim_;
-        p.nlist = nlist_;
         p.nprobe = nprobe;
         p.m = m_;
-        p.ksub = ksub_;
+        p.pq_bits = pq_bits_;
         p.r = r;
-        p.cap = (r + kIvfThreads + 31u) / 32u * 32u;
+        p.capq = capq;
+        p.lut_stride = lut_stride;
         p.metric = metric_;
-        const size_t smem = static_cast<size_t>(m_) * ksub_ * 4 + 2ull * dim_ * 4 + btk_bytes(p.cap);
-        if (smem > device_props(device_).max_smem_optin) fail(ELIPS_B200_INVALID_ARGUMENT, "model too large for the scan");
-        check_cuda(cudaFuncSetAttribute(ivfpq_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
-                   ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
-        {
-            Profiler::Scope prof("ivfpq_scan", stream, nq * nprobe);
-            ivfpq_scan_kernel<<<static_cast<uint32_t>(nq * nprobe), kIvfThreads, smem, stream>>>(p);
-            launch_ok("ivf-pq scan kernel");
-        }
+        const uint64_t max_items = std::min<uint64_t>(npairs, npairs / G + nlist_);
+        launch_group_scan(G, p, L.total, props, max_items, stream);
         // 3. R best approximate candidates per query across its probed lists
         //    (keys are final approximate distances: no transform, metric 0)
         merge_candidates(device_, part, static_cast<uint32_t>(nq), nprobe, r, static_cast<uint64_t>(nprobe) * r, r, 0,
@@ -186,6 +239,65 @@ public:
     }
 
 private:
+    // Queries per scan group: about as many as share a probed list on
+    // average, at most 8, and no more than shared memory holds.
+    uint32_t group_size(size_t npairs, uint32_t r) const {
+        const double share = static_cast<double>(npairs) / static_cast<double>(std::min<size_t>(nlist_, npairs));
+        uint32_t G = 1;
+        while (G < 8 && 2.0 * G <= share) G <<= 1;
+        const size_t optin = device_props(device_).max_smem_optin;
+        while (G > 1 && group_layout(G, dim_, group_lut_stride(m_, ksub_), group_capacity(G, r)).total > optin) G >>= 1;
+        return G;
+    }
+
+    template <int G, int MB, int BITS>
+    void launch_group(const IvfGroupParams& p, size_t smem, const DeviceProps& props, uint64_t max_items,
+                      cudaStream_t stream) {
+        auto kern = ivfpq_group_scan_kernel<G, MB, BITS>;
+        check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+                   ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+        int per_sm = 0;
+        check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGroupThreads, smem),
+                   ELIPS_B200_KERNEL_LAUNCH_FAILED, "occupancy");
+        if (per_sm < 1) fail(ELIPS_B200_INVALID_ARGUMENT, "ivf-pq scan does not fit on an SM");
+        const uint64_t grid = std::max<uint64_t>(1, std::min<uint64_t>(static_cast<uint64_t>(props.num_sms) * per_sm,
+                                                                       max_items));
+        Profiler::Scope prof("ivfpq_scan", stream, max_items);
+        kern<<<static_cast<uint32_t>(grid), kGroupThreads, smem, stream>>>(p);
+        launch_ok("ivf-pq group scan kernel");
+    }
+
+    template <int G>
+    void launch_group_mb(const IvfGroupParams& p, size_t smem, const DeviceProps& props, uint64_t max_items,
+                         cudaStream_t stream) {
+        if (pq_bits_ == 8) {
+            switch (m_) {
+                case 8: return launch_group<G, 8, 8>(p, smem, props, max_items, stream);
+                case 16: return launch_group<G, 16, 8>(p, smem, props, max_items, stream);
+                case 32: return launch_group<G, 32, 8>(p, smem, props, max_items, stream);
+                default: break;
+            }
+        }
+        switch (m_) {
+            case 4: return launch_group<G, 4, 0>(p, smem, props, max_items, stream);
+            case 8: return launch_group<G, 8, 0>(p, smem, props, max_items, stream);
+            case 16: return launch_group<G, 16, 0>(p, smem, props, max_items, stream);
+            case 32: return launch_group<G, 32, 0>(p, smem, props, max_items, stream);
+            default: return launch_group<G, 0, 0>(p, smem, props, max_items, stream);
+        }
+    }
+
+    void launch_group_scan(uint32_t G, const IvfGroupParams& p, size_t smem, const DeviceProps& props,
+                           uint64_t max_items, cudaStream_t stream) {
+        if (smem > props.max_smem_optin) fail(ELIPS_B200_INVALID_ARGUMENT, "ivf-pq scan needs too much shared memory");
+        switch (G) {
+            case 8: return launch_group_mb<8>(p, smem, props, max_items, stream);
+            case 4: return launch_group_mb<4>(p, smem, props, max_items, stream);
+            case 2: return launch_group_mb<2>(p, smem, props, max_items, stream);
+            default: return launch_group_mb<1>(p, smem, props, max_items, stream);
+        }
+    }
+
     void reserve(size_t rows) {
         if (rows <= capacity_) return;
         const size_t cap = std::max<size_t>(rows, capacity_ + capacity_ / 2);
@@ -231,7 +343,7 @@ private:
     }
 
     int device_, metric_;
-    uint32_t dim_, nlist_, nprobe_, m_, ksub_ = 256;
+    uint32_t dim_, nlist_, nprobe_, m_, ksub_ = 256, pq_bits_ = 8;
     size_t n_ = 0, capacity_ = 0;
     bool dirty_ = false;
     std::vector<uint32_t> assign_;
