@@ -26,6 +26,20 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return n * rank // world, n * (rank + 1) // world
 
 
+def exchange_candidates(cand, world: int, group=None):
+    """All-gather of every rank's candidate block [nq, k, ...] into
+    [world, nq, k, ...], rank-major (rank r's block at index r). The output is
+    gathered flat, which every backend accepts: NCCL over NVLink for CUDA
+    tensors, gloo for CPU tensors. Collective: every rank of the group calls
+    it with blocks of the same shape."""
+    import torch
+    import torch.distributed as dist
+    cand = cand.contiguous()
+    flat = torch.empty((world * cand.shape[0],) + tuple(cand.shape[1:]), dtype=cand.dtype, device=cand.device)
+    dist.all_gather_into_tensor(flat, cand, group=group)
+    return flat.view((world,) + tuple(cand.shape))
+
+
 class ShardedExactIndex:
     """One rank's share of a row-sharded index. Every rank of the process group
     must call each method with the same arguments (collective semantics)."""
@@ -59,8 +73,7 @@ class ShardedExactIndex:
             return self.local.search_device(queries, k, mask=mask)
         cand = torch.empty((nq, k, 2), dtype=torch.int32, device=dev)
         self.local.search_candidates_device(queries, k, self.row_begin, cand, mask=mask)
-        gathered = torch.empty((self.world, nq, k, 2), dtype=torch.int32, device=dev)
-        self.dist.all_gather_into_tensor(gathered, cand, group=self.group)
+        gathered = exchange_candidates(cand, self.world, self.group)
         if self.rank != 0:
             return None, None
         return merge_candidates_device(gathered, self.world, k, self.metric)

@@ -1,0 +1,126 @@
+"""Multi-process host logic of the row-sharded search, on CPU with gloo ranks
+(world sizes 2 and 3): contiguous row ranges as split_ids
+(GpuDistributedIndex.cpp:12-22), global row offsets, the rank-major candidate
+exchange, and the root's merge, checked against the unsharded search. Each
+rank's local top-k comes from the oracle here (the per-shard device search is
+covered by the GPU tests); the exchange is the product's. Also: a rank that
+never joins makes the others' exchange end with an error within the process
+group's short timeout instead of hanging."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+import oracle as O
+from elips_b200.distributed import exchange_candidates, shard_range
+from tests import helpers as H
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+CASES = [("euclidean", 3000), ("cosine", 2999), ("euclidean", 5), ("dot_product", 1000)]
+
+
+def _case_data(metric, n):
+    base = H.gaussian(n, 16, seed=71 + n)
+    queries = H.gaussian(7, 16, seed=72)
+    if metric == "cosine":
+        base, queries = H.normalize(base), H.normalize(queries)
+    return base, queries
+
+
+def _worker(rank, world, port, k, out_dir):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        for c, (metric, n) in enumerate(CASES):
+            base, queries = _case_data(metric, n)
+            lo, hi = shard_range(base.shape[0], rank, world)
+            d, r = O.exact_search(metric, base[lo:hi], queries, k, 1)
+            # candidate block: (distance bits, global row); absent entries keep row -1
+            block = torch.empty((queries.shape[0], k, 2), dtype=torch.int64)
+            block[..., 0] = torch.from_numpy(d.view(np.int32).astype(np.int64))
+            block[..., 1] = torch.from_numpy(np.where(r >= 0, r + lo, -1))
+            gathered = exchange_candidates(block, world).numpy()
+            if rank == 0:
+                np.save(os.path.join(out_dir, f"gathered{c}.npy"), gathered)
+    finally:
+        dist.destroy_process_group()
+
+
+def _merge(gathered, k):
+    """Root merge: k smallest by (distance, row) over the rank-major blocks."""
+    world, nq = gathered.shape[:2]
+    dist = gathered[..., 0].astype(np.int32).view(np.float32)
+    rows = gathered[..., 1]
+    out_d = np.zeros((nq, k), np.float32)
+    out_r = np.full((nq, k), -1, np.int64)
+    for q in range(nq):
+        dq = dist[:, q].reshape(-1)
+        rq = rows[:, q].reshape(-1)
+        keep = rq >= 0
+        order = np.lexsort((rq[keep], dq[keep]))[:k]
+        out_d[q, :len(order)] = dq[keep][order]
+        out_r[q, :len(order)] = rq[keep][order]
+    return out_d, out_r
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_exchange_matches_unsharded_search(tmp_path, world):
+    k = 4
+    mp.spawn(_worker, args=(world, _free_port(), k, str(tmp_path)), nprocs=world, join=True)
+    for c, (metric, n) in enumerate(CASES):
+        base, queries = _case_data(metric, n)
+        d, r = _merge(np.load(tmp_path / f"gathered{c}.npy"), k)
+        d_ref, r_ref = O.exact_search(metric, base, queries, k, 1)
+        assert np.array_equal(r, r_ref) and np.array_equal(d, d_ref), (metric, n)
+
+
+def test_shard_ranges_partition_the_rows():
+    for n in (0, 1, 7, 1000, 2_000_000):
+        for world in (1, 2, 3, 8):
+            spans = [shard_range(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            assert max(b - a for a, b in spans) - min(b - a for a, b in spans) <= 1
+
+
+def _absent_rank_worker(rank, world, port, out_dir):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        return  # leaves between steps: never joins the exchange
+    try:
+        exchange_candidates(torch.zeros((2, 3, 2), dtype=torch.int64), world)
+        outcome = "completed"
+    except Exception as e:  # the short process-group timeout or the closed peer
+        outcome = "error: " + type(e).__name__
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(outcome)
+
+
+def test_absent_rank_fails_the_exchange_instead_of_hanging(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_absent_rank_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert (tmp_path / "rank0.txt").read_text().startswith("error")
