@@ -82,6 +82,16 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
     ("elips_b200_ivfpq_codes_device", c_int, [c_void_p, c_void_p, c_void_p]),
     ("elips_b200_ivfpq_destroy", c_int, [c_void_p]),
+    ("elips_b200_ivfflat_create", c_int,
+     [c_int, c_int, c_uint32, c_uint32, c_uint32, c_void_p, POINTER(c_void_p)]),
+    ("elips_b200_ivfflat_add", c_int, [c_void_p, c_void_p, c_void_p, c_size_t]),
+    ("elips_b200_ivfflat_add_device", c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("elips_b200_ivfflat_size", c_int, [c_void_p, POINTER(c_size_t)]),
+    ("elips_b200_ivfflat_set_nprobe", c_int, [c_void_p, c_uint32]),
+    ("elips_b200_ivfflat_search", c_int, [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p]),
+    ("elips_b200_ivfflat_search_device", c_int,
+     [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_ivfflat_destroy", c_int, [c_void_p]),
     ("elips_b200_profiler_enable", c_int, [c_int]),
     ("elips_b200_profiler_stats", c_int,
      [c_char_p, POINTER(ctypes.c_uint64), POINTER(ctypes.c_double), POINTER(ctypes.c_uint64)]),

@@ -144,6 +144,46 @@ static __global__ void ivf_pair_scatter_kernel(const uint32_t* __restrict__ prob
     if (l < nlist) pairs[list_start[l] + atomicAdd(&cursor[l], 1u)] = i;
 }
 
+// Gather position of each pair's first candidate: the candidates of a query
+// are its probed lists' members in probe order, then member order
+// (IvfIndexState::gather_candidates, IvfIndexState.cpp:466-504).
+static __global__ void ivf_pair_offsets_kernel(const uint32_t* __restrict__ probes, uint32_t nq, uint32_t nprobe,
+                                               uint32_t nlist, const uint32_t* __restrict__ list_off,
+                                               uint32_t* __restrict__ pair_off) {
+    const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= nq) return;
+    uint32_t at = 0;
+    for (uint32_t i = 0; i < nprobe; ++i) {
+        const size_t pair = static_cast<size_t>(q) * nprobe + i;
+        pair_off[pair] = at;
+        const uint32_t l = probes[pair];
+        if (l < nlist) at += list_off[l + 1] - list_off[l];
+    }
+}
+
+// rows[q][i]: gather position -> slot (the probed list holding it, then the
+// member at that offset). -1 stays -1.
+static __global__ void ivf_gather_to_slot_kernel(int64_t* __restrict__ rows, uint32_t nq, uint32_t k,
+                                                 const uint32_t* __restrict__ probes, uint32_t nprobe,
+                                                 const uint32_t* __restrict__ pair_off,
+                                                 const uint32_t* __restrict__ list_off,
+                                                 const uint32_t* __restrict__ list_rows) {
+    const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= static_cast<uint64_t>(nq) * k) return;
+    const int64_t gp = rows[t];
+    if (gp < 0) return;
+    const uint32_t q = static_cast<uint32_t>(t / k);
+    const uint32_t* off = pair_off + static_cast<size_t>(q) * nprobe;
+    uint32_t lo = 0, hi = nprobe - 1;  // largest i with off[i] <= gp (that list holds gp)
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi + 1) / 2;
+        if (off[mid] <= static_cast<uint64_t>(gp)) lo = mid;
+        else hi = mid - 1;
+    }
+    const uint32_t l = probes[static_cast<size_t>(q) * nprobe + lo];
+    rows[t] = list_rows[list_off[l] + static_cast<uint32_t>(gp - off[lo])];
+}
+
 // ----------------------------------------------------------------- scan
 
 constexpr uint32_t kGroupWarps = 16;
@@ -207,8 +247,10 @@ struct IvfGroupParams {
     const uint32_t* pairs;      // pair ids grouped by list
     const uint2* items;         // {list, first pair}
     uint32_t* ctrl;             // [0] item count, [1] work-queue cursor
-    uint2* partial;             // [npairs][r] {approximate key bits, slot}
+    uint2* partial;             // [npairs][r] {key bits, slot (PQ) or gather position (flat)}
     uint32_t* qbound;           // [nq] ordered key: the query's R-th best so far, over all lists
+    const float* list_vecs;     // flat: [n][d] raw rows, list-major
+    const uint32_t* pair_off;   // flat: [npairs] gather position of the pair's first member
     uint32_t d, nprobe, m, pq_bits, r, capq, lut_stride;
     int metric;
 };
@@ -463,6 +505,55 @@ __device__ __forceinline__ CodeWords<MB> load_code(const uint8_t* __restrict__ c
     return c;
 }
 
+// Exact elips::distance sums of one raw row against the G queries of the
+// group (Metrics.cpp:20-37: sequential over dimensions, no FMA).
+template <int G>
+__device__ __forceinline__ void flat_sums(const float* __restrict__ x, const float* qv, uint32_t d, bool l2,
+                                          float (&acc)[G]) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+    auto term = [&](uint32_t t, float xv, const float (&qx)[G]) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            if (l2) {
+                const float df = __fsub_rn(qx[g], xv);
+                acc[g] = __fadd_rn(acc[g], __fmul_rn(df, df));
+            } else {
+                acc[g] = __fadd_rn(acc[g], __fmul_rn(qx[g], xv));
+            }
+        }
+        (void)t;
+    };
+    if ((d & 3u) == 0) {
+        for (uint32_t t = 0; t < d; t += 4) {
+            const float4 xv = __ldg(reinterpret_cast<const float4*>(x + t));
+            float4 q4[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) q4[g] = *reinterpret_cast<const float4*>(qv + g * d + t);
+            float qx[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) qx[g] = q4[g].x;
+            term(t, xv.x, qx);
+#pragma unroll
+            for (int g = 0; g < G; ++g) qx[g] = q4[g].y;
+            term(t + 1, xv.y, qx);
+#pragma unroll
+            for (int g = 0; g < G; ++g) qx[g] = q4[g].z;
+            term(t + 2, xv.z, qx);
+#pragma unroll
+            for (int g = 0; g < G; ++g) qx[g] = q4[g].w;
+            term(t + 3, xv.w, qx);
+        }
+    } else {
+        for (uint32_t t = 0; t < d; ++t) {
+            float qx[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) qx[g] = qv[g * d + t];
+            term(t, __ldg(x + t), qx);
+        }
+    }
+}
+
 // Persistent CTAs over the plan's items (a work queue). Per item: list l and
 // up to G of its pairs. Each query of the group keeps its R best candidates
 // of the list by (approximate key, slot) in a shared-memory buffer:
@@ -475,9 +566,14 @@ __device__ __forceinline__ CodeWords<MB> load_code(const uint8_t* __restrict__ c
 //     z domain (warp_sum_bound), the key is computed for appended ones only;
 //   * at a round boundary a buffer that could overflow is compacted to R by
 //     one warp, and the bounds are refreshed.
-template <int G, int MB, int BITS>
+//
+// FLAT = true scores exact distances on the raw rows instead (IVF-Flat,
+// GpuIVFFlatIndex.cpp:44-103): a lane computes one candidate for all G
+// queries, and the id kept is the candidate's gather position, which orders
+// ties as the reference's top_k over the gathered candidates does.
+template <int G, int MB, int BITS, bool FLAT>
 __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(const IvfGroupParams p) {
-    constexpr uint32_t QP = group_qp(G);               // queries per lane
+    constexpr uint32_t QP = FLAT ? G : group_qp(G);    // queries per lane
     constexpr uint32_t P = G / QP;                      // lanes per candidate
     constexpr uint32_t kCpi = 32u / P;                  // candidates per warp step
     constexpr uint32_t kRound = group_round(G);         // candidates per round
@@ -494,6 +590,7 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
     uint32_t* s_thr = reinterpret_cast<uint32_t*>(smem + L.thr);      // [G] list bound, [G] applied T
     uint32_t* s_bound = reinterpret_cast<uint32_t*>(smem + L.bound);  // [G] z bound, [G] query ids
     uint32_t* s_item = reinterpret_cast<uint32_t*>(smem + L.item);    // next item: live, list, first, ng
+    __shared__ uint32_t s_pairoff[G];                                 // flat: gather offset of each pair
 
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t pq = lane % P, j = lane / P;  // this lane: quad pq of candidate j
@@ -549,23 +646,28 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
             s_thr[G + tid] = 0xFFFFFFFFu;
             s_bound[tid] = 0xFFFFFFFFu;
             s_bound[G + tid] = tid < ng ? p.pairs[first + tid] / p.nprobe : 0u;
+            if constexpr (FLAT) s_pairoff[tid] = tid < ng ? p.pair_off[p.pairs[first + tid]] : 0u;
         }
         __syncthreads();
         if (warp < ng) refresh_bound(warp, p.qbound[s_bound[G + warp]]);
-        build_group_lut<G>(lut, p.lut_stride, qv, cv, p.codebook, p.d, p.m, p.pq_bits, ng, p.metric);
-        __syncthreads();
+        if constexpr (!FLAT) {
+            build_group_lut<G>(lut, p.lut_stride, qv, cv, p.codebook, p.d, p.m, p.pq_bits, ng, p.metric);
+            __syncthreads();
+        }
 
         const uint32_t b0 = p.list_off[list], b1 = p.list_off[list + 1];
         bool qvalid[QP];
 #pragma unroll
         for (uint32_t qi = 0; qi < QP; ++qi) qvalid[qi] = pq * QP + qi < ng;
         // L1 prefetch of the code lines one round ahead (the first round's now)
-        const uint32_t round_lines = (kRound * p.m + 127u) / 128u;
         auto prefetch_round = [&](uint32_t start) {
-            if (tid < round_lines && start < b1) {
-                const uint8_t* a = p.list_codes + static_cast<size_t>(start) * p.m + tid * 128u;
-                if (a < p.list_codes + static_cast<size_t>(b1) * p.m)
-                    asm volatile("prefetch.global.L1 [%0];" ::"l"(a));
+            if constexpr (!FLAT) {
+                const uint32_t round_lines = (kRound * p.m + 127u) / 128u;
+                if (tid < round_lines && start < b1) {
+                    const uint8_t* a = p.list_codes + static_cast<size_t>(start) * p.m + tid * 128u;
+                    if (a < p.list_codes + static_cast<size_t>(b1) * p.m)
+                        asm volatile("prefetch.global.L1 [%0];" ::"l"(a));
+                }
             }
         };
         prefetch_round(b0);
@@ -582,18 +684,28 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
                 }
                 const uint32_t qb = warp < ng ? p.qbound[s_bound[G + warp]] : 0u;
                 prefetch_round(base + kRound);
-                CodeWords<MB> cur[kSteps];
+                CodeWords<MB> cur[FLAT ? 1 : kSteps];
+                if constexpr (!FLAT) {
 #pragma unroll
-                for (uint32_t st = 0; st < kSteps; ++st) {
-                    const uint32_t pos = base + (st * kGroupWarps + warp) * kCpi + j;
-                    cur[st] = load_code<MB>(p.list_codes, pos, pos < b1);
+                    for (uint32_t st = 0; st < kSteps; ++st) {
+                        const uint32_t pos = base + (st * kGroupWarps + warp) * kCpi + j;
+                        cur[st] = load_code<MB>(p.list_codes, pos, pos < b1);
+                    }
+                } else {
+                    (void)cur;
                 }
                 float sums[kSteps][QP];
 #pragma unroll
                 for (uint32_t st = 0; st < kSteps; ++st)
 #pragma unroll
                     for (uint32_t qi = 0; qi < QP; ++qi) sums[st][qi] = 0.0f;
-                if constexpr (MB >= 4) {
+                if constexpr (FLAT) {
+#pragma unroll
+                    for (uint32_t st = 0; st < kSteps; ++st) {
+                        const uint32_t pos = base + (st * kGroupWarps + warp) * kCpi + j;
+                        if (pos < b1) flat_sums<G>(p.list_vecs + static_cast<size_t>(pos) * p.d, qv, p.d, kL2, sums[st]);
+                    }
+                } else if constexpr (MB >= 4) {
                     // subspace-major over the round's steps: independent chains,
                     // each summed in subspace order
 #pragma unroll
@@ -651,8 +763,9 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
                                 if (admit && lane == leader) at = atomicAdd(&s_cnt[gq], static_cast<uint32_t>(__popc(bal)));
                                 at = __shfl_sync(0xffffffffu, at, leader);
                                 if (admit) {
+                                    const uint32_t id = FLAT ? s_pairoff[gq] + (pos - b0) : p.list_rows[pos];
                                     buf[gq * p.capq + at + __popc(bal & lanemask_lt())] =
-                                        make_uint2(__float_as_uint(group_key(p.metric, sums[st][qi])), p.list_rows[pos]);
+                                        make_uint2(__float_as_uint(group_key(p.metric, sums[st][qi])), id);
                                     if (at + __popc(bal) + kRound > p.capq) need = true;
                                 }
                             }
@@ -777,6 +890,16 @@ static __global__ void residuals_kernel(const float* __restrict__ vectors, const
     const uint64_t r = t / d;
     const uint32_t i = static_cast<uint32_t>(t % d);
     out[t] = __fsub_rn(vectors[t], centroids[static_cast<size_t>(assign[r]) * d + i]);
+}
+
+// Gathers raw rows into list-major order: dst[pos] = src[rows[pos]] (d floats).
+static __global__ void gather_rows_kernel(const float* __restrict__ src, const uint32_t* __restrict__ rows,
+                                          uint64_t n, uint32_t d, float* __restrict__ dst) {
+    const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= n * d) return;
+    const uint64_t pos = t / d;
+    const uint32_t j = static_cast<uint32_t>(t % d);
+    dst[t] = src[static_cast<size_t>(rows[pos]) * d + j];
 }
 
 // Gathers codes into list-major order: dst[pos] = src[rows[pos]].

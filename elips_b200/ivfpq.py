@@ -1,5 +1,6 @@
-"""IVF-PQ index on one B200: GpuIVFPQIndex (src/gpu_engine/GpuIVFPQIndex.cpp)
-with its trained model imported as import_snapshot does (:327-348).
+"""IVF indexes on one B200: GpuIVFPQIndex (src/gpu_engine/GpuIVFPQIndex.cpp)
+and GpuIVFFlatIndex (src/gpu_engine/GpuIVFFlatIndex.cpp), with their trained
+model imported as import_snapshot does (GpuIVFPQIndex.cpp:327-348).
 
 Search follows GpuIVFPQIndex::search (:161-237): exact probe of the nprobe
 nearest lists, approximate scoring of their members from the residual codes,
@@ -100,6 +101,83 @@ class IvfPqIndex:
     def close(self) -> None:
         if getattr(self, "_h", None):
             capi.LIB.elips_b200_ivfpq_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class IvfFlatIndex:
+    """GpuIVFFlatIndex: probe the nprobe nearest lists, rank their members
+    exactly (GpuIVFFlatIndex.cpp:44-103). Results ascend by (distance, gather
+    position): the probed lists' members in probe order, then member order."""
+
+    def __init__(self, metric: str, dimension: int, centroids: np.ndarray, nprobe: int, device: int = 0):
+        self.metric, self.dimension, self.device = metric, int(dimension), int(device)
+        cent = np.ascontiguousarray(centroids, np.float32)
+        if cent.shape[1] != self.dimension:
+            raise DimensionMismatch("centroid dimension does not match index")
+        self.n_lists = cent.shape[0]
+        h = ctypes.c_void_p()
+        capi.check(capi.LIB.elips_b200_ivfflat_create(self.device, METRICS[metric], self.dimension, self.n_lists,
+                                                      int(nprobe), _ptr(cent), ctypes.byref(h)),
+                   "elips_b200_ivfflat_create")
+        self._h = h
+
+    def add(self, vectors: np.ndarray, assignments: np.ndarray) -> None:
+        v = np.ascontiguousarray(vectors, np.float32)
+        a = np.ascontiguousarray(assignments, np.uint32)
+        if v.ndim != 2 or v.shape[1] != self.dimension:
+            raise DimensionMismatch("vector dimension does not match index")
+        capi.check(capi.LIB.elips_b200_ivfflat_add(self._h, _ptr(v), _ptr(a), v.shape[0]), "elips_b200_ivfflat_add")
+
+    def add_device(self, vectors, assignments, stream=None) -> None:
+        """CUDA tensors: vectors [n, d] float32, assignments [n] int32 (list ids)."""
+        import torch
+        if vectors.shape[1] != self.dimension:
+            raise DimensionMismatch("vector dimension does not match index")
+        vectors, assignments = vectors.contiguous(), assignments.contiguous()
+        s = stream if stream is not None else torch.cuda.current_stream(vectors.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_ivfflat_add_device(self._h, vectors.data_ptr(), assignments.data_ptr(),
+                                                          vectors.shape[0], s), "elips_b200_ivfflat_add_device")
+
+    def size(self) -> int:
+        n = ctypes.c_size_t(0)
+        capi.check(capi.LIB.elips_b200_ivfflat_size(self._h, ctypes.byref(n)), "elips_b200_ivfflat_size")
+        return n.value
+
+    def set_nprobe(self, nprobe: int) -> None:
+        capi.check(capi.LIB.elips_b200_ivfflat_set_nprobe(self._h, int(nprobe)), "elips_b200_ivfflat_set_nprobe")
+
+    def search_batch(self, queries: np.ndarray, k: int, out_dist=None, out_rows=None):
+        q = np.ascontiguousarray(queries, np.float32)
+        if q.ndim != 2 or q.shape[1] != self.dimension:
+            raise DimensionMismatch("query dimension does not match index")
+        nq = q.shape[0]
+        dist = np.empty((nq, k), np.float32) if out_dist is None else out_dist
+        rows = np.empty((nq, k), np.int64) if out_rows is None else out_rows
+        capi.check(capi.LIB.elips_b200_ivfflat_search(self._h, _ptr(q), nq, k, _ptr(dist), _ptr(rows)),
+                   "elips_b200_ivfflat_search")
+        return dist, rows
+
+    def search_device(self, queries, k: int, out_dist=None, out_rows=None, stream=None):
+        import torch
+        nq = queries.shape[0]
+        if out_dist is None:
+            out_dist = torch.empty((nq, k), dtype=torch.float32, device=queries.device)
+            out_rows = torch.empty((nq, k), dtype=torch.int64, device=queries.device)
+        s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_ivfflat_search_device(self._h, queries.data_ptr(), nq, k, out_dist.data_ptr(),
+                                                             out_rows.data_ptr(), s),
+                   "elips_b200_ivfflat_search_device")
+        return out_dist, out_rows
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            capi.LIB.elips_b200_ivfflat_destroy(self._h)
             self._h = None
 
     def __del__(self):

@@ -276,6 +276,49 @@ ELIPS_B200_API int elips_b200_ivfpq_codes_device(const elips_b200_ivfpq* index, 
 
 ELIPS_B200_API int elips_b200_ivfpq_destroy(elips_b200_ivfpq* index);
 
+/* -------------------------------------------------------------- IVF-Flat */
+/* GpuIVFFlatIndex (src/gpu_engine/GpuIVFFlatIndex.cpp): the same inverted
+ * file, candidates ranked exactly. search / search_batch (:84-103,
+ * :123-164) = probe the nprobe nearest lists (IvfIndexState.cpp:395-423),
+ * gather their members in probe order then member order (:466-504), exact
+ * elips::distance to each and the k best, ties by gather position
+ * (rank_candidates, GpuIVFFlatIndex.cpp:44-82). Centroids
+ * [n_lists][dimension] HOST, copied (import_snapshot, :202-205). */
+typedef struct elips_b200_ivfflat elips_b200_ivfflat;
+
+ELIPS_B200_API int elips_b200_ivfflat_create(int device, int metric, uint32_t dimension,
+                                             uint32_t n_lists, uint32_t nprobe,
+                                             const float* centroids, elips_b200_ivfflat** out);
+
+/* Appends n rows with their list ids (HOST pointers, synchronous). Slots are
+ * assigned in call order; an id >= n_lists is INVALID_ARGUMENT and nothing is
+ * added. */
+ELIPS_B200_API int elips_b200_ivfflat_add(elips_b200_ivfflat* index, const float* vectors,
+                                          const uint32_t* assignments, size_t n);
+
+/* Same with DEVICE pointers on `stream`. */
+ELIPS_B200_API int elips_b200_ivfflat_add_device(elips_b200_ivfflat* index, const float* vectors,
+                                                 const uint32_t* assignments, size_t n,
+                                                 void* stream);
+
+ELIPS_B200_API int elips_b200_ivfflat_size(const elips_b200_ivfflat* index, size_t* n_out);
+
+ELIPS_B200_API int elips_b200_ivfflat_set_nprobe(elips_b200_ivfflat* index, uint32_t nprobe);
+
+/* k <= 1024. HOST pointers, synchronous: out_dist[nq][k], out_rows[nq][k]
+ * ascending by (distance, gather position); rows past the candidate count are
+ * -1 (distance +inf). */
+ELIPS_B200_API int elips_b200_ivfflat_search(elips_b200_ivfflat* index, const float* queries,
+                                             size_t nq, size_t k, float* out_dist,
+                                             int64_t* out_rows);
+
+/* Same with DEVICE pointers, asynchronous on `stream`. */
+ELIPS_B200_API int elips_b200_ivfflat_search_device(elips_b200_ivfflat* index, const float* queries,
+                                                    size_t nq, size_t k, float* out_dist,
+                                                    int64_t* out_rows, void* stream);
+
+ELIPS_B200_API int elips_b200_ivfflat_destroy(elips_b200_ivfflat* index);
+
 /* ------------------------------------------------------------ profiling */
 /* Device-side counterpart of GpuProfiler (src/gpu_engine/GpuProfiler.cpp:
  * 5-23) and GpuConfig::enable_profiling (GpuConfig.hpp:83): while enabled,

@@ -67,7 +67,7 @@ def ref() -> ctypes.CDLL:
         _ref.ref_distance.restype = c_float
         _ref.ref_distance.argtypes = [c_int, c_void_p, c_void_p, c_size_t]
         for name in ("ref_exact_create", "ref_sq8_exact_create", "ref_pq_exact_create", "ref_opq_exact_create",
-                     "ref_ivfpq_create"):
+                     "ref_ivfpq_create", "ref_ivfflat_create"):
             getattr(_ref, name).restype = c_void_p
     return _ref
 
@@ -236,6 +236,21 @@ def ivfpq_search(metric, centroids, codebook, codes, vectors, assignments, queri
     return (dist, rows, gap) if with_gap else (dist, rows)
 
 
+def ivfflat_search(metric, centroids, vectors, assignments, queries, nprobe, k, nthreads=None):
+    """GpuIVFFlatIndex::search: probe, gather (probe order, member order), exact
+    distances, top-k with ties by gather position."""
+    centroids, vectors, queries = _f32(centroids), _f32(vectors), _f32(queries)
+    nlist, d = centroids.shape
+    offsets, order_rows = lists_csr(assignments, nlist)
+    nq = queries.shape[0]
+    dist = np.empty((nq, k), np.float32)
+    rows = np.empty((nq, k), np.int64)
+    orc().orc_ivfflat_search(METRIC[metric], c_size_t(d), c_size_t(nlist), c_size_t(nprobe), _p(centroids),
+                             _p(vectors), _p(offsets), _p(order_rows), _p(queries), c_size_t(nq), c_size_t(k),
+                             c_int(_threads(nthreads)), _p(dist), _p(rows))
+    return dist, rows
+
+
 # --------------------------------------------------- reference, compiled
 
 class RefExactIndex:
@@ -275,6 +290,47 @@ class RefExactIndex:
     def __del__(self):
         try:
             ref().ref_exact_destroy(self.h)
+        except Exception:
+            pass
+
+
+class RefIvfFlatIndex:
+    """The reference's GpuIVFFlatIndex on a CPU GpuPort, loaded via import_snapshot."""
+
+    def __init__(self, metric, centroids, assignments, vectors, nprobe):
+        centroids, vectors = _f32(centroids), _f32(vectors)
+        assignments = np.ascontiguousarray(assignments, np.uint32)
+        self.dim = vectors.shape[1]
+        h = ref().ref_ivfflat_create(METRIC[metric], c_uint32(self.dim), c_size_t(centroids.shape[0]),
+                                     c_size_t(nprobe), _p(centroids), _p(assignments), _p(vectors),
+                                     c_size_t(vectors.shape[0]))
+        if not h:
+            raise RuntimeError("reference IVF-Flat import_snapshot failed")
+        self.h = c_void_p(h)
+
+    def search(self, queries, k, nthreads=None):
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        dist = np.empty((nq, k), np.float32)
+        rows = np.empty((nq, k), np.int64)
+        ref().ref_ivfflat_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+                                 c_int(_threads(nthreads)), _p(dist), _p(rows))
+        return dist, rows
+
+    def search_batch(self, queries, k):
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        dist = np.empty((nq, k), np.float32)
+        rows = np.empty((nq, k), np.int64)
+        rc = ref().ref_ivfflat_search_batch(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+                                            _p(dist), _p(rows))
+        if rc != 0:
+            raise RuntimeError(f"reference IVF-Flat search_batch failed ({rc})")
+        return dist, rows
+
+    def __del__(self):
+        try:
+            ref().ref_ivfflat_destroy(self.h)
         except Exception:
             pass
 

@@ -685,6 +685,53 @@ static void ivfpq_one(const void* c, size_t q, hit_t* scratch) {
     free(dec); free(cands); free(lists);
 }
 
+/* GpuIVFFlatIndex::search, GpuIVFFlatIndex.cpp:84-103 (search_batch,
+ * :123-164, ranks each query the same way): probe_lists -> gather_candidates
+ * (probe order, then list member order, IvfIndexState.cpp:466-504) ->
+ * rank_candidates (:44-82): elips::distance to every candidate
+ * (compute_distances_batch) and top_k, ties by gather position. */
+typedef struct {
+    int metric; size_t d, nlist, nprobe;
+    const float* centroids; const float* vectors;
+    const uint32_t* list_offsets; const uint32_t* list_rows;
+    const float* queries; size_t k; float* out_d; int64_t* out_r;
+} ivfflat_ctx;
+
+static void ivfflat_one(const void* c, size_t q, hit_t* scratch) {
+    const ivfflat_ctx* x = (const ivfflat_ctx*)c;
+    const float* qv = x->queries + q * x->d;
+    uint32_t* lists = (uint32_t*)malloc(sizeof(uint32_t) * x->nprobe);
+    orc_ivf_probe(x->metric, qv, x->d, x->centroids, x->nlist, x->nprobe, lists, NULL);
+    size_t total = 0;
+    for (size_t p = 0; p < x->nprobe; ++p)
+        if (lists[p] < x->nlist) total += x->list_offsets[lists[p] + 1] - x->list_offsets[lists[p]];
+    uint32_t* rows = (uint32_t*)malloc(sizeof(uint32_t) * (total ? total : 1));
+    heap_t hp = { scratch, 0, x->k };
+    size_t pos = 0;
+    for (size_t p = 0; p < x->nprobe; ++p) {
+        const uint32_t l = lists[p];
+        if (l >= x->nlist) continue;
+        for (uint32_t j = x->list_offsets[l]; j < x->list_offsets[l + 1]; ++j, ++pos) {
+            rows[pos] = x->list_rows[j];
+            hit_t h = { orc_distance(x->metric, qv, x->vectors + (size_t)rows[pos] * x->d, x->d), (int64_t)pos };
+            heap_push(&hp, h);
+        }
+    }
+    float* od = x->out_d + q * x->k;
+    int64_t* orow = x->out_r + q * x->k;
+    heap_emit(&hp, x->k, od, orow);
+    for (size_t i = 0; i < x->k; ++i) if (orow[i] >= 0) orow[i] = rows[orow[i]];
+    free(rows); free(lists);
+}
+
+void orc_ivfflat_search(int metric, size_t d, size_t nlist, size_t nprobe, const float* centroids,
+                        const float* vectors, const uint32_t* list_offsets, const uint32_t* list_rows,
+                        const float* queries, size_t nq, size_t k, int nthreads, float* out_d, int64_t* out_r) {
+    ivfflat_ctx c = { metric, d, nlist, nprobe, centroids, vectors, list_offsets, list_rows, queries, k,
+                      out_d, out_r };
+    run_queries(&c, ivfflat_one, nq, nthreads, k);
+}
+
 void orc_ivfpq_search(int metric, size_t d, size_t m, size_t ksub, size_t nlist, size_t nprobe,
                       const float* centroids, const float* codebook, const uint8_t* codes,
                       const float* vectors, const uint32_t* list_offsets,

@@ -21,6 +21,7 @@
 
 #include "elips/Config.hpp"
 #include "elips/domain/RecordID.hpp"
+#include "elips/gpu_engine/GpuIVFFlatIndex.hpp"
 #include "elips/gpu_engine/GpuIVFPQIndex.hpp"
 #include "elips/gpu_engine/GpuPort.hpp"
 #include "elips/index_engine/ExactIndex.hpp"
@@ -144,6 +145,11 @@ struct ExactHandle {
 struct IvfPqHandle {
     CpuPort port;
     std::unique_ptr<elips::gpu::GpuIVFPQIndex> index;
+};
+
+struct IvfFlatHandle {
+    CpuPort port;
+    std::unique_ptr<elips::gpu::GpuIVFFlatIndex> index;
 };
 
 }  // namespace
@@ -355,5 +361,69 @@ int ref_ivfpq_search(void* handle, uint32_t dim, const float* queries, size_t nq
 }
 
 void ref_ivfpq_destroy(void* handle) { delete static_cast<IvfPqHandle*>(handle); }
+
+// GpuIVFFlatIndex on the CPU port, loaded through import_snapshot
+// (GpuIVFFlatIndex.cpp:202-205, IvfIndexState.cpp:339-374).
+void* ref_ivfflat_create(int metric, uint32_t dim, size_t n_lists, size_t nprobe, const float* centroids,
+                         const uint32_t* assignments, const float* vectors, size_t n) {
+    auto* h = new IvfFlatHandle;
+    elips::gpu::GpuConfig config;
+    config.default_ef_search_gpu = nprobe;
+    config.ivf_pq_params.n_lists = n_lists;
+    h->index = std::make_unique<elips::gpu::GpuIVFFlatIndex>(h->port, static_cast<Metric>(metric),
+                                                             static_cast<std::uint16_t>(dim), config);
+    elips::IndexSnapshot snap;
+    snap.kind = elips::IndexSnapshotKind::gpu_ivf_flat;
+    snap.metric = static_cast<Metric>(metric);
+    snap.dimension = static_cast<std::uint16_t>(dim);
+    snap.ids.reserve(n);
+    for (size_t i = 0; i < n; ++i) snap.ids.push_back(row_id(i));
+    snap.vectors.assign(vectors, vectors + n * dim);
+    elips::IvfSnapshot ivf;
+    ivf.n_lists = n_lists;
+    ivf.n_probe = nprobe;
+    ivf.centroids.assign(centroids, centroids + n_lists * dim);
+    ivf.assignments.assign(assignments, assignments + n);
+    snap.ivf = std::move(ivf);
+    auto imported = h->index->import_snapshot(snap);
+    if (!imported.has_value()) {
+        delete h;
+        return nullptr;
+    }
+    return h;
+}
+
+int ref_ivfflat_search(void* handle, uint32_t dim, const float* queries, size_t nq, size_t k, int nthreads,
+                       float* out_dist, std::int64_t* out_rows) {
+    auto* h = static_cast<IvfFlatHandle*>(handle);
+    parallel_queries(nq, nthreads, [&](size_t q) {
+        const auto hits = h->index->search(std::span<const float>{queries + q * dim, dim}, k);
+        write_hits(hits, k, out_dist + q * k, out_rows + q * k);
+    });
+    return 0;
+}
+
+// search_batch (GpuIVFFlatIndex.cpp:123-164): batched probe, per-query rank.
+int ref_ivfflat_search_batch(void* handle, uint32_t dim, const float* queries, size_t nq, size_t k,
+                             float* out_dist, std::int64_t* out_rows) {
+    auto* h = static_cast<IvfFlatHandle*>(handle);
+    auto res = h->index->search_batch(std::span<const float>{queries, nq * dim}, k, 0);
+    if (!res.has_value()) return 1 + static_cast<int>(res.error());
+    for (size_t q = 0; q < nq; ++q) {
+        const auto& row = (*res)[q];
+        for (size_t i = 0; i < k; ++i) {
+            if (i < row.size()) {
+                out_dist[q * k + i] = row[i].distance;
+                out_rows[q * k + i] = id_row(row[i].id);
+            } else {
+                out_dist[q * k + i] = 0.0f;
+                out_rows[q * k + i] = -1;
+            }
+        }
+    }
+    return 0;
+}
+
+void ref_ivfflat_destroy(void* handle) { delete static_cast<IvfFlatHandle*>(handle); }
 
 }  // extern "C"

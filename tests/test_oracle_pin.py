@@ -107,3 +107,20 @@ def test_ivfpq_tie_order_matches_reference(nprobe, k):
     assert (gap == 0).sum() >= 20  # the model really exercises boundary ties
     differ = [q for q in range(len(r1)) if not (np.array_equal(r1[q], r2[q]) and np.array_equal(d1[q], d2[q]))]
     assert all(gap[q] == 0 for q in differ)
+
+
+@pytest.mark.parametrize("metric", METRICS)
+def test_ivfflat_search_matches_reference(metric):
+    """GpuIVFFlatIndex::search and search_batch, ties by gather position."""
+    m = H.ivfpq_tie_model()
+    base, q = m["base"][:20000], m["queries"][:60]
+    if metric != "euclidean":
+        base, q = H.normalize(base), H.normalize(q)
+    asg = O.ivf_assign(metric, base, m["cent"])
+    for nprobe, k in [(8, 10), (1, 5), (200, 3)]:
+        d1, r1 = O.ivfflat_search(metric, m["cent"], base, asg, q, nprobe, k)
+        ref = O.RefIvfFlatIndex(metric, m["cent"], asg, base, nprobe)
+        d2, r2 = ref.search(q, k)
+        d3, r3 = ref.search_batch(q, k)
+        assert np.array_equal(d1, d2) and np.array_equal(r1, r2)
+        assert np.array_equal(d2, d3) and np.array_equal(r2, r3)
