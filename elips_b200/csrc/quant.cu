@@ -5,6 +5,8 @@
 #include <cstring>
 #include <vector>
 
+#include <cub/device/device_segmented_radix_sort.cuh>
+
 #include "../../include/elips_b200.h"
 #include "engine.cuh"
 #include "profiler.cuh"
@@ -52,13 +54,79 @@ void compute_distances_device(int device, const float* q, const float* db, float
     launch_check("distances kernel");
 }
 
+namespace {
+
+__global__ void column_index_kernel(uint32_t* __restrict__ idx, uint64_t total, uint32_t nb) {
+    const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t < total) idx[t] = static_cast<uint32_t>(t % nb);
+}
+
+__global__ void row_offsets_kernel(uint64_t* __restrict__ off, uint32_t rows, uint64_t nb) {
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t <= rows) off[t] = static_cast<uint64_t>(t) * nb;
+}
+
+__global__ void take_first_k_kernel(const float* __restrict__ sval, const uint32_t* __restrict__ sidx, uint32_t rows,
+                                    uint64_t nb, uint64_t k, float* __restrict__ val, uint32_t* __restrict__ idx) {
+    const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= static_cast<uint64_t>(rows) * k) return;
+    const uint64_t q = t / k, i = t % k;
+    const bool in = i < nb;
+    val[t] = in ? sval[q * nb + i] : __int_as_float(0x7f800000);
+    idx[t] = in ? sidx[q * nb + i] : 0xFFFFFFFFu;
+}
+
+// GpuPort::top_k for k above the block select's reach: every row sorted by
+// value with a stable segmented radix sort (columns enter in order, so equal
+// values keep ascending column order, the port's tie rule), then the first k.
+// Rows go in chunks of at most 2^30 values.
+void top_k_sorted(const float* dist, uint32_t* idx, float* val, size_t nq, size_t nb, size_t k, cudaStream_t stream) {
+    const size_t rows_per = std::max<size_t>(1, (size_t{1} << 30) / std::max<size_t>(nb, 1));
+    for (size_t q0 = 0; q0 < nq; q0 += rows_per) {
+        const uint32_t rows = static_cast<uint32_t>(std::min(rows_per, nq - q0));
+        const uint64_t total = static_cast<uint64_t>(rows) * nb;
+        size_t temp = 0;
+        cub::DeviceSegmentedRadixSort::SortPairs(nullptr, temp, static_cast<const float*>(nullptr),
+                                                 static_cast<float*>(nullptr), static_cast<const uint32_t*>(nullptr),
+                                                 static_cast<uint32_t*>(nullptr), static_cast<int64_t>(total),
+                                                 static_cast<int64_t>(rows), static_cast<const uint64_t*>(nullptr),
+                                                 static_cast<const uint64_t*>(nullptr), 0, 32, stream);
+        const size_t a_val = align256(total * 4), a_idx = align256(total * 4), a_off = align256((rows + 1ull) * 8);
+        StreamScratch s(a_val + 2 * a_idx + a_off + align256(temp), stream);
+        float* sval = reinterpret_cast<float*>(s.get());
+        uint32_t* in_idx = reinterpret_cast<uint32_t*>(s.get() + a_val);
+        uint32_t* sidx = reinterpret_cast<uint32_t*>(s.get() + a_val + a_idx);
+        uint64_t* off = reinterpret_cast<uint64_t*>(s.get() + a_val + 2 * a_idx);
+        void* tmp = s.get() + a_val + 2 * a_idx + a_off;
+        Profiler::Scope prof("topk_sorted", stream, total);
+        column_index_kernel<<<static_cast<uint32_t>((total + 255) / 256), 256, 0, stream>>>(
+            in_idx, total, static_cast<uint32_t>(nb));
+        row_offsets_kernel<<<(rows + 256) / 256, 256, 0, stream>>>(off, rows, nb);
+        launch_check("top-k sort setup");
+        check_cuda(cub::DeviceSegmentedRadixSort::SortPairs(tmp, temp, dist + q0 * nb, sval, in_idx, sidx,
+                                                            static_cast<int64_t>(total), static_cast<int64_t>(rows),
+                                                            off, off + 1, 0, 32, stream),
+                   ELIPS_B200_KERNEL_LAUNCH_FAILED, "segmented sort");
+        const uint64_t outs = static_cast<uint64_t>(rows) * k;
+        take_first_k_kernel<<<static_cast<uint32_t>((outs + 255) / 256), 256, 0, stream>>>(
+            sval, sidx, rows, nb, k, val + q0 * k, idx + q0 * k);
+        launch_check("top-k take");
+    }
+}
+
+}  // namespace
+
 void top_k_device(int device, const float* dist, uint32_t* idx, float* val, size_t nq, size_t nb, size_t k,
                   cudaStream_t stream) {
     if (nq == 0 || k == 0) return;
-    if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
     if (nb > 0xFFFFFFFEull || nq > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "batch too large");
     DeviceGuard g(device);
     device_props(device);
+    if (k > kMaxK) {
+        if (nb == 0) fail(ELIPS_B200_INVALID_ARGUMENT, "empty distance rows");
+        top_k_sorted(dist, idx, val, nq, nb, k, stream);
+        return;
+    }
     const uint32_t cap = btk_cap(static_cast<uint32_t>(k));
     const uint32_t kp = pow2_at_least(static_cast<uint32_t>(k));
     const size_t smem = btk_bytes(cap) + static_cast<size_t>(kp) * 8;

@@ -1,12 +1,16 @@
 """CPU checkers for the parity tests. TEST INFRASTRUCTURE ONLY.
 
-Two libraries, both built by oracle/Makefile:
+Libraries built by oracle/Makefile:
   * liboracle.so             -- oracle.c, a C restatement of the reference's
                                 search arithmetic (each function cites the
                                 reference file:line it follows);
   * _ref/libelips_ref.so     -- the reference's own sources compiled in place
                                 plus ref_driver.cpp, used to pin the
-                                restatement and as the timed CPU baseline.
+                                restatement and as the timed CPU baseline;
+  * _ref/libelips_ref_b200.so -- the same reference classes able to run on
+                                the B200 CudaBackend adapter
+                                (elips_b200/integration), for the drop-in check
+                                of the GpuPort boundary (GPU tests only).
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
 legs may import this package; the product path (elips_b200/) never does.
@@ -24,6 +28,8 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libelips_ref.so"
+REF_B200_SO = HERE / "_ref" / "libelips_ref_b200.so"
+PRODUCT_SO = HERE.parent / "elips_b200" / "libelips_b200.so"
 REF_ROOT = Path(os.environ.get("ELIPS_REF_ROOT", "/root/reference"))
 
 METRIC = {"cosine": 0, "euclidean": 1, "dot_product": 2}
@@ -33,11 +39,13 @@ def build(ref: bool = True) -> None:
     """Builds liboracle.so and, when the reference sources are present, _ref."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     if ref and REF_ROOT.exists():
-        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref", f"REF_ROOT={REF_ROOT}"], check=True)
+        targets = ["ref", "ref_b200"] if PRODUCT_SO.exists() else ["ref"]
+        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), *targets, f"REF_ROOT={REF_ROOT}"], check=True)
 
 
 _orc = None
 _ref = None
+_ref_b200 = None
 
 
 def orc() -> ctypes.CDLL:
@@ -58,18 +66,44 @@ def ref_available() -> bool:
     return REF_SO.exists() or REF_ROOT.exists()
 
 
+def _declare(lib: ctypes.CDLL) -> ctypes.CDLL:
+    lib.ref_distance.restype = c_float
+    lib.ref_distance.argtypes = [c_int, c_void_p, c_void_p, c_size_t]
+    for name in ("ref_exact_create", "ref_sq8_exact_create", "ref_pq_exact_create", "ref_opq_exact_create",
+                 "ref_ivfpq_create", "ref_ivfflat_create", "ref_brute_create"):
+        getattr(lib, name).restype = c_void_p
+    return lib
+
+
 def ref() -> ctypes.CDLL:
     global _ref
     if _ref is None:
         if not REF_SO.exists():
             build(ref=True)
-        _ref = ctypes.CDLL(str(REF_SO))
-        _ref.ref_distance.restype = c_float
-        _ref.ref_distance.argtypes = [c_int, c_void_p, c_void_p, c_size_t]
-        for name in ("ref_exact_create", "ref_sq8_exact_create", "ref_pq_exact_create", "ref_opq_exact_create",
-                     "ref_ivfpq_create", "ref_ivfflat_create"):
-            getattr(_ref, name).restype = c_void_p
+        _ref = _declare(ctypes.CDLL(str(REF_SO)))
     return _ref
+
+
+def ref_b200() -> ctypes.CDLL:
+    """The reference classes on the B200 CudaBackend (needs a GPU to run)."""
+    global _ref_b200
+    if _ref_b200 is None:
+        if not REF_B200_SO.exists():
+            build(ref=True)
+        _ref_b200 = _declare(ctypes.CDLL(str(REF_B200_SO)))
+    return _ref_b200
+
+
+def _port_lib(port: str) -> ctypes.CDLL:
+    """Library whose next index handle is built on `port` ("cpu" or "b200")."""
+    if port == "cpu":
+        return ref()
+    if port != "b200":
+        raise ValueError(f"unknown port {port!r}")
+    lib = ref_b200()
+    if lib.ref_use_b200_port(1) != 1:
+        raise RuntimeError("reference driver built without the B200 port")
+    return lib
 
 
 def _p(a: np.ndarray):
@@ -294,14 +328,54 @@ class RefExactIndex:
             pass
 
 
+class RefBruteForceIndex:
+    """The reference's GpuBruteForceIndex (build_from_batch) on a GpuPort."""
+
+    def __init__(self, metric, base, port="cpu"):
+        base = _f32(base)
+        self.dim = base.shape[1]
+        self.lib = _port_lib(port)
+        h = self.lib.ref_brute_create(METRIC[metric], c_uint32(self.dim), _p(base), c_size_t(base.shape[0]))
+        if not h:
+            raise RuntimeError("reference brute-force build failed")
+        self.h = c_void_p(h)
+
+    def search(self, queries, k, nthreads=None):
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        dist = np.empty((nq, k), np.float32)
+        rows = np.empty((nq, k), np.int64)
+        self.lib.ref_brute_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+                                  c_int(_threads(nthreads)), _p(dist), _p(rows))
+        return dist, rows
+
+    def search_batch(self, queries, k):
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        dist = np.empty((nq, k), np.float32)
+        rows = np.empty((nq, k), np.int64)
+        rc = self.lib.ref_brute_search_batch(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+                                             _p(dist), _p(rows))
+        if rc != 0:
+            raise RuntimeError(f"reference brute-force search_batch failed ({rc})")
+        return dist, rows
+
+    def __del__(self):
+        try:
+            self.lib.ref_brute_destroy(self.h)
+        except Exception:
+            pass
+
+
 class RefIvfFlatIndex:
     """The reference's GpuIVFFlatIndex on a CPU GpuPort, loaded via import_snapshot."""
 
-    def __init__(self, metric, centroids, assignments, vectors, nprobe):
+    def __init__(self, metric, centroids, assignments, vectors, nprobe, port="cpu"):
         centroids, vectors = _f32(centroids), _f32(vectors)
         assignments = np.ascontiguousarray(assignments, np.uint32)
         self.dim = vectors.shape[1]
-        h = ref().ref_ivfflat_create(METRIC[metric], c_uint32(self.dim), c_size_t(centroids.shape[0]),
+        self.lib = _port_lib(port)
+        h = self.lib.ref_ivfflat_create(METRIC[metric], c_uint32(self.dim), c_size_t(centroids.shape[0]),
                                      c_size_t(nprobe), _p(centroids), _p(assignments), _p(vectors),
                                      c_size_t(vectors.shape[0]))
         if not h:
@@ -313,7 +387,7 @@ class RefIvfFlatIndex:
         nq = queries.shape[0]
         dist = np.empty((nq, k), np.float32)
         rows = np.empty((nq, k), np.int64)
-        ref().ref_ivfflat_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+        self.lib.ref_ivfflat_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
                                  c_int(_threads(nthreads)), _p(dist), _p(rows))
         return dist, rows
 
@@ -322,7 +396,7 @@ class RefIvfFlatIndex:
         nq = queries.shape[0]
         dist = np.empty((nq, k), np.float32)
         rows = np.empty((nq, k), np.int64)
-        rc = ref().ref_ivfflat_search_batch(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+        rc = self.lib.ref_ivfflat_search_batch(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
                                             _p(dist), _p(rows))
         if rc != 0:
             raise RuntimeError(f"reference IVF-Flat search_batch failed ({rc})")
@@ -330,7 +404,7 @@ class RefIvfFlatIndex:
 
     def __del__(self):
         try:
-            ref().ref_ivfflat_destroy(self.h)
+            self.lib.ref_ivfflat_destroy(self.h)
         except Exception:
             pass
 
@@ -338,12 +412,13 @@ class RefIvfFlatIndex:
 class RefIvfPqIndex:
     """The reference's GpuIVFPQIndex on a CPU GpuPort, loaded via import_snapshot."""
 
-    def __init__(self, metric, centroids, assignments, codebook, codes, vectors, nprobe, pq_bits=8):
+    def __init__(self, metric, centroids, assignments, codebook, codes, vectors, nprobe, pq_bits=8, port="cpu"):
         centroids, codebook, vectors = _f32(centroids), _f32(codebook), _f32(vectors)
         assignments = np.ascontiguousarray(assignments, np.uint32)
         codes = np.ascontiguousarray(codes, np.uint8)
         self.dim = vectors.shape[1]
-        h = ref().ref_ivfpq_create(METRIC[metric], c_uint32(self.dim), c_size_t(centroids.shape[0]),
+        self.lib = _port_lib(port)
+        h = self.lib.ref_ivfpq_create(METRIC[metric], c_uint32(self.dim), c_size_t(centroids.shape[0]),
                                    c_size_t(nprobe), c_uint32(codebook.shape[0]), c_uint32(pq_bits),
                                    _p(centroids), _p(assignments), _p(codebook), _p(codes), _p(vectors),
                                    c_size_t(vectors.shape[0]))
@@ -356,13 +431,13 @@ class RefIvfPqIndex:
         nq = queries.shape[0]
         dist = np.empty((nq, k), np.float32)
         rows = np.empty((nq, k), np.int64)
-        ref().ref_ivfpq_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+        self.lib.ref_ivfpq_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
                                c_int(_threads(nthreads)), _p(dist), _p(rows))
         return dist, rows
 
     def __del__(self):
         try:
-            ref().ref_ivfpq_destroy(self.h)
+            self.lib.ref_ivfpq_destroy(self.h)
         except Exception:
             pass
 

@@ -1,10 +1,14 @@
 // Test infrastructure only: a C-ABI driver over the reference's own compiled
 // classes (ExactIndex, ScalarQuantizer, ProductQuantizer, quant::detail
-// k-means, GpuIVFPQIndex on a CPU GpuPort). It is linked with the reference
-// sources by oracle/Makefile into oracle/_ref/libelips_ref.so, and is used by
-// the tests to pin the C restatement in oracle/oracle.c, to generate golden
-// fixtures, and by bench.py's CPU baseline / reference arm. Nothing in the
-// product path loads it.
+// k-means, GpuIVFPQIndex / GpuIVFFlatIndex / GpuBruteForceIndex on a GpuPort).
+// It is linked with the reference sources by oracle/Makefile into
+// oracle/_ref/libelips_ref.so (a CPU GpuPort), and is used by the tests to pin
+// the C restatement in oracle/oracle.c, to generate golden fixtures, and by
+// bench.py's CPU baseline / reference arm. Nothing in the product path loads
+// it. Built with REF_WITH_B200 (oracle/_ref/libelips_ref_b200.so) it can also
+// run those reference classes on elips::gpu::cuda::CudaBackend
+// (elips_b200/integration/CudaBackend.cpp): the drop-in check of the GpuPort
+// boundary.
 //
 // Row identity: every row i is given RecordID(bytes) whose last eight bytes are
 // i in big-endian order, so search results map back to row indexes
@@ -21,6 +25,7 @@
 
 #include "elips/Config.hpp"
 #include "elips/domain/RecordID.hpp"
+#include "elips/gpu_engine/GpuBruteForceIndex.hpp"
 #include "elips/gpu_engine/GpuIVFFlatIndex.hpp"
 #include "elips/gpu_engine/GpuIVFPQIndex.hpp"
 #include "elips/gpu_engine/GpuPort.hpp"
@@ -30,6 +35,9 @@
 #include "elips/quant_engine/ScalarQuantizer.hpp"
 #include "elips/quant_engine/detail/KMeans.hpp"
 #include "elips/vector_engine/Metrics.hpp"
+#ifdef REF_WITH_B200
+#include "backends/cuda/CudaBackend.hpp"
+#endif
 
 namespace {
 
@@ -142,14 +150,36 @@ struct ExactHandle {
     std::unique_ptr<elips::ExactIndex> index;
 };
 
+// The GpuPort the next index handle is built on: the CPU port, or (in the
+// REF_WITH_B200 build, after ref_use_b200_port(1)) the B200 CudaBackend.
+std::atomic<int> g_use_b200{0};
+
+std::unique_ptr<elips::gpu::GpuPort> make_port() {
+#ifdef REF_WITH_B200
+    if (g_use_b200.load()) {
+        auto port = std::make_unique<elips::gpu::cuda::CudaBackend>();
+        elips::gpu::GpuConfig config;
+        config.device_index = 0;
+        if (!port->initialize(config).has_value()) return nullptr;
+        return port;
+    }
+#endif
+    return std::make_unique<CpuPort>();
+}
+
 struct IvfPqHandle {
-    CpuPort port;
+    std::unique_ptr<elips::gpu::GpuPort> port = make_port();
     std::unique_ptr<elips::gpu::GpuIVFPQIndex> index;
 };
 
 struct IvfFlatHandle {
-    CpuPort port;
+    std::unique_ptr<elips::gpu::GpuPort> port = make_port();
     std::unique_ptr<elips::gpu::GpuIVFFlatIndex> index;
+};
+
+struct BruteHandle {
+    std::unique_ptr<elips::gpu::GpuPort> port = make_port();
+    std::unique_ptr<elips::gpu::GpuBruteForceIndex> index;
 };
 
 }  // namespace
@@ -315,12 +345,16 @@ void* ref_ivfpq_create(int metric, uint32_t dim, size_t n_lists, size_t nprobe, 
                        const float* codebook, const std::uint8_t* codes, const float* vectors,
                        size_t n) {
     auto* h = new IvfPqHandle;
+    if (!h->port) {
+        delete h;
+        return nullptr;
+    }
     elips::gpu::GpuConfig config;
     config.default_ef_search_gpu = nprobe;
     config.ivf_pq_params.n_lists = n_lists;
     config.ivf_pq_params.pq_dim = pq_dim;
     config.ivf_pq_params.pq_bits = pq_bits;
-    h->index = std::make_unique<elips::gpu::GpuIVFPQIndex>(h->port, static_cast<Metric>(metric),
+    h->index = std::make_unique<elips::gpu::GpuIVFPQIndex>(*h->port, static_cast<Metric>(metric),
                                                            static_cast<std::uint16_t>(dim), config);
     elips::IndexSnapshot snap;
     snap.kind = elips::IndexSnapshotKind::gpu_ivf_pq;
@@ -367,10 +401,14 @@ void ref_ivfpq_destroy(void* handle) { delete static_cast<IvfPqHandle*>(handle);
 void* ref_ivfflat_create(int metric, uint32_t dim, size_t n_lists, size_t nprobe, const float* centroids,
                          const uint32_t* assignments, const float* vectors, size_t n) {
     auto* h = new IvfFlatHandle;
+    if (!h->port) {
+        delete h;
+        return nullptr;
+    }
     elips::gpu::GpuConfig config;
     config.default_ef_search_gpu = nprobe;
     config.ivf_pq_params.n_lists = n_lists;
-    h->index = std::make_unique<elips::gpu::GpuIVFFlatIndex>(h->port, static_cast<Metric>(metric),
+    h->index = std::make_unique<elips::gpu::GpuIVFFlatIndex>(*h->port, static_cast<Metric>(metric),
                                                              static_cast<std::uint16_t>(dim), config);
     elips::IndexSnapshot snap;
     snap.kind = elips::IndexSnapshotKind::gpu_ivf_flat;
@@ -425,5 +463,67 @@ int ref_ivfflat_search_batch(void* handle, uint32_t dim, const float* queries, s
 }
 
 void ref_ivfflat_destroy(void* handle) { delete static_cast<IvfFlatHandle*>(handle); }
+
+// GpuBruteForceIndex (GpuBruteForceIndex.cpp:77-170) over rows with ids
+// row_id(i), loaded by build_from_batch (:126-145).
+void* ref_brute_create(int metric, uint32_t dim, const float* rows, size_t n) {
+    auto* h = new BruteHandle;
+    if (!h->port) {
+        delete h;
+        return nullptr;
+    }
+    elips::gpu::GpuConfig config;
+    h->index = std::make_unique<elips::gpu::GpuBruteForceIndex>(*h->port, static_cast<Metric>(metric),
+                                                                static_cast<std::uint16_t>(dim), config);
+    std::vector<RecordID> ids;
+    ids.reserve(n);
+    for (size_t i = 0; i < n; ++i) ids.push_back(row_id(i));
+    auto built = h->index->build_from_batch(std::span<const float>{rows, n * dim}, ids, {});
+    if (!built.has_value()) {
+        delete h;
+        return nullptr;
+    }
+    return h;
+}
+
+int ref_brute_search(void* handle, uint32_t dim, const float* queries, size_t nq, size_t k, int nthreads,
+                     float* out_dist, std::int64_t* out_rows) {
+    auto* h = static_cast<BruteHandle*>(handle);
+    parallel_queries(nq, nthreads, [&](size_t q) {
+        const auto hits = h->index->search(std::span<const float>{queries + q * dim, dim}, k);
+        write_hits(hits, k, out_dist + q * k, out_rows + q * k);
+    });
+    return 0;
+}
+
+// search_batch through GpuSearchPipeline::batch_search (GpuSearchPipeline.cpp:10-41).
+int ref_brute_search_batch(void* handle, uint32_t dim, const float* queries, size_t nq, size_t k, float* out_dist,
+                           std::int64_t* out_rows) {
+    auto* h = static_cast<BruteHandle*>(handle);
+    auto res = h->index->search_batch(std::span<const float>{queries, nq * dim}, k, 0);
+    if (!res.has_value()) return 1 + static_cast<int>(res.error());
+    for (size_t q = 0; q < nq; ++q) {
+        const auto& row = (*res)[q];
+        for (size_t i = 0; i < k; ++i) {
+            out_dist[q * k + i] = i < row.size() ? row[i].distance : 0.0f;
+            out_rows[q * k + i] = i < row.size() ? id_row(row[i].id) : -1;
+        }
+    }
+    return 0;
+}
+
+void ref_brute_destroy(void* handle) { delete static_cast<BruteHandle*>(handle); }
+
+// Selects the GpuPort of the handles created next: 1 = the B200 CudaBackend
+// (REF_WITH_B200 build only), 0 = the CPU port. Returns the selection made.
+int ref_use_b200_port(int on) {
+#ifdef REF_WITH_B200
+    g_use_b200.store(on ? 1 : 0);
+    return on ? 1 : 0;
+#else
+    (void)on;
+    return 0;
+#endif
+}
 
 }  // extern "C"

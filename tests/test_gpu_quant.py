@@ -44,7 +44,7 @@ def test_compute_distances_device_pointers_match_host():
     assert np.array_equal(out.cpu().numpy(), host)
 
 
-@pytest.mark.parametrize("nb,k", [(10, 3), (5000, 64), (300, 1000), (70_000, 17)])
+@pytest.mark.parametrize("nb,k", [(10, 3), (5000, 64), (300, 1000), (70_000, 17), (5000, 4000), (3000, 5000), (200_000, 1500)])
 def test_top_k_matches_stable_sort(nb, k):
     from elips_b200.quant import top_k
     rng = np.random.default_rng(45)
