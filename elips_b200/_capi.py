@@ -71,6 +71,7 @@ SIGNATURES = [
     ("elips_b200_quant_search_device", c_int,
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
     ("elips_b200_quant_destroy", c_int, [c_void_p]),
+    ("elips_b200_normalize_rows", c_int, [c_int, c_void_p, c_void_p, c_size_t, c_size_t, c_int, c_void_p]),
     ("elips_b200_ivfpq_create", c_int,
      [c_int, c_int, c_uint32, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, POINTER(c_void_p)]),
     ("elips_b200_ivfpq_add", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t]),

@@ -138,6 +138,18 @@ void top_k_device(int device, const float* dist, uint32_t* idx, float* val, size
     launch_check("top-k kernel");
 }
 
+void normalize_rows_device(int device, const float* in, float* out, size_t n, size_t d, cudaStream_t stream) {
+    if (n == 0 || d == 0) return;
+    if (d > 65535) fail(ELIPS_B200_INVALID_ARGUMENT, "dimension must be in [1, 65535]");
+    DeviceGuard g(device);
+    device_props(device);
+    const uint64_t blocks = (n + kNormRows - 1) / kNormRows;
+    if (blocks > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "too many rows in one call");
+    Profiler::Scope prof("normalize_rows", stream, n);
+    normalize_rows_kernel<<<static_cast<uint32_t>(blocks), 256, 0, stream>>>(in, out, n, static_cast<uint32_t>(d));
+    launch_check("normalize kernel");
+}
+
 // ExactIndex with a Quantizer attached, codes resident on the device.
 class QuantIndex {
 public:
@@ -368,6 +380,31 @@ struct OwnedStream {
 }  // namespace
 
 extern "C" {
+
+int elips_b200_normalize_rows(int device, const float* in, float* out, size_t n, size_t d, int pointers_on_device,
+                              void* stream) {
+    if (n > 0 && d > 0 && (in == nullptr || out == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        if (pointers_on_device) {
+            eb::normalize_rows_device(device, in, out, n, d, static_cast<cudaStream_t>(stream));
+            return;
+        }
+        if (n == 0 || d == 0) return;
+        eb::DeviceGuard g(device);
+        OwnedStream st;
+        {
+            eb::StreamScratch s(2 * n * d * 4 + 512, st.s);
+            float* din = reinterpret_cast<float*>(s.get());
+            float* dout = din + n * d;
+            eb::check_cuda(cudaMemcpyAsync(din, in, n * d * 4, cudaMemcpyHostToDevice, st.s), ELIPS_B200_TRANSFER_FAILED,
+                           "row upload");
+            eb::normalize_rows_device(device, din, dout, n, d, st.s);
+            eb::check_cuda(cudaMemcpyAsync(out, dout, n * d * 4, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "row download");
+        }
+        eb::check_cuda(cudaStreamSynchronize(st.s), ELIPS_B200_KERNEL_LAUNCH_FAILED, "normalize");
+    });
+}
 
 int elips_b200_compute_distances_batch(int device, const float* queries, const float* database,
                                        float* distances_out, size_t nq, size_t nb, size_t dim, int metric,

@@ -83,6 +83,48 @@ static __global__ void __launch_bounds__(kDistRows)
     }
 }
 
+// --------------------------------------------------------- normalisation
+
+constexpr int kNormRows = 32;  // rows per CTA (one per thread of warp 0)
+constexpr int kNormDims = 32;  // dimensions staged per step
+
+// out = Vector::normalized (include/elips/domain/Vector.hpp:25-44) of every
+// row: magnitude = sqrt of the sequential sum of v*v (no FMA), each value
+// divided by it (IEEE), zero rows copied unchanged. A CTA stages 32 rows x 32
+// dimensions at a time (coalesced) so each of its first 32 threads can sum
+// its row in order; all threads then write the quotients.
+static __global__ void __launch_bounds__(256)
+    normalize_rows_kernel(const float* __restrict__ in, float* __restrict__ out, uint64_t n, uint32_t d) {
+    __shared__ float tile[kNormRows][kNormDims + 1];
+    __shared__ float mag[kNormRows];
+    const uint64_t r0 = static_cast<uint64_t>(blockIdx.x) * kNormRows;
+    const uint32_t tid = threadIdx.x;
+    float sum = 0.0f;
+    for (uint32_t c0 = 0; c0 < d; c0 += kNormDims) {
+        for (uint32_t e = tid; e < kNormRows * kNormDims; e += blockDim.x) {
+            const uint32_t rr = e / kNormDims, cc = e % kNormDims;
+            const uint64_t row = r0 + rr;
+            tile[rr][cc] = (row < n && c0 + cc < d) ? in[row * d + c0 + cc] : 0.0f;
+        }
+        __syncthreads();
+        if (tid < kNormRows) {
+            const uint32_t lim = min(static_cast<uint32_t>(kNormDims), d - c0);
+            for (uint32_t cc = 0; cc < lim; ++cc) sum = __fadd_rn(sum, __fmul_rn(tile[tid][cc], tile[tid][cc]));
+        }
+        __syncthreads();
+    }
+    if (tid < kNormRows) mag[tid] = sqrtf(sum);
+    __syncthreads();
+    const uint64_t left = n > r0 ? n - r0 : 0ull;
+    const uint64_t rows = left < static_cast<uint64_t>(kNormRows) ? left : static_cast<uint64_t>(kNormRows);
+    for (uint64_t e = tid; e < rows * d; e += blockDim.x) {
+        const uint32_t rr = static_cast<uint32_t>(e / d);
+        const float m = mag[rr];
+        const float x = in[r0 * d + e];
+        out[r0 * d + e] = m == 0.0f ? x : __fdiv_rn(x, m);
+    }
+}
+
 // ------------------------------------------------------------ block sort
 
 // Ascending bitonic sort of n (power of two) composites in shared memory.

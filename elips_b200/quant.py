@@ -133,3 +133,13 @@ def top_k(distances: np.ndarray, k: int, device: int = 0) -> tuple[np.ndarray, n
     capi.check(capi.LIB.elips_b200_top_k(device, _ptr(d), _ptr(idx), _ptr(val), nq, nb, k, 0, None),
                "elips_b200_top_k")
     return idx, val
+
+
+def normalize_rows(rows: np.ndarray, device: int = 0) -> np.ndarray:
+    """Vector::normalized of every row (Vector.hpp:25-44), on the device."""
+    x = np.ascontiguousarray(rows, np.float32)
+    out = np.empty_like(x)
+    n, d = x.shape
+    capi.check(capi.LIB.elips_b200_normalize_rows(device, x.ctypes.data, out.ctypes.data, n, d, 0, None),
+               "elips_b200_normalize_rows")
+    return out

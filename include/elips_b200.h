@@ -179,6 +179,14 @@ ELIPS_B200_API int elips_b200_top_k(int device, const float* distances, uint32_t
                                     float* values_out, size_t nq, size_t nb, size_t k,
                                     int pointers_on_device, void* stream);
 
+/* Vector::normalized (include/elips/domain/Vector.hpp:25-44) of n rows of
+ * width d, as Vault::prepare applies it to cosine vaults on insert and query
+ * (src/Database.cpp:823-832): magnitude = sqrt(sequential sum of v*v), every
+ * value divided by it, zero rows unchanged; bit-identical. in == out is
+ * allowed. HOST pointers (synchronous) or DEVICE pointers on `stream`. */
+ELIPS_B200_API int elips_b200_normalize_rows(int device, const float* in, float* out, size_t n, size_t d,
+                                             int pointers_on_device, void* stream);
+
 /* ---------------------------------------------- quantized exhaustive index */
 /* ExactIndex with a trained Quantizer attached (include/elips/index_engine/
  * ExactIndex.hpp:26-66, search at src/ExactIndex.cpp:62-71): codes resident

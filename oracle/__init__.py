@@ -270,6 +270,22 @@ def ivfpq_search(metric, centroids, codebook, codes, vectors, assignments, queri
     return (dist, rows, gap) if with_gap else (dist, rows)
 
 
+def normalize_rows(rows):
+    """Vector::normalized of every row (C restatement)."""
+    x = _f32(rows)
+    out = np.empty_like(x)
+    orc().orc_normalize_rows(_p(x), _p(out), c_size_t(x.shape[0]), c_size_t(x.shape[1]))
+    return out
+
+
+def ref_normalize_rows(rows):
+    """Vector::normalized of every row (the reference's own code)."""
+    x = _f32(rows)
+    out = np.empty_like(x)
+    ref().ref_normalize_rows(_p(x), _p(out), c_size_t(x.shape[0]), c_size_t(x.shape[1]))
+    return out
+
+
 def ivfflat_search(metric, centroids, vectors, assignments, queries, nprobe, k, nthreads=None):
     """GpuIVFFlatIndex::search: probe, gather (probe order, member order), exact
     distances, top-k with ties by gather position."""

@@ -59,6 +59,18 @@ float orc_distance(int metric, const float* a, const float* b, size_t n) {
     return 0.0f;
 }
 
+/* Vector::normalized, include/elips/domain/Vector.hpp:25-44: magnitude =
+ * sqrt(sequential sum of v*v); zero vectors unchanged; else v / magnitude. */
+void orc_normalize_rows(const float* in, float* out, size_t n, size_t d) {
+    for (size_t r = 0; r < n; ++r) {
+        const float* x = in + r * d;
+        float sum = 0.0f;
+        for (size_t i = 0; i < d; ++i) sum += x[i] * x[i];
+        const float mag = sqrtf(sum);
+        for (size_t i = 0; i < d; ++i) out[r * d + i] = mag == 0.0f ? x[i] : x[i] / mag;
+    }
+}
+
 /* ------------------------------------------------------------------------ */
 /* k smallest by (distance, row): a bounded max-heap                          */
 /* ------------------------------------------------------------------------ */

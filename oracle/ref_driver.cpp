@@ -25,6 +25,7 @@
 
 #include "elips/Config.hpp"
 #include "elips/domain/RecordID.hpp"
+#include "elips/domain/Vector.hpp"
 #include "elips/gpu_engine/GpuBruteForceIndex.hpp"
 #include "elips/gpu_engine/GpuIVFFlatIndex.hpp"
 #include "elips/gpu_engine/GpuIVFPQIndex.hpp"
@@ -185,6 +186,15 @@ struct BruteHandle {
 }  // namespace
 
 extern "C" {
+
+// Vector::normalized (Vector.hpp:34-44) of every row.
+void ref_normalize_rows(const float* in, float* out, size_t n, size_t d) {
+    for (size_t r = 0; r < n; ++r) {
+        const elips::Vector v{std::vector<float>(in + r * d, in + (r + 1) * d)};
+        const auto out_v = v.normalized();
+        std::copy(out_v.values().begin(), out_v.values().end(), out + r * d);
+    }
+}
 
 float ref_distance(int metric, const float* a, const float* b, size_t n) {
     return elips::distance(static_cast<Metric>(metric), std::span<const float>{a, n},

@@ -149,3 +149,13 @@ def test_quantized_edge_cases():
     ix.add(np.arange(24, dtype=np.float32).reshape(3, 8))
     d, r = ix.search_batch(np.zeros((1, 8), np.float32), 5)
     assert list(r[0, :3]) == [0, 1, 2] and (r[0, 3:] == -1).all()
+
+
+@pytest.mark.parametrize("n,d", [(1, 1), (33, 768), (1000, 37), (70_001, 128)])
+def test_normalize_rows_bit_exact(n, d):
+    from elips_b200.quant import normalize_rows
+    rng = np.random.default_rng(n + d)
+    x = (rng.standard_normal((n, d)) * rng.uniform(1e-3, 1e3, (n, 1))).astype(np.float32)
+    x[0] = 0.0
+    got = normalize_rows(x)
+    assert np.array_equal(got.view(np.uint32), O.normalize_rows(x).view(np.uint32))

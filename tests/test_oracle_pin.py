@@ -124,3 +124,12 @@ def test_ivfflat_search_matches_reference(metric):
         d3, r3 = ref.search_batch(q, k)
         assert np.array_equal(d1, d2) and np.array_equal(r1, r2)
         assert np.array_equal(d2, d3) and np.array_equal(r2, r3)
+
+
+def test_normalize_matches_reference():
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((300, 77)) * rng.uniform(1e-3, 1e3, (300, 1))).astype(np.float32)
+    x[5] = 0.0
+    x[6, :] = 0.0
+    x[6, 3] = -0.0
+    assert np.array_equal(O.normalize_rows(x).view(np.uint32), O.ref_normalize_rows(x).view(np.uint32))
