@@ -293,9 +293,10 @@ def train_ivfpq_model(cfg, base):
     return cent.contiguous(), assign.to(torch.int32), cb.contiguous()
 
 
-def ivfpq_inputs(cfg, dev):
+def ivfpq_inputs(cfg, dev, train=True):
     """Seeded base rows and queries of the IVF-PQ workload and its trained
-    model, all on `dev`: (base, queries, centroids, assignments, codebook)."""
+    model, all on `dev`: (base, queries, centroids, assignments, codebook);
+    the model entries are None when train is False."""
     import torch
     n, d = cfg["n"], cfg["d"]
     cents = _centroids(cfg, dev)
@@ -304,6 +305,8 @@ def ivfpq_inputs(cfg, dev):
         cnt = min(1 << 20, n - r0)
         base[r0:r0 + cnt] = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev)
     queries = gen_rows(cfg, 0, cfg["q"], SEED + 2, cfg["q"], cents, device=dev)
+    if not train:
+        return base, queries, None, None, None
     centroids, assign, codebook = train_ivfpq_model(cfg, base)
     return base, queries, centroids, assign, codebook
 
@@ -322,45 +325,75 @@ def encode_residuals(base, centroids, assign, codebook, chunk=1 << 20):
     return codes
 
 
-def scanned_bytes(cfg, centroids, queries, assign):
+def scanned_bytes(cfg, centroids, queries, assign, lists=None):
     """Algorithmic bytes of one IVF-PQ scan: for every (query, probed list),
-    each member's code (pq_dim bytes) and slot id (4 bytes)."""
+    each member's code (pq_dim bytes) and slot id (4 bytes); only lists in
+    [lo, hi) when `lists` is given (one GPU's share)."""
     import torch
     nprobe = min(cfg["nprobe"], centroids.shape[0])
     probes = _nearest_k(queries, centroids, nprobe)
     sizes = torch.bincount(assign.long(), minlength=centroids.shape[0])
+    if lists is not None:
+        keep = torch.zeros_like(sizes)
+        keep[lists[0]:lists[1]] = 1
+        sizes = sizes * keep
     return int(sizes[probes].sum().item()) * (cfg["pq_dim"] + 4)
 
 
 # ------------------------------------------------------------ b200 arm
 
 def run_b200_ivfpq(args, cfg, world, rank, local):
-    """IVF-PQ on one GPU (the list-sharded multi-GPU path is not built yet)."""
+    """IVF-PQ on one GPU, or list-sharded over N (ShardedIvfPqIndex: rank 0
+    trains the model and broadcasts it with the assignments; every rank keeps
+    the rows of its own lists)."""
     import torch
     from elips_b200 import _capi
+    from elips_b200.distributed import ShardedIvfPqIndex, list_range
     from elips_b200.ivfpq import IvfPqIndex
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     n, d, nq, k = cfg["n"], cfg["d"], cfg["q"], cfg["k"]
     t0 = time.perf_counter()
-    base, q_dev, centroids, assign, codebook = ivfpq_inputs(cfg, dev)
-    index = IvfPqIndex(cfg["metric"], d, centroids.cpu().numpy(), codebook.cpu().numpy(), nprobe=cfg["nprobe"],
-                       pq_bits=cfg["pq_bits"], device=local)
-    for r0 in range(0, n, 1 << 21):
-        index.add_device(base[r0:r0 + (1 << 21)], assign[r0:r0 + (1 << 21)])
-    alg_bytes = scanned_bytes(cfg, centroids, q_dev, assign)
+    base, q_dev, centroids, assign, codebook = ivfpq_inputs(cfg, dev, train=(rank == 0))
+    if world > 1:
+        import torch.distributed as dist
+        if rank != 0:
+            centroids = torch.empty((cfg["nlist"], d), dtype=torch.float32, device=dev)
+            codebook = torch.empty((cfg["pq_dim"], 1 << cfg["pq_bits"], d // cfg["pq_dim"]), dtype=torch.float32,
+                                   device=dev)
+            assign = torch.empty((n,), dtype=torch.int32, device=dev)
+        for t in (centroids, codebook, assign):
+            dist.broadcast(t, src=0)
+    cent_np, cb_np = centroids.cpu().numpy(), codebook.cpu().numpy()
+    if world == 1:
+        index = IvfPqIndex(cfg["metric"], d, cent_np, cb_np, nprobe=cfg["nprobe"], pq_bits=cfg["pq_bits"],
+                           device=local)
+        for r0 in range(0, n, 1 << 21):
+            index.add_device(base[r0:r0 + (1 << 21)], assign[r0:r0 + (1 << 21)])
+        lists = None
+    else:
+        index = ShardedIvfPqIndex(cfg["metric"], d, cent_np, cb_np, cfg["nprobe"], pq_bits=cfg["pq_bits"],
+                                  rank=rank, world=world, device=local)
+        for r0 in range(0, n, 1 << 21):
+            index.add_device(base[r0:r0 + (1 << 21)], assign[r0:r0 + (1 << 21)], r0)
+        lists = list_range(cfg["nlist"], rank, world)
+    alg_bytes = scanned_bytes(cfg, centroids, q_dev, assign, lists)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
     out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
     out_r = torch.empty((nq, k), dtype=torch.int64, device=dev)
 
     def step():
-        index.search_device(q_dev, k, out_dist=out_d, out_rows=out_r)
+        if world == 1:
+            index.search_device(q_dev, k, out_dist=out_d, out_rows=out_r)
+        else:
+            index.search_device(q_dev, k)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    barrier(world)
     _capi.profiler_reset()
     _capi.profiler_enable(True)
     launches0 = _capi.launch_count()
@@ -376,32 +409,51 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
         ev1.record(stream)
         torch.cuda.synchronize()
         sampler.active = False
+    barrier(world)
     launches = _capi.launch_count() - launches0
     _capi.profiler_enable(False)
-    ms = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
     scan = _capi.profiler_stats("ivfpq_scan")
     allk = _capi.profiler_stats(None)
     per_kernel = {name: round(_capi.profiler_stats(name)["total_ms"] / args.steps, 4)
                   for name in ("distances", "topk_rows", "ivfpq_plan", "ivfpq_scan", "merge_topk", "ivfpq_rerank")}
     value = nq * args.steps / (ms / 1e3)
 
-    q_np = q_dev.cpu().pin_memory().numpy()
-    od = torch.empty((nq, k), dtype=torch.float32).pin_memory().numpy()
-    orr = torch.empty((nq, k), dtype=torch.int64).pin_memory().numpy()
+    q_pin = q_dev.cpu().pin_memory()
+    q_np = q_pin.numpy()
+    od_t = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    or_t = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    od, orr = od_t.numpy(), or_t.numpy()
+
+    def e2e_step():
+        if world == 1:
+            index.search_batch(q_np, k, out_dist=od, out_rows=orr)
+            return
+        dd, rr = index.search_device(q_pin.to(dev, non_blocking=True), k)
+        if rank == 0:
+            od_t.copy_(dd, non_blocking=True)
+            or_t.copy_(rr, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
     for _ in range(max(1, args.warmup)):
-        index.search_batch(q_np, k, out_dist=od, out_rows=orr)
+        e2e_step()
+    barrier(world)
     t = time.perf_counter()
     for _ in range(args.steps):
-        index.search_batch(q_np, k, out_dist=od, out_rows=orr)
-    e2e_s = time.perf_counter() - t
-    e2e = {"value": round(nq * args.steps / e2e_s, 2), "unit": "queries/s", "h2d_bytes_per_step": int(q_np.nbytes),
-           "d2h_bytes_per_step": int(nq * k * 12), "api": "elips_b200_ivfpq_search (host buffers)"}
+        e2e_step()
+    e2e_s = max_over_ranks(time.perf_counter() - t, world)
+    barrier(world)
+    e2e = {"value": round(nq * args.steps / e2e_s, 2), "unit": "queries/s",
+           "h2d_bytes_per_step": int(q_np.nbytes) * world, "d2h_bytes_per_step": int(nq * k * 12),
+           "api": "elips_b200_ivfpq_search (host buffers)" if world == 1 else
+                  "ShardedIvfPqIndex.search_device from pinned host queries (NCCL all-gathers, merge kernels)"}
 
     peaks, peak_src = load_peaks()
     scan_ms = scan["total_ms"] / max(1, scan["launches"])
     achieved = alg_bytes / (scan_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(peaks["hbm_gbs"], 1), "unit": "GB/s",
-                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": load_traffic(args.config, n),
+                "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": load_traffic(args.config, n if world == 1 else index.local.size()),
                 "kernel": "ivfpq_scan_kernel", "kernel_ms_avg": round(scan_ms, 4),
                 "kernel_share_of_step": round(scan["total_ms"] / max(1e-9, allk["total_ms"]), 4),
                 "algorithmic_bytes_per_launch": alg_bytes, "per_kernel_ms_per_step": per_kernel,
@@ -417,7 +469,9 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
                    "l2": "inputs larger than L2 (codes 160 MB, vectors 5.1 GB); no flush"},
         "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "clocks": sampler.summary(),
         "build_s": round(build_s, 2)}
-    if not args.no_cpu_baseline and rank == 0:
+    if world > 1:
+        result["config"]["parallelism"] = f"lists sharded over {world} GPUs (contiguous list ids)"
+    if not args.no_cpu_baseline and world == 1:
         import oracle
         host_base = base.cpu().numpy()
         codes = index.codes()
@@ -771,8 +825,6 @@ def main():
     world, rank, local = dist_setup(args)
     try:
         if args.config == "ivfpq":
-            if world > 1:
-                raise SystemExit("the list-sharded multi-GPU IVF-PQ path is not built yet")
             result = run_b200_ivfpq(args, cfg, world, rank, local)
         else:
             result = run_b200(args, cfg, world, rank, local)

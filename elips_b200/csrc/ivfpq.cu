@@ -33,7 +33,8 @@ void launch_ok(const char* what) { check_cuda(cudaGetLastError(), ELIPS_B200_KER
 class IvfLists {
 public:
     IvfLists(int device, int metric, uint32_t dim, uint32_t nlist, uint32_t nprobe, const float* centroids)
-        : device_(device), metric_(metric), dim_(dim), nlist_(nlist), nprobe_(std::max<uint32_t>(1, nprobe)) {
+        : device_(device), metric_(metric), dim_(dim), nlist_(nlist), nprobe_(std::max<uint32_t>(1, nprobe)),
+          list_hi_(nlist) {
         if (metric < 0 || metric > 2) fail(ELIPS_B200_UNSUPPORTED_METRIC, "unknown metric");
         if (dim == 0 || dim > 65535 || nlist == 0) fail(ELIPS_B200_INVALID_ARGUMENT, "bad dimension or list count");
         if (centroids == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "centroids are null");
@@ -49,6 +50,17 @@ public:
     size_t size() const { return n_; }
     void set_nprobe(uint32_t nprobe) { nprobe_ = std::max<uint32_t>(1, nprobe); }
 
+    // Lists [lo, hi) are this index's share of a list-sharded index
+    // (GpuDistributedIndex over IVF lists): rows may only name them, and a
+    // search scans only them. Default: every list.
+    void set_list_range(uint32_t lo, uint32_t hi) {
+        if (lo > hi || hi > nlist_) fail(ELIPS_B200_INVALID_ARGUMENT, "list range outside [0, n_lists]");
+        for (uint32_t a : assign_)
+            if (a < lo || a >= hi) fail(ELIPS_B200_INVALID_ARGUMENT, "rows already added outside the list range");
+        list_lo_ = lo;
+        list_hi_ = hi;
+    }
+
 protected:
     // Validates the list ids (they must name a list), grows the row store and
     // appends the rows (DEVICE pointers). Returns the host copy of the ids;
@@ -60,8 +72,10 @@ protected:
         check_cuda(cudaMemcpyAsync(host_assign.data(), assign, n * 4, cudaMemcpyDeviceToHost, stream),
                    ELIPS_B200_TRANSFER_FAILED, "assignment copy");
         check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_TRANSFER_FAILED, "assignment copy");
-        for (uint32_t a : host_assign)
+        for (uint32_t a : host_assign) {
             if (a >= nlist_) fail(ELIPS_B200_INVALID_ARGUMENT, "assignment names a list past n_lists");
+            if (a < list_lo_ || a >= list_hi_) fail(ELIPS_B200_INVALID_ARGUMENT, "assignment outside the list range");
+        }
         if (n_ + n > capacity_) {
             const size_t cap = std::max<size_t>(n_ + n, capacity_ + capacity_ / 2);
             DeviceBuffer v(device_, cap * dim_ * 4);
@@ -170,8 +184,8 @@ protected:
         const uint32_t* loff = static_cast<const uint32_t*>(list_off_.get());
         {
             Profiler::Scope prof("ivfpq_plan", stream, pl.npairs);
-            ivf_pair_count_kernel<<<pblocks, 256, 0, stream>>>(pl.probes, static_cast<uint32_t>(pl.npairs), nlist_,
-                                                               pl.counts, pl.part, r);
+            ivf_pair_count_kernel<<<pblocks, 256, 0, stream>>>(pl.probes, static_cast<uint32_t>(pl.npairs), list_lo_,
+                                                               list_hi_, pl.counts, pl.part, r);
             launch_ok("pair count kernel");
         }
         {
@@ -188,8 +202,8 @@ protected:
         }
         {
             Profiler::Scope prof("ivfpq_plan", stream, pl.npairs);
-            ivf_pair_scatter_kernel<<<pblocks, 256, 0, stream>>>(pl.probes, static_cast<uint32_t>(pl.npairs), nlist_,
-                                                                 pl.list_start, cursor, pl.pairs);
+            ivf_pair_scatter_kernel<<<pblocks, 256, 0, stream>>>(pl.probes, static_cast<uint32_t>(pl.npairs), list_lo_,
+                                                                 list_hi_, pl.list_start, cursor, pl.pairs);
             launch_ok("pair scatter kernel");
         }
         if (flat) {
@@ -255,7 +269,7 @@ protected:
     }
 
     int device_, metric_;
-    uint32_t dim_, nlist_, nprobe_;
+    uint32_t dim_, nlist_, nprobe_, list_lo_ = 0, list_hi_ = 0;
     size_t n_ = 0, capacity_ = 0;
     bool dirty_ = false;
     std::vector<uint32_t> assign_;
@@ -326,25 +340,40 @@ public:
     void search_device(const float* queries, size_t nq, size_t k, float* out_dist, int64_t* out_rows,
                        cudaStream_t stream) {
         if (nq == 0 || k == 0) return;
-        if (k > 256) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 256 is not supported (rerank set is 4k)");
-        if (nq * nprobe_ > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "too many queries in one call");
-        if (queries == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "queries is null");
+        check_search(queries, nq, k);
         DeviceGuard g(device_);
         if (n_ == 0) {
             merge_candidates(device_, nullptr, static_cast<uint32_t>(nq), 0, static_cast<uint32_t>(k), 0, 0, 0, out_dist,
                              out_rows, nullptr, stream);
             return;
         }
-        finalize(stream);
         const uint32_t r = static_cast<uint32_t>(4 * k);
+        StreamScratch s(a256(nq * static_cast<size_t>(r) * 8), stream);
+        uint2* cand = reinterpret_cast<uint2*>(s.get());
+        candidates(queries, nq, k, cand, stream);
+        rerank(queries, nq, k, cand, out_dist, out_rows, stream);
+    }
+
+    // Steps 1-4 of search: the R = 4k best (approximate key, slot) per query
+    // over the probed lists this index owns, ascending, padded with
+    // {+inf, 0xFFFFFFFF}. out_cand: [nq][R] DEVICE.
+    void candidates(const float* queries, size_t nq, size_t k, uint2* out_cand, cudaStream_t stream) {
+        if (nq == 0 || k == 0) return;
+        check_search(queries, nq, k);
+        DeviceGuard g(device_);
+        const uint32_t r = static_cast<uint32_t>(4 * k);
+        if (n_ == 0) {
+            merge_candidates(device_, nullptr, static_cast<uint32_t>(nq), 0, r, 0, 0, 0, nullptr, nullptr, out_cand,
+                             stream);
+            return;
+        }
+        finalize(stream);
         const uint32_t nprobe = std::min(nprobe_, nlist_);
         const uint32_t lut_stride = group_lut_stride(m_, ksub_);
         const uint32_t G = group_size(nq * nprobe, r, lut_stride);
         const uint32_t capq = group_capacity(G, r);
-        StreamScratch s(plan_bytes(nq, r, false) + a256(nq * static_cast<size_t>(r) * 8), stream);
+        StreamScratch s(plan_bytes(nq, r, false), stream);
         uint8_t* w = s.get();
-        uint2* cand = reinterpret_cast<uint2*>(w);
-        w += a256(nq * static_cast<size_t>(r) * 8);
         // 1-2. probe and plan
         const Plan pl = probe_and_plan(queries, nq, r, G, false, w, stream);
         // 3. per (list, query group) approximate scan, R best per (query, list)
@@ -364,8 +393,19 @@ public:
         // 4. R best approximate candidates per query across its probed lists
         //    (keys are final approximate distances: no transform, metric 0)
         merge_candidates(device_, pl.part, static_cast<uint32_t>(nq), pl.nprobe, r,
-                         static_cast<uint64_t>(pl.nprobe) * r, r, 0, nullptr, nullptr, cand, stream);
-        // 5. exact rerank (exact_rank)
+                         static_cast<uint64_t>(pl.nprobe) * r, r, 0, nullptr, nullptr, out_cand, stream);
+    }
+
+    // Step 5 (exact_rank, GpuIVFPQIndex.cpp:37-71): exact distances of the
+    // R candidates per query on this index's raw rows (slot 0xFFFFFFFF =
+    // none), top-k by (distance, slot). cand: [nq][4k] DEVICE.
+    void rerank(const float* queries, size_t nq, size_t k, const uint2* cand, float* out_dist, int64_t* out_rows,
+                cudaStream_t stream) {
+        if (nq == 0 || k == 0) return;
+        check_search(queries, nq, k);
+        if (cand == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "candidates are null");
+        DeviceGuard g(device_);
+        const uint32_t r = static_cast<uint32_t>(4 * k);
         uint32_t rp = 1;
         while (rp < r) rp <<= 1;
         constexpr uint32_t warps = 4;
@@ -376,11 +416,17 @@ public:
         Profiler::Scope prof("ivfpq_rerank", stream, nq * r);
         ivfpq_rerank_kernel<<<static_cast<uint32_t>((nq + warps - 1) / warps), warps * 32, rsmem, stream>>>(
             queries, static_cast<const float*>(vectors_.get()), cand, static_cast<uint32_t>(nq), dim_, r,
-            static_cast<uint32_t>(k), rp, metric_, out_dist, out_rows);
+            static_cast<uint32_t>(k), rp, static_cast<uint32_t>(n_), metric_, out_dist, out_rows);
         launch_ok("ivf-pq rerank kernel");
     }
 
 private:
+    void check_search(const float* queries, size_t nq, size_t k) const {
+        if (k > 256) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 256 is not supported (rerank set is 4k)");
+        if (nq * nprobe_ > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "too many queries in one call");
+        if (queries == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "queries is null");
+    }
+
     void grow(size_t rows) override {
         DeviceBuffer c(device_, rows * m_);
         if (n_ > 0)
@@ -626,6 +672,31 @@ int elips_b200_ivfpq_search_device(elips_b200_ivfpq* index, const float* queries
     if (nq > 0 && k > 0 && (queries == nullptr || out_dist == nullptr || out_rows == nullptr))
         return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] { index->index.search_device(queries, nq, k, out_dist, out_rows, static_cast<cudaStream_t>(stream)); });
+}
+
+int elips_b200_ivfpq_set_list_range(elips_b200_ivfpq* index, uint32_t list_lo, uint32_t list_hi) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.set_list_range(list_lo, list_hi); });
+}
+
+int elips_b200_ivfpq_search_candidates_device(elips_b200_ivfpq* index, const float* queries, size_t nq, size_t k,
+                                              uint32_t* out_cand, void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (queries == nullptr || out_cand == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        index->index.candidates(queries, nq, k, reinterpret_cast<uint2*>(out_cand), static_cast<cudaStream_t>(stream));
+    });
+}
+
+int elips_b200_ivfpq_rerank_device(elips_b200_ivfpq* index, const float* queries, size_t nq, size_t k,
+                                   const uint32_t* cand, float* out_dist, int64_t* out_rows, void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (queries == nullptr || cand == nullptr || out_dist == nullptr || out_rows == nullptr))
+        return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        index->index.rerank(queries, nq, k, reinterpret_cast<const uint2*>(cand), out_dist, out_rows,
+                            static_cast<cudaStream_t>(stream));
+    });
 }
 
 int elips_b200_ivfpq_codes_device(const elips_b200_ivfpq* index, uint8_t* codes_out, void* stream) {

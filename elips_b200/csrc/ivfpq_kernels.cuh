@@ -40,15 +40,16 @@ namespace eb {
 constexpr uint32_t kPlanThreads = 1024;
 constexpr uint32_t kPlanSortMax = 8192;  // lists visited largest first up to this many
 
-// pair = q * nprobe + p. Counts the pairs of every list; a pair without a
-// list (probe slot past the list count) gets an empty candidate list.
-static __global__ void ivf_pair_count_kernel(const uint32_t* __restrict__ probes, uint32_t npairs, uint32_t nlist,
-                                             uint32_t* __restrict__ counts, uint2* __restrict__ partial,
-                                             uint32_t r) {
+// pair = q * nprobe + p. Counts the pairs of every list this index owns
+// ([lo, hi): all lists, or one GPU's share of a list-sharded index); a pair
+// whose list is not owned gets an empty candidate list.
+static __global__ void ivf_pair_count_kernel(const uint32_t* __restrict__ probes, uint32_t npairs, uint32_t lo,
+                                             uint32_t hi, uint32_t* __restrict__ counts,
+                                             uint2* __restrict__ partial, uint32_t r) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= npairs) return;
     const uint32_t l = probes[i];
-    if (l < nlist) {
+    if (l >= lo && l < hi) {
         atomicAdd(&counts[l], 1u);
         return;
     }
@@ -135,13 +136,13 @@ static __global__ void __launch_bounds__(kPlanThreads)
     }
 }
 
-static __global__ void ivf_pair_scatter_kernel(const uint32_t* __restrict__ probes, uint32_t npairs, uint32_t nlist,
-                                               const uint32_t* __restrict__ list_start, uint32_t* __restrict__ cursor,
-                                               uint32_t* __restrict__ pairs) {
+static __global__ void ivf_pair_scatter_kernel(const uint32_t* __restrict__ probes, uint32_t npairs, uint32_t lo,
+                                               uint32_t hi, const uint32_t* __restrict__ list_start,
+                                               uint32_t* __restrict__ cursor, uint32_t* __restrict__ pairs) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= npairs) return;
     const uint32_t l = probes[i];
-    if (l < nlist) pairs[list_start[l] + atomicAdd(&cursor[l], 1u)] = i;
+    if (l >= lo && l < hi) pairs[list_start[l] + atomicAdd(&cursor[l], 1u)] = i;
 }
 
 // Gather position of each pair's first candidate: the candidates of a query
@@ -820,11 +821,11 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
 
 // One warp per query: exact distances of the R merged candidates, top-k by
 // (distance, slot), written sorted. cand[q][r] = {approximate key, slot}
-// (slot 0xFFFFFFFF = empty).
+// (slot 0xFFFFFFFF = empty; any slot >= n is skipped the same way).
 static __global__ void ivfpq_rerank_kernel(const float* __restrict__ queries, const float* __restrict__ vectors,
                                            const uint2* __restrict__ cand, uint32_t nq, uint32_t d, uint32_t r,
-                                           uint32_t k, uint32_t rpow2, int metric, float* __restrict__ out_dist,
-                                           int64_t* __restrict__ out_rows) {
+                                           uint32_t k, uint32_t rpow2, uint32_t n, int metric,
+                                           float* __restrict__ out_dist, int64_t* __restrict__ out_rows) {
     extern __shared__ unsigned long long sbuf[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t warps = blockDim.x >> 5;
@@ -836,7 +837,7 @@ static __global__ void ivfpq_rerank_kernel(const float* __restrict__ queries, co
         unsigned long long c = ~0ull;
         if (i < r) {
             const uint2 e = cand[static_cast<size_t>(q) * r + i];
-            if (e.y != 0xFFFFFFFFu) {
+            if (e.y < n) {  // 0xFFFFFFFF (none) and out-of-range slots are skipped
                 const float* v = vectors + static_cast<size_t>(e.y) * d;
                 float acc = 0.0f;
                 if (metric == kMetricL2) {

@@ -95,3 +95,107 @@ class ShardedExactIndex:
         out_rows.copy_(r, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         return out_dist, out_rows
+
+
+def list_range(nlist: int, rank: int, world: int) -> tuple[int, int]:
+    """The IVF lists a rank owns: contiguous list ids, split as split_ids splits
+    rows (GpuDistributedIndex.cpp:12-22)."""
+    return nlist * rank // world, nlist * (rank + 1) // world
+
+
+def _pairs(dist, rows):
+    """(dist [nq, m] float32, rows [nq, m] int64, -1 = none) -> [nq, m, 2] int32
+    candidate pairs (distance bits, row)."""
+    import torch
+    return torch.stack((dist.contiguous().view(torch.int32), rows.to(torch.int32)), dim=-1)
+
+
+class ShardedIvfPqIndex:
+    """One rank's share of a list-sharded IVF-PQ index. The reference shards
+    rows in GpuDistributedIndex and retrains a model per shard (:318-320);
+    here every rank holds the one global model and the ranks together answer
+    exactly what a single index answers.
+
+    Rank r owns lists list_range(nlist, r, world) and only their rows. A search
+    (every rank calls it with the same queries):
+      1. each rank: probe (replicated centroids), scan its own probed lists,
+         R = 4k best approximate (distance, global slot);
+      2. all-gather; every rank merges the R best over all ranks, the set a
+         single index would rerank;
+      3. each rank reranks the ones it holds, exactly, on its raw rows;
+      4. all-gather of the k best per rank; the root merges them by
+         (distance, global slot).
+    The phases are methods, so a test can drive several ranks in one process;
+    `exchange` defaults to exchange_candidates over the process group."""
+
+    def __init__(self, metric: str, dimension: int, centroids, codebook, nprobe: int, pq_bits: int = 8,
+                 rank: int = 0, world: int = 1, device: int = 0, group=None, exchange=None):
+        from .ivfpq import IvfPqIndex
+        self.metric, self.rank, self.world, self.group = metric, rank, world, group
+        self.nlist = np.asarray(centroids).shape[0]
+        self.lo, self.hi = list_range(self.nlist, rank, world)
+        self.local = IvfPqIndex(metric, dimension, centroids, codebook, nprobe=nprobe, pq_bits=pq_bits,
+                                device=device)
+        self.local.set_list_range(self.lo, self.hi)
+        self.global_rows = None  # int64 device tensor, ascending: local slot -> global slot
+        self.exchange = exchange if exchange is not None else (
+            lambda t: exchange_candidates(t, self.world, self.group))
+
+    def add_device(self, vectors, assignments, first_row: int, codes=None) -> None:
+        """Offers rows [first_row, first_row + n) in global order (CUDA tensors;
+        assignments int32); this rank keeps those of its own lists."""
+        import torch
+        a = assignments.long()
+        idx = torch.nonzero((a >= self.lo) & (a < self.hi)).flatten()
+        if idx.numel() == 0:
+            return
+        self.local.add_device(vectors[idx].contiguous(), assignments[idx].contiguous(),
+                              None if codes is None else codes[idx].contiguous())
+        g = idx + first_row
+        self.global_rows = g if self.global_rows is None else torch.cat((self.global_rows, g))
+
+    def _to_global(self, rows):
+        import torch
+        if self.global_rows is None:
+            return torch.full_like(rows, -1)
+        return torch.where(rows >= 0, self.global_rows[rows.clamp(min=0)], rows)
+
+    def _to_local(self, rows):
+        import torch
+        if self.global_rows is None:
+            return torch.full_like(rows, -1)
+        pos = torch.searchsorted(self.global_rows, rows.clamp(min=0)).clamp(max=self.global_rows.numel() - 1)
+        held = (rows >= 0) & (self.global_rows[pos] == rows)
+        return torch.where(held, pos, torch.full_like(pos, -1))
+
+    def approx_candidates(self, queries, k: int):
+        """Phase 1: [nq, 4k, 2] int32 (distance bits, global slot)."""
+        import torch
+        cand = self.local.search_candidates_device(queries, k)
+        return _pairs(cand[..., 0].contiguous().view(torch.float32), self._to_global(cand[..., 1].long()))
+
+    def rerank_owned(self, queries, k: int, gathered):
+        """Phases 2-3: gathered [world, nq, 4k, 2] -> this rank's [nq, k, 2]
+        (distance bits, global slot) over the global R best it holds."""
+        from .exact import merge_candidates_device
+        world, r = gathered.shape[0], gathered.shape[2]
+        d, rows = merge_candidates_device(gathered, world, r, "dot_product")  # keys kept as they are
+        dist, lrows = self.local.rerank_device(queries, k, _pairs(d, self._to_local(rows)))
+        return _pairs(dist, self._to_global(lrows))
+
+    @staticmethod
+    def merge_final(gathered, k: int):
+        """Phase 4 (root): gathered [world, nq, k, 2] -> (dist, global rows) [nq, k]."""
+        from .exact import merge_candidates_device
+        return merge_candidates_device(gathered, gathered.shape[0], k, "dot_product")
+
+    def search_device(self, queries, k: int):
+        """Every rank calls it; (dist, global rows) on the root, (None, None) elsewhere."""
+        if self.world == 1:
+            d, r = self.local.search_device(queries, k)
+            return d, self._to_global(r)
+        mine = self.rerank_owned(queries, k, self.exchange(self.approx_candidates(queries, k)))
+        gathered = self.exchange(mine)
+        if self.rank != 0:
+            return None, None
+        return self.merge_final(gathered, k)

@@ -66,6 +66,37 @@ class IvfPqIndex:
     def set_nprobe(self, nprobe: int) -> None:
         capi.check(capi.LIB.elips_b200_ivfpq_set_nprobe(self._h, int(nprobe)), "elips_b200_ivfpq_set_nprobe")
 
+    def set_list_range(self, lo: int, hi: int) -> None:
+        """Own only lists [lo, hi) (one GPU's share of a list-sharded index)."""
+        capi.check(capi.LIB.elips_b200_ivfpq_set_list_range(self._h, int(lo), int(hi)),
+                   "elips_b200_ivfpq_set_list_range")
+
+    def search_candidates_device(self, queries, k: int, out=None, stream=None):
+        """The approximate stage: [nq, 4k, 2] int32 (distance bits, slot), ascending."""
+        import torch
+        nq = queries.shape[0]
+        if out is None:
+            out = torch.empty((nq, 4 * k, 2), dtype=torch.int32, device=queries.device)
+        s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_ivfpq_search_candidates_device(self._h, queries.data_ptr(), nq, k,
+                                                                      out.data_ptr(), s),
+                   "elips_b200_ivfpq_search_candidates_device")
+        return out
+
+    def rerank_device(self, queries, k: int, cand, out_dist=None, out_rows=None, stream=None):
+        """The exact stage over cand [nq, 4k, 2] (slot -1 = none): (dist, slot) [nq, k]."""
+        import torch
+        nq = queries.shape[0]
+        if out_dist is None:
+            out_dist = torch.empty((nq, k), dtype=torch.float32, device=queries.device)
+            out_rows = torch.empty((nq, k), dtype=torch.int64, device=queries.device)
+        cand = cand.contiguous()
+        s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_ivfpq_rerank_device(self._h, queries.data_ptr(), nq, k, cand.data_ptr(),
+                                                           out_dist.data_ptr(), out_rows.data_ptr(), s),
+                   "elips_b200_ivfpq_rerank_device")
+        return out_dist, out_rows
+
     def codes(self) -> np.ndarray:
         """Residual codes of every row in slot order (export_snapshot's pq.codes)."""
         import torch

@@ -282,6 +282,29 @@ ELIPS_B200_API int elips_b200_ivfpq_search_device(elips_b200_ivfpq* index, const
 ELIPS_B200_API int elips_b200_ivfpq_codes_device(const elips_b200_ivfpq* index, uint8_t* codes_out,
                                                  void* stream);
 
+/* List-sharded IVF-PQ over several GPUs (GpuDistributedIndex's shard mode,
+ * src/gpu_engine/GpuDistributedIndex.cpp:12-34, applied to IVF lists): this
+ * index owns lists [list_lo, list_hi) only; rows may only name them, and a
+ * search scans only them. Set before adding rows. */
+ELIPS_B200_API int elips_b200_ivfpq_set_list_range(elips_b200_ivfpq* index, uint32_t list_lo,
+                                                   uint32_t list_hi);
+
+/* The approximate stage of search (probe, scan, merge): the R = 4k best
+ * {approximate distance bits, slot} per query over the owned probed lists,
+ * ascending by (distance, slot), padded with {+inf, 0xFFFFFFFF}; out_cand is
+ * nq x R pairs of uint32 (2*nq*R words). DEVICE pointers on `stream`. */
+ELIPS_B200_API int elips_b200_ivfpq_search_candidates_device(elips_b200_ivfpq* index,
+                                                             const float* queries, size_t nq,
+                                                             size_t k, uint32_t* out_cand,
+                                                             void* stream);
+
+/* The exact stage (exact_rank, GpuIVFPQIndex.cpp:37-71): for nq x R pairs
+ * {any, slot} (slot 0xFFFFFFFF or past size = none), exact distances on this
+ * index's raw rows, the k best ascending by (distance, slot). DEVICE. */
+ELIPS_B200_API int elips_b200_ivfpq_rerank_device(elips_b200_ivfpq* index, const float* queries,
+                                                  size_t nq, size_t k, const uint32_t* cand,
+                                                  float* out_dist, int64_t* out_rows, void* stream);
+
 ELIPS_B200_API int elips_b200_ivfpq_destroy(elips_b200_ivfpq* index);
 
 /* -------------------------------------------------------------- IVF-Flat */

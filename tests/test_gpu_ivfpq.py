@@ -113,3 +113,37 @@ def test_ivfpq_rejects_bad_assignment(model):
     with pytest.raises(ElipsB200Error):
         ix.add(m["base"][:10], bad)
     assert ix.size() == 0
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("metric", ["euclidean", "dot_product"])
+def test_list_sharded_search_equals_single_index(model, world, metric):
+    """List-sharded IVF-PQ (one rank per list range), its ranks driven phase by
+    phase in one process on one GPU: the result equals the single index's."""
+    import torch
+    from elips_b200.distributed import ShardedIvfPqIndex
+    from elips_b200.ivfpq import IvfPqIndex
+    m = model
+    base, q = m["base"], m["queries"]
+    asg, codes = m["asg"], m["codes"]
+    if metric != "euclidean":
+        base, q = H.normalize(base), H.normalize(q)
+        asg = O.ivf_assign(metric, base, m["cent"])
+        codes = O.ref_encode_pq(m["cb"], base - m["cent"][asg])
+    k, nprobe = 10, 8
+    single = IvfPqIndex(metric, 64, m["cent"], m["cb"], nprobe=nprobe)
+    single.add(base, asg, codes)
+    d_ref, r_ref = single.search_batch(q, k)
+    vd, ad, cd = (torch.from_numpy(base).cuda(), torch.from_numpy(asg.view(np.int32)).cuda(),
+                  torch.from_numpy(codes).cuda())
+    ranks = [ShardedIvfPqIndex(metric, 64, m["cent"], m["cb"], nprobe, rank=r, world=world) for r in range(world)]
+    for ix in ranks:
+        for r0 in range(0, len(base), 25_000):  # rows offered in global order, in batches
+            ix.add_device(vd[r0:r0 + 25_000], ad[r0:r0 + 25_000], r0, cd[r0:r0 + 25_000])
+    assert sum(ix.local.size() for ix in ranks) == len(base)
+    qd = torch.from_numpy(q).cuda()
+    gathered = torch.stack([ix.approx_candidates(qd, k) for ix in ranks])
+    mine = torch.stack([ix.rerank_owned(qd, k, gathered) for ix in ranks])
+    d, r = ShardedIvfPqIndex.merge_final(mine, k)
+    torch.cuda.synchronize()
+    assert np.array_equal(r.cpu().numpy(), r_ref) and np.array_equal(d.cpu().numpy(), d_ref)
