@@ -327,16 +327,14 @@ def encode_residuals(base, centroids, assign, codebook, chunk=1 << 20):
 
 def scanned_bytes(cfg, centroids, queries, assign, lists=None):
     """Algorithmic bytes of one IVF-PQ scan: for every (query, probed list),
-    each member's code (pq_dim bytes) and slot id (4 bytes); only lists in
-    [lo, hi) when `lists` is given (one GPU's share)."""
+    each member's code (pq_dim bytes) and slot id (4 bytes); only the lists
+    where `lists` (bool per list) is true when given (one GPU's share)."""
     import torch
     nprobe = min(cfg["nprobe"], centroids.shape[0])
     probes = _nearest_k(queries, centroids, nprobe)
     sizes = torch.bincount(assign.long(), minlength=centroids.shape[0])
     if lists is not None:
-        keep = torch.zeros_like(sizes)
-        keep[lists[0]:lists[1]] = 1
-        sizes = sizes * keep
+        sizes = sizes * torch.as_tensor(lists, device=sizes.device).to(sizes.dtype)
     return int(sizes[probes].sum().item()) * (cfg["pq_dim"] + 4)
 
 
@@ -348,7 +346,7 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
     the rows of its own lists)."""
     import torch
     from elips_b200 import _capi
-    from elips_b200.distributed import ShardedIvfPqIndex, list_range
+    from elips_b200.distributed import ShardedIvfPqIndex, balanced_lists
     from elips_b200.ivfpq import IvfPqIndex
 
     torch.cuda.set_device(local)
@@ -373,11 +371,12 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
             index.add_device(base[r0:r0 + (1 << 21)], assign[r0:r0 + (1 << 21)])
         lists = None
     else:
+        owner = balanced_lists(torch.bincount(assign.long(), minlength=cfg["nlist"]).cpu().numpy(), world)
         index = ShardedIvfPqIndex(cfg["metric"], d, cent_np, cb_np, cfg["nprobe"], pq_bits=cfg["pq_bits"],
-                                  rank=rank, world=world, device=local)
+                                  rank=rank, world=world, device=local, owner=owner)
         for r0 in range(0, n, 1 << 21):
             index.add_device(base[r0:r0 + (1 << 21)], assign[r0:r0 + (1 << 21)], r0)
-        lists = list_range(cfg["nlist"], rank, world)
+        lists = owner == rank
     alg_bytes = scanned_bytes(cfg, centroids, q_dev, assign, lists)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
@@ -470,7 +469,7 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
         "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "clocks": sampler.summary(),
         "build_s": round(build_s, 2)}
     if world > 1:
-        result["config"]["parallelism"] = f"lists sharded over {world} GPUs (contiguous list ids)"
+        result["config"]["parallelism"] = f"lists sharded over {world} GPUs (balanced by size^2)"
     if not args.no_cpu_baseline and world == 1:
         import oracle
         host_base = base.cpu().numpy()

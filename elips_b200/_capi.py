@@ -83,6 +83,7 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
     ("elips_b200_ivfpq_codes_device", c_int, [c_void_p, c_void_p, c_void_p]),
     ("elips_b200_ivfpq_set_list_range", c_int, [c_void_p, c_uint32, c_uint32]),
+    ("elips_b200_ivfpq_set_owned_lists", c_int, [c_void_p, c_void_p, c_size_t]),
     ("elips_b200_ivfpq_search_candidates_device", c_int, [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p]),
     ("elips_b200_ivfpq_rerank_device", c_int,
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p]),

@@ -34,7 +34,7 @@ class IvfLists {
 public:
     IvfLists(int device, int metric, uint32_t dim, uint32_t nlist, uint32_t nprobe, const float* centroids)
         : device_(device), metric_(metric), dim_(dim), nlist_(nlist), nprobe_(std::max<uint32_t>(1, nprobe)),
-          list_hi_(nlist) {
+          owned_host_(nlist, true) {
         if (metric < 0 || metric > 2) fail(ELIPS_B200_UNSUPPORTED_METRIC, "unknown metric");
         if (dim == 0 || dim > 65535 || nlist == 0) fail(ELIPS_B200_INVALID_ARGUMENT, "bad dimension or list count");
         if (centroids == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "centroids are null");
@@ -50,15 +50,30 @@ public:
     size_t size() const { return n_; }
     void set_nprobe(uint32_t nprobe) { nprobe_ = std::max<uint32_t>(1, nprobe); }
 
-    // Lists [lo, hi) are this index's share of a list-sharded index
-    // (GpuDistributedIndex over IVF lists): rows may only name them, and a
+    // The lists this index owns as one GPU's share of a list-sharded index
+    // (GpuDistributedIndex over IVF lists): bit l & 31 of words[l >> 5]
+    // (ceil(n_lists / 32) words, HOST). Rows may only name owned lists, and a
     // search scans only them. Default: every list.
+    void set_owned_lists(const uint32_t* words, size_t n_words) {
+        if (words == nullptr || n_words != (nlist_ + 31u) / 32u)
+            fail(ELIPS_B200_INVALID_ARGUMENT, "owned-list mask must have ceil(n_lists / 32) words");
+        std::vector<bool> owned(nlist_);
+        for (uint32_t l = 0; l < nlist_; ++l) owned[l] = (words[l >> 5] >> (l & 31u)) & 1u;
+        for (uint32_t a : assign_)
+            if (!owned[a]) fail(ELIPS_B200_INVALID_ARGUMENT, "rows already added on a list outside the mask");
+        DeviceGuard g(device_);
+        owned_ = DeviceBuffer(device_, n_words * 4);
+        check_cuda(cudaMemcpy(owned_.get(), words, n_words * 4, cudaMemcpyHostToDevice), ELIPS_B200_TRANSFER_FAILED,
+                   "owned lists");
+        owned_host_ = std::move(owned);
+    }
+
+    // Lists [lo, hi) only (a contiguous share).
     void set_list_range(uint32_t lo, uint32_t hi) {
         if (lo > hi || hi > nlist_) fail(ELIPS_B200_INVALID_ARGUMENT, "list range outside [0, n_lists]");
-        for (uint32_t a : assign_)
-            if (a < lo || a >= hi) fail(ELIPS_B200_INVALID_ARGUMENT, "rows already added outside the list range");
-        list_lo_ = lo;
-        list_hi_ = hi;
+        std::vector<uint32_t> words((nlist_ + 31u) / 32u, 0u);
+        for (uint32_t l = lo; l < hi; ++l) words[l >> 5] |= 1u << (l & 31u);
+        set_owned_lists(words.data(), words.size());
     }
 
 protected:
@@ -74,7 +89,7 @@ protected:
         check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_TRANSFER_FAILED, "assignment copy");
         for (uint32_t a : host_assign) {
             if (a >= nlist_) fail(ELIPS_B200_INVALID_ARGUMENT, "assignment names a list past n_lists");
-            if (a < list_lo_ || a >= list_hi_) fail(ELIPS_B200_INVALID_ARGUMENT, "assignment outside the list range");
+            if (!owned_host_[a]) fail(ELIPS_B200_INVALID_ARGUMENT, "assignment names a list this index does not own");
         }
         if (n_ + n > capacity_) {
             const size_t cap = std::max<size_t>(n_ + n, capacity_ + capacity_ / 2);
@@ -184,8 +199,8 @@ protected:
         const uint32_t* loff = static_cast<const uint32_t*>(list_off_.get());
         {
             Profiler::Scope prof("ivfpq_plan", stream, pl.npairs);
-            ivf_pair_count_kernel<<<pblocks, 256, 0, stream>>>(pl.probes, static_cast<uint32_t>(pl.npairs), list_lo_,
-                                                               list_hi_, pl.counts, pl.part, r);
+            ivf_pair_count_kernel<<<pblocks, 256, 0, stream>>>(pl.probes, static_cast<uint32_t>(pl.npairs), nlist_,
+                                                               owned_words(), pl.counts, pl.part, r);
             launch_ok("pair count kernel");
         }
         {
@@ -202,8 +217,8 @@ protected:
         }
         {
             Profiler::Scope prof("ivfpq_plan", stream, pl.npairs);
-            ivf_pair_scatter_kernel<<<pblocks, 256, 0, stream>>>(pl.probes, static_cast<uint32_t>(pl.npairs), list_lo_,
-                                                                 list_hi_, pl.list_start, cursor, pl.pairs);
+            ivf_pair_scatter_kernel<<<pblocks, 256, 0, stream>>>(pl.probes, static_cast<uint32_t>(pl.npairs), nlist_,
+                                                                 owned_words(), pl.list_start, cursor, pl.pairs);
             launch_ok("pair scatter kernel");
         }
         if (flat) {
@@ -269,7 +284,11 @@ protected:
     }
 
     int device_, metric_;
-    uint32_t dim_, nlist_, nprobe_, list_lo_ = 0, list_hi_ = 0;
+    uint32_t dim_, nlist_, nprobe_;
+    std::vector<bool> owned_host_;
+    DeviceBuffer owned_;  // empty: every list
+
+    const uint32_t* owned_words() const { return static_cast<const uint32_t*>(owned_.get()); }
     size_t n_ = 0, capacity_ = 0;
     bool dirty_ = false;
     std::vector<uint32_t> assign_;
@@ -677,6 +696,11 @@ int elips_b200_ivfpq_search_device(elips_b200_ivfpq* index, const float* queries
 int elips_b200_ivfpq_set_list_range(elips_b200_ivfpq* index, uint32_t list_lo, uint32_t list_hi) {
     if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] { index->index.set_list_range(list_lo, list_hi); });
+}
+
+int elips_b200_ivfpq_set_owned_lists(elips_b200_ivfpq* index, const uint32_t* mask_words, size_t n_words) {
+    if (index == nullptr || mask_words == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.set_owned_lists(mask_words, n_words); });
 }
 
 int elips_b200_ivfpq_search_candidates_device(elips_b200_ivfpq* index, const float* queries, size_t nq, size_t k,

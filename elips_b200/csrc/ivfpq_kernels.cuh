@@ -40,16 +40,22 @@ namespace eb {
 constexpr uint32_t kPlanThreads = 1024;
 constexpr uint32_t kPlanSortMax = 8192;  // lists visited largest first up to this many
 
-// pair = q * nprobe + p. Counts the pairs of every list this index owns
-// ([lo, hi): all lists, or one GPU's share of a list-sharded index); a pair
-// whose list is not owned gets an empty candidate list.
-static __global__ void ivf_pair_count_kernel(const uint32_t* __restrict__ probes, uint32_t npairs, uint32_t lo,
-                                             uint32_t hi, uint32_t* __restrict__ counts,
+// Whether list l (< nlist) is one this index owns: owned = null for all
+// lists, else a bitmask (bit l & 31 of word l >> 5) of one GPU's share of a
+// list-sharded index.
+__device__ __forceinline__ bool ivf_owned(const uint32_t* owned, uint32_t l, uint32_t nlist) {
+    return l < nlist && (owned == nullptr || ((owned[l >> 5] >> (l & 31u)) & 1u));
+}
+
+// pair = q * nprobe + p. Counts the pairs of every list this index owns; a
+// pair whose list is not owned gets an empty candidate list.
+static __global__ void ivf_pair_count_kernel(const uint32_t* __restrict__ probes, uint32_t npairs, uint32_t nlist,
+                                             const uint32_t* __restrict__ owned, uint32_t* __restrict__ counts,
                                              uint2* __restrict__ partial, uint32_t r) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= npairs) return;
     const uint32_t l = probes[i];
-    if (l >= lo && l < hi) {
+    if (ivf_owned(owned, l, nlist)) {
         atomicAdd(&counts[l], 1u);
         return;
     }
@@ -136,13 +142,14 @@ static __global__ void __launch_bounds__(kPlanThreads)
     }
 }
 
-static __global__ void ivf_pair_scatter_kernel(const uint32_t* __restrict__ probes, uint32_t npairs, uint32_t lo,
-                                               uint32_t hi, const uint32_t* __restrict__ list_start,
+static __global__ void ivf_pair_scatter_kernel(const uint32_t* __restrict__ probes, uint32_t npairs, uint32_t nlist,
+                                               const uint32_t* __restrict__ owned,
+                                               const uint32_t* __restrict__ list_start,
                                                uint32_t* __restrict__ cursor, uint32_t* __restrict__ pairs) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= npairs) return;
     const uint32_t l = probes[i];
-    if (l >= lo && l < hi) pairs[list_start[l] + atomicAdd(&cursor[l], 1u)] = i;
+    if (ivf_owned(owned, l, nlist)) pairs[list_start[l] + atomicAdd(&cursor[l], 1u)] = i;
 }
 
 // Gather position of each pair's first candidate: the candidates of a query

@@ -103,6 +103,23 @@ def list_range(nlist: int, rank: int, world: int) -> tuple[int, int]:
     return nlist * rank // world, nlist * (rank + 1) // world
 
 
+def balanced_lists(list_sizes, world: int) -> np.ndarray:
+    """Owner rank of every IVF list, balancing the scan work: a probed list
+    costs about its size times the queries that probe it, and queries probe
+    lists about in proportion to their size, so the weight is size^2. Greedy
+    longest-first: heaviest list to the least loaded rank (ties: lower list id,
+    lower rank). Deterministic, so every rank computes the same partition."""
+    sizes = np.asarray(list_sizes, np.float64)
+    order = np.lexsort((np.arange(sizes.size), -sizes * sizes))
+    load = np.zeros(world)
+    owner = np.empty(sizes.size, np.int64)
+    for l in order:
+        r = int(np.argmin(load))
+        owner[l] = r
+        load[r] += sizes[l] * sizes[l]
+    return owner
+
+
 def _pairs(dist, rows):
     """(dist [nq, m] float32, rows [nq, m] int64, -1 = none) -> [nq, m, 2] int32
     candidate pairs (distance bits, row)."""
@@ -116,7 +133,9 @@ class ShardedIvfPqIndex:
     here every rank holds the one global model and the ranks together answer
     exactly what a single index answers.
 
-    Rank r owns lists list_range(nlist, r, world) and only their rows. A search
+    Rank r owns the lists that `owner` (one rank per list, e.g. balanced_lists
+    of the global list sizes) gives it, by default list_range(nlist, r, world),
+    and only their rows. A search
     (every rank calls it with the same queries):
       1. each rank: probe (replicated centroids), scan its own probed lists,
          R = 4k best approximate (distance, global slot);
@@ -129,14 +148,21 @@ class ShardedIvfPqIndex:
     `exchange` defaults to exchange_candidates over the process group."""
 
     def __init__(self, metric: str, dimension: int, centroids, codebook, nprobe: int, pq_bits: int = 8,
-                 rank: int = 0, world: int = 1, device: int = 0, group=None, exchange=None):
+                 rank: int = 0, world: int = 1, device: int = 0, group=None, exchange=None, owner=None):
+        import torch
         from .ivfpq import IvfPqIndex
         self.metric, self.rank, self.world, self.group = metric, rank, world, group
         self.nlist = np.asarray(centroids).shape[0]
-        self.lo, self.hi = list_range(self.nlist, rank, world)
+        if owner is None:
+            owner = np.empty(self.nlist, np.int64)
+            for r in range(world):
+                lo, hi = list_range(self.nlist, r, world)
+                owner[lo:hi] = r
+        owned = np.asarray(owner) == rank
         self.local = IvfPqIndex(metric, dimension, centroids, codebook, nprobe=nprobe, pq_bits=pq_bits,
                                 device=device)
-        self.local.set_list_range(self.lo, self.hi)
+        self.local.set_owned_lists(owned)
+        self.owned = torch.from_numpy(owned).to(f"cuda:{device}")
         self.global_rows = None  # int64 device tensor, ascending: local slot -> global slot
         self.exchange = exchange if exchange is not None else (
             lambda t: exchange_candidates(t, self.world, self.group))
@@ -145,8 +171,7 @@ class ShardedIvfPqIndex:
         """Offers rows [first_row, first_row + n) in global order (CUDA tensors;
         assignments int32); this rank keeps those of its own lists."""
         import torch
-        a = assignments.long()
-        idx = torch.nonzero((a >= self.lo) & (a < self.hi)).flatten()
+        idx = torch.nonzero(self.owned[assignments.long()]).flatten()
         if idx.numel() == 0:
             return
         self.local.add_device(vectors[idx].contiguous(), assignments[idx].contiguous(),

@@ -71,6 +71,15 @@ class IvfPqIndex:
         capi.check(capi.LIB.elips_b200_ivfpq_set_list_range(self._h, int(lo), int(hi)),
                    "elips_b200_ivfpq_set_list_range")
 
+    def set_owned_lists(self, owned) -> None:
+        """Own only the lists where `owned` (bool array [n_lists]) is true."""
+        owned = np.asarray(owned, bool)
+        words = np.zeros((self.n_lists + 31) // 32, np.uint32)
+        idx = np.nonzero(owned)[0]
+        np.bitwise_or.at(words, idx >> 5, (np.uint32(1) << (idx & 31).astype(np.uint32)))
+        capi.check(capi.LIB.elips_b200_ivfpq_set_owned_lists(self._h, _ptr(words), words.size),
+                   "elips_b200_ivfpq_set_owned_lists")
+
     def search_candidates_device(self, queries, k: int, out=None, stream=None):
         """The approximate stage: [nq, 4k, 2] int32 (distance bits, slot), ascending."""
         import torch

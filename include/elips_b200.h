@@ -289,6 +289,11 @@ ELIPS_B200_API int elips_b200_ivfpq_codes_device(const elips_b200_ivfpq* index, 
 ELIPS_B200_API int elips_b200_ivfpq_set_list_range(elips_b200_ivfpq* index, uint32_t list_lo,
                                                    uint32_t list_hi);
 
+/* The same with any set of lists: bit (l & 31) of mask_words[l >> 5] set =
+ * list l owned; n_words = ceil(n_lists / 32), HOST, copied. */
+ELIPS_B200_API int elips_b200_ivfpq_set_owned_lists(elips_b200_ivfpq* index, const uint32_t* mask_words,
+                                                    size_t n_words);
+
 /* The approximate stage of search (probe, scan, merge): the R = 4k best
  * {approximate distance bits, slot} per query over the owned probed lists,
  * ascending by (distance, slot), padded with {+inf, 0xFFFFFFFF}; out_cand is

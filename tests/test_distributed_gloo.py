@@ -124,3 +124,15 @@ def test_absent_rank_fails_the_exchange_instead_of_hanging(tmp_path):
         if p.is_alive():
             p.kill()
     assert (tmp_path / "rank0.txt").read_text().startswith("error")
+
+
+def test_balanced_lists_partition():
+    from elips_b200.distributed import balanced_lists
+    rng = np.random.default_rng(5)
+    sizes = rng.integers(0, 5000, 4096)
+    for world in (1, 2, 3, 8):
+        owner = balanced_lists(sizes, world)
+        assert owner.shape == sizes.shape and set(owner.tolist()) <= set(range(world))
+        load = np.bincount(owner, weights=sizes.astype(float) ** 2, minlength=world)
+        assert load.max() <= load.mean() + (sizes.astype(float) ** 2).max()
+        assert np.array_equal(owner, balanced_lists(sizes, world))

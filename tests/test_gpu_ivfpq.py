@@ -115,9 +115,9 @@ def test_ivfpq_rejects_bad_assignment(model):
     assert ix.size() == 0
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world,balanced", [(2, False), (3, False), (3, True)])
 @pytest.mark.parametrize("metric", ["euclidean", "dot_product"])
-def test_list_sharded_search_equals_single_index(model, world, metric):
+def test_list_sharded_search_equals_single_index(model, world, balanced, metric):
     """List-sharded IVF-PQ (one rank per list range), its ranks driven phase by
     phase in one process on one GPU: the result equals the single index's."""
     import torch
@@ -136,7 +136,10 @@ def test_list_sharded_search_equals_single_index(model, world, metric):
     d_ref, r_ref = single.search_batch(q, k)
     vd, ad, cd = (torch.from_numpy(base).cuda(), torch.from_numpy(asg.view(np.int32)).cuda(),
                   torch.from_numpy(codes).cuda())
-    ranks = [ShardedIvfPqIndex(metric, 64, m["cent"], m["cb"], nprobe, rank=r, world=world) for r in range(world)]
+    from elips_b200.distributed import balanced_lists
+    owner = balanced_lists(np.bincount(asg, minlength=len(m["cent"])), world) if balanced else None
+    ranks = [ShardedIvfPqIndex(metric, 64, m["cent"], m["cb"], nprobe, rank=r, world=world, owner=owner)
+             for r in range(world)]
     for ix in ranks:
         for r0 in range(0, len(base), 25_000):  # rows offered in global order, in batches
             ix.add_device(vd[r0:r0 + 25_000], ad[r0:r0 + 25_000], r0, cd[r0:r0 + 25_000])
