@@ -634,6 +634,8 @@ def run_b200(args, cfg, world, rank, local):
         "frac": round(achieved / peak, 4), "traffic": load_traffic(args.config, n_shard),
         "kernel": "exact_topk_kernel", "kernel_ms_avg": round(avg_kernel_ms, 4),
         "kernel_share_of_step": round(kstats["total_ms"] / max(1e-9, allstats["total_ms"]), 4),
+        "per_kernel_ms_per_step": {name: round(_capi.profiler_stats(name)["total_ms"] / args.steps, 4)
+                                   for name in ("exact_topk", "merge_topk", "prep_rows")},
         "algorithmic_flops_per_launch": flops, "algorithmic_bytes_per_launch": bytes_alg,
         "hbm_time_ms_at_peak": round(bytes_alg / (peaks["hbm_gbs"] * 1e9) * 1e3, 4),
         "peak_source": peak_note}

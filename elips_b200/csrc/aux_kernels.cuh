@@ -64,52 +64,35 @@ __global__ void prep_rows_i8_kernel(const int8_t* __restrict__ in, uint64_t rows
     out[i] = j < d ? in[r * d + j] : int8_t(0);
 }
 
-// Final top-k per query: one warp selects the k smallest (key, row) pairs
-// among `lists` candidate lists of length k and writes them sorted.
-// List l of query q starts at cand + q*stride_q + l*stride_l (entries).
-// Composite 64-bit keys (ordered key << 32 | row) are unique, so an 8-pass
-// radix select finds the exact k-th and a bitonic sort orders the survivors.
-// Dynamic smem per warp: 256 words of histogram + kpow2 u64 sort buffer.
-__global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, uint32_t lists,
-                                  uint32_t k, uint64_t stride_q, uint64_t stride_l, uint32_t kpow2,
-                                  int metric, float* __restrict__ out_dist,
-                                  int64_t* __restrict__ out_rows, uint2* __restrict__ out_cand) {
-    extern __shared__ uint8_t smem[];
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t warps = blockDim.x >> 5;
-    uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + warp * 256u;
-    unsigned long long* buf =
-        reinterpret_cast<unsigned long long*>(smem + warps * 1024u) + static_cast<size_t>(warp) * kpow2;
-    const uint32_t q = blockIdx.x * warps + warp;
-    if (q >= nq) return;
-    const uint32_t count = lists * k;
-    auto composite = [&](uint32_t idx) -> unsigned long long {
-        const uint32_t l = idx / k, i = idx - l * k;
-        const uint2 e = cand[q * stride_q + l * stride_l + i];
-        return (static_cast<unsigned long long>(ordered_key(__uint_as_float(e.x))) << 32) | e.y;
-    };
-    const uint32_t take = min(k, count);
-    if (take == 0) {
-        for (uint32_t i = lane; i < k; i += 32) {
-            if (out_dist != nullptr) {
-                out_dist[static_cast<size_t>(q) * k + i] = __int_as_float(0x7f800000);
-                out_rows[static_cast<size_t>(q) * k + i] = -1;
-            }
-            if (out_cand != nullptr) out_cand[static_cast<size_t>(q) * k + i] = make_uint2(0x7f800000u, 0xFFFFFFFFu);
-        }
-        return;
-    }
-    // radix select the take-th smallest composite
-    unsigned long long prefix = 0, pmask = 0;
-    uint32_t rank = take;
+// Radix select, 8 bits per pass, over n composites read by get(j): finds
+// the group of the rank-th smallest (1-based) among those whose bits under
+// `pmask` equal `prefix` (pass the common high bits in, zero for none).
+// Passes start at byte `first` (0 = the top byte); selection stops as soon as
+// the chosen bin holds exactly the remaining rank, so on return the selected
+// elements are: every composite with (c & pmask) < prefix, and of those with
+// (c & pmask) == prefix, `rank` in any order (all of them when it stopped
+// early; copies of one value otherwise). One warp; hist = its 256 words.
+template <class Get>
+__device__ __forceinline__ void warp_radix_select(Get get, uint32_t n, uint32_t& rank, unsigned long long& prefix,
+                                                  unsigned long long& pmask, int first, uint32_t* hist) {
+    const uint32_t lane = threadIdx.x & 31u;
 #pragma unroll 1
-    for (int pass = 0; pass < 8; ++pass) {
+    for (int pass = first; pass < 8; ++pass) {
         const uint32_t shift = 56u - 8u * static_cast<uint32_t>(pass);
         for (uint32_t b = lane; b < 256; b += 32) hist[b] = 0;
         __syncwarp();
-        for (uint32_t j = lane; j < count; j += 32) {
-            const unsigned long long c = composite(j);
-            if ((c & pmask) == prefix) atomicAdd(&hist[(c >> shift) & 255u], 1u);
+        for (uint32_t j0 = 0; j0 < n; j0 += 128) {
+            unsigned long long c[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t j = j0 + u * 32 + lane;
+                c[u] = j < n ? get(j) : 0ull;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t j = j0 + u * 32 + lane;
+                if (j < n && (c[u] & pmask) == prefix) atomicAdd(&hist[(c[u] >> shift) & 255u], 1u);
+            }
         }
         __syncwarp();
         uint32_t bins[8], local = 0;
@@ -126,7 +109,7 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
         }
         const uint32_t excl = incl - local;
         const bool mine = excl < rank && rank <= incl;
-        uint32_t digit = 0, before = excl;
+        uint32_t digit = 0, before = excl, inbin = 0;
         if (mine) {
             uint32_t acc = excl;
 #pragma unroll
@@ -134,6 +117,7 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
                 if (acc + bins[i] >= rank) {
                     digit = lane * 8 + i;
                     before = acc;
+                    inbin = bins[i];
                     break;
                 }
                 acc += bins[i];
@@ -142,38 +126,21 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
         const uint32_t owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
         digit = __shfl_sync(0xffffffffu, digit, owner);
         before = __shfl_sync(0xffffffffu, before, owner);
+        inbin = __shfl_sync(0xffffffffu, inbin, owner);
         rank -= before;
         prefix |= static_cast<unsigned long long>(digit) << shift;
         pmask |= 255ull << shift;
         __syncwarp();
+        if (inbin == rank) break;  // the whole bin is selected
     }
-    // Gather the survivors: every composite below the take-th, then copies of
-    // the take-th itself up to `take` in total (only the padding composite
-    // can repeat, so the surplus copies are interchangeable).
-    const uint32_t lt = lanemask_lt();
-    uint32_t w = 0;
-    for (uint32_t j0 = 0; j0 < count; j0 += 32) {
-        const uint32_t j = j0 + lane;
-        const unsigned long long c = j < count ? composite(j) : ~0ull;
-        const bool keep = j < count && c < prefix;
-        const uint32_t m = __ballot_sync(0xffffffffu, keep);
-        if (keep) buf[w + __popc(m & lt)] = c;
-        w += __popc(m);
-    }
-    for (uint32_t j0 = 0; j0 < count && w < take; j0 += 32) {
-        const uint32_t j = j0 + lane;
-        const unsigned long long c = j < count ? composite(j) : ~0ull;
-        const bool eq = j < count && c == prefix;
-        const uint32_t m = __ballot_sync(0xffffffffu, eq);
-        const uint32_t pos = w + __popc(m & lt);
-        if (eq && pos < take) buf[pos] = c;
-        w = min(take, w + __popc(m));
-    }
-    for (uint32_t i = w + lane; i < kpow2; i += 32) buf[i] = ~0ull;
-    __syncwarp();
-    for (uint32_t size = 2; size <= kpow2; size <<= 1) {
+}
+
+// Ascending bitonic sort of n (power of two) composites by one warp.
+__device__ __forceinline__ void warp_bitonic_sort(unsigned long long* buf, uint32_t n) {
+    const uint32_t lane = threadIdx.x & 31u;
+    for (uint32_t size = 2; size <= n; size <<= 1) {
         for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-            for (uint32_t i = lane; i < kpow2; i += 32) {
+            for (uint32_t i = lane; i < n; i += 32) {
                 const uint32_t j = i ^ stride;
                 if (j > i) {
                     const unsigned long long a = buf[i], b = buf[j];
@@ -187,8 +154,101 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
             __syncwarp();
         }
     }
+}
+
+// Final top-k per query: one warp selects the k smallest (key, row) pairs
+// among `lists` candidate lists of length k and writes them sorted.
+// List l of query q starts at cand + q*stride_q + l*stride_l (entries).
+// Composite 64-bit keys (ordered key << 32 | row) are unique except the
+// padding {+inf, 0xFFFFFFFF}. A first pass finds the leading bits shared by
+// all real candidates (the keys of one query's candidates are close, so the
+// top byte or two agree), the radix select starts below them and stops once
+// a bin is taken whole; the survivors are then gathered and sorted.
+// Dynamic smem per warp: 256 words of histogram + kpow2 u64 sort buffer.
+__global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, uint32_t lists,
+                                  uint32_t k, uint64_t stride_q, uint64_t stride_l, uint32_t kpow2,
+                                  int metric, float* __restrict__ out_dist,
+                                  int64_t* __restrict__ out_rows, uint2* __restrict__ out_cand) {
+    extern __shared__ uint8_t smem[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t warps = blockDim.x >> 5;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + warp * 256u;
+    unsigned long long* buf =
+        reinterpret_cast<unsigned long long*>(smem + warps * 1024u) + static_cast<size_t>(warp) * kpow2;
+    const uint32_t q = blockIdx.x * warps + warp;
+    if (q >= nq) return;
+    const uint32_t count = lists * k;
+    const uint32_t lt = lanemask_lt();
+    auto composite = [&](uint32_t idx) -> unsigned long long {
+        const uint32_t l = idx / k, i = idx - l * k;
+        const uint2 e = cand[q * stride_q + l * stride_l + i];
+        return (static_cast<unsigned long long>(ordered_key(__uint_as_float(e.x))) << 32) | e.y;
+    };
+    const uint32_t take = min(k, count);
+    uint32_t w = 0;
+    if (take > 0) {
+        // the real candidates: how many, and the high bits they all share
+        uint32_t real = 0;
+        unsigned long long first_c = 0, diff = 0;
+        bool have = false;
+        for (uint32_t j0 = 0; j0 < count; j0 += 128) {
+            unsigned long long c[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t j = j0 + u * 32 + lane;
+                c[u] = j < count ? composite(j) : ~0ull;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const bool is_real = (c[u] & 0xFFFFFFFFull) != 0xFFFFFFFFull;
+                const uint32_t m = __ballot_sync(0xffffffffu, is_real);
+                real += __popc(m);
+                if (m != 0 && !have) {
+                    first_c = __shfl_sync(0xffffffffu, c[u], __ffs(m) - 1);
+                    have = true;
+                }
+                if (is_real) diff |= c[u] ^ first_c;
+            }
+        }
+        unsigned long long prefix = 0, pmask = 0;
+        uint32_t rank = take;
+        int first = 0;
+        if (real >= take) {
+            // select among the real ones only: start below their common bits
+            diff = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(diff >> 32)) * (1ull << 32) |
+                   __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(diff));
+            const int top = diff == 0 ? 0 : 63 - __clzll(static_cast<long long>(diff));
+            first = (63 - top) / 8;
+            pmask = first == 0 ? 0ull : ~0ull << (64 - 8 * first);
+            prefix = first_c & pmask;
+        }
+        warp_radix_select(composite, count, rank, prefix, pmask, first, hist);
+        // every composite below the selected group, then `rank` of the group
+        for (uint32_t j0 = 0; j0 < count; j0 += 32) {
+            const uint32_t j = j0 + lane;
+            const unsigned long long c = j < count ? composite(j) : ~0ull;
+            const bool keep = j < count && (c & pmask) < prefix &&
+                              (real < take || (c & 0xFFFFFFFFull) != 0xFFFFFFFFull);
+            const uint32_t m = __ballot_sync(0xffffffffu, keep);
+            if (keep) buf[w + __popc(m & lt)] = c;
+            w += __popc(m);
+        }
+        const uint32_t target = w + rank;
+        for (uint32_t j0 = 0; j0 < count && w < target; j0 += 32) {
+            const uint32_t j = j0 + lane;
+            const unsigned long long c = j < count ? composite(j) : ~0ull;
+            const bool eq = j < count && (c & pmask) == prefix;
+            const uint32_t m = __ballot_sync(0xffffffffu, eq);
+            const uint32_t pos = w + __popc(m & lt);
+            if (eq && pos < target) buf[pos] = c;
+            w = min(target, w + __popc(m));
+        }
+    }
+    for (uint32_t i = w + lane; i < kpow2; i += 32) buf[i] = ~0ull;
+    __syncwarp();
+    warp_bitonic_sort(buf, kpow2);
     for (uint32_t i = lane; i < k; i += 32) {
-        const unsigned long long c = i < take ? buf[i] : ~0ull;
+        const unsigned long long c = i < w ? buf[i] : ~0ull;
         const uint32_t row = static_cast<uint32_t>(c & 0xFFFFFFFFull);
         const float key = key_to_float(static_cast<uint32_t>(c >> 32));
         const bool valid = row != 0xFFFFFFFFu;

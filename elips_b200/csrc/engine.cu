@@ -510,7 +510,6 @@ void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists
                       int64_t* out_rows, uint2* out_cand, cudaStream_t stream) {
     if (nq == 0 || k == 0) return;
     if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
-    (void)device;
     uint32_t kpow2 = 1;
     while (kpow2 < k) kpow2 <<= 1;
     constexpr uint32_t warps = 4;
