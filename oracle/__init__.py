@@ -227,6 +227,40 @@ def kmeans(rows, k, iters):
     return cent
 
 
+def ivf_train(metric, rows, nlist, iters):
+    """IvfIndexState::train_centroids then the final assignment (C restatement)."""
+    rows = _f32(rows)
+    n, d = rows.shape
+    cent = np.empty((nlist, d), np.float32)
+    asg = np.empty(n, np.uint32)
+    orc().orc_ivf_train(METRIC[metric], _p(rows), c_size_t(n), c_size_t(d), c_size_t(nlist), c_size_t(iters),
+                        _p(cent), _p(asg))
+    return cent, asg
+
+
+def ref_ivf_train(metric, rows, nlist, iters):
+    """The same through the reference's GpuIVFFlatIndex::build_from_batch."""
+    rows = _f32(rows)
+    n, d = rows.shape
+    cent = np.empty((nlist, d), np.float32)
+    asg = np.empty(n, np.uint32)
+    rc = ref().ref_ivf_train(METRIC[metric], c_uint32(d), _p(rows), c_size_t(n), c_size_t(nlist), c_size_t(iters),
+                             _p(cent), _p(asg))
+    if rc != 0:
+        raise RuntimeError(f"reference IVF training failed ({rc})")
+    return cent, asg
+
+
+def train_pq_codebook(rows, m, ksub, iters):
+    """train_pq_codebook (C restatement): codebook [m][ksub][d/m]."""
+    rows = _f32(rows)
+    n, d = rows.shape
+    cb = np.empty((m, ksub, d // m), np.float32)
+    orc().orc_train_pq_codebook(_p(rows), c_size_t(n), c_size_t(d), c_size_t(m), c_size_t(ksub), c_size_t(iters),
+                                _p(cb))
+    return cb
+
+
 def ivf_assign(metric, rows, centroids):
     rows, centroids = _f32(rows), _f32(centroids)
     out = np.empty(rows.shape[0], np.uint32)

@@ -509,6 +509,69 @@ void orc_ivf_assign(int metric, const float* rows, size_t n, size_t d, const flo
 
 /* IvfIndexState::probe_lists, IvfIndexState.cpp:395-423: distances to every
  * centroid, then the nprobe smallest (ties by list id). */
+/* IvfIndexState::train_centroids (IvfIndexState.cpp:118-165): strided seeds
+ * (min(n-1, list*stride)), max(1, iters) Lloyd rounds with no early stop:
+ * assign by elips::distance (strict '<', lowest list wins, :167-191), sums in
+ * row order, centroid = sum / count (division), an empty list reseeded from
+ * row min(n-1, list % n), then normalize_if_needed (cosine: divide by the
+ * sequential magnitude when it is > 0, :20-35). Then the final assignment. */
+void orc_ivf_train(int metric, const float* rows, size_t n, size_t d, size_t nlist, size_t iters,
+                   float* cent, uint32_t* assign) {
+    if (n == 0 || d == 0 || nlist == 0) return;
+    const size_t stride = (n / nlist) > 1 ? (n / nlist) : 1;
+    for (size_t l = 0; l < nlist; ++l) {
+        size_t sample = l * stride;
+        if (sample > n - 1) sample = n - 1;
+        memcpy(cent + l * d, rows + sample * d, sizeof(float) * d);
+    }
+    float* sums = (float*)malloc(sizeof(float) * nlist * d);
+    size_t* counts = (size_t*)malloc(sizeof(size_t) * nlist);
+    const size_t rounds = iters > 0 ? iters : 1;
+    for (size_t it = 0; it < rounds; ++it) {
+        orc_ivf_assign(metric, rows, n, d, cent, nlist, assign);
+        memset(sums, 0, sizeof(float) * nlist * d);
+        memset(counts, 0, sizeof(size_t) * nlist);
+        for (size_t r = 0; r < n; ++r) {
+            const uint32_t l = assign[r];
+            ++counts[l];
+            for (size_t i = 0; i < d; ++i) sums[l * d + i] += rows[r * d + i];
+        }
+        for (size_t l = 0; l < nlist; ++l) {
+            float* c = cent + l * d;
+            if (counts[l] == 0) {
+                size_t fb = l % n;
+                if (fb > n - 1) fb = n - 1;
+                memcpy(c, rows + fb * d, sizeof(float) * d);
+            } else {
+                for (size_t i = 0; i < d; ++i) c[i] = sums[l * d + i] / (float)counts[l];
+            }
+            if (metric == ORC_COSINE) {
+                float norm = 0.0f;
+                for (size_t i = 0; i < d; ++i) norm += c[i] * c[i];
+                norm = sqrtf(norm);
+                if (norm > 0.0f)
+                    for (size_t i = 0; i < d; ++i) c[i] /= norm;
+            }
+        }
+    }
+    orc_ivf_assign(metric, rows, n, d, cent, nlist, assign);
+    free(sums); free(counts);
+}
+
+/* train_pq_codebook, KMeans.cpp:249-268: each subspace gathered into dense
+ * rows, then kmeans (codebook [m][ksub][sub]). */
+void orc_train_pq_codebook(const float* rows, size_t n, size_t d, size_t m, size_t ksub, size_t iters,
+                           float* codebook) {
+    if (n == 0 || m == 0 || d == 0 || d % m != 0 || ksub == 0) return;
+    const size_t sub = d / m;
+    float* scratch = (float*)malloc(sizeof(float) * n * sub);
+    for (size_t s = 0; s < m; ++s) {
+        for (size_t r = 0; r < n; ++r) memcpy(scratch + r * sub, rows + r * d + s * sub, sizeof(float) * sub);
+        orc_kmeans(scratch, n, sub, ksub, iters, codebook + s * ksub * sub);
+    }
+    free(scratch);
+}
+
 void orc_ivf_probe(int metric, const float* query, size_t d, const float* centroids, size_t nlist,
                    size_t nprobe, uint32_t* out_lists, float* out_dist) {
     hit_t* scratch = (hit_t*)malloc(sizeof(hit_t) * (nprobe ? nprobe : 1));

@@ -326,6 +326,29 @@ void ref_encode_pq(const float* rows, const float* codebook, size_t n, size_t di
         std::span<std::uint8_t>{codes_out, n * pq_dim});
 }
 
+// IvfIndexState::train_centroids + assign_vectors_to_centroids, run by
+// GpuIVFFlatIndex::build_from_batch on the CPU port and read back through
+// export_snapshot (IvfIndexState.cpp:118-208, 328-337).
+int ref_ivf_train(int metric, uint32_t dim, const float* rows, size_t n, size_t n_lists, size_t iters,
+                  float* centroids_out, uint32_t* assignments_out) {
+    CpuPort port;
+    elips::gpu::GpuConfig config;
+    config.ivf_pq_params.n_lists = n_lists;
+    config.ivf_pq_params.kmeans_n_iters = iters;
+    elips::gpu::GpuIVFFlatIndex index(port, static_cast<Metric>(metric), static_cast<std::uint16_t>(dim), config);
+    std::vector<RecordID> ids;
+    ids.reserve(n);
+    for (size_t i = 0; i < n; ++i) ids.push_back(row_id(i));
+    if (!index.build_from_batch(std::span<const float>{rows, n * dim}, ids, {}).has_value()) return 1;
+    const auto snap = index.export_snapshot();
+    if (!snap.has_value() || !snap->ivf.has_value()) return 2;
+    const auto& ivf = *snap->ivf;
+    if (ivf.centroids.size() != n_lists * dim || ivf.assignments.size() != n) return 3;
+    std::copy(ivf.centroids.begin(), ivf.centroids.end(), centroids_out);
+    std::copy(ivf.assignments.begin(), ivf.assignments.end(), assignments_out);
+    return 0;
+}
+
 // quant::detail::kmeans (KMeans.cpp:182-247).
 void ref_kmeans(const float* rows, size_t n, size_t dim, size_t k, size_t iters,
                 float* centroids_out) {

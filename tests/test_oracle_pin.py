@@ -133,3 +133,23 @@ def test_normalize_matches_reference():
     x[6, :] = 0.0
     x[6, 3] = -0.0
     assert np.array_equal(O.normalize_rows(x).view(np.uint32), O.ref_normalize_rows(x).view(np.uint32))
+
+
+@pytest.mark.parametrize("metric", METRICS)
+def test_ivf_train_matches_reference(metric):
+    """IvfIndexState::train_centroids + final assignment, restated vs the
+    reference's own (GpuIVFFlatIndex::build_from_batch), bit-exact."""
+    cents = H.gaussian(24, 16, seed=101)
+    rows = H.mixture(3000, 16, cents, 0.3, seed=102)
+    if metric == "cosine":
+        rows = H.normalize(rows)
+    c1, a1 = O.ivf_train(metric, rows, 24, 5)
+    c2, a2 = O.ref_ivf_train(metric, rows, 24, 5)
+    assert np.array_equal(c1.view(np.uint32), c2.view(np.uint32)) and np.array_equal(a1, a2)
+
+
+def test_train_pq_codebook_matches_reference():
+    rows = H.gaussian(4000, 24, seed=103)
+    c1 = O.train_pq_codebook(rows, 3, 32, 10)
+    c2 = O.ref_train_pq_codebook(rows, 3, 32, 10)
+    assert np.array_equal(c1.view(np.uint32), c2.view(np.uint32))
