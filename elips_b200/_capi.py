@@ -72,6 +72,16 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
     ("elips_b200_quant_destroy", c_int, [c_void_p]),
     ("elips_b200_normalize_rows", c_int, [c_int, c_void_p, c_void_p, c_size_t, c_size_t, c_int, c_void_p]),
+    ("elips_b200_kmeans", c_int, [c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p, c_int, c_void_p]),
+    ("elips_b200_train_pq_codebook", c_int,
+     [c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p, c_int, c_void_p]),
+    ("elips_b200_ivf_assign", c_int,
+     [c_int, c_int, c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_int, c_void_p]),
+    ("elips_b200_ivf_train", c_int,
+     [c_int, c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p, c_void_p, c_int, c_void_p]),
+    ("elips_b200_ivfpq_train", c_int,
+     [c_int, c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_size_t, c_uint32, c_void_p, c_void_p,
+      c_void_p, c_void_p, c_int, c_void_p]),
     ("elips_b200_ivfpq_create", c_int,
      [c_int, c_int, c_uint32, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, POINTER(c_void_p)]),
     ("elips_b200_ivfpq_add", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t]),

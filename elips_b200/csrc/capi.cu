@@ -5,6 +5,7 @@
 
 #include "../../include/elips_b200.h"
 #include "engine.cuh"
+#include "capi_util.cuh"
 #include "profiler.cuh"
 
 struct elips_b200_exact {
@@ -13,20 +14,7 @@ struct elips_b200_exact {
 
 namespace {
 
-template <class Fn>
-int guarded(Fn&& fn) {
-    try {
-        fn();
-        return ELIPS_B200_OK;
-    } catch (const eb::Error& e) {
-        std::fprintf(stderr, "elips_b200: %s\n", e.what.c_str());
-        return e.code;
-    } catch (const std::bad_alloc&) {
-        return ELIPS_B200_INSUFFICIENT_MEMORY;
-    } catch (...) {
-        return ELIPS_B200_KERNEL_LAUNCH_FAILED;
-    }
-}
+using eb::guarded;
 
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 

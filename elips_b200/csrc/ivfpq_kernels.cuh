@@ -266,7 +266,7 @@ struct IvfGroupParams {
 // Reduces buf[0, n) (n > r) in place to its r smallest composites
 // (ordered key << 32 | slot; unique, slots are unique) and returns the
 // ordered key of the r-th. One warp; hist is 256 words of its own.
-__device__ __noinline__ uint32_t warp_select_compact(uint2* buf, uint32_t n, uint32_t r, uint32_t* hist) {
+static __device__ __noinline__ uint32_t warp_select_compact(uint2* buf, uint32_t n, uint32_t r, uint32_t* hist) {
     const uint32_t lane = threadIdx.x & 31u;
     unsigned long long prefix = 0, pmask = 0;
     uint32_t rank = r;
@@ -441,7 +441,7 @@ __device__ __forceinline__ uint32_t group_z(int metric, float sum) {
 // search over the z values of non-NaN sums (L2 sums are never below +0):
 // [ordered(+0), ordered(+inf)] for L2, [~ordered(+inf), ~ordered(-inf)] for
 // the inner products. 0xFFFFFFFF when no finite or infinite sum reaches T.
-__device__ __noinline__ uint32_t warp_sum_bound(uint32_t T, int metric) {
+static __device__ __noinline__ uint32_t warp_sum_bound(uint32_t T, int metric) {
     const uint32_t lane = threadIdx.x & 31u;
     auto reaches = [&](uint64_t z) {
         const uint32_t o = metric == kMetricL2 ? static_cast<uint32_t>(z) : ~static_cast<uint32_t>(z);

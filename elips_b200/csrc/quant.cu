@@ -9,6 +9,7 @@
 
 #include "../../include/elips_b200.h"
 #include "engine.cuh"
+#include "capi_util.cuh"
 #include "profiler.cuh"
 #include "scan_kernels.cuh"
 
@@ -351,31 +352,11 @@ struct elips_b200_quant {
 
 namespace {
 
-template <class Fn>
-int guarded(Fn&& fn) {
-    try {
-        fn();
-        return ELIPS_B200_OK;
-    } catch (const eb::Error& e) {
-        std::fprintf(stderr, "elips_b200: %s\n", e.what.c_str());
-        return e.code;
-    } catch (const std::bad_alloc&) {
-        return ELIPS_B200_INSUFFICIENT_MEMORY;
-    } catch (...) {
-        return ELIPS_B200_KERNEL_LAUNCH_FAILED;
-    }
-}
+using eb::guarded;
 
 size_t align_up(size_t x) { return (x + 255) / 256 * 256; }
 
-struct OwnedStream {
-    cudaStream_t s = nullptr;
-    OwnedStream() {
-        eb::check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), ELIPS_B200_INITIALIZATION_FAILED,
-                       "cudaStreamCreate");
-    }
-    ~OwnedStream() { cudaStreamDestroy(s); }
-};
+using eb::OwnedStream;
 
 }  // namespace
 

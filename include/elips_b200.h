@@ -355,6 +355,51 @@ ELIPS_B200_API int elips_b200_ivfflat_search_device(elips_b200_ivfflat* index, c
 
 ELIPS_B200_API int elips_b200_ivfflat_destroy(elips_b200_ivfflat* index);
 
+/* ----------------------------------------------------------- index build */
+/* Trainers, bit-identical to the reference's CPU loops (sequential fp32 sums,
+ * strict '<' argmin with the lowest index kept). Host pointers unless
+ * pointers_on_device is nonzero (then device pointers on `stream`). */
+
+/* quant::detail::kmeans (src/quant_engine/KMeans.cpp:182-247): `k` centroids
+ * [k][dim] of `rows` [n][dim], seeded from rows min(n-1, c*max(1,n/k)),
+ * squared-L2 Lloyd rounds, at most `iters`, stopping once none moved. */
+ELIPS_B200_API int elips_b200_kmeans(int device, const float* rows, size_t n, size_t dim, size_t k,
+                                     size_t iters, float* centroids_out, int pointers_on_device,
+                                     void* stream);
+
+/* quant::detail::train_pq_codebook (KMeans.cpp:249-268), as called by
+ * GpuQuantizationPipeline::train_pq_codebook (GpuQuantizationPipeline.cpp:
+ * 17-33, iters = 10): one kmeans per subspace; codebook [pq_dim][ksub][dim/pq_dim]. */
+ELIPS_B200_API int elips_b200_train_pq_codebook(int device, const float* rows, size_t n, size_t dim,
+                                                size_t pq_dim, size_t ksub, size_t iters,
+                                                float* codebook_out, int pointers_on_device,
+                                                void* stream);
+
+/* IvfIndexState::assign_vectors_to_centroids (src/gpu_engine/detail/
+ * IvfIndexState.cpp:167-191): nearest list of every row by elips::distance. */
+ELIPS_B200_API int elips_b200_ivf_assign(int device, int metric, const float* rows, size_t n,
+                                         size_t dim, const float* centroids, size_t n_lists,
+                                         uint32_t* assignments_out, int pointers_on_device,
+                                         void* stream);
+
+/* IvfIndexState::train_centroids + the final assignment (IvfIndexState.cpp:
+ * 118-165, 193-208): max(1, iters) rounds; cosine centroids normalised.
+ * n_lists in [1, n] (rebuild_from_current_data passes max(1, min(requested, n)));
+ * assignments_out may be NULL. */
+ELIPS_B200_API int elips_b200_ivf_train(int device, int metric, const float* rows, size_t n, size_t dim,
+                                        size_t n_lists, size_t iters, float* centroids_out,
+                                        uint32_t* assignments_out, int pointers_on_device,
+                                        void* stream);
+
+/* GpuIVFPQIndex's model build: ivf_train, residuals v - centroid, the PQ
+ * codebook of the residuals (10 rounds, ksub = 1 << pq_bits) and the residual
+ * codes [n][pq_dim] (GpuIVFPQIndex.cpp:88-131). codes_out may be NULL. */
+ELIPS_B200_API int elips_b200_ivfpq_train(int device, int metric, const float* rows, size_t n,
+                                          size_t dim, size_t n_lists, size_t iters, size_t pq_dim,
+                                          uint32_t pq_bits, float* centroids_out,
+                                          uint32_t* assignments_out, float* codebook_out,
+                                          uint8_t* codes_out, int pointers_on_device, void* stream);
+
 /* ------------------------------------------------------------ profiling */
 /* Device-side counterpart of GpuProfiler (src/gpu_engine/GpuProfiler.cpp:
  * 5-23) and GpuConfig::enable_profiling (GpuConfig.hpp:83): while enabled,

@@ -549,7 +549,7 @@ void orc_ivf_train(int metric, const float* rows, size_t n, size_t d, size_t nli
                 float norm = 0.0f;
                 for (size_t i = 0; i < d; ++i) norm += c[i] * c[i];
                 norm = sqrtf(norm);
-                if (norm > 0.0f)
+                if (!(norm <= 0.0f))
                     for (size_t i = 0; i < d; ++i) c[i] /= norm;
             }
         }
