@@ -55,7 +55,7 @@ CONFIGS = {
                  "(k-means), PQ 16 x 8 bits on residuals, nprobe=32, Q=10,000, k=10",
         n=10_000_000, d=128, q=10_000, k=10, metric="euclidean", precision="fp32", data="mixture",
         centroids=4096, sigma=0.2, normalized=False, nlist=4096, pq_dim=16, pq_bits=8, nprobe=32,
-        kmeans_iters=4, pq_train_rows=262_144, pq_iters=6, dtype="f32 (u8 PQ codes)"),
+        kmeans_iters=4, dtype="f32 (u8 PQ codes)"),
 }
 DEFAULT_CONFIG = "exact_fp16_cosine"
 METRIC_NAME = "k-NN queries/sec (exact d=768 N=2M k=100; IVF-PQ) at 1/2/4/8 B200, % roofline"
@@ -241,62 +241,35 @@ def load_traffic(config: str, n_shard: int):
 
 # ------------------------------------------------- IVF-PQ model (setup)
 
-def _nearest(x, c, chunk=131072):
-    """Index of the nearest row of c (squared L2) for every row of x (torch)."""
-    import torch
-    cn = (c * c).sum(1)
-    out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
-    for i in range(0, x.shape[0], chunk):
-        xb = x[i:i + chunk]
-        out[i:i + chunk] = (cn[None, :] - 2.0 * (xb @ c.T)).argmin(1)
-    return out
-
-
 def _nearest_k(x, c, k):
     cn = (c * c).sum(1)
     return (cn[None, :] - 2.0 * (x @ c.T)).topk(k, dim=1, largest=False).indices
 
 
-def _lloyd(x, init, iters):
-    import torch
-    c = init.clone()
-    for _ in range(iters):
-        a = _nearest(x, c)
-        sums = torch.zeros_like(c).index_add_(0, a, x)
-        cnt = torch.bincount(a, minlength=c.shape[0]).to(x.dtype)
-        nz = cnt > 0
-        c[nz] = sums[nz] / cnt[nz, None]
-    return c
-
-
 def train_ivfpq_model(cfg, base):
-    """Input preparation for the IVF-PQ workload (not part of the timed search):
-    coarse k-means seeded with strided rows as IvfIndexState::train_centroids
-    (IvfIndexState.cpp:118-127), the final assignment, and a residual PQ
-    codebook trained on a strided sample; torch ops on the base's device.
-    Returns (centroids [nlist, d], assignments int32 [n], codebook [m, ksub, d/m])."""
+    """The IVF-PQ model of the base rows, built on their GPU by
+    elips_b200_ivfpq_train: bit-identical to what the reference's
+    GpuIVFPQIndex::build_from_batch computes (IvfIndexState::train_centroids
+    with kmeans_n_iters rounds and the final assignment, then rebuild_codes:
+    a 10-round PQ codebook on all residuals and the residual codes).
+    Returns (centroids [nlist, d], assignments int32 [n], codebook
+    [m, ksub, d/m], codes uint8 [n, m], build seconds)."""
     import torch
-    n, d, nlist = base.shape[0], base.shape[1], cfg["nlist"]
-    stride = max(1, n // nlist)
-    seeds = base[torch.arange(nlist, device=base.device) * stride]
-    cent = _lloyd(base, seeds, cfg["kmeans_iters"])
-    assign = _nearest(base, cent)
-    step = max(1, n // cfg["pq_train_rows"])
-    sample = base[::step] - cent[assign[::step]]
-    m, ksub = cfg["pq_dim"], 1 << cfg["pq_bits"]
-    sub = d // m
-    cb = torch.empty((m, ksub, sub), dtype=torch.float32, device=base.device)
-    for j in range(m):
-        xs = sample[:, j * sub:(j + 1) * sub].contiguous()
-        init = xs[torch.arange(ksub, device=base.device) * max(1, xs.shape[0] // ksub)]
-        cb[j] = _lloyd(xs, init, cfg["pq_iters"])
-    return cent.contiguous(), assign.to(torch.int32), cb.contiguous()
+    from elips_b200 import train
+    if not base.is_cuda:
+        raise RuntimeError("the IVF-PQ model is built on a CUDA device")
+    torch.cuda.synchronize(base.device)
+    t = time.perf_counter()
+    cent, assign, cb, codes = train.ivfpq_train_device(cfg["metric"], base, cfg["nlist"], cfg["kmeans_iters"],
+                                                       cfg["pq_dim"], cfg["pq_bits"])
+    torch.cuda.synchronize(base.device)
+    return cent, assign, cb, codes, time.perf_counter() - t
 
 
 def ivfpq_inputs(cfg, dev, train=True):
     """Seeded base rows and queries of the IVF-PQ workload and its trained
-    model, all on `dev`: (base, queries, centroids, assignments, codebook);
-    the model entries are None when train is False."""
+    model, all on `dev`: (base, queries, centroids, assignments, codebook,
+    codes, build seconds); the model entries are None when train is False."""
     import torch
     n, d = cfg["n"], cfg["d"]
     cents = _centroids(cfg, dev)
@@ -306,23 +279,8 @@ def ivfpq_inputs(cfg, dev, train=True):
         base[r0:r0 + cnt] = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev)
     queries = gen_rows(cfg, 0, cfg["q"], SEED + 2, cfg["q"], cents, device=dev)
     if not train:
-        return base, queries, None, None, None
-    centroids, assign, codebook = train_ivfpq_model(cfg, base)
-    return base, queries, centroids, assign, codebook
-
-
-def encode_residuals(base, centroids, assign, codebook, chunk=1 << 20):
-    """Residual PQ codes (nearest codeword per subspace) with torch ops: the
-    snapshot codes the reference arm imports (import_snapshot takes codes as
-    given, GpuIVFPQIndex.cpp:327-348)."""
-    import torch
-    m, ksub, sub = codebook.shape
-    codes = torch.empty((base.shape[0], m), dtype=torch.uint8, device=base.device)
-    for i in range(0, base.shape[0], chunk):
-        res = base[i:i + chunk] - centroids[assign[i:i + chunk].long()]
-        for j in range(m):
-            codes[i:i + chunk, j] = _nearest(res[:, j * sub:(j + 1) * sub].contiguous(), codebook[j]).to(torch.uint8)
-    return codes
+        return base, queries, None, None, None, None, None
+    return (base, queries) + train_ivfpq_model(cfg, base)
 
 
 def scanned_bytes(cfg, centroids, queries, assign, lists=None):
@@ -353,7 +311,7 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
     dev = torch.device("cuda", local)
     n, d, nq, k = cfg["n"], cfg["d"], cfg["q"], cfg["k"]
     t0 = time.perf_counter()
-    base, q_dev, centroids, assign, codebook = ivfpq_inputs(cfg, dev, train=(rank == 0))
+    base, q_dev, centroids, assign, codebook, _, model_s = ivfpq_inputs(cfg, dev, train=(rank == 0))
     if world > 1:
         import torch.distributed as dist
         if rank != 0:
@@ -467,7 +425,10 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
                    "pq": f"{cfg['pq_dim']}x{cfg['pq_bits']}",
                    "l2": "inputs larger than L2 (codes 160 MB, vectors 5.1 GB); no flush"},
         "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "clocks": sampler.summary(),
-        "build_s": round(build_s, 2)}
+        "build_s": round(build_s, 2),
+        "model_build": {"s": round(model_s, 3) if model_s is not None else None, "rows": n, "nlist": cfg["nlist"],
+                        "kmeans_rounds": cfg["kmeans_iters"], "pq_rounds": 10,
+                        "api": "elips_b200_ivfpq_train (bit-identical to GpuIVFPQIndex::build_from_batch)"}}
     if world > 1:
         result["config"]["parallelism"] = f"lists sharded over {world} GPUs (balanced by size^2)"
     if not args.no_cpu_baseline and world == 1:
@@ -730,17 +691,17 @@ def cpu_baseline(cfg, base, queries, mask_words):
 def _reference_ivfpq(cfg):
     """(search, kind, description, base rows, queries) for the reference's
     GpuIVFPQIndex::search on a CPU GpuPort, the trained model imported as a
-    snapshot. Inputs are prepared with torch (on the GPU when one is visible)."""
+    snapshot. The rows are generated and the model built on the GPU (the
+    build equals the reference's own build_from_batch bit for bit, which on
+    the CPU would take hours at this size); only the search is timed."""
     import torch
     oracle, kind = _ref_or_port()
-    gdev = "cuda" if torch.cuda.is_available() else "cpu"
-    base, q, cent, assign, cb = ivfpq_inputs(cfg, gdev)
-    codes = encode_residuals(base, cent, assign, cb).cpu().numpy()
+    base, q, cent, assign, cb, codes, _ = ivfpq_inputs(cfg, "cuda")
+    codes = codes.cpu().numpy()
     base_np, q_np = base.cpu().numpy(), q.cpu().numpy()
     cent_np, cb_np, a_np = cent.cpu().numpy(), cb.cpu().numpy(), assign.cpu().numpy().view(np.uint32)
     del base, q, cent, assign, cb
-    if gdev == "cuda":
-        torch.cuda.empty_cache()
+    torch.cuda.empty_cache()
     if kind == "reference":
         idx = oracle.RefIvfPqIndex(cfg["metric"], cent_np, a_np, cb_np, codes, base_np, cfg["nprobe"],
                                    pq_bits=cfg["pq_bits"])
