@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -133,6 +134,19 @@ StreamScratch::~StreamScratch() {
     if (ptr_ != nullptr) cudaFreeAsync(ptr_, stream_);
 }
 
+void allow_dynamic_smem(const void* func, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, const void*>, size_t> granted;
+    int device = 0;
+    check_cuda(cudaGetDevice(&device), ELIPS_B200_DEVICE_NOT_FOUND, "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& cur = granted[{device, func}];
+    if (bytes <= cur) return;
+    check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+               ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+    cur = bytes;
+}
+
 CUtensorMap make_operand_map(const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
                              uint64_t cols, uint64_t rows, uint32_t box_rows) {
     CUtensorMap map;
@@ -149,10 +163,12 @@ CUtensorMap make_operand_map(const void* base, CUtensorMapDataType dtype, uint32
     return map;
 }
 
-ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int num_sms) {
+ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int groups, uint32_t cg) {
     ExactPlan p;
     p.bn = bn;
-    p.n_qt = (nq + kTileM - 1) / kTileM;
+    p.cg = cg;
+    const int num_sms = groups;
+    p.n_qt = (nq + kTileM * cg - 1) / (kTileM * cg);
     p.n_bt = (n + bn - 1) / bn;
     // Pick the smallest number of base splits whose (query tile, split)
     // units fill the SMs in whole waves; each split keeps >= 4 base tiles.
@@ -171,7 +187,7 @@ ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int num_s
     }
     p.splits = best_s;
     const uint64_t units = static_cast<uint64_t>(p.n_qt) * p.splits;
-    p.grid = static_cast<uint32_t>(std::min<uint64_t>(units, static_cast<uint64_t>(num_sms)));
+    p.grid = static_cast<uint32_t>(std::min<uint64_t>(units, static_cast<uint64_t>(num_sms))) * cg;
     // List capacity: k survivors plus at least one whole half-tile of
     // admissions (compaction is checked once per tile); lists up to 512
     // entries are compacted in registers.
@@ -225,41 +241,97 @@ void prep_operands(OperandKind kind, const void* src, size_t rows, uint32_t dim,
     check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "prep kernel launch");
 }
 
-template <OperandKind KIND, int BN, int STAGES, int METRIC>
+// Launch configuration of one exact kernel instantiation; CTA pairs are
+// launched as clusters of two.
+template <OperandKind KIND, int BN, int STAGES, int METRIC, int CG>
+cudaLaunchConfig_t exact_launch_config(uint32_t grid, cudaStream_t stream, cudaLaunchAttribute* attr) {
+    using Cfg = ExactConfig<KIND, BN, STAGES, CG>;
+    auto kernel = exact_topk_kernel<KIND, BN, STAGES, METRIC, CG>;
+    allow_dynamic_smem(reinterpret_cast<const void*>(kernel), Cfg::kSmemBytes);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kExactThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = CG == 2 ? 1 : 0;
+    return cfg;
+}
+
+template <OperandKind KIND, int BN, int STAGES, int METRIC, int CG>
 void launch_exact_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& alo,
                          const CUtensorMap& blo, const ExactParams& params, uint32_t grid,
                          cudaStream_t stream) {
-    using Cfg = ExactConfig<KIND, BN, STAGES>;
-    auto kernel = exact_topk_kernel<KIND, BN, STAGES, METRIC>;
-    check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(Cfg::kSmemBytes)),
-               ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = exact_launch_config<KIND, BN, STAGES, METRIC, CG>(grid, stream, attr);
     Profiler::Scope prof("exact_topk", stream, static_cast<uint64_t>(params.nq) * params.n);
-    kernel<<<grid, kExactThreads, Cfg::kSmemBytes, stream>>>(a, b, alo, blo, params);
-    check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "exact kernel launch");
+    check_cuda(cudaLaunchKernelEx(&cfg, exact_topk_kernel<KIND, BN, STAGES, METRIC, CG>, a, b, alo, blo, params),
+               ELIPS_B200_KERNEL_LAUNCH_FAILED, "exact kernel launch");
 }
 
 uint32_t bn_of(OperandKind k) { return k == OperandKind::TF32X3 ? 128u : 256u; }
 
-template <OperandKind KIND, int BN, int STAGES>
+// Pipeline depth: the stages that fit 192 KB of shared memory.
+constexpr int stages_of(OperandKind k, int cg) {
+    return k == OperandKind::TF32X3 ? (cg == 2 ? 4 : 3) : (cg == 2 ? 6 : 4);
+}
+
+template <OperandKind KIND, int BN, int CG>
 void dispatch_metric(int metric, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& alo,
                      const CUtensorMap& blo, const ExactParams& prm, uint32_t grid, cudaStream_t stream) {
-    switch (metric) {
-        case kCosine: launch_exact_kernel<KIND, BN, STAGES, kCosine>(a, b, alo, blo, prm, grid, stream); break;
-        case kEuclidean: launch_exact_kernel<KIND, BN, STAGES, kEuclidean>(a, b, alo, blo, prm, grid, stream); break;
-        default: launch_exact_kernel<KIND, BN, STAGES, kDot>(a, b, alo, blo, prm, grid, stream); break;
+    constexpr int S = stages_of(KIND, CG);
+    if constexpr (KIND == OperandKind::I8) {
+        launch_exact_kernel<KIND, BN, S, kDot, CG>(a, b, alo, blo, prm, grid, stream);
+    } else {
+        switch (metric) {
+            case kCosine: launch_exact_kernel<KIND, BN, S, kCosine, CG>(a, b, alo, blo, prm, grid, stream); break;
+            case kEuclidean: launch_exact_kernel<KIND, BN, S, kEuclidean, CG>(a, b, alo, blo, prm, grid, stream); break;
+            default: launch_exact_kernel<KIND, BN, S, kDot, CG>(a, b, alo, blo, prm, grid, stream); break;
+        }
+    }
+}
+
+template <int CG>
+void dispatch_kind(OperandKind kind, int metric, const CUtensorMap& a, const CUtensorMap& b,
+                   const CUtensorMap& alo, const CUtensorMap& blo, const ExactParams& prm, uint32_t grid,
+                   cudaStream_t stream) {
+    switch (kind) {
+        case OperandKind::F16: dispatch_metric<OperandKind::F16, 256, CG>(metric, a, b, alo, blo, prm, grid, stream); break;
+        case OperandKind::BF16: dispatch_metric<OperandKind::BF16, 256, CG>(metric, a, b, alo, blo, prm, grid, stream); break;
+        case OperandKind::TF32X3: dispatch_metric<OperandKind::TF32X3, 128, CG>(metric, a, b, alo, blo, prm, grid, stream); break;
+        case OperandKind::I8: dispatch_metric<OperandKind::I8, 256, CG>(metric, a, b, alo, blo, prm, grid, stream); break;
     }
 }
 
 void dispatch_exact(OperandKind kind, int metric, const CUtensorMap& a, const CUtensorMap& b,
-                    const CUtensorMap& alo, const CUtensorMap& blo, const ExactParams& prm, uint32_t grid,
+                    const CUtensorMap& alo, const CUtensorMap& blo, const ExactParams& prm, const ExactPlan& plan,
                     cudaStream_t stream) {
-    switch (kind) {
-        case OperandKind::F16: dispatch_metric<OperandKind::F16, 256, 4>(metric, a, b, alo, blo, prm, grid, stream); break;
-        case OperandKind::BF16: dispatch_metric<OperandKind::BF16, 256, 4>(metric, a, b, alo, blo, prm, grid, stream); break;
-        case OperandKind::TF32X3: dispatch_metric<OperandKind::TF32X3, 128, 3>(metric, a, b, alo, blo, prm, grid, stream); break;
-        case OperandKind::I8: launch_exact_kernel<OperandKind::I8, 256, 4, kDot>(a, b, alo, blo, prm, grid, stream); break;
-    }
+    if (plan.cg == 2) dispatch_kind<2>(kind, metric, a, b, alo, blo, prm, plan.grid, stream);
+    else dispatch_kind<1>(kind, metric, a, b, alo, blo, prm, plan.grid, stream);
+}
+
+// CTA pairs that can be resident at once (cluster occupancy of the pair
+// kernel: 1 CTA per SM, two SMs of one GPC per pair), cached per device.
+int pair_groups(int device) {
+    static int cached[64] = {0};
+    if (device >= 0 && device < 64 && cached[device] > 0) return cached[device];
+    const DeviceProps& props = device_props(device);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg =
+        exact_launch_config<OperandKind::F16, 256, stages_of(OperandKind::F16, 2), kCosine, 2>(
+            static_cast<uint32_t>(props.num_sms / 2 * 2), nullptr, attr);
+    int clusters = 0;
+    check_cuda(cudaOccupancyMaxActiveClusters(&clusters, exact_topk_kernel<OperandKind::F16, 256,
+                                                                           stages_of(OperandKind::F16, 2), kCosine, 2>,
+                                              &cfg),
+               ELIPS_B200_KERNEL_LAUNCH_FAILED, "cluster occupancy");
+    if (clusters <= 0) fail(ELIPS_B200_KERNEL_LAUNCH_FAILED, "no CTA pair fits on this device");
+    if (device >= 0 && device < 64) cached[device] = clusters;
+    return clusters;
 }
 
 }  // namespace
@@ -375,8 +447,10 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
         return;
     }
     const uint32_t n = static_cast<uint32_t>(n_);
-    const ExactPlan plan = plan_exact(static_cast<uint32_t>(nq), n, static_cast<uint32_t>(k),
-                                      bn_of(kind_), props.num_sms);
+    // More than one 128-query tile: CTA pairs (M = 256 per MMA).
+    const bool pair = nq > kTileM;
+    const ExactPlan plan = plan_exact(static_cast<uint32_t>(nq), n, static_cast<uint32_t>(k), bn_of(kind_),
+                                      pair ? pair_groups(device_) : props.num_sms, pair ? 2u : 1u);
     const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
     auto align = [](size_t x) { return (x + 255) / 256 * 256; };
     const size_t q_ops = align(nq * row_bytes);
@@ -399,11 +473,11 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
 
     const CUtensorMapDataType dt = tma_dtype_of(kind_);
     const CUtensorMap ma = make_operand_map(qa, dt, elem_bytes_, d_pad_, nq, kTileM);
-    const CUtensorMap mb = make_operand_map(ops_.get(), dt, elem_bytes_, d_pad_, n, plan.bn);
+    const CUtensorMap mb = make_operand_map(ops_.get(), dt, elem_bytes_, d_pad_, n, plan.bn / plan.cg);
     CUtensorMap malo = ma, mblo = mb;
     if (kind_ == OperandKind::TF32X3) {
         malo = make_operand_map(qlo, dt, elem_bytes_, d_pad_, nq, kTileM);
-        mblo = make_operand_map(ops_lo_.get(), dt, elem_bytes_, d_pad_, n, plan.bn);
+        mblo = make_operand_map(ops_lo_.get(), dt, elem_bytes_, d_pad_, n, plan.bn / plan.cg);
     }
     ExactParams prm{};
     prm.base_norms = static_cast<const float*>(norms_.get());
@@ -423,7 +497,7 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     prm.kblocks = d_pad_ * elem_bytes_ / kKBlockBytes;
     prm.row_offset = row_offset;
     prm.metric = metric_;
-    dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan.grid, stream);
+    dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan, stream);
     merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits * 2, static_cast<uint32_t>(k),
                      static_cast<uint64_t>(plan.splits) * 2 * k, k, metric_, out_dist, out_rows, out_cand,
                      stream);
@@ -476,11 +550,11 @@ void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t
     prep_operands(kind_, queries, nq, dim_, d_pad_, qa, qlo, qn, stream);
     const CUtensorMapDataType dt = tma_dtype_of(kind_);
     const CUtensorMap ma = make_operand_map(qa, dt, elem_bytes_, d_pad_, nq, kTileM);
-    const CUtensorMap mb = make_operand_map(ops_.get(), dt, elem_bytes_, d_pad_, n, plan.bn);
+    const CUtensorMap mb = make_operand_map(ops_.get(), dt, elem_bytes_, d_pad_, n, plan.bn / plan.cg);
     CUtensorMap malo = ma, mblo = mb;
     if (kind_ == OperandKind::TF32X3) {
         malo = make_operand_map(qlo, dt, elem_bytes_, d_pad_, nq, kTileM);
-        mblo = make_operand_map(ops_lo_.get(), dt, elem_bytes_, d_pad_, n, plan.bn);
+        mblo = make_operand_map(ops_lo_.get(), dt, elem_bytes_, d_pad_, n, plan.bn / plan.cg);
     }
     ExactParams prm{};
     prm.base_norms = static_cast<const float*>(norms_.get());
@@ -500,7 +574,7 @@ void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t
     prm.kblocks = d_pad_ * elem_bytes_ / kKBlockBytes;
     prm.row_offset = 0;
     prm.metric = metric_;
-    dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan.grid, stream);
+    dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan, stream);
     merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits * 2, static_cast<uint32_t>(k),
                      static_cast<uint64_t>(plan.splits) * 2 * k, k, metric_, out_dist, out_rows, nullptr, stream);
 }
@@ -514,9 +588,7 @@ void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists
     while (kpow2 < k) kpow2 <<= 1;
     constexpr uint32_t warps = 4;
     const size_t smem = warps * (1024 + static_cast<size_t>(kpow2) * 8);
-    check_cuda(cudaFuncSetAttribute(merge_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(smem)),
-               ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+    allow_dynamic_smem(reinterpret_cast<const void*>(merge_topk_kernel), smem);
     const uint32_t blocks = (nq + warps - 1) / warps;
     Profiler::Scope prof("merge_topk", stream, static_cast<uint64_t>(nq) * lists * k);
     merge_topk_kernel<<<blocks, warps * 32, smem, stream>>>(cand, nq, lists, k, stride_q, stride_l, kpow2,

@@ -45,6 +45,12 @@ struct DeviceProps {
 // stream-ordered memory pool on first use.
 const DeviceProps& device_props(int device);
 
+// Lets `func` launch with up to `bytes` of dynamic shared memory on the
+// current device. The limit is a process-wide attribute of the function, so
+// it is only ever raised (under a lock): concurrent callers asking for
+// different sizes never lower it below another caller's launch.
+void allow_dynamic_smem(const void* func, size_t bytes);
+
 // Owning device allocation (cudaMalloc / cudaFree).
 class DeviceBuffer {
 public:
@@ -84,11 +90,13 @@ private:
 CUtensorMap make_operand_map(const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
                              uint64_t cols, uint64_t rows, uint32_t box_rows);
 
-// Partitioning of one exact search launch.
+// Partitioning of one exact search launch over `groups` MMA groups of `cg`
+// CTAs (1: single CTAs, 2: CTA pairs sharing each M = 256 MMA). grid counts
+// CTAs; n_qt counts query tiles of 128 * cg queries.
 struct ExactPlan {
-    uint32_t n_qt = 0, n_bt = 0, splits = 0, grid = 0, cap = 0, bn = 0;
+    uint32_t n_qt = 0, n_bt = 0, splits = 0, grid = 0, cap = 0, bn = 0, cg = 1;
 };
-ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int num_sms);
+ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int groups, uint32_t cg = 1);
 
 // Device-resident brute-force index over one base shard.
 class ExactIndex {

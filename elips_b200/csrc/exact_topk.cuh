@@ -19,6 +19,16 @@
 // MMA issuer, warps 2-9 = epilogue. Two epilogue warps share each 32-lane
 // TMEM quadrant and split the tile's columns in halves; a thread owns one
 // (query, column half) pair and its own candidate list.
+//
+// CTA pairs (CG = 2). Two CTAs of a cluster run one M = 256 MMA per step
+// (tcgen05 cta_group::2): each CTA loads its own 128 queries and its own half
+// of the BN base rows, rank 0 issues the MMAs over both CTAs' shared memory
+// and each CTA's TMEM receives its 128 queries x BN distances. Per CTA, a
+// pipeline stage then carries A + B/2 instead of A + B, which is what bounds
+// the single-CTA kernel (operand traffic from L2). Rank 0's barriers gate the
+// MMA: the peer's loads complete on rank 0's full barrier, the MMA commit
+// releases the stage in both CTAs, and the peer's epilogue warps release the
+// accumulator on rank 0's barrier.
 #pragma once
 
 #include <cstdint>
@@ -76,11 +86,12 @@ struct KindTraits<OperandKind::I8> {
     static constexpr bool x3 = false, integer = true;
 };
 
-template <OperandKind KIND, int BN, int STAGES>
+template <OperandKind KIND, int BN, int STAGES, int CG = 1>
 struct ExactConfig {
     using T = KindTraits<KIND>;
+    static constexpr uint32_t kBRows = BN / CG;  // base rows this CTA loads per tile
     static constexpr uint32_t kABytes = kTileM * kKBlockBytes;
-    static constexpr uint32_t kBBytes = BN * kKBlockBytes;
+    static constexpr uint32_t kBBytes = kBRows * kKBlockBytes;
     static constexpr uint32_t kOperands = T::x3 ? 2 : 1;
     static constexpr uint32_t kStageBytes = (kABytes + kBBytes) * kOperands;
     static constexpr uint32_t kTmemCols = 2 * BN;
@@ -177,12 +188,13 @@ __device__ __forceinline__ float chunk_min_key(const uint32_t (&v)[32], const fl
     }
 }
 
-template <OperandKind KIND, int BN, int STAGES, int METRIC>
+template <OperandKind KIND, int BN, int STAGES, int METRIC, int CG = 1>
 __global__ void __launch_bounds__(kExactThreads, 1)
     exact_topk_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                       const __grid_constant__ CUtensorMap tm_a_lo,
                       const __grid_constant__ CUtensorMap tm_b_lo, const __grid_constant__ ExactParams p) {
-    using Cfg = ExactConfig<KIND, BN, STAGES>;
+    using Cfg = ExactConfig<KIND, BN, STAGES, CG>;
+    static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair");
     using Tr = KindTraits<KIND>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -191,6 +203,15 @@ __global__ void __launch_bounds__(kExactThreads, 1)
 
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31u;
+    // Work is distributed over MMA groups: single CTAs, or CTA pairs.
+    uint32_t rank = 0, group = blockIdx.x, groups = gridDim.x;
+    if constexpr (CG == 2) {
+        rank = cluster_ctarank();
+        group = cluster_id_x();
+        groups = cluster_count_x();
+    }
+    const bool leader = rank == 0;
+    constexpr uint32_t kGroupM = kTileM * CG;  // queries per unit
 
     const uint32_t bar0 = sbase + Cfg::kMiscOffset;
     auto full_bar = [&](uint32_t s) { return bar0 + 8u * s; };
@@ -215,18 +236,25 @@ __global__ void __launch_bounds__(kExactThreads, 1)
         }
         for (uint32_t a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), kEpilogueWarps);
+            mbar_init(tempty_bar(a), kEpilogueWarps * CG);
         }
         mbar_init(mma_done_bar, 1);
         *abort_flag = 0;
         fence_mbarrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
-        tmem_relinquish();
+        if constexpr (CG == 2) {
+            tmem_alloc_pair(smem_u32(tmem_slot), Cfg::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // The peer's barriers must be initialised before either CTA signals them.
+    if constexpr (CG == 2) cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -244,27 +272,38 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             uint32_t stage = 0, phase = 0;
             uint32_t issued_mask = 0, issued_parity = 0;
             bool ok = true;
-            for (uint32_t unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+            for (uint32_t unit = group; ok && unit < num_units; unit += groups) {
                 const uint32_t qt = unit % p.n_qt, sp = unit / p.n_qt;
                 const uint32_t bt0 = static_cast<uint32_t>((uint64_t)sp * p.n_bt / p.splits);
                 const uint32_t bt1 = static_cast<uint32_t>((uint64_t)(sp + 1) * p.n_bt / p.splits);
+                const int32_t a_row = static_cast<int32_t>(qt * kGroupM + rank * kTileM);
                 for (uint32_t bt = bt0; ok && bt < bt1; ++bt) {
+                    const int32_t b_row = static_cast<int32_t>(bt * BN + rank * Cfg::kBRows);
                     for (uint32_t kb = 0; kb < p.kblocks; ++kb) {
                         if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
                         const int32_t x = static_cast<int32_t>(kb * Cfg::kElemsPerKBlock);
-                        tma_load_2d(a_addr(stage), &tm_a, full_bar(stage), x,
-                                    static_cast<int32_t>(qt * kTileM));
-                        tma_load_2d(b_addr(stage), &tm_b, full_bar(stage), x,
-                                    static_cast<int32_t>(bt * BN));
-                        if constexpr (Tr::x3) {
-                            tma_load_2d(alo_addr(stage), &tm_a_lo, full_bar(stage), x,
-                                        static_cast<int32_t>(qt * kTileM));
-                            tma_load_2d(blo_addr(stage), &tm_b_lo, full_bar(stage), x,
-                                        static_cast<int32_t>(bt * BN));
+                        if constexpr (CG == 2) {
+                            // Both halves complete on rank 0's barrier, which
+                            // rank 0 arms with the bytes of both.
+                            if (leader) mbar_arrive_expect_tx(full_bar(stage), 2u * Cfg::kStageBytes);
+                            const uint32_t fb = mapa_shared(full_bar(stage), 0);
+                            tma_load_2d_pair(a_addr(stage), &tm_a, fb, x, a_row);
+                            tma_load_2d_pair(b_addr(stage), &tm_b, fb, x, b_row);
+                            if constexpr (Tr::x3) {
+                                tma_load_2d_pair(alo_addr(stage), &tm_a_lo, fb, x, a_row);
+                                tma_load_2d_pair(blo_addr(stage), &tm_b_lo, fb, x, b_row);
+                            }
+                        } else {
+                            mbar_arrive_expect_tx(full_bar(stage), Cfg::kStageBytes);
+                            tma_load_2d(a_addr(stage), &tm_a, full_bar(stage), x, a_row);
+                            tma_load_2d(b_addr(stage), &tm_b, full_bar(stage), x, b_row);
+                            if constexpr (Tr::x3) {
+                                tma_load_2d(alo_addr(stage), &tm_a_lo, full_bar(stage), x, a_row);
+                                tma_load_2d(blo_addr(stage), &tm_b_lo, full_bar(stage), x, b_row);
+                            }
                         }
                         issued_mask |= 1u << stage;
                         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -276,24 +315,30 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                 }
             }
             // Every load this thread issued must land before the CTA exits.
-            for (uint32_t s = 0; s < STAGES; ++s) {
-                if (issued_mask & (1u << s)) drain_wait(full_bar(s), (issued_parity >> s) & 1u);
+            // In a pair, rank 0's full barriers count the peer's bytes too,
+            // and the peer leaves only after the closing cluster barrier.
+            if (leader) {
+                for (uint32_t s = 0; s < STAGES; ++s) {
+                    if (issued_mask & (1u << s)) drain_wait(full_bar(s), (issued_parity >> s) & 1u);
+                }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (elect_one_sync()) {
-            constexpr uint32_t idesc = make_idesc(Tr::c_fmt, Tr::idesc_fmt, kTileM, BN);
+        // ------------------------------------------------ MMA issuer (rank 0 of a pair)
+        if (leader && elect_one_sync()) {
+            constexpr uint32_t idesc = make_idesc(Tr::c_fmt, Tr::idesc_fmt, kGroupM, BN);
             uint32_t stage = 0, phase = 0, tile_iter = 0;
             bool ok = true;
-            for (uint32_t unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+            for (uint32_t unit = group; ok && unit < num_units; unit += groups) {
                 const uint32_t sp = unit / p.n_qt;
                 const uint32_t bt0 = static_cast<uint32_t>((uint64_t)sp * p.n_bt / p.splits);
                 const uint32_t bt1 = static_cast<uint32_t>((uint64_t)(sp + 1) * p.n_bt / p.splits);
                 for (uint32_t bt = bt0; ok && bt < bt1; ++bt, ++tile_iter) {
                     const uint32_t acc = tile_iter & 1u;
                     const uint32_t acc_phase = (tile_iter >> 1) & 1u;
-                    if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) {
+                    const bool freed = CG == 2 ? mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1u, abort_flag)
+                                               : mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag);
+                    if (!freed) {
                         ok = false;
                         break;
                     }
@@ -313,25 +358,28 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                             if constexpr (Tr::x3) {
                                 const uint64_t adl = smem_desc_k128(alo_addr(stage) + 32u * k);
                                 const uint64_t bdl = smem_desc_k128(blo_addr(stage) + 32u * k);
-                                tc_mma<Tr::mma>(d_tmem, adl, bd, idesc, first);
-                                tc_mma<Tr::mma>(d_tmem, ad, bdl, idesc, 1u);
-                                tc_mma<Tr::mma>(d_tmem, ad, bd, idesc, 1u);
+                                tc_mma<Tr::mma, CG>(d_tmem, adl, bd, idesc, first);
+                                tc_mma<Tr::mma, CG>(d_tmem, ad, bdl, idesc, 1u);
+                                tc_mma<Tr::mma, CG>(d_tmem, ad, bd, idesc, 1u);
                             } else {
-                                tc_mma<Tr::mma>(d_tmem, ad, bd, idesc, first);
+                                tc_mma<Tr::mma, CG>(d_tmem, ad, bd, idesc, first);
                             }
                         }
-                        tc_commit(empty_bar(stage));
+                        if constexpr (CG == 2) tc_commit_pair_both(empty_bar(stage), 0x3);
+                        else tc_commit(empty_bar(stage));
                         if (++stage == STAGES) {
                             stage = 0;
                             phase ^= 1u;
                         }
                     }
                     if (!ok) break;
-                    tc_commit(tfull_bar(acc));
+                    if constexpr (CG == 2) tc_commit_pair_both(tfull_bar(acc), 0x3);
+                    else tc_commit(tfull_bar(acc));
                 }
             }
             // All MMAs this thread issued must finish before TMEM is freed.
-            tc_commit(mma_done_bar);
+            if constexpr (CG == 2) tc_commit_pair(mma_done_bar);
+            else tc_commit(mma_done_bar);
             drain_wait(mma_done_bar, 0);
         }
     } else {
@@ -349,11 +397,14 @@ __global__ void __launch_bounds__(kExactThreads, 1)
         const uint32_t lane_base = (quad * 32u) << 16;
         uint32_t tile_iter = 0;
         bool ok = true;
-        for (uint32_t unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+        // Rank 0's accumulator-free barrier, released by both CTAs' epilogues.
+        const uint32_t tempty_remote0 = CG == 2 ? mapa_shared(tempty_bar(0), 0) : 0u;
+        const uint32_t tempty_remote1 = CG == 2 ? mapa_shared(tempty_bar(1), 0) : 0u;
+        for (uint32_t unit = group; ok && unit < num_units; unit += groups) {
             const uint32_t qt = unit % p.n_qt, sp = unit / p.n_qt;
             const uint32_t bt0 = static_cast<uint32_t>((uint64_t)sp * p.n_bt / p.splits);
             const uint32_t bt1 = static_cast<uint32_t>((uint64_t)(sp + 1) * p.n_bt / p.splits);
-            const uint32_t q = qt * kTileM + lane_row;
+            const uint32_t q = qt * kGroupM + rank * kTileM + lane_row;
             const bool qvalid = q < p.nq;
             float qn = 0.0f;
             if constexpr (METRIC == kEuclidean) {
@@ -389,7 +440,10 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                     if (c == kChunks - 1) {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(tempty_bar(acc));
+                        if (lane == 0) {
+                            if constexpr (CG == 2) mbar_arrive_cluster(acc ? tempty_remote1 : tempty_remote0);
+                            else mbar_arrive(tempty_bar(acc));
+                        }
                     }
                     const uint32_t row0 = row_half + c * 32u;
                     if (row0 >= p.n) continue;
@@ -401,12 +455,13 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                     // Fast reject: most chunks hold nothing below the threshold.
                     const bool slow = mword != 0u && chunk_min_key<KIND, METRIC>(v, xn, qn) < thr;
                     if (__any_sync(0xffffffffu, slow)) {
-                        // Predicated appends: no per-value branches.
+                        // Predicated appends (a predicated store instruction,
+                        // not a branch around a store: lanes disagree often).
 #pragma unroll
                         for (uint32_t i = 0; i < 32; ++i) {
                             const float key = key_of<KIND, METRIC>(v[i], xn[i], qn);
                             const bool take = slow && ((mword >> i) & 1u) && key < thr;
-                            if (take) my_list[cnt] = make_uint2(__float_as_uint(key), p.row_offset + row0 + i);
+                            st_global_pred(my_list + cnt, __float_as_uint(key), p.row_offset + row0 + i, take);
                             cnt += take ? 1u : 0u;
                         }
                     }
@@ -456,9 +511,13 @@ __global__ void __launch_bounds__(kExactThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    // Neither CTA of a pair leaves while the other may still signal its
+    // barriers, read its shared memory (MMA) or land loads in it.
+    if constexpr (CG == 2) cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+        if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+        else tmem_dealloc(tmem_base, Cfg::kTmemCols);
     }
 }
 

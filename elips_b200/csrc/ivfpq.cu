@@ -11,6 +11,7 @@
 #include "../../include/elips_b200.h"
 #include "engine.cuh"
 #include "capi_util.cuh"
+#include "train.cuh"
 #include "ivfpq_kernels.cuh"
 #include "profiler.cuh"
 
@@ -208,9 +209,7 @@ protected:
             uint32_t npow2 = 1;
             while (npow2 < nlist_) npow2 <<= 1;
             const size_t psmem = nlist_ <= kPlanSortMax ? static_cast<size_t>(npow2) * 8 : 0;
-            check_cuda(cudaFuncSetAttribute(ivf_group_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(psmem)),
-                       ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+            allow_dynamic_smem(reinterpret_cast<const void*>(ivf_group_plan_kernel), psmem);
             Profiler::Scope prof("ivfpq_plan", stream, nlist_);
             ivf_group_plan_kernel<<<1, kPlanThreads, psmem, stream>>>(pl.counts, loff, nlist_, G, pl.list_start,
                                                                       cursor, pl.items, pl.ctrl);
@@ -271,8 +270,7 @@ protected:
         const auto& props = device_props(device_);
         if (smem > props.max_smem_optin) fail(ELIPS_B200_INVALID_ARGUMENT, "ivf scan needs too much shared memory");
         auto kern = ivfpq_group_scan_kernel<G, MB, BITS, FLAT>;
-        check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
-                   ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+        allow_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
         int per_sm = 0;
         check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGroupThreads, smem),
                    ELIPS_B200_KERNEL_LAUNCH_FAILED, "occupancy");
@@ -339,12 +337,8 @@ public:
                     reinterpret_cast<float*>(res.get()));
                 launch_ok("residual kernel");
             }
-            const uint64_t tc = static_cast<uint64_t>(n) * m_;
-            Profiler::Scope prof("pq_encode", stream, n);
-            pq_encode_kernel<<<static_cast<uint32_t>((tc + 127) / 128), 128, 0, stream>>>(
-                reinterpret_cast<const float*>(res.get()), static_cast<const float*>(codebook_.get()), n, dim_, m_,
-                ksub_, cdst);
-            launch_ok("pq encode kernel");
+            pq_encode_device(reinterpret_cast<const float*>(res.get()), n, dim_, m_, ksub_,
+                             static_cast<const float*>(codebook_.get()), cdst, stream);
         }
         commit_rows(host_assign, stream);
     }
@@ -430,9 +424,7 @@ public:
         while (rp < r) rp <<= 1;
         constexpr uint32_t warps = 4;
         const size_t rsmem = static_cast<size_t>(warps) * rp * 8;
-        check_cuda(cudaFuncSetAttribute(ivfpq_rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(rsmem)),
-                   ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+        allow_dynamic_smem(reinterpret_cast<const void*>(ivfpq_rerank_kernel), rsmem);
         Profiler::Scope prof("ivfpq_rerank", stream, nq * r);
         ivfpq_rerank_kernel<<<static_cast<uint32_t>((nq + warps - 1) / warps), warps * 32, rsmem, stream>>>(
             queries, static_cast<const float*>(vectors_.get()), cand, static_cast<uint32_t>(nq), dim_, r,

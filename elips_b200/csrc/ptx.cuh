@@ -106,6 +106,84 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// ------------------------------------------------------------ CTA pairs
+// A CTA pair is a cluster of two CTAs whose MMAs run as one (cta_group::2):
+// rank 0 issues them over both CTAs' shared memory and both CTAs' TMEM.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_count_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory object in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+// Every thread of both CTAs: arrive (release) and wait (acquire).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier that may live in another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait for a barrier that also receives arrivals from the peer CTA.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const long long start = clock64();
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if (*abort) return false;
+        if (clock64() - start > kWaitTimeoutCycles) {
+            record_device_error(kDevErrWaitTimeout);
+            *abort = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+// 2-D tiled load of one CTA's half of a pair operand into its own shared
+// memory, completion signalled on rank 0's barrier (`bar_cluster`, a
+// shared::cluster address). No multicast: each CTA fetches its own half.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
@@ -138,32 +216,62 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                  : "memory");
 }
 
+// Pair (cta_group::2) forms: both CTAs' warp 1 allocate / free together
+// (same columns in both TMEMs); rank 0 issues the MMAs and commits.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+// Completion of this thread's pair MMAs arrives once on the barrier at the
+// same offset in every CTA of `cta_mask` (this is an mbarrier signal from the
+// tensor core, not a memory load).
+__device__ __forceinline__ void tc_commit_pair_both(uint32_t bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"(cta_mask)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
 enum class MmaKind { F16, TF32, I8 };
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, one instruction, issued by one
-// thread. `accumulate` = 0 overwrites D.
-template <MmaKind K>
+// thread. `accumulate` = 0 overwrites D. CG = 2: the pair form, M = 256 over
+// both CTAs' A halves and N over both CTAs' B halves.
+template <MmaKind K, int CG = 1>
 __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                        uint32_t idesc, uint32_t accumulate) {
-    if constexpr (K == MmaKind::F16) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-            : "memory");
-    } else if constexpr (K == MmaKind::TF32) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-            : "memory");
+#define EB_TC_MMA(GROUP, KINDSTR)                                                              \
+    asm volatile(                                                                             \
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"                                   \
+        "tcgen05.mma.cta_group::" GROUP ".kind::" KINDSTR " [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d), \
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)                                    \
+        : "memory")
+    if constexpr (CG == 1) {
+        if constexpr (K == MmaKind::F16) EB_TC_MMA("1", "f16");
+        else if constexpr (K == MmaKind::TF32) EB_TC_MMA("1", "tf32");
+        else EB_TC_MMA("1", "i8");
     } else {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-            : "memory");
+        if constexpr (K == MmaKind::F16) EB_TC_MMA("2", "f16");
+        else if constexpr (K == MmaKind::TF32) EB_TC_MMA("2", "tf32");
+        else EB_TC_MMA("2", "i8");
     }
+#undef EB_TC_MMA
 }
 
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
@@ -217,7 +325,20 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+
 // ------------------------------------------------------------ misc helpers
+
+// Global 8-byte store executed only where `pred` holds, as a predicated
+// instruction: a per-lane condition never becomes a divergent branch.
+__device__ __forceinline__ void st_global_pred(uint2* addr, uint32_t x, uint32_t y, bool pred) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %3, 0;\n\t"
+        "@p st.global.v2.u32 [%0], {%1, %2};\n\t}"
+        :
+        : "l"(addr), "r"(x), "r"(y), "r"(pred ? 1u : 0u)
+        : "memory");
+}
 
 __device__ __forceinline__ bool elect_one_sync() {
     uint32_t pred = 0;

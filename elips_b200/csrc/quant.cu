@@ -10,6 +10,7 @@
 #include "../../include/elips_b200.h"
 #include "engine.cuh"
 #include "capi_util.cuh"
+#include "train.cuh"
 #include "profiler.cuh"
 #include "scan_kernels.cuh"
 
@@ -131,8 +132,7 @@ void top_k_device(int device, const float* dist, uint32_t* idx, float* val, size
     const uint32_t cap = btk_cap(static_cast<uint32_t>(k));
     const uint32_t kp = pow2_at_least(static_cast<uint32_t>(k));
     const size_t smem = btk_bytes(cap) + static_cast<size_t>(kp) * 8;
-    check_cuda(cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
-               ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+    allow_dynamic_smem(reinterpret_cast<const void*>(topk_rows_kernel), smem);
     Profiler::Scope prof("topk_rows", stream, static_cast<uint64_t>(nq) * nb);
     topk_rows_kernel<<<static_cast<uint32_t>(nq), kScanThreads, smem, stream>>>(
         dist, static_cast<uint32_t>(nq), static_cast<uint32_t>(nb), static_cast<uint32_t>(k), cap, kp, idx, val);
@@ -235,10 +235,7 @@ public:
             sq8_encode_kernel<<<static_cast<uint32_t>((total + 255) / 256), 256, 0, stream>>>(src, mins, mins + dim_, n,
                                                                                            dim_, dst);
         } else {
-            const uint64_t total = static_cast<uint64_t>(n) * pq_dim_;
-            Profiler::Scope prof("pq_encode", stream, n);
-            pq_encode_kernel<<<static_cast<uint32_t>((total + 127) / 128), 128, 0, stream>>>(
-                src, static_cast<const float*>(params_.get()), n, dim_, pq_dim_, ksub_, dst);
+            pq_encode_device(src, n, dim_, pq_dim_, ksub_, static_cast<const float*>(params_.get()), dst, stream);
         }
         launch_check("encode kernel");
         check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "encode");
@@ -292,9 +289,7 @@ public:
             }
             const bool in_smem = dim_ <= 192;
             const size_t smem = btk_bytes(cap) + (in_smem ? static_cast<size_t>(dim_) * 256 * sizeof(float) : 0);
-            check_cuda(cudaFuncSetAttribute(sq8_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(smem)),
-                       ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+            allow_dynamic_smem(reinterpret_cast<const void*>(sq8_scan_kernel), smem);
             Profiler::Scope prof("sq8_scan", stream, static_cast<uint64_t>(nq) * n);
             sq8_scan_kernel<<<dim3(splits, static_cast<uint32_t>(nq)), kScanThreads, smem, stream>>>(
                 lut, static_cast<const uint8_t*>(codes_.get()), n, dim_, metric_, static_cast<uint32_t>(k), cap, splits,
@@ -310,9 +305,7 @@ public:
             const size_t smem = kPqQueriesPerCta * (lut_floats * sizeof(float) + btk_bytes(cap));
             if (smem > device_props(device_).max_smem_optin)
                 fail(ELIPS_B200_INVALID_ARGUMENT, "pq_dim x 2^pq_bits too large for the scan kernel");
-            check_cuda(cudaFuncSetAttribute(pq_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(smem)),
-                       ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaFuncSetAttribute");
+            allow_dynamic_smem(reinterpret_cast<const void*>(pq_scan_kernel), smem);
             const dim3 grid(splits, static_cast<uint32_t>((nq + kPqQueriesPerCta - 1) / kPqQueriesPerCta));
             Profiler::Scope prof("pq_scan", stream, static_cast<uint64_t>(nq) * n);
             pq_scan_kernel<<<grid, kScanThreads, smem, stream>>>(lut, static_cast<const uint8_t*>(codes_.get()), n,

@@ -10,8 +10,6 @@
 //   sq8_lut / sq8_scan   ScalarQuantizer::make_lut + lut_distance
 //                        (src/quant_engine/ScalarQuantizer.cpp:83-128)
 //   sq8_encode           ScalarQuantizer::encode (ScalarQuantizer.cpp:52-68)
-//   pq_encode            quant::detail::encode_pq / nearest_centroid
-//                        (src/quant_engine/KMeans.cpp:166-180, 270-285)
 //   rotate_rows          detail::apply_matrix for OPQ (KMeans.cpp:295-305)
 #pragma once
 
@@ -379,33 +377,6 @@ static __global__ void sq8_encode_kernel(const float* __restrict__ rows, const f
     const float level = __fdiv_rn(__fsub_rn(rows[t], mins[i]), scales[i]);
     const float clamped = fminf(fmaxf(level, 0.0f), 255.0f);
     codes[t] = static_cast<uint8_t>(lroundf(clamped));
-}
-
-// encode_pq / nearest_centroid: per (row, subspace), the codeword with the
-// smallest sequential squared distance; strict '<' keeps the lowest index.
-static __global__ void pq_encode_kernel(const float* __restrict__ rows, const float* __restrict__ codebook, uint64_t n,
-                                 uint32_t d, uint32_t m_sub, uint32_t ksub, uint8_t* __restrict__ codes) {
-    const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= n * m_sub) return;
-    const uint64_t r = t / m_sub;
-    const uint32_t m = static_cast<uint32_t>(t % m_sub);
-    const uint32_t sub = d / m_sub;
-    const float* v = rows + r * d + static_cast<size_t>(m) * sub;
-    const float* cb = codebook + static_cast<size_t>(m) * ksub * sub;
-    float best = 3.40282347e+38f;
-    uint32_t arg = 0;
-    for (uint32_t c = 0; c < ksub; ++c) {
-        float acc = 0.0f;
-        for (uint32_t i = 0; i < sub; ++i) {
-            const float df = __fsub_rn(v[i], cb[c * sub + i]);
-            acc = __fadd_rn(acc, __fmul_rn(df, df));
-        }
-        if (acc < best) {
-            best = acc;
-            arg = c;
-        }
-    }
-    codes[t] = static_cast<uint8_t>(arg);
 }
 
 }  // namespace eb

@@ -104,9 +104,13 @@ __device__ __forceinline__ float warp_compact_list(uint2* list, uint32_t count, 
 }
 
 // Same contract as warp_compact_list for count <= 32*E, with the list held in
-// registers for the whole selection: one batch of independent loads, four
-// histogram passes over registers, one stable write-back. Entry j of the list
-// lives in slot j/32 of lane j%32, so the write-back walks positions in order.
+// registers for the whole selection: one batch of independent loads, radix
+// passes over registers, one stable write-back. Entry j of the list lives in
+// slot j/32 of lane j%32, so the write-back walks positions in order.
+// The passes start at the first byte in which the keys differ (a list's keys
+// share their high bytes, and a pass over a shared byte only piles every
+// entry onto one histogram bin), and stop early once the bin holding rank k
+// is taken whole; the threshold is then that bin's largest key.
 template <int E>
 __device__ __forceinline__ float warp_compact_regs(uint2* list, uint32_t count, uint32_t k,
                                                    uint32_t* hist) {
@@ -120,16 +124,27 @@ __device__ __forceinline__ float warp_compact_regs(uint2* list, uint32_t count, 
         key[i] = ordered_key(__uint_as_float(e.x));
         row[i] = e.y;
     }
-    uint32_t prefix = 0, prefix_mask = 0, rank = k;
+    // Bytes shared by every entry (entry 0 exists: count >= k >= 1).
+    const uint32_t key0 = __shfl_sync(0xffffffffu, key[0], 0);
+    uint32_t diff = 0;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const uint32_t j = static_cast<uint32_t>(i) * 32u + lane;
+        if (j < count) diff |= key[i] ^ key0;
+    }
+    diff = __reduce_or_sync(0xffffffffu, diff);
+    const int first = diff == 0u ? 4 : static_cast<int>(__clz(diff) >> 3);
+    uint32_t pmask = first == 0 ? 0u : (first >= 4 ? 0xFFFFFFFFu : (0xFFFFFFFFu << (32 - 8 * first)));
+    uint32_t prefix = key0 & pmask, rank = k;
 #pragma unroll 1
-    for (int pass = 0; pass < 4; ++pass) {
+    for (int pass = first; pass < 4; ++pass) {
         const uint32_t shift = 24u - 8u * static_cast<uint32_t>(pass);
         for (uint32_t b = lane; b < 256; b += 32) hist[b] = 0;
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < E; ++i) {
             const uint32_t j = static_cast<uint32_t>(i) * 32u + lane;
-            if (j < count && (key[i] & prefix_mask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
+            if (j < count && (key[i] & pmask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
         }
         __syncwarp();
         uint32_t bins[8];
@@ -147,7 +162,7 @@ __device__ __forceinline__ float warp_compact_regs(uint2* list, uint32_t count, 
         }
         const uint32_t excl = incl - local;
         const bool mine = excl < rank && rank <= incl;
-        uint32_t digit = 0, before = excl;
+        uint32_t digit = 0, before = excl, inbin = 0;
         if (mine) {
             uint32_t acc = excl;
 #pragma unroll
@@ -155,6 +170,7 @@ __device__ __forceinline__ float warp_compact_regs(uint2* list, uint32_t count, 
                 if (acc + bins[i] >= rank) {
                     digit = lane * 8 + i;
                     before = acc;
+                    inbin = bins[i];
                     break;
                 }
                 acc += bins[i];
@@ -163,20 +179,35 @@ __device__ __forceinline__ float warp_compact_regs(uint2* list, uint32_t count, 
         const uint32_t owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
         digit = __shfl_sync(0xffffffffu, digit, owner);
         before = __shfl_sync(0xffffffffu, before, owner);
+        inbin = __shfl_sync(0xffffffffu, inbin, owner);
         rank -= before;
         prefix |= digit << shift;
-        prefix_mask |= 255u << shift;
+        pmask |= 255u << shift;
         __syncwarp();
+        if (inbin == rank) break;  // the whole bin is selected
     }
-    const uint32_t kth = prefix, need_eq = rank;
+    // Keep every entry below the selected group and the first `rank` entries
+    // of the group (all of it after an early stop).
+    uint32_t kth = prefix;
+    if (pmask != 0xFFFFFFFFu) {
+        uint32_t mx = 0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const uint32_t j = static_cast<uint32_t>(i) * 32u + lane;
+            if (j < count && (key[i] & pmask) == prefix) mx = max(mx, key[i]);
+        }
+        kth = __reduce_max_sync(0xffffffffu, mx);
+    }
+    const uint32_t need_eq = rank;
     const uint32_t lt_mask = lanemask_lt();
     uint32_t w = 0, eq_taken = 0;
 #pragma unroll
     for (int i = 0; i < E; ++i) {
         const uint32_t j = static_cast<uint32_t>(i) * 32u + lane;
         const bool valid = j < count;
-        const bool lt = valid && key[i] < kth;
-        const bool eq = valid && key[i] == kth;
+        const uint32_t km = key[i] & pmask;
+        const bool lt = valid && km < prefix;
+        const bool eq = valid && km == prefix;
         const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
         const uint32_t eq_rank = eq_taken + __popc(eq_mask & lt_mask);
         const bool keep = lt || (eq && eq_rank < need_eq);

@@ -26,6 +26,7 @@
 #include "ivfpq_kernels.cuh"
 #include "profiler.cuh"
 #include "scan_kernels.cuh"
+#include "train.cuh"
 #include "train_kernels.cuh"
 
 namespace eb {
@@ -178,6 +179,26 @@ void lloyd(const TrainRows& p, uint32_t K, size_t iters, bool ivf, int mode, flo
 
 }  // namespace
 
+void pq_encode_device(const float* rows, size_t n, size_t d, size_t m, size_t ksub, const float* codebook,
+                      uint8_t* codes, cudaStream_t stream) {
+    if (n == 0) return;
+    if (m == 0 || d % m != 0 || m > 65535) fail(ELIPS_B200_INVALID_ARGUMENT, "dimension must divide by pq_dim");
+    if (ksub == 0 || ksub > 256) fail(ELIPS_B200_INVALID_ARGUMENT, "ksub must be in [1, 256]");
+    const uint32_t sub = static_cast<uint32_t>(d / m);
+    const size_t chunk = std::max<size_t>(1, (size_t{1} << 26) / m);
+    StreamScratch s(std::min(n, chunk) * m * 4, stream);
+    uint32_t* keys = reinterpret_cast<uint32_t*>(s.get());
+    for (size_t r0 = 0; r0 < n; r0 += chunk) {
+        const size_t rows_here = std::min(chunk, n - r0);
+        const TrainRows p{rows + r0 * d, d, rows_here, sub, static_cast<uint32_t>(m), sub};
+        launch_nearest(kTrainSqL2, p, codebook, static_cast<uint32_t>(ksub), 0u, keys, nullptr, stream);
+        const uint64_t total = static_cast<uint64_t>(rows_here) * m;
+        keys_to_codes_kernel<<<blocks_for(total, 256), 256, 0, stream>>>(keys, rows_here, static_cast<uint32_t>(m),
+                                                                        codes + r0 * m);
+        launch_ok("code transpose kernel");
+    }
+}
+
 void kmeans_device(int device, const float* rows, size_t n, size_t d, size_t k, size_t iters, float* cents,
                    cudaStream_t stream) {
     DeviceGuard g(device);
@@ -242,14 +263,7 @@ void ivfpq_train_device(int device, int metric, const float* rows, size_t n, siz
     launch_ok("residuals kernel");
     const size_t ksub = size_t{1} << pq_bits;
     train_pq_codebook_device(device, r, n, d, m, ksub, 10, codebook, stream);
-    if (codes != nullptr) {
-        const uint64_t tc = static_cast<uint64_t>(n) * m;
-        Profiler::Scope prof("pq_encode", stream, n);
-        pq_encode_kernel<<<blocks_for(tc, 128), 128, 0, stream>>>(r, codebook, n, static_cast<uint32_t>(d),
-                                                                 static_cast<uint32_t>(m), static_cast<uint32_t>(ksub),
-                                                                 codes);
-        launch_ok("pq encode kernel");
-    }
+    if (codes != nullptr) pq_encode_device(r, n, d, m, ksub, codebook, codes, stream);
 }
 
 }  // namespace eb

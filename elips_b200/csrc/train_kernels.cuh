@@ -236,6 +236,17 @@ static __global__ void centroid_normalize_kernel(float* __restrict__ cents, uint
     for (uint32_t i = 0; i < d; ++i) v[i] = __fdiv_rn(v[i], norm);
 }
 
+// codes[r * m + s] = keys[s * n + r] (the [subspace][row] argmin output
+// turned into row-major PQ codes).
+static __global__ void keys_to_codes_kernel(const uint32_t* __restrict__ keys, uint64_t n, uint32_t m,
+                                            uint8_t* __restrict__ codes) {
+    const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= n * m) return;
+    const uint64_t r = t / m;
+    const uint32_t s = static_cast<uint32_t>(t % m);
+    codes[t] = static_cast<uint8_t>(keys[static_cast<uint64_t>(s) * n + r]);
+}
+
 // done[b] |= !moved[b]; moved[b] = 0 (the early stop of KMeans.cpp:243-245).
 static __global__ void kmeans_flags_kernel(uint32_t* __restrict__ moved, uint32_t* __restrict__ done, uint32_t batch) {
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
