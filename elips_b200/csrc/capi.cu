@@ -84,6 +84,42 @@ int elips_b200_exact_size(const elips_b200_exact* index, size_t* n_out) {
     return ELIPS_B200_OK;
 }
 
+int elips_b200_exact_live(const elips_b200_exact* index, size_t* n_out) {
+    if (index == nullptr || n_out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *n_out = index->index.live();
+    return ELIPS_B200_OK;
+}
+
+int elips_b200_exact_remove(elips_b200_exact* index, size_t row, int* removed_out) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        const bool r = index->index.remove(row);
+        if (removed_out != nullptr) *removed_out = r ? 1 : 0;
+    });
+}
+
+int elips_b200_exact_compact(elips_b200_exact* index, uint32_t* new_to_old, size_t capacity) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (new_to_old != nullptr && capacity < index->index.live()) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.compact(new_to_old); });
+}
+
+int elips_b200_exact_snapshot_bytes(const elips_b200_exact* index, size_t* bytes_out) {
+    if (index == nullptr || bytes_out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *bytes_out = index->index.blob_bytes();
+    return ELIPS_B200_OK;
+}
+
+int elips_b200_exact_export(const elips_b200_exact* index, void* out, size_t bytes) {
+    if (index == nullptr || out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.export_blob(out, bytes); });
+}
+
+int elips_b200_exact_import(elips_b200_exact* index, const void* blob, size_t bytes) {
+    if (index == nullptr || blob == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.import_blob(blob, bytes); });
+}
+
 int elips_b200_exact_destroy(elips_b200_exact* index) {
     if (index == nullptr) return ELIPS_B200_OK;
     return guarded([&] {

@@ -377,6 +377,196 @@ void ExactIndex::reserve(size_t rows) {
     ops_lo_ = std::move(lo);
     norms_ = std::move(norms);
     capacity_ = cap;
+    if (live_.get() != nullptr) {
+        DeviceBuffer live(device_, (cap + 31) / 32 * 4);
+        check_cuda(cudaMemcpy(live.get(), live_.get(), live_host_.size() * 4, cudaMemcpyDeviceToDevice),
+                   ELIPS_B200_TRANSFER_FAILED, "grow copy");
+        live_ = std::move(live);
+    }
+}
+
+void ExactIndex::upload_live_words(size_t w0, size_t w1) {
+    if (live_.get() == nullptr || w1 <= w0) return;
+    check_cuda(cudaMemcpy(static_cast<uint32_t*>(live_.get()) + w0, live_host_.data() + w0, (w1 - w0) * 4,
+                          cudaMemcpyHostToDevice),
+               ELIPS_B200_TRANSFER_FAILED, "removal bits upload");
+}
+
+// Rows [first, first + count) become live (called for appended rows).
+void ExactIndex::mark_live(size_t first, size_t count) {
+    if (live_.get() == nullptr || count == 0) return;
+    live_host_.resize((first + count + 31) / 32, 0u);
+    for (size_t r = first; r < first + count; ++r) live_host_[r >> 5] |= 1u << (r & 31);
+    upload_live_words(first >> 5, live_host_.size());
+}
+
+namespace {
+
+// dst row i = src row idx[i], rows of `row_bytes` (a multiple of 16) bytes.
+__global__ void gather_row_bytes_kernel(const uint4* __restrict__ src, const uint32_t* __restrict__ idx,
+                                        uint64_t rows, uint32_t row_words, uint4* __restrict__ dst) {
+    const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= rows * row_words) return;
+    const uint64_t r = t / row_words;
+    const uint32_t w = static_cast<uint32_t>(t % row_words);
+    dst[t] = src[static_cast<uint64_t>(idx[r]) * row_words + w];
+}
+
+__global__ void gather_u32_kernel(const uint32_t* __restrict__ src, const uint32_t* __restrict__ idx, uint64_t rows,
+                                  uint32_t* __restrict__ dst) {
+    const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t < rows) dst[t] = src[idx[t]];
+}
+
+void gather_rows(const void* src, const uint32_t* idx, size_t rows, size_t row_bytes, void* dst,
+                 cudaStream_t stream) {
+    if (rows == 0 || row_bytes == 0) return;
+    const uint64_t words = static_cast<uint64_t>(rows) * (row_bytes / 16);
+    Profiler::Scope prof("compact_rows", stream, rows);
+    gather_row_bytes_kernel<<<static_cast<uint32_t>((words + 255) / 256), 256, 0, stream>>>(
+        static_cast<const uint4*>(src), idx, rows, static_cast<uint32_t>(row_bytes / 16), static_cast<uint4*>(dst));
+    check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "compaction kernel");
+}
+
+constexpr uint32_t kBlobMagic = 0x58324245u;  // "EB2X"
+constexpr uint32_t kBlobVersion = 1;
+
+struct BlobHeader {
+    uint32_t magic, version;
+    int32_t metric, precision;
+    uint32_t dim, d_pad, elem_bytes, flags;  // flags: 1 = lo plane, 2 = norms, 4 = removal bits
+    uint64_t rows, removed;
+};
+
+}  // namespace
+
+void ExactIndex::compact(uint32_t* new_to_old) {
+    DeviceGuard g(device_);
+    check_cuda(cudaDeviceSynchronize(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "compact sync");
+    const size_t keep = live();
+    std::vector<uint32_t> order;
+    order.reserve(keep);
+    for (size_t r = 0; r < n_; ++r)
+        if (live_.get() == nullptr || ((live_host_[r >> 5] >> (r & 31)) & 1u)) order.push_back(static_cast<uint32_t>(r));
+    if (new_to_old != nullptr) std::copy(order.begin(), order.end(), new_to_old);
+    if (removed_ == 0) return;
+    const size_t cap = std::max<size_t>(keep, 1);
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    DeviceBuffer idx(device_, cap * 4);
+    DeviceBuffer ops(device_, cap * row_bytes);
+    DeviceBuffer lo(device_, ops_lo_.get() ? cap * row_bytes : 0);
+    DeviceBuffer norms(device_, norms_.get() ? cap * sizeof(float) : 0);
+    if (keep > 0) {
+        check_cuda(cudaMemcpy(idx.get(), order.data(), keep * 4, cudaMemcpyHostToDevice), ELIPS_B200_TRANSFER_FAILED,
+                   "order upload");
+        const uint32_t* ix = static_cast<const uint32_t*>(idx.get());
+        gather_rows(ops_.get(), ix, keep, row_bytes, ops.get(), nullptr);
+        if (lo.get()) gather_rows(ops_lo_.get(), ix, keep, row_bytes, lo.get(), nullptr);
+        if (norms.get()) {
+            gather_u32_kernel<<<static_cast<uint32_t>((keep + 255) / 256), 256>>>(
+                static_cast<const uint32_t*>(norms_.get()), ix, keep, static_cast<uint32_t*>(norms.get()));
+            check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "compaction kernel");
+        }
+        check_cuda(cudaDeviceSynchronize(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "compaction");
+    }
+    ops_ = std::move(ops);
+    ops_lo_ = std::move(lo);
+    norms_ = std::move(norms);
+    capacity_ = cap;
+    n_ = keep;
+    removed_ = 0;
+    live_ = DeviceBuffer();
+    live_host_.clear();
+}
+
+size_t ExactIndex::blob_bytes() const {
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    return sizeof(BlobHeader) + n_ * row_bytes * (ops_lo_.get() ? 2 : 1) + (norms_.get() ? n_ * 4 : 0) +
+           (live_.get() ? live_host_.size() * 4 : 0);
+}
+
+void ExactIndex::export_blob(void* out, size_t bytes) const {
+    if (out == nullptr || bytes < blob_bytes()) fail(ELIPS_B200_INVALID_ARGUMENT, "snapshot buffer too small");
+    DeviceGuard g(device_);
+    check_cuda(cudaDeviceSynchronize(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "export sync");
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    BlobHeader h{kBlobMagic, kBlobVersion, metric_, precision_, dim_, d_pad_, elem_bytes_,
+                 (ops_lo_.get() ? 1u : 0u) | (norms_.get() ? 2u : 0u) | (live_.get() ? 4u : 0u), n_, removed_};
+    uint8_t* o = static_cast<uint8_t*>(out);
+    std::memcpy(o, &h, sizeof(h));
+    o += sizeof(h);
+    auto down = [&](const DeviceBuffer& b, size_t nbytes) {
+        if (nbytes == 0) return;
+        check_cuda(cudaMemcpy(o, b.get(), nbytes, cudaMemcpyDeviceToHost), ELIPS_B200_TRANSFER_FAILED, "snapshot");
+        o += nbytes;
+    };
+    down(ops_, n_ * row_bytes);
+    if (ops_lo_.get()) down(ops_lo_, n_ * row_bytes);
+    if (norms_.get()) down(norms_, n_ * 4);
+    if (live_.get()) {
+        std::memcpy(o, live_host_.data(), live_host_.size() * 4);
+        o += live_host_.size() * 4;
+    }
+}
+
+void ExactIndex::import_blob(const void* blob, size_t bytes) {
+    if (blob == nullptr || bytes < sizeof(BlobHeader)) fail(ELIPS_B200_INVALID_ARGUMENT, "snapshot too short");
+    if (n_ != 0) fail(ELIPS_B200_INVALID_ARGUMENT, "snapshots load into an empty index");
+    BlobHeader h;
+    std::memcpy(&h, blob, sizeof(h));
+    if (h.magic != kBlobMagic || h.version != kBlobVersion) fail(ELIPS_B200_INVALID_ARGUMENT, "not an index snapshot");
+    if (h.metric != metric_ || h.precision != precision_ || h.dim != dim_ || h.d_pad != d_pad_ ||
+        h.elem_bytes != elem_bytes_)
+        fail(ELIPS_B200_DIMENSION_MISMATCH, "snapshot of a different metric, precision or dimension");
+    const bool has_lo = (h.flags & 1u) != 0, has_norms = (h.flags & 2u) != 0, has_live = (h.flags & 4u) != 0;
+    if (has_lo != (kind_ == OperandKind::TF32X3) || has_norms != (metric_ == kEuclidean))
+        fail(ELIPS_B200_INVALID_ARGUMENT, "snapshot planes do not match the index");
+    const size_t rows = h.rows, row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    const size_t words = (rows + 31) / 32;
+    const size_t need = sizeof(h) + rows * row_bytes * (has_lo ? 2 : 1) + (has_norms ? rows * 4 : 0) +
+                        (has_live ? words * 4 : 0);
+    if (bytes < need) fail(ELIPS_B200_INVALID_ARGUMENT, "snapshot truncated");
+    if (rows >= 0xFFFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "index limited to 2^32-2 rows");
+    DeviceGuard g(device_);
+    reserve(std::max<size_t>(rows, 1));
+    const uint8_t* in = static_cast<const uint8_t*>(blob) + sizeof(h);
+    auto up = [&](DeviceBuffer& b, size_t nbytes) {
+        if (nbytes == 0) return;
+        check_cuda(cudaMemcpy(b.get(), in, nbytes, cudaMemcpyHostToDevice), ELIPS_B200_TRANSFER_FAILED, "snapshot");
+        in += nbytes;
+    };
+    up(ops_, rows * row_bytes);
+    if (has_lo) up(ops_lo_, rows * row_bytes);
+    if (has_norms) up(norms_, rows * 4);
+    n_ = rows;
+    if (has_live) {
+        live_ = DeviceBuffer(device_, (capacity_ + 31) / 32 * 4);
+        live_host_.assign(reinterpret_cast<const uint32_t*>(in), reinterpret_cast<const uint32_t*>(in) + words);
+        removed_ = 0;
+        for (size_t r = 0; r < rows; ++r) removed_ += ((live_host_[r >> 5] >> (r & 31)) & 1u) ? 0 : 1;
+        if (removed_ != h.removed) fail(ELIPS_B200_INVALID_ARGUMENT, "snapshot removal bits inconsistent");
+        upload_live_words(0, words);
+    }
+}
+
+bool ExactIndex::remove(size_t row) {
+    if (row >= n_) fail(ELIPS_B200_INVALID_ARGUMENT, "row out of range");
+    DeviceGuard g(device_);
+    // Searches still running on any stream may be reading the bits.
+    check_cuda(cudaDeviceSynchronize(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "remove sync");
+    if (live_.get() == nullptr) {
+        live_ = DeviceBuffer(device_, (capacity_ + 31) / 32 * 4);
+        live_host_.assign((n_ + 31) / 32, 0u);
+        for (size_t r = 0; r < n_; ++r) live_host_[r >> 5] |= 1u << (r & 31);
+        upload_live_words(0, live_host_.size());
+    }
+    uint32_t& w = live_host_[row >> 5];
+    const uint32_t bit = 1u << (row & 31);
+    if ((w & bit) == 0) return false;
+    w &= ~bit;
+    ++removed_;
+    upload_live_words(row >> 5, (row >> 5) + 1);
+    return true;
 }
 
 void ExactIndex::add(const void* rows_host, size_t n) {
@@ -412,6 +602,7 @@ void ExactIndex::add(const void* rows_host, size_t n) {
         throw;
     }
     cudaStreamDestroy(stream);
+    mark_live(n_, n);
     n_ += n;
 }
 
@@ -428,6 +619,7 @@ void ExactIndex::add_device(const void* rows, size_t n, cudaStream_t stream) {
                   ops_lo_.get() ? static_cast<uint8_t*>(ops_lo_.get()) + n_ * row_bytes : nullptr,
                   norms_.get() ? static_cast<float*>(norms_.get()) + n_ : nullptr, stream);
     check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "row prep");
+    mark_live(n_, n);
     n_ += n;
 }
 
@@ -483,6 +675,7 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     prm.base_norms = static_cast<const float*>(norms_.get());
     prm.query_norms = qn;
     prm.mask = mask;
+    prm.live = static_cast<const uint32_t*>(live_.get());
     prm.cand = cand_buf;
     prm.partial = part_buf;
     prm.qtau = qtau_buf;
@@ -560,6 +753,7 @@ void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t
     prm.base_norms = static_cast<const float*>(norms_.get());
     prm.query_norms = qn;
     prm.mask = mask;
+    prm.live = static_cast<const uint32_t*>(live_.get());
     prm.cand = cand_buf;
     prm.partial = part_buf;
     prm.qtau = qtau_buf;

@@ -9,6 +9,7 @@
 #include <cstdint>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "exact_topk.cuh"
 
@@ -106,7 +107,27 @@ public:
     void add(const void* rows_host, size_t n);
     // rows: device memory, same element type as add(); converted on `stream`.
     void add_device(const void* rows, size_t n, cudaStream_t stream);
+    // Rows ever added (the row-number space searches report in).
     size_t size() const { return n_; }
+    // Rows not removed.
+    size_t live() const { return n_ - removed_; }
+
+    // Removes one row in place: its row number stays reserved and no search
+    // reports it again (a tombstone bit folded into the eligibility mask), so
+    // no buffer is rebuilt and the other rows keep their numbers and order.
+    // Returns false when the row was already removed.
+    bool remove(size_t row);
+    // Drops the removed rows, keeping the others in order; new_to_old (host,
+    // live() entries) receives each kept row's former number.
+    void compact(uint32_t* new_to_old);
+
+    // Device snapshot: the stored operand rows (with their norms and the
+    // removal bits) as one host blob that import_blob restores into an empty
+    // index of the same metric, precision and dimension without converting
+    // the rows again.
+    size_t blob_bytes() const;
+    void export_blob(void* out, size_t bytes) const;
+    void import_blob(const void* blob, size_t bytes);
     int device() const { return device_; }
     int metric() const { return metric_; }
     uint32_t dim() const { return dim_; }
@@ -136,6 +157,12 @@ private:
     uint32_t dim_, d_pad_, elem_bytes_;
     size_t n_ = 0, capacity_ = 0;
     DeviceBuffer ops_, ops_lo_, norms_;
+    // Removal bits: created at the first remove (null = every row live).
+    DeviceBuffer live_;
+    std::vector<uint32_t> live_host_;
+    size_t removed_ = 0;
+    void mark_live(size_t first, size_t count);
+    void upload_live_words(size_t w0, size_t w1);
 };
 
 // Final merge over candidate lists (see merge_topk_kernel).

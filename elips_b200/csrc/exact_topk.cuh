@@ -51,6 +51,7 @@ struct ExactParams {
     const float* base_norms;   // [n] squared norms (euclidean only)
     const float* query_norms;  // [nq] squared norms (euclidean only)
     const uint32_t* mask;      // [ceil(n/32)] eligibility bits, or null
+    const uint32_t* live;      // [ceil(n/32)] 0 bits = removed rows, or null (none removed)
     uint2* cand;               // [gridDim.x][2][128][cap] candidate lists per (column half, query)
     uint2* partial;            // [nq][splits][2][k]
     uint32_t* qtau;            // [nq] shared admission bound per query (ordered key)
@@ -450,6 +451,7 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                     const uint32_t valid_rows = min(32u, p.n - row0);
                     uint32_t mword = valid_rows == 32u ? 0xFFFFFFFFu : ((1u << valid_rows) - 1u);
                     if (p.mask != nullptr) mword &= __ldg(p.mask + (row0 >> 5));
+                    if (p.live != nullptr) mword &= __ldg(p.live + (row0 >> 5));
                     if (!qvalid) mword = 0;
                     const float* xn = xs + c * 32u;
                     // Fast reject: most chunks hold nothing below the threshold.

@@ -83,9 +83,41 @@ class ExactIndex:
         self.add(np.asarray(vector, dtype=self._in_dtype).reshape(1, -1))
 
     def size(self) -> int:
+        """Rows ever added: the slot-number space results are reported in."""
         n = ctypes.c_size_t(0)
         capi.check(capi.LIB.elips_b200_exact_size(self._h, ctypes.byref(n)), "elips_b200_exact_size")
         return n.value
+
+    def live(self) -> int:
+        """Rows not removed."""
+        n = ctypes.c_size_t(0)
+        capi.check(capi.LIB.elips_b200_exact_live(self._h, ctypes.byref(n)), "elips_b200_exact_live")
+        return n.value
+
+    def remove(self, slot: int) -> bool:
+        """Removes one row on the device (no rebuild); False if already removed."""
+        r = ctypes.c_int(0)
+        capi.check(capi.LIB.elips_b200_exact_remove(self._h, int(slot), ctypes.byref(r)), "elips_b200_exact_remove")
+        return bool(r.value)
+
+    def compact(self) -> np.ndarray:
+        """Drops removed rows keeping order; returns each kept row's former slot."""
+        out = np.empty(max(1, self.live()), np.uint32)
+        capi.check(capi.LIB.elips_b200_exact_compact(self._h, _ptr(out), out.shape[0]), "elips_b200_exact_compact")
+        return out[:self.live()]
+
+    def export_snapshot(self) -> bytes:
+        """The device rows (operands, norms, removal bits) as one blob."""
+        n = ctypes.c_size_t(0)
+        capi.check(capi.LIB.elips_b200_exact_snapshot_bytes(self._h, ctypes.byref(n)), "elips_b200_exact_snapshot_bytes")
+        buf = np.empty(n.value, np.uint8)
+        capi.check(capi.LIB.elips_b200_exact_export(self._h, _ptr(buf), buf.shape[0]), "elips_b200_exact_export")
+        return buf.tobytes()
+
+    def import_snapshot(self, blob: bytes) -> None:
+        """Restores export_snapshot's blob into this (empty) index."""
+        buf = np.frombuffer(blob, np.uint8)
+        capi.check(capi.LIB.elips_b200_exact_import(self._h, _ptr(buf), buf.shape[0]), "elips_b200_exact_import")
 
     def search(self, query: np.ndarray, k: int) -> list[tuple[int, float]]:
         """IndexPort::search for one query: up to k (slot, distance) pairs."""

@@ -103,6 +103,32 @@ ELIPS_B200_API int elips_b200_exact_add_device(elips_b200_exact* index, const vo
 /* IndexPort::size. */
 ELIPS_B200_API int elips_b200_exact_size(const elips_b200_exact* index, size_t* n_out);
 
+/* Rows not removed (elips_b200_exact_size counts every row ever added: the
+ * row-number space results are reported in). */
+ELIPS_B200_API int elips_b200_exact_live(const elips_b200_exact* index, size_t* n_out);
+
+/* Incremental removal on the device, in place of GpuBruteForceIndex::remove's
+ * full re-upload (src/gpu_engine/GpuBruteForceIndex.cpp:84-99): the row keeps
+ * its number but no search returns it again (a removal bit folded into the
+ * eligibility mask); the other rows keep their numbers and relative order, so
+ * equal distances still rank as the reference's erase-based order ranks them.
+ * removed_out (may be NULL) is 0 when the row was already removed. Not
+ * concurrent with searches (the reference removes under Vault's unique lock). */
+ELIPS_B200_API int elips_b200_exact_remove(elips_b200_exact* index, size_t row, int* removed_out);
+
+/* Drops the removed rows on the device, keeping the order of the others.
+ * new_to_old (may be NULL; `capacity` entries, at least the live count)
+ * receives each kept row's former number, so the caller can renumber its ids. */
+ELIPS_B200_API int elips_b200_exact_compact(elips_b200_exact* index, uint32_t* new_to_old, size_t capacity);
+
+/* Device snapshot (IndexSnapshot, include/elips/index_engine/IndexSnapshot.hpp:
+ * 26-56, without the ids the caller keeps): the stored operand rows, norms and
+ * removal bits as one host blob, reloaded into an empty index of the same
+ * metric, precision and dimension without converting the rows again. */
+ELIPS_B200_API int elips_b200_exact_snapshot_bytes(const elips_b200_exact* index, size_t* bytes_out);
+ELIPS_B200_API int elips_b200_exact_export(const elips_b200_exact* index, void* out, size_t bytes);
+ELIPS_B200_API int elips_b200_exact_import(elips_b200_exact* index, const void* blob, size_t bytes);
+
 ELIPS_B200_API int elips_b200_exact_destroy(elips_b200_exact* index);
 
 /* GpuIndexPort::search_batch (GpuIndexPort.hpp:120-124) / ExactIndex::search
