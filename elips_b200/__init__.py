@@ -7,7 +7,7 @@ it is missing: there is no CPU fallback.
 """
 from . import _capi
 from ._capi import ElipsB200Error, device_count, status_name
-from .exact import DimensionMismatch, ExactIndex, merge_candidates_device
+from .exact import DimensionMismatch, DynamicBatcher, ExactIndex, merge_candidates_device
 
-__all__ = ["ElipsB200Error", "DimensionMismatch", "ExactIndex", "merge_candidates_device",
+__all__ = ["ElipsB200Error", "DimensionMismatch", "DynamicBatcher", "ExactIndex", "merge_candidates_device",
            "device_count", "status_name"]

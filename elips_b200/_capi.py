@@ -6,7 +6,7 @@ missing or fails to load, importing this module raises.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libelips_b200.so"
@@ -77,6 +77,12 @@ SIGNATURES = [
     ("elips_b200_exact_snapshot_bytes", c_int, [c_void_p, POINTER(c_size_t)]),
     ("elips_b200_exact_export", c_int, [c_void_p, c_void_p, c_size_t]),
     ("elips_b200_exact_import", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("elips_b200_ivfpq_export", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_ivfflat_export", c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_batcher_create", c_int, [c_void_p, c_size_t, c_size_t, POINTER(c_void_p)]),
+    ("elips_b200_batcher_search", c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    ("elips_b200_batcher_stats", c_int, [c_void_p, POINTER(c_uint64), POINTER(c_uint64)]),
+    ("elips_b200_batcher_destroy", c_int, [c_void_p]),
     ("elips_b200_normalize_rows", c_int, [c_int, c_void_p, c_void_p, c_size_t, c_size_t, c_int, c_void_p]),
     ("elips_b200_kmeans", c_int, [c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p, c_int, c_void_p]),
     ("elips_b200_train_pq_codebook", c_int,

@@ -18,7 +18,7 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 LIB = PKG / "libelips_b200.so"
 
-SOURCES = ["engine.cu", "capi.cu", "noalloc.cu", "quant.cu", "ivfpq.cu", "train.cu"]
+SOURCES = ["engine.cu", "capi.cu", "noalloc.cu", "quant.cu", "ivfpq.cu", "train.cu", "batcher.cu"]
 
 NVCC_FLAGS = [
     "-O3",

@@ -282,6 +282,23 @@ protected:
         launch_ok("ivf group scan kernel");
     }
 
+public:
+    // IndexSnapshot's IVF section and vectors (IndexSnapshot.hpp:26-56) in
+    // slot order, into host memory; any output may be null.
+    void export_ivf(float* centroids, uint32_t* assignments, float* vectors) const {
+        DeviceGuard g(device_);
+        check_cuda(cudaDeviceSynchronize(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "export sync");
+        if (centroids != nullptr)
+            check_cuda(cudaMemcpy(centroids, centroids_.get(), static_cast<size_t>(nlist_) * dim_ * 4,
+                                  cudaMemcpyDeviceToHost),
+                       ELIPS_B200_TRANSFER_FAILED, "centroid export");
+        if (assignments != nullptr) std::copy(assign_.begin(), assign_.end(), assignments);
+        if (vectors != nullptr && n_ > 0)
+            check_cuda(cudaMemcpy(vectors, vectors_.get(), n_ * dim_ * 4, cudaMemcpyDeviceToHost),
+                       ELIPS_B200_TRANSFER_FAILED, "vector export");
+    }
+
+protected:
     int device_, metric_;
     uint32_t dim_, nlist_, nprobe_;
     std::vector<bool> owned_host_;
@@ -315,6 +332,19 @@ public:
     }
 
     uint32_t pq_dim() const { return m_; }
+
+    // The PQ section of IndexSnapshot: codebook [pq_dim][ksub][dim/pq_dim] and
+    // codes [n][pq_dim] in slot order, into host memory; either may be null.
+    void export_pq(float* codebook, uint8_t* codes) const {
+        DeviceGuard g(device_);
+        check_cuda(cudaDeviceSynchronize(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "export sync");
+        if (codebook != nullptr)
+            check_cuda(cudaMemcpy(codebook, codebook_.get(), static_cast<size_t>(ksub_) * dim_ * 4, cudaMemcpyDeviceToHost),
+                       ELIPS_B200_TRANSFER_FAILED, "codebook export");
+        if (codes != nullptr && n_ > 0)
+            check_cuda(cudaMemcpy(codes, codes_.get(), n_ * m_, cudaMemcpyDeviceToHost), ELIPS_B200_TRANSFER_FAILED,
+                       "code export");
+    }
 
     // Appends n rows (DEVICE pointers). assign: list of each row; codes may be
     // null, in which case the residuals are encoded on the device exactly as
@@ -696,6 +726,15 @@ int elips_b200_ivfpq_rerank_device(elips_b200_ivfpq* index, const float* queries
     });
 }
 
+int elips_b200_ivfpq_export(const elips_b200_ivfpq* index, float* centroids_out, uint32_t* assignments_out,
+                            float* vectors_out, float* codebook_out, uint8_t* codes_out) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        index->index.export_ivf(centroids_out, assignments_out, vectors_out);
+        index->index.export_pq(codebook_out, codes_out);
+    });
+}
+
 int elips_b200_ivfpq_codes_device(const elips_b200_ivfpq* index, uint8_t* codes_out, void* stream) {
     if (index == nullptr || codes_out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] { index->index.read_codes(codes_out, static_cast<cudaStream_t>(stream)); });
@@ -741,6 +780,12 @@ int elips_b200_ivfflat_add_device(elips_b200_ivfflat* index, const float* vector
                                   size_t n, void* stream) {
     if (index == nullptr || (n > 0 && (vectors == nullptr || assignments == nullptr))) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] { index->index.add_device(vectors, assignments, n, static_cast<cudaStream_t>(stream)); });
+}
+
+int elips_b200_ivfflat_export(const elips_b200_ivfflat* index, float* centroids_out, uint32_t* assignments_out,
+                              float* vectors_out) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.export_ivf(centroids_out, assignments_out, vectors_out); });
 }
 
 int elips_b200_ivfflat_size(const elips_b200_ivfflat* index, size_t* n_out) {

@@ -205,3 +205,45 @@ def merge_candidates_device(cand, lists: int, k: int, metric: str, out_dist=None
         dev.index, cand.data_ptr(), nq, lists, k, METRICS[metric], out_dist.data_ptr(),
         out_rows.data_ptr(), s), "elips_b200_merge_candidates_device")
     return out_dist, out_rows
+
+
+class DynamicBatcher:
+    """Coalesces concurrent single-query searches on an ExactIndex into batched
+    launches (elips::gpu::DynamicBatcher, src/gpu_engine/DynamicBatcher.cpp).
+    search() blocks until the caller's batch ran; safe to call from many
+    threads (the GIL is released inside the C call)."""
+
+    def __init__(self, index: ExactIndex, window_us: int = 500, max_batch: int = 256):
+        self.index = index
+        h = ctypes.c_void_p()
+        capi.check(capi.LIB.elips_b200_batcher_create(index._h, int(window_us), int(max_batch), ctypes.byref(h)),
+                   "elips_b200_batcher_create")
+        self._h = h
+
+    def search(self, query: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+        q = np.ascontiguousarray(query, dtype=self.index._in_dtype).reshape(-1)
+        if q.shape[0] != self.index.dimension:
+            raise DimensionMismatch("query dimension does not match index")
+        dist = np.empty(k, np.float32)
+        rows = np.empty(k, np.int64)
+        capi.check(capi.LIB.elips_b200_batcher_search(self._h, _ptr(q), k, _ptr(dist), _ptr(rows)),
+                   "elips_b200_batcher_search")
+        return dist, rows
+
+    def stats(self) -> dict:
+        l, q = ctypes.c_uint64(0), ctypes.c_uint64(0)
+        capi.check(capi.LIB.elips_b200_batcher_stats(self._h, ctypes.byref(l), ctypes.byref(q)),
+                   "elips_b200_batcher_stats")
+        return {"kernel_launches": l.value, "queries_coalesced": q.value,
+                "avg_batch_size": q.value / l.value if l.value else 0.0}
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            capi.LIB.elips_b200_batcher_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -30,7 +30,7 @@ class IvfPqIndex:
         cb = np.ascontiguousarray(codebook, np.float32)
         if cent.shape[1] != self.dimension:
             raise DimensionMismatch("centroid dimension does not match index")
-        self.n_lists, self.pq_dim = cent.shape[0], cb.shape[0]
+        self.n_lists, self.pq_dim, self.pq_bits = cent.shape[0], cb.shape[0], int(pq_bits)
         h = ctypes.c_void_p()
         capi.check(capi.LIB.elips_b200_ivfpq_create(self.device, METRICS[metric], self.dimension, self.n_lists,
                                                     int(nprobe), self.pq_dim, int(pq_bits), _ptr(cent), _ptr(cb),
@@ -57,6 +57,19 @@ class IvfPqIndex:
         capi.check(capi.LIB.elips_b200_ivfpq_add_device(self._h, vectors.data_ptr(), assignments.data_ptr(),
                                                         codes.data_ptr() if codes is not None else None,
                                                         vectors.shape[0], s), "elips_b200_ivfpq_add_device")
+
+    def export_snapshot(self) -> dict:
+        """IndexSnapshot's fields in slot order: centroids, assignments,
+        vectors, codebook, codes (elips_b200_ivfpq_create + add rebuild it)."""
+        n, d = self.size(), self.dimension
+        out = {"centroids": np.empty((self.n_lists, d), np.float32), "assignments": np.empty(n, np.uint32),
+               "vectors": np.empty((n, d), np.float32),
+               "codebook": np.empty((self.pq_dim, 1 << self.pq_bits, d // self.pq_dim), np.float32),
+               "codes": np.empty((n, self.pq_dim), np.uint8)}
+        capi.check(capi.LIB.elips_b200_ivfpq_export(self._h, _ptr(out["centroids"]), _ptr(out["assignments"]),
+                                                    _ptr(out["vectors"]), _ptr(out["codebook"]), _ptr(out["codes"])),
+                   "elips_b200_ivfpq_export")
+        return out
 
     def size(self) -> int:
         n = ctypes.c_size_t(0)
@@ -183,6 +196,15 @@ class IvfFlatIndex:
         s = stream if stream is not None else torch.cuda.current_stream(vectors.device).cuda_stream
         capi.check(capi.LIB.elips_b200_ivfflat_add_device(self._h, vectors.data_ptr(), assignments.data_ptr(),
                                                           vectors.shape[0], s), "elips_b200_ivfflat_add_device")
+
+    def export_snapshot(self) -> dict:
+        """centroids, assignments and vectors in slot order."""
+        n, d = self.size(), self.dimension
+        out = {"centroids": np.empty((self.n_lists, d), np.float32), "assignments": np.empty(n, np.uint32),
+               "vectors": np.empty((n, d), np.float32)}
+        capi.check(capi.LIB.elips_b200_ivfflat_export(self._h, _ptr(out["centroids"]), _ptr(out["assignments"]),
+                                                      _ptr(out["vectors"])), "elips_b200_ivfflat_export")
+        return out
 
     def size(self) -> int:
         n = ctypes.c_size_t(0)

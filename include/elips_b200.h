@@ -336,6 +336,16 @@ ELIPS_B200_API int elips_b200_ivfpq_rerank_device(elips_b200_ivfpq* index, const
                                                   size_t nq, size_t k, const uint32_t* cand,
                                                   float* out_dist, int64_t* out_rows, void* stream);
 
+/* Snapshot readback (IndexSnapshot, IndexSnapshot.hpp:26-56): centroids
+ * [n_lists][dim], assignments [n], vectors [n][dim], codebook
+ * [pq_dim][ksub][dim/pq_dim] and codes [n][pq_dim], all in slot order into host
+ * memory (any output may be NULL). elips_b200_ivfpq_create + _add with these
+ * rebuilds the same index (GpuIVFPQIndex::import_snapshot, GpuIVFPQIndex.cpp:
+ * 327-348, takes the codes as given). */
+ELIPS_B200_API int elips_b200_ivfpq_export(const elips_b200_ivfpq* index, float* centroids_out,
+                                           uint32_t* assignments_out, float* vectors_out,
+                                           float* codebook_out, uint8_t* codes_out);
+
 ELIPS_B200_API int elips_b200_ivfpq_destroy(elips_b200_ivfpq* index);
 
 /* -------------------------------------------------------------- IVF-Flat */
@@ -379,7 +389,31 @@ ELIPS_B200_API int elips_b200_ivfflat_search_device(elips_b200_ivfflat* index, c
                                                     size_t nq, size_t k, float* out_dist,
                                                     int64_t* out_rows, void* stream);
 
+/* Snapshot readback: centroids, assignments and vectors in slot order (any may be NULL). */
+ELIPS_B200_API int elips_b200_ivfflat_export(const elips_b200_ivfflat* index, float* centroids_out,
+                                             uint32_t* assignments_out, float* vectors_out);
+
 ELIPS_B200_API int elips_b200_ivfflat_destroy(elips_b200_ivfflat* index);
+
+/* ------------------------------------------------------ dynamic batching */
+/* elips::gpu::DynamicBatcher (src/gpu_engine/DynamicBatcher.cpp:1-124) over a
+ * device exact index: concurrent single-query callers are coalesced (up to
+ * max_batch queries, waiting at most window_us after the first) into one fused
+ * search launch. elips_b200_batcher_search blocks until the caller's batch has
+ * run and fills its k results exactly as elips_b200_exact_search would. Each
+ * caller keeps its own k (the reference uses the first query's k for the
+ * whole batch). The index must outlive the batcher and not change while it
+ * runs; destroying the batcher serves the queries still pending. */
+typedef struct elips_b200_batcher elips_b200_batcher;
+
+ELIPS_B200_API int elips_b200_batcher_create(const elips_b200_exact* index, size_t window_us,
+                                             size_t max_batch, elips_b200_batcher** out);
+ELIPS_B200_API int elips_b200_batcher_search(elips_b200_batcher* batcher, const void* query, size_t k,
+                                             float* out_dist, int64_t* out_rows);
+/* Launches and queries so far (BatchStats::kernel_launches / queries_coalesced). */
+ELIPS_B200_API int elips_b200_batcher_stats(const elips_b200_batcher* batcher, uint64_t* launches,
+                                            uint64_t* queries);
+ELIPS_B200_API int elips_b200_batcher_destroy(elips_b200_batcher* batcher);
 
 /* ----------------------------------------------------------- index build */
 /* Trainers, bit-identical to the reference's CPU loops (sequential fp32 sums,
