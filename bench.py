@@ -56,6 +56,18 @@ CONFIGS = {
         n=10_000_000, d=128, q=10_000, k=10, metric="euclidean", precision="fp32", data="mixture",
         centroids=4096, sigma=0.2, normalized=False, nlist=4096, pq_dim=16, pq_bits=8, nprobe=32,
         kmeans_iters=4, dtype="f32 (u8 PQ codes)"),
+    "ivf_build": dict(
+        workload="IVF-PQ model build as GpuIVFPQIndex::build_from_batch (IVF k-means 4 rounds + final "
+                 "assignment, PQ 16 x 8 bits trained 10 rounds on all residuals, residual codes), N=10,000,000 x "
+                 "d=128 Gaussian mixture (4,096 centroids, sigma=0.2, fp32), nlist=4,096",
+        n=10_000_000, d=128, q=0, k=0, metric="euclidean", precision="fp32", data="mixture",
+        centroids=4096, sigma=0.2, normalized=False, nlist=4096, pq_dim=16, pq_bits=8, nprobe=32,
+        kmeans_iters=4, dtype="f32 (sequential sums, no FMA)"),
+    "batcher": dict(
+        workload="DynamicBatcher: 64 concurrent callers of single-query exact L2 bf16 search, N=1,000,000 x "
+                 "d=384 N(0,1), k=20, window 200 us, max batch 256",
+        n=1_000_000, d=384, q=4096, k=20, metric="euclidean", precision="bf16", data="gaussian",
+        callers=64, window_us=200, max_batch=256, dtype="bf16 (fp32 accumulate)"),
 }
 DEFAULT_CONFIG = "exact_fp16_cosine"
 METRIC_NAME = "k-NN queries/sec (exact d=768 N=2M k=100; IVF-PQ) at 1/2/4/8 B200, % roofline"
@@ -266,17 +278,24 @@ def train_ivfpq_model(cfg, base):
     return cent, assign, cb, codes, time.perf_counter() - t
 
 
-def ivfpq_inputs(cfg, dev, train=True):
-    """Seeded base rows and queries of the IVF-PQ workload and its trained
-    model, all on `dev`: (base, queries, centroids, assignments, codebook,
-    codes, build seconds); the model entries are None when train is False."""
+def ivf_base_rows(cfg, dev, cents=None):
+    """The seeded base rows of an IVF workload, [n, d] float32 on `dev`."""
     import torch
     n, d = cfg["n"], cfg["d"]
-    cents = _centroids(cfg, dev)
+    cents = _centroids(cfg, dev) if cents is None else cents
     base = torch.empty((n, d), dtype=torch.float32, device=dev)
     for r0 in range(0, n, 1 << 20):
         cnt = min(1 << 20, n - r0)
         base[r0:r0 + cnt] = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev)
+    return base
+
+
+def ivfpq_inputs(cfg, dev, train=True):
+    """Seeded base rows and queries of the IVF-PQ workload and its trained
+    model, all on `dev`: (base, queries, centroids, assignments, codebook,
+    codes, build seconds); the model entries are None when train is False."""
+    cents = _centroids(cfg, dev)
+    base = ivf_base_rows(cfg, dev, cents)
     queries = gen_rows(cfg, 0, cfg["q"], SEED + 2, cfg["q"], cents, device=dev)
     if not train:
         return base, queries, None, None, None, None, None
@@ -636,6 +655,200 @@ def _ref_or_port():
         return oracle, "port"
 
 
+# ------------------------------------------------------------ index build
+
+def _build_flops(n, d, nlist, m, ksub, iters):
+    """Lane operations of the assignment passes of one IVF-PQ build: 3 per
+    (row, centroid, dimension) (subtract, multiply, add): max(1, iters) + 1
+    IVF passes, 10 PQ rounds plus the encode pass over every subspace."""
+    ivf = (max(1, iters) + 1) * n * nlist * d
+    pq = 11 * n * ksub * d
+    return 3.0 * (ivf + pq), 3.0 * n * nlist * d
+
+
+def _reference_build_rate(cfg, base_np):
+    """The reference's own build (IvfIndexState::train_centroids through
+    GpuIVFFlatIndex::build_from_batch, single-threaded as it is) on a bounded
+    sample at the workload's nlist and dimension: seconds per row per IVF
+    assignment pass, extrapolated to the workload's build. Returns
+    (rows/s, description, cores, kind)."""
+    oracle, kind = _ref_or_port()
+    ns = max(cfg["nlist"] * 2, 8192)
+    sample = np.ascontiguousarray(base_np[:ns])
+    t = time.perf_counter()
+    if kind == "reference":
+        oracle.ref_ivf_train(cfg["metric"], sample, cfg["nlist"], 1)
+    else:
+        oracle.ivf_train(cfg["metric"], sample, cfg["nlist"], 1)
+    dt = time.perf_counter() - t
+    per_row_pass = dt / (ns * 2)
+    total, per_pass = _build_flops(cfg["n"], cfg["d"], cfg["nlist"], cfg["pq_dim"], 1 << cfg["pq_bits"],
+                                   cfg["kmeans_iters"])
+    passes = total / per_pass
+    rate = 1.0 / (per_row_pass * passes)
+    what = (f"{'reference GpuIVFFlatIndex::build_from_batch' if kind == 'reference' else 'C restatement'} "
+            f"on {ns} rows, nlist {cfg['nlist']}, 1 round (2 assignment passes) in {dt:.2f} s; extrapolated to "
+            f"{passes:.2f} pass-equivalents per row for the full build (PQ rounds counted by their lane "
+            f"operations)")
+    return rate, what, 1, kind
+
+
+def run_b200_build(args, cfg):
+    """Rows/s of the whole IVF-PQ model build on one GPU (device-resident rows)."""
+    import torch
+    from elips_b200 import _capi, train
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, d = cfg["n"], cfg["d"]
+    base = ivf_base_rows(cfg, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return train.ivfpq_train_device(cfg["metric"], base, cfg["nlist"], cfg["kmeans_iters"], cfg["pq_dim"],
+                                        cfg["pq_bits"])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _capi.profiler_reset()
+    _capi.profiler_enable(True)
+    launches0 = _capi.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(0)
+    with sampler:
+        time.sleep(0.25)
+        sampler.active = True
+        ev0.record(stream)
+        for _ in range(args.steps):
+            out = step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        sampler.active = False
+    launches = _capi.launch_count() - launches0
+    ms = ev0.elapsed_time(ev1)
+    near = _capi.profiler_stats("nearest_centroid")
+    _capi.profiler_enable(False)
+    cent, asg, cb, codes = (t.cpu().numpy() for t in out)
+    # e2e: the host-buffer entry point, rows copied in and the model copied out.
+    host = base.cpu().numpy()
+    t = time.perf_counter()
+    train.ivfpq_train("euclidean", host, cfg["nlist"], cfg["kmeans_iters"], cfg["pq_dim"], cfg["pq_bits"])
+    e2e_s = time.perf_counter() - t
+    total, _ = _build_flops(n, d, cfg["nlist"], cfg["pq_dim"], 1 << cfg["pq_bits"], cfg["kmeans_iters"])
+    near_ms = near["total_ms"] / max(1, args.steps)
+    achieved = total / (near_ms / 1e3) / 1e12
+    sm_max = load_peaks()[0].get("sm_max_mhz", 1965.0)
+    peak = 148 * 128 * sm_max * 1e6 / 1e12
+    result = {
+        "metric": "IVF-PQ model build rows/s (build_from_batch semantics, bit-identical)", "value": round(n * args.steps / (ms / 1e3), 1),
+        "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes and distributions of the configuration)",
+        "config": {"workload": cfg["workload"], "config": args.config, "rows": n, "dim": d, "nlist": cfg["nlist"],
+                   "pq": f"{cfg['pq_dim']}x{cfg['pq_bits']}", "l2": "inputs larger than L2 (rows 5.1 GB); no flush"},
+        "e2e": {"value": round(n / e2e_s, 1), "unit": "rows/s", "h2d_bytes_per_step": int(host.nbytes),
+                "d2h_bytes_per_step": int(cent.nbytes + asg.nbytes + cb.nbytes + codes.nbytes),
+                "api": "elips_b200_ivfpq_train (host buffers)"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "fp32-simt", "achieved": round(achieved, 2), "peak": round(peak, 2),
+                     "unit": "T lane-ops/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": "nearest_centroid_kernel", "kernel_ms_per_step": round(near_ms, 2),
+                     "kernel_share_of_step": round(near["total_ms"] / max(1e-9, ms), 4),
+                     "algorithmic_lane_ops_per_step": total,
+                     "peak_source": "nominal FP32 issue rate (148 SMs x 128 lanes x max SM clock): the exact "
+                                    "sequential sums cannot use FMA or tensor cores; no measured figure exists"},
+        "clocks": sampler.summary()}
+    if not args.no_cpu_baseline:
+        rate, what, cores, kind = _reference_build_rate(cfg, host)
+        result["cpu_baseline"] = {"value": round(rate, 3), "unit": "rows/s", "cores": cores, "kind": kind,
+                                  "sample": what}
+    return result
+
+
+# ------------------------------------------------------ dynamic batching
+
+def run_b200_batcher(args, cfg):
+    """Queries/s of `callers` host threads, each issuing single-query searches
+    through DynamicBatcher (host buffers in and out: the value is end to end)."""
+    import threading
+    import torch
+    from elips_b200 import DynamicBatcher, ExactIndex, _capi
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, d, k, callers = cfg["n"], cfg["d"], cfg["k"], cfg["callers"]
+    ix = ExactIndex(cfg["metric"], d, precision=cfg["precision"])
+    for r0 in range(0, n, CHUNK):
+        ix.add_device(gen_rows(cfg, r0, min(CHUNK, n - r0), SEED + 1, n, None, device=dev))
+    queries = gen_rows(cfg, 0, cfg["q"], SEED + 2, cfg["q"], None, device=dev).cpu().numpy()
+    b = DynamicBatcher(ix, window_us=cfg["window_us"], max_batch=cfg["max_batch"])
+    per = max(1, args.steps)
+
+    def drive(count):
+        lat = []
+        def work(t):
+            for i in range(count):
+                x = queries[(t * count + i) % len(queries)]
+                t0 = time.perf_counter()
+                b.search(x, k)
+                lat.append(time.perf_counter() - t0)
+        ts = [threading.Thread(target=work, args=(t,)) for t in range(callers)]
+        t0 = time.perf_counter()
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        return time.perf_counter() - t0, np.array(lat)
+
+    drive(max(1, args.warmup))
+    _capi.profiler_reset()
+    _capi.profiler_enable(True)
+    launches0 = _capi.launch_count()
+    st0 = b.stats()
+    sampler = ClockSampler(0)
+    with sampler:
+        sampler.active = True
+        wall, lat = drive(per)
+        sampler.active = False
+    st1 = b.stats()
+    kern = _capi.profiler_stats("exact_topk")
+    launches = _capi.launch_count() - launches0
+    _capi.profiler_enable(False)
+    b.close()
+    total = callers * per
+    batches = st1["kernel_launches"] - st0["kernel_launches"]
+    kms = kern["total_ms"] / max(1, kern["launches"])
+    bytes_per_launch = n * d * 2
+    achieved = bytes_per_launch / (kms / 1e3) / 1e9
+    peaks, peak_src = load_peaks()
+    result = {
+        "metric": "k-NN queries/sec through DynamicBatcher (concurrent single-query callers)",
+        "value": round(total / wall, 1), "unit": "queries/s", "n_gpus": 1, "steps": per, "warmup": args.warmup,
+        "ms_per_step": round(wall / per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic (seeded; shapes and distributions of the configuration)",
+        "config": {"workload": cfg["workload"], "config": args.config, "base_rows": n, "dim": d, "k": k,
+                   "callers": callers, "queries_per_caller_per_run": per,
+                   "l2": "base 768 MB > L2, read by every launch; no flush"},
+        "e2e": {"value": round(total / wall, 1), "unit": "queries/s", "h2d_bytes_per_step": callers * d * 4,
+                "d2h_bytes_per_step": callers * k * 12,
+                "api": "elips_b200_batcher_search from host buffers (the value itself is end to end)",
+                "latency_us_p50": round(float(np.percentile(lat, 50)) * 1e6, 1),
+                "latency_us_p99": round(float(np.percentile(lat, 99)) * 1e6, 1),
+                "avg_batch": round(total / max(1, batches), 2)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(peaks["hbm_gbs"], 1),
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "kernel": "exact_topk_kernel", "kernel_ms_avg": round(kms, 4),
+                     "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "peak_source": f"{peak_src} HBM copy bandwidth (small batches: the base read bounds a launch)"},
+        "clocks": sampler.summary()}
+    if not args.no_cpu_baseline:
+        base = np.concatenate([gen_rows(cfg, r0, min(1 << 18, n - r0), SEED + 1, n, None, device=dev).cpu().numpy()
+                               for r0 in range(0, n, 1 << 18)])
+        result["cpu_baseline"] = cpu_baseline(cfg, base, queries, None)
+    return result
+
+
 def _cpu_searcher(cfg, base, mask_words):
     """Returns (search(queries, k, threads), kind, description) for the reference's
     CPU path on this configuration."""
@@ -724,6 +937,19 @@ def run_reference(args, cfg):
         threads = os.cpu_count() or 1
         search, kind, what, base, queries = _reference_ivfpq(cfg)
         return _time_reference(args, cfg, search, kind, what, base, queries, threads)
+    if args.config == "ivf_build":
+        gdev = "cuda" if torch.cuda.is_available() else "cpu"
+        cents = _centroids(cfg, gdev)
+        ns = max(cfg["nlist"] * 2, 8192)
+        base = gen_rows(cfg, 0, ns, SEED + 1, cfg["n"], cents, device=gdev).cpu().numpy()
+        rate, what, cores, kind = _reference_build_rate(cfg, base)
+        return {"metric": "IVF-PQ model build rows/s (build_from_batch semantics, bit-identical)",
+                "value": round(rate, 3), "unit": "rows/s", "n_gpus": args.gpus, "steps": 1, "warmup": 0,
+                "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded; shapes and distributions of the configuration)",
+                "config": {"workload": cfg["workload"], "config": args.config}, "impl": "reference",
+                "cpu_baseline": {"value": round(rate, 3), "unit": "rows/s", "cores": cores, "kind": kind, "sample": what},
+                "e2e": {"value": round(rate, 3), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     # Data generation only (untimed): on the GPU when one is visible, else CPU.
     gdev = "cuda" if torch.cuda.is_available() else "cpu"
     cents = _centroids(cfg, gdev) if cfg["data"] == "mixture" else None
@@ -792,6 +1018,10 @@ def main():
     try:
         if args.config == "ivfpq":
             result = run_b200_ivfpq(args, cfg, world, rank, local)
+        elif args.config in ("ivf_build", "batcher"):
+            if world > 1:
+                raise SystemExit(f"--config {args.config} runs on one GPU")
+            result = (run_b200_build if args.config == "ivf_build" else run_b200_batcher)(args, cfg)
         else:
             result = run_b200(args, cfg, world, rank, local)
         if rank == 0:
