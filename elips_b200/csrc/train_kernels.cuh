@@ -11,7 +11,8 @@
 //   centroid_normalize_kernel normalize_if_needed (IvfIndexState.cpp:20-35)
 //
 // Every distance is a strictly sequential single-precision chain with no
-// fused multiply-add, as the reference's scalar loops; the argmin keeps the
+// fused multiply-add, as the reference's scalar loops (two chains per packed
+// f32x2 instruction, each element rounded as the scalar one); the argmin keeps the
 // lowest centroid among equal distances (strict '<' from FLT_MAX, centroid
 // order ascending) and falls back to centroid 0 when no distance is below
 // FLT_MAX (all NaN or infinite).
@@ -31,6 +32,34 @@ constexpr int kAsgStride = 68;  // smem row pitch: float4-aligned, conflict-free
 __device__ __forceinline__ uint32_t train_ordered(float x) {
     const uint32_t u = __float_as_uint(x);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Packed pairs of fp32 (element 0 in the low half): sm_100's f32x2 add, sub
+// and mul round each element exactly as the scalar .rn instructions do, so a
+// pair of independent sequential chains advances with one instruction per
+// step instead of two.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_sub(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
 }
 
 template <int MODE>
@@ -83,11 +112,10 @@ __global__ void __launch_bounds__(256)
         arg[i] = 0xFFFFFFFFu;
     }
     for (uint32_t c0 = 0; c0 < K; c0 += kAsgCents) {
-        float acc[4][4];
+        // acc2[i][h]: the chains of row i against centroids 2h and 2h + 1.
+        unsigned long long acc2[4][2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+        for (int i = 0; i < 4; ++i) acc2[i][0] = acc2[i][1] = 0ull;
         for (uint32_t k0 = 0; k0 < d; k0 += kAsgDims) {
             const uint32_t w = min(static_cast<uint32_t>(kAsgDims), d - k0);
             __syncthreads();
@@ -99,19 +127,27 @@ __global__ void __launch_bounds__(256)
                 const float4 a4 = *reinterpret_cast<const float4*>(rs + cc * kAsgStride + ty * 4u);
                 const float4 c4 = *reinterpret_cast<const float4*>(cs + cc * kAsgStride + tx * 4u);
                 const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+                const unsigned long long cp[2] = {f2_pack(c4.x, c4.y), f2_pack(c4.z, c4.w)};
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
+                for (int i = 0; i < 4; ++i) {
+                    const unsigned long long aa = f2_pack(av[i], av[i]);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                    for (int h = 0; h < 2; ++h) {
                         if (MODE == kTrainSqL2 || MODE == kTrainL2) {
-                            const float df = __fsub_rn(av[i], cv[j]);
-                            acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(df, df));
+                            const unsigned long long df = f2_sub(aa, cp[h]);
+                            acc2[i][h] = f2_add(acc2[i][h], f2_mul(df, df));
                         } else {
-                            acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], cv[j]));
+                            acc2[i][h] = f2_add(acc2[i][h], f2_mul(aa, cp[h]));
                         }
                     }
+                }
             }
+        }
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            f2_unpack(acc2[i][0], acc[i][0], acc[i][1]);
+            f2_unpack(acc2[i][1], acc[i][2], acc[i][3]);
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
