@@ -613,9 +613,18 @@ def run_b200(args, cfg, world, rank, local):
     avg_kernel_ms = kstats["total_ms"] / max(1, kstats["launches"])
     achieved = flops / (avg_kernel_ms / 1e3) / 1e12
     bytes_alg = n_shard * d * (2 if cfg["precision"] in ("fp16", "bf16") else (1 if cfg["precision"] == "int8" else 4))
+    # The roofline is the slower of the GEMM at tensor peak and one read of
+    # the base at HBM bandwidth; small query batches are bound by the latter.
+    t_tensor = flops / (peak * 1e12)
+    t_hbm = bytes_alg / (peaks["hbm_gbs"] * 1e9)
+    if t_hbm > t_tensor:
+        bound, ach, pk, unit = "hbm", bytes_alg / (avg_kernel_ms / 1e3) / 1e9, peaks["hbm_gbs"], "GB/s"
+        peak_note = f"{peak_src} HBM copy bandwidth (base bytes / HBM exceeds FLOPs / tensor peak here)"
+    else:
+        bound, ach, pk, unit = "tensor", achieved, peak, "TFLOP/s"
     roofline = {
-        "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
-        "frac": round(achieved / peak, 4), "traffic": load_traffic(args.config, n_shard),
+        "bound": bound, "achieved": round(ach, 1), "peak": round(pk, 1), "unit": unit,
+        "frac": round(ach / pk, 4), "traffic": load_traffic(args.config, n_shard),
         "kernel": "exact_topk_kernel", "kernel_ms_avg": round(avg_kernel_ms, 4),
         "kernel_share_of_step": round(kstats["total_ms"] / max(1e-9, allstats["total_ms"]), 4),
         "per_kernel_ms_per_step": {name: round(_capi.profiler_stats(name)["total_ms"] / args.steps, 4)

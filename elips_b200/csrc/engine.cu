@@ -190,8 +190,11 @@ ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int group
     p.grid = static_cast<uint32_t>(std::min<uint64_t>(units, static_cast<uint64_t>(num_sms))) * cg;
     // List capacity: k survivors plus at least one whole half-tile of
     // admissions (compaction is checked once per tile); lists up to 512
-    // entries are compacted in registers.
-    p.cap = std::max<uint32_t>(512u, (k + bn / 2 + 32u + 31u) / 32u * 32u);
+    // entries are compacted in registers. Batches of one query tile run in a
+    // single wave with no bound published yet, so their lists get a smaller
+    // floor and compact (and tighten their own threshold) sooner.
+    const uint32_t floor_cap = (cg == 1 && p.n_qt == 1) ? 256u : 512u;
+    p.cap = std::max<uint32_t>(floor_cap, (k + bn / 2 + 32u + 31u) / 32u * 32u);
     return p;
 }
 
@@ -274,6 +277,17 @@ void launch_exact_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUten
 }
 
 uint32_t bn_of(OperandKind k) { return k == OperandKind::TF32X3 ? 128u : 256u; }
+
+// Lists merged per first-stage warp when a batch has too few queries to give
+// every SM work in a one-stage merge (one warp per query): the largest
+// divisor of `lists` in [4, 16], or 1 (one stage) when there is none or the
+// batch is large enough.
+uint32_t merge_group_size(uint32_t nq, uint32_t lists, int num_sms) {
+    if (nq >= 8u * static_cast<uint32_t>(num_sms) || lists < 8) return 1;
+    for (uint32_t g = 16; g >= 4; --g)
+        if (lists % g == 0 && lists / g >= 2) return g;
+    return 1;
+}
 
 // Pipeline depth: the stages that fit 192 KB of shared memory.
 constexpr int stages_of(OperandKind k, int cg) {
@@ -651,7 +665,10 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     const size_t cand = align(static_cast<size_t>(plan.grid) * 2 * kTileM * plan.cap * sizeof(uint2));
     const size_t partial = align(nq * plan.splits * 2 * k * sizeof(uint2));
     const size_t qtau = align(nq * sizeof(uint32_t));
-    StreamScratch scratch(q_ops + q_lo + q_norm + cand + partial + qtau, stream);
+    const uint32_t merge_group = merge_group_size(static_cast<uint32_t>(nq), plan.splits * 2, props.num_sms);
+    const uint32_t groups = merge_group > 1 ? plan.splits * 2 / merge_group : 0;
+    const size_t stage = align(static_cast<size_t>(nq) * groups * k * sizeof(uint2));
+    StreamScratch scratch(q_ops + q_lo + q_norm + cand + partial + qtau + stage, stream);
     uint8_t* s = scratch.get();
     void* qa = s;
     void* qlo = q_lo ? s + q_ops : nullptr;
@@ -691,6 +708,19 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     prm.row_offset = row_offset;
     prm.metric = metric_;
     dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan, stream);
+    if (groups > 0) {
+        // Few queries: one warp per query would walk all lists alone. First
+        // every group of merge_group lists is reduced to its k best (one warp
+        // per (query, group)), then the groups; the k smallest (key, row)
+        // of the k smallest of each group are the k smallest overall.
+        uint2* stage_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand + partial + qtau);
+        merge_candidates(device_, part_buf, static_cast<uint32_t>(nq) * groups, merge_group,
+                         static_cast<uint32_t>(k), static_cast<uint64_t>(merge_group) * k, k, metric_, nullptr,
+                         nullptr, stage_buf, stream);
+        merge_candidates(device_, stage_buf, static_cast<uint32_t>(nq), groups, static_cast<uint32_t>(k),
+                         static_cast<uint64_t>(groups) * k, k, metric_, out_dist, out_rows, out_cand, stream);
+        return;
+    }
     merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits * 2, static_cast<uint32_t>(k),
                      static_cast<uint64_t>(plan.splits) * 2 * k, k, metric_, out_dist, out_rows, out_cand,
                      stream);
