@@ -88,7 +88,7 @@ SIGNATURES = [
     ("elips_b200_train_pq_codebook", c_int,
      [c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p, c_int, c_void_p]),
     ("elips_b200_ivf_assign", c_int,
-     [c_int, c_int, c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_int, c_void_p]),
+     [c_int, c_int, c_void_p, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_void_p, c_int, c_void_p]),
     ("elips_b200_ivf_train", c_int,
      [c_int, c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p, c_void_p, c_int, c_void_p]),
     ("elips_b200_ivfpq_train", c_int,

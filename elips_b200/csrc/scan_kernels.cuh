@@ -16,6 +16,7 @@
 #include <cstdint>
 
 #include "block_select.cuh"
+#include "f32x2.cuh"
 
 namespace eb {
 
@@ -33,17 +34,43 @@ constexpr int kDistRows = 128;   // database rows per CTA (one per thread)
 constexpr int kDistQ = 8;        // queries per CTA
 constexpr int kDistDims = 32;    // dimensions staged per step
 
-// out[q * nb + r] = elips::distance(metric, queries[q], db[r]) exactly.
+// out[q * nb + r] = elips::distance(metric, queries[q], db[r]) exactly. A
+// thread owns one base row and 8 queries: 8 sequential chains, advanced in
+// pairs by packed f32x2 operations (each element rounded as the scalar .rn
+// operation); the 8 query values of a dimension are read as two float4.
+template <bool L2>
+__device__ __forceinline__ void distance_chains(const float (*dbs)[kDistDims + 1], const float (*qst)[kDistQ],
+                                                uint32_t t, uint32_t w, unsigned long long (&acc)[kDistQ / 2]) {
+    for (uint32_t c = 0; c < w; ++c) {
+        const float b = dbs[t][c];
+        const unsigned long long bb = f2_pack(b, b);
+        const float4 qa = *reinterpret_cast<const float4*>(&qst[c][0]);
+        const float4 qb = *reinterpret_cast<const float4*>(&qst[c][4]);
+        const unsigned long long qp[kDistQ / 2] = {f2_pack(qa.x, qa.y), f2_pack(qa.z, qa.w), f2_pack(qb.x, qb.y),
+                                                   f2_pack(qb.z, qb.w)};
+#pragma unroll
+        for (int j = 0; j < kDistQ / 2; ++j) {
+            if (L2) {
+                const unsigned long long df = f2_sub(qp[j], bb);
+                acc[j] = f2_add(acc[j], f2_prod(df, df));
+            } else {
+                acc[j] = f2_add(acc[j], f2_prod(qp[j], bb));
+            }
+        }
+    }
+}
+
 static __global__ void __launch_bounds__(kDistRows)
     distances_kernel(const float* __restrict__ queries, const float* __restrict__ db, uint32_t nq,
                      uint32_t nb, uint32_t d, int metric, float* __restrict__ out) {
+    static_assert(kDistQ == 8, "two float4 of queries per dimension");
     __shared__ float dbs[kDistRows][kDistDims + 1];
-    __shared__ float qs[kDistQ][kDistDims];
+    __shared__ __align__(16) float qst[kDistDims][kDistQ];
     const uint32_t r0 = blockIdx.x * kDistRows, q0 = blockIdx.y * kDistQ;
     const uint32_t t = threadIdx.x;
-    float acc[kDistQ];
+    unsigned long long acc[kDistQ / 2];
 #pragma unroll
-    for (int j = 0; j < kDistQ; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < kDistQ / 2; ++j) acc[j] = 0ull;
     for (uint32_t base = 0; base < d; base += kDistDims) {
         const uint32_t w = min(static_cast<uint32_t>(kDistDims), d - base);
         __syncthreads();
@@ -55,29 +82,22 @@ static __global__ void __launch_bounds__(kDistRows)
         for (uint32_t i = t; i < kDistQ * kDistDims; i += kDistRows) {
             const uint32_t qq = i / kDistDims, c = i % kDistDims;
             const uint32_t q = q0 + qq;
-            qs[qq][c] = (q < nq && c < w) ? queries[static_cast<size_t>(q) * d + base + c] : 0.0f;
+            qst[c][qq] = (q < nq && c < w) ? queries[static_cast<size_t>(q) * d + base + c] : 0.0f;
         }
         __syncthreads();
-        for (uint32_t c = 0; c < w; ++c) {
-            const float b = dbs[t][c];
-#pragma unroll
-            for (int j = 0; j < kDistQ; ++j) {
-                if (metric == kMetricL2) {
-                    const float df = __fsub_rn(qs[j][c], b);
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(df, df));
-                } else {
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(qs[j][c], b));
-                }
-            }
-        }
+        if (metric == kMetricL2) distance_chains<true>(dbs, qst, t, w, acc);
+        else distance_chains<false>(dbs, qst, t, w, acc);
     }
     const uint32_t r = r0 + t;
     if (r >= nb) return;
+    float accs[kDistQ];
+#pragma unroll
+    for (int j = 0; j < kDistQ / 2; ++j) f2_unpack(acc[j], accs[2 * j], accs[2 * j + 1]);
 #pragma unroll
     for (int j = 0; j < kDistQ; ++j) {
         const uint32_t q = q0 + j;
         if (q >= nq) break;
-        out[static_cast<size_t>(q) * nb + r] = metric == kMetricL2 ? sqrtf(acc[j]) : finish_dot(metric, acc[j]);
+        out[static_cast<size_t>(q) * nb + r] = metric == kMetricL2 ? sqrtf(accs[j]) : finish_dot(metric, accs[j]);
     }
 }
 

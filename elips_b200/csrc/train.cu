@@ -57,7 +57,7 @@ struct TrainRows {
 };
 
 void launch_nearest(int mode, const TrainRows& p, const float* cents, uint32_t K, uint32_t key_stride, uint32_t* keys,
-                    const uint32_t* done, cudaStream_t stream) {
+                    const uint32_t* done, cudaStream_t stream, float* best = nullptr) {
     const uint64_t tiles = (p.n + kAsgRows - 1) / kAsgRows;
     if (tiles > 0x7FFFFFFFull || p.batch > 65535u) fail(ELIPS_B200_INVALID_ARGUMENT, "too many rows in one call");
     const dim3 grid(static_cast<uint32_t>(tiles), p.batch);
@@ -65,19 +65,19 @@ void launch_nearest(int mode, const TrainRows& p, const float* cents, uint32_t K
     switch (mode) {
         case kTrainSqL2:
             nearest_centroid_kernel<kTrainSqL2><<<grid, 256, 0, stream>>>(p.rows, p.ld, p.n, p.d, p.batch_cols, cents,
-                                                                         K, key_stride, keys, done);
+                                                                         K, key_stride, keys, done, best);
             break;
         case kTrainL2:
             nearest_centroid_kernel<kTrainL2><<<grid, 256, 0, stream>>>(p.rows, p.ld, p.n, p.d, p.batch_cols, cents, K,
-                                                                       key_stride, keys, done);
+                                                                       key_stride, keys, done, best);
             break;
         case kTrainCos:
             nearest_centroid_kernel<kTrainCos><<<grid, 256, 0, stream>>>(p.rows, p.ld, p.n, p.d, p.batch_cols, cents,
-                                                                        K, key_stride, keys, done);
+                                                                        K, key_stride, keys, done, best);
             break;
         default:
             nearest_centroid_kernel<kTrainDot><<<grid, 256, 0, stream>>>(p.rows, p.ld, p.n, p.d, p.batch_cols, cents,
-                                                                        K, key_stride, keys, done);
+                                                                        K, key_stride, keys, done, best);
             break;
     }
     launch_ok("nearest centroid kernel");
@@ -220,7 +220,7 @@ void train_pq_codebook_device(int device, const float* rows, size_t n, size_t d,
 }
 
 void ivf_assign_device(int device, int metric, const float* rows, size_t n, size_t d, const float* cents,
-                       size_t n_lists, uint32_t* assign, cudaStream_t stream) {
+                       size_t n_lists, uint32_t* assign, float* dist, cudaStream_t stream) {
     if (n == 0) return;
     DeviceGuard g(device);
     device_props(device);
@@ -229,7 +229,7 @@ void ivf_assign_device(int device, int metric, const float* rows, size_t n, size
     const TrainRows p{rows, d, n, static_cast<uint32_t>(d), 1u, 0u};
     check_rows(p, static_cast<uint32_t>(n_lists));
     if (n_lists > 0xFFFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "too many lists");
-    launch_nearest(mode, p, cents, static_cast<uint32_t>(n_lists), 0u, assign, nullptr, stream);
+    launch_nearest(mode, p, cents, static_cast<uint32_t>(n_lists), 0u, assign, nullptr, stream, dist);
 }
 
 void ivf_train_device(int device, int metric, const float* rows, size_t n, size_t d, size_t n_lists, size_t iters,
@@ -330,13 +330,14 @@ int elips_b200_train_pq_codebook(int device, const float* rows, size_t n, size_t
 }
 
 int elips_b200_ivf_assign(int device, int metric, const float* rows, size_t n, size_t dim, const float* centroids,
-                          size_t n_lists, uint32_t* assignments_out, int pointers_on_device, void* stream) {
+                          size_t n_lists, uint32_t* assignments_out, float* distances_out, int pointers_on_device,
+                          void* stream) {
     if (n > 0 && (rows == nullptr || centroids == nullptr || assignments_out == nullptr))
         return ELIPS_B200_INVALID_ARGUMENT;
     if (n > 0 && (dim == 0 || n_lists == 0)) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] {
         if (pointers_on_device) {
-            eb::ivf_assign_device(device, metric, rows, n, dim, centroids, n_lists, assignments_out,
+            eb::ivf_assign_device(device, metric, rows, n, dim, centroids, n_lists, assignments_out, distances_out,
                                   static_cast<cudaStream_t>(stream));
             return;
         }
@@ -345,17 +346,22 @@ int elips_b200_ivf_assign(int device, int metric, const float* rows, size_t n, s
         OwnedStream st;
         {
             const size_t a_rows = eb::up256(n * dim * 4), a_cent = eb::up256(n_lists * dim * 4);
-            eb::StreamScratch s(a_rows + a_cent + n * 4, st.s);
+            const size_t a_asg = eb::up256(n * 4);
+            eb::StreamScratch s(a_rows + a_cent + a_asg + n * 4, st.s);
             float* dr = reinterpret_cast<float*>(s.get());
             float* dc = reinterpret_cast<float*>(s.get() + a_rows);
             uint32_t* da = reinterpret_cast<uint32_t*>(s.get() + a_rows + a_cent);
+            float* dd = reinterpret_cast<float*>(s.get() + a_rows + a_cent + a_asg);
             eb::check_cuda(cudaMemcpyAsync(dr, rows, n * dim * 4, cudaMemcpyHostToDevice, st.s),
                            ELIPS_B200_TRANSFER_FAILED, "row upload");
             eb::check_cuda(cudaMemcpyAsync(dc, centroids, n_lists * dim * 4, cudaMemcpyHostToDevice, st.s),
                            ELIPS_B200_TRANSFER_FAILED, "centroid upload");
-            eb::ivf_assign_device(device, metric, dr, n, dim, dc, n_lists, da, st.s);
+            eb::ivf_assign_device(device, metric, dr, n, dim, dc, n_lists, da, distances_out ? dd : nullptr, st.s);
             eb::check_cuda(cudaMemcpyAsync(assignments_out, da, n * 4, cudaMemcpyDeviceToHost, st.s),
                            ELIPS_B200_TRANSFER_FAILED, "assignment download");
+            if (distances_out != nullptr)
+                eb::check_cuda(cudaMemcpyAsync(distances_out, dd, n * 4, cudaMemcpyDeviceToHost, st.s),
+                               ELIPS_B200_TRANSFER_FAILED, "distance download");
         }
         eb::check_cuda(cudaStreamSynchronize(st.s), ELIPS_B200_KERNEL_LAUNCH_FAILED, "ivf_assign");
     });

@@ -20,6 +20,8 @@
 
 #include <cstdint>
 
+#include "f32x2.cuh"
+
 namespace eb {
 
 enum : int { kTrainSqL2 = 0, kTrainL2 = 1, kTrainCos = 2, kTrainDot = 3 };
@@ -32,34 +34,6 @@ constexpr int kAsgStride = 68;  // smem row pitch: float4-aligned, conflict-free
 __device__ __forceinline__ uint32_t train_ordered(float x) {
     const uint32_t u = __float_as_uint(x);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Packed pairs of fp32 (element 0 in the low half): sm_100's f32x2 add, sub
-// and mul round each element exactly as the scalar .rn instructions do, so a
-// pair of independent sequential chains advances with one instruction per
-// step instead of two.
-__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
-    unsigned long long r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ unsigned long long f2_sub(unsigned long long a, unsigned long long b) {
-    unsigned long long r;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
-    unsigned long long r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
 }
 
 template <int MODE>
@@ -95,7 +69,8 @@ template <int MODE>
 __global__ void __launch_bounds__(256)
     nearest_centroid_kernel(const float* __restrict__ rows, uint64_t ld, uint64_t n, uint32_t d, uint32_t batch_cols,
                             const float* __restrict__ cents, uint32_t K, uint32_t key_stride,
-                            uint32_t* __restrict__ keys, const uint32_t* __restrict__ done) {
+                            uint32_t* __restrict__ keys, const uint32_t* __restrict__ done,
+                            float* __restrict__ best_out) {
     __shared__ __align__(16) float rs[kAsgDims * kAsgStride];
     __shared__ __align__(16) float cs[kAsgDims * kAsgStride];
     const uint32_t b = blockIdx.y;
@@ -135,9 +110,9 @@ __global__ void __launch_bounds__(256)
                     for (int h = 0; h < 2; ++h) {
                         if (MODE == kTrainSqL2 || MODE == kTrainL2) {
                             const unsigned long long df = f2_sub(aa, cp[h]);
-                            acc2[i][h] = f2_add(acc2[i][h], f2_mul(df, df));
+                            acc2[i][h] = f2_add(acc2[i][h], f2_prod(df, df));
                         } else {
-                            acc2[i][h] = f2_add(acc2[i][h], f2_mul(aa, cp[h]));
+                            acc2[i][h] = f2_add(acc2[i][h], f2_prod(aa, cp[h]));
                         }
                     }
                 }
@@ -181,6 +156,16 @@ __global__ void __launch_bounds__(256)
         if (tx == 0 && r < n)
             keys[static_cast<uint64_t>(b) * n + r] =
                 b * key_stride + (key == ~0ull ? 0u : static_cast<uint32_t>(key & 0xFFFFFFFFull));
+        // The winner's distance (optional), written by the thread that owns
+        // the winning centroid (its own bits: -0 stays -0); FLT_MAX when no
+        // distance was below it, the reference's best_distance in that case.
+        if (best_out != nullptr && r < n) {
+            if (key == ~0ull) {
+                if (tx == 0) best_out[static_cast<uint64_t>(b) * n + r] = 3.40282347e+38f;
+            } else if (arg[i] == static_cast<uint32_t>(key & 0xFFFFFFFFull)) {
+                best_out[static_cast<uint64_t>(b) * n + r] = best[i];
+            }
+        }
     }
 }
 

@@ -50,11 +50,22 @@ def train_pq_codebook(rows, pq_dim: int, ksub: int, iters: int = 10, device: int
     return out
 
 
+def ivf_nearest(metric: str, rows, centroids, device: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """(nearest list [n] uint32, its distance [n] float32) for every row."""
+    x, c = _rows(rows), _rows(centroids)
+    out = np.empty(x.shape[0], np.uint32)
+    dist = np.empty(x.shape[0], np.float32)
+    capi.check(capi.LIB.elips_b200_ivf_assign(device, METRICS[metric], x.ctypes.data, x.shape[0], x.shape[1],
+                                              c.ctypes.data, c.shape[0], out.ctypes.data, dist.ctypes.data, 0,
+                                              None), "elips_b200_ivf_assign")
+    return out, dist
+
+
 def ivf_assign(metric: str, rows, centroids, device: int = 0) -> np.ndarray:
     x, c = _rows(rows), _rows(centroids)
     out = np.empty(x.shape[0], np.uint32)
     capi.check(capi.LIB.elips_b200_ivf_assign(device, METRICS[metric], x.ctypes.data, x.shape[0], x.shape[1],
-                                              c.ctypes.data, c.shape[0], out.ctypes.data, 0, None),
+                                              c.ctypes.data, c.shape[0], out.ctypes.data, None, 0, None),
                "elips_b200_ivf_assign")
     return out
 

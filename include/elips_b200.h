@@ -436,11 +436,13 @@ ELIPS_B200_API int elips_b200_train_pq_codebook(int device, const float* rows, s
                                                 void* stream);
 
 /* IvfIndexState::assign_vectors_to_centroids (src/gpu_engine/detail/
- * IvfIndexState.cpp:167-191): nearest list of every row by elips::distance. */
+ * IvfIndexState.cpp:167-191): nearest list of every row by elips::distance,
+ * and (distances_out, may be NULL) that distance, FLT_MAX where no distance
+ * was below FLT_MAX (the reference's best_distance). */
 ELIPS_B200_API int elips_b200_ivf_assign(int device, int metric, const float* rows, size_t n,
                                          size_t dim, const float* centroids, size_t n_lists,
-                                         uint32_t* assignments_out, int pointers_on_device,
-                                         void* stream);
+                                         uint32_t* assignments_out, float* distances_out,
+                                         int pointers_on_device, void* stream);
 
 /* IvfIndexState::train_centroids + the final assignment (IvfIndexState.cpp:
  * 118-165, 193-208): max(1, iters) rounds; cosine centroids normalised.

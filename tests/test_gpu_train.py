@@ -115,3 +115,18 @@ def test_ivf_train_device_tensors_large():
     pick = rng.choice(len(x), 3000, replace=False)
     assert np.array_equal(a[pick], O.ivf_assign("euclidean", x[pick], c))
     assert np.array_equal(train.ivf_assign("euclidean", x, c), a)
+
+
+@pytest.mark.parametrize("metric", METRICS)
+def test_ivf_nearest_distances_bit_exact(metric):
+    """The argmin kernel's winning distance for every row equals
+    elips::distance(row, its centroid) bit for bit: every sequential chain is
+    rounded as the reference's scalar loop (a fused multiply-add anywhere would
+    show up here even where it does not change the argmin)."""
+    from elips_b200 import train
+    x = _rows(4000, 72, seed=81, metric=metric)
+    cent = _rows(130, 72, seed=82, metric=metric)
+    a, dist = train.ivf_nearest(metric, x, cent)
+    assert np.array_equal(a, O.ivf_assign(metric, x, cent))
+    ref = np.array([O.distance(metric, x[i], cent[a[i]]) for i in range(len(x))], np.float32)
+    assert np.array_equal(_bits(dist), _bits(ref))
