@@ -199,7 +199,7 @@ constexpr uint32_t kGroupThreads = kGroupWarps * 32;
 
 // Candidates of one list each query of a group sees per round (between two
 // block barriers), for G queries per group.
-__host__ __device__ constexpr uint32_t group_round(uint32_t) { return 512u; }
+__host__ __device__ constexpr uint32_t group_round(uint32_t) { return 1024u; }
 
 // Queries per lane (one vector table lookup serves them all).
 __host__ __device__ constexpr uint32_t group_qp(uint32_t G) { return G < 4u ? G : 4u; }
@@ -210,7 +210,7 @@ __host__ __device__ constexpr uint32_t group_lut_stride(uint32_t m, uint32_t ksu
 // Per-query candidate buffer: the R kept plus room for a round of appends,
 // with slack so that compactions are rare.
 __host__ __device__ constexpr uint32_t group_capacity(uint32_t G, uint32_t r) {
-    return ((r + 512u > 2u * r ? r + 512u : 2u * r) + group_round(G) + 31u) / 32u * 32u;
+    return ((r + 256u > 2u * r ? r + 256u : 2u * r) + group_round(G) + 31u) / 32u * 32u;
 }
 
 struct GroupLayout {
