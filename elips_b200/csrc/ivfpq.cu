@@ -169,8 +169,31 @@ protected:
     // distances to the centroids, then the nprobe best) and group the
     // (query, probe) pairs by list for G queries per scan item. Carves its
     // scratch from w.
+public:
+    // The nprobe nearest lists of every query (IvfIndexState::probe_lists,
+    // IvfIndexState.cpp:395-464): exact distances to every centroid, then the
+    // nprobe smallest, ties by list id. probes: [nq][nprobe] DEVICE.
+    void probe(const float* queries, size_t nq, uint32_t* probes, cudaStream_t stream) const {
+        if (nq == 0) return;
+        if (queries == nullptr || probes == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "null pointer");
+        DeviceGuard g(device_);
+        const uint32_t nprobe = std::min(nprobe_, nlist_);
+        StreamScratch s(a256(nq * nlist_ * 4) + a256(nq * nprobe * 4), stream);
+        float* dist = reinterpret_cast<float*>(s.get());
+        float* pval = reinterpret_cast<float*>(s.get() + a256(nq * nlist_ * 4));
+        compute_distances_device(device_, queries, static_cast<const float*>(centroids_.get()), dist, nq, nlist_, dim_,
+                                 metric_, stream);
+        top_k_device(device_, dist, probes, pval, nq, nlist_, nprobe, stream);
+    }
+
+    uint32_t probes_per_query() const { return std::min(nprobe_, nlist_); }
+
+protected:
+
+    // probes_in (optional, DEVICE [nq][nprobe]): probe lists computed
+    // elsewhere (another rank's slice of the batch), used instead of probing.
     Plan probe_and_plan(const float* queries, size_t nq, uint32_t r, uint32_t G, bool flat, uint8_t*& w,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const uint32_t* probes_in = nullptr) {
         Plan pl;
         pl.nprobe = std::min(nprobe_, nlist_);
         pl.npairs = nq * pl.nprobe;
@@ -191,9 +214,14 @@ protected:
         pl.ctrl = reinterpret_cast<uint32_t*>(carve(256));
         pl.qbound = reinterpret_cast<uint32_t*>(carve(a256(nq * 4)));
         if (flat) pl.pair_off = reinterpret_cast<uint32_t*>(carve(a256(pl.npairs * 4)));
-        compute_distances_device(device_, queries, static_cast<const float*>(centroids_.get()), dist, nq, nlist_, dim_,
-                                 metric_, stream);
-        top_k_device(device_, dist, pl.probes, pval, nq, nlist_, pl.nprobe, stream);
+        if (probes_in != nullptr) {
+            check_cuda(cudaMemcpyAsync(pl.probes, probes_in, pl.npairs * 4, cudaMemcpyDeviceToDevice, stream),
+                       ELIPS_B200_TRANSFER_FAILED, "probe copy");
+        } else {
+            compute_distances_device(device_, queries, static_cast<const float*>(centroids_.get()), dist, nq, nlist_,
+                                     dim_, metric_, stream);
+            top_k_device(device_, dist, pl.probes, pval, nq, nlist_, pl.nprobe, stream);
+        }
         check_cuda(cudaMemsetAsync(pl.counts, 0, static_cast<size_t>(nlist_) * 4, stream),
                    ELIPS_B200_KERNEL_LAUNCH_FAILED, "pair counts");
         check_cuda(cudaMemsetAsync(pl.qbound, 0xFF, nq * 4, stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "query bounds");
@@ -401,7 +429,8 @@ public:
     // Steps 1-4 of search: the R = 4k best (approximate key, slot) per query
     // over the probed lists this index owns, ascending, padded with
     // {+inf, 0xFFFFFFFF}. out_cand: [nq][R] DEVICE.
-    void candidates(const float* queries, size_t nq, size_t k, uint2* out_cand, cudaStream_t stream) {
+    void candidates(const float* queries, size_t nq, size_t k, uint2* out_cand, cudaStream_t stream,
+                    const uint32_t* probes_in = nullptr) {
         if (nq == 0 || k == 0) return;
         check_search(queries, nq, k);
         DeviceGuard g(device_);
@@ -419,7 +448,7 @@ public:
         StreamScratch s(plan_bytes(nq, r, false), stream);
         uint8_t* w = s.get();
         // 1-2. probe and plan
-        const Plan pl = probe_and_plan(queries, nq, r, G, false, w, stream);
+        const Plan pl = probe_and_plan(queries, nq, r, G, false, w, stream, probes_in);
         // 3. per (list, query group) approximate scan, R best per (query, list)
         IvfGroupParams p = group_params(queries, pl, r, capq, lut_stride);
         p.codebook = static_cast<const float*>(codebook_.get());
@@ -712,6 +741,25 @@ int elips_b200_ivfpq_search_candidates_device(elips_b200_ivfpq* index, const flo
     if (nq > 0 && k > 0 && (queries == nullptr || out_cand == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] {
         index->index.candidates(queries, nq, k, reinterpret_cast<uint2*>(out_cand), static_cast<cudaStream_t>(stream));
+    });
+}
+
+int elips_b200_ivfpq_probe_device(const elips_b200_ivfpq* index, const float* queries, size_t nq,
+                                  uint32_t* probes_out, void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && (queries == nullptr || probes_out == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] { index->index.probe(queries, nq, probes_out, static_cast<cudaStream_t>(stream)); });
+}
+
+int elips_b200_ivfpq_search_candidates_probed_device(elips_b200_ivfpq* index, const float* queries, size_t nq,
+                                                     size_t k, const uint32_t* probes, uint32_t* out_cand,
+                                                     void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (queries == nullptr || probes == nullptr || out_cand == nullptr))
+        return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        index->index.candidates(queries, nq, k, reinterpret_cast<uint2*>(out_cand), static_cast<cudaStream_t>(stream),
+                                probes);
     });
 }
 

@@ -144,6 +144,8 @@ class ShardedIvfPqIndex:
       3. each rank reranks the ones it holds, exactly, on its raw rows;
       4. all-gather of the k best per rank; the root merges them by
          (distance, global slot).
+    Before step 1 the probe itself is split: each rank probes a slice of the
+    batch and the slices are exchanged (probe_slice, probe_table).
     The phases are methods, so a test can drive several ranks in one process;
     `exchange` defaults to exchange_candidates over the process group."""
 
@@ -193,10 +195,29 @@ class ShardedIvfPqIndex:
         held = (rows >= 0) & (self.global_rows[pos] == rows)
         return torch.where(held, pos, torch.full_like(pos, -1))
 
-    def approx_candidates(self, queries, k: int):
-        """Phase 1: [nq, 4k, 2] int32 (distance bits, global slot)."""
+    def probe_slice(self, queries):
+        """Phase 0: this rank's slice of the probe, padded to ceil(nq / world)
+        rows so that every rank's block has the same shape: [chunk, nprobe] int32."""
         import torch
-        cand = self.local.search_candidates_device(queries, k)
+        nq = queries.shape[0]
+        chunk = (nq + self.world - 1) // self.world
+        lo, hi = min(nq, self.rank * chunk), min(nq, (self.rank + 1) * chunk)
+        out = torch.zeros((chunk, min(self.local.nprobe, self.nlist)), dtype=torch.int32, device=queries.device)
+        if hi > lo:
+            out[:hi - lo] = self.local.probe_device(queries[lo:hi].contiguous())
+        return out
+
+    @staticmethod
+    def probe_table(gathered, nq: int):
+        """The full probe table from the gathered slices [world, chunk, nprobe]."""
+        return gathered.reshape(-1, gathered.shape[-1])[:nq].contiguous()
+
+    def approx_candidates(self, queries, k: int, probes=None):
+        """Phase 1: [nq, 4k, 2] int32 (distance bits, global slot). `probes`
+        (the full [nq, nprobe] table, e.g. from probe_slice + exchange) skips
+        this rank's own probe of the whole batch."""
+        import torch
+        cand = self.local.search_candidates_device(queries, k, probes=probes)
         return _pairs(cand[..., 0].contiguous().view(torch.float32), self._to_global(cand[..., 1].long()))
 
     def rerank_owned(self, queries, k: int, gathered):
@@ -219,7 +240,10 @@ class ShardedIvfPqIndex:
         if self.world == 1:
             d, r = self.local.search_device(queries, k)
             return d, self._to_global(r)
-        mine = self.rerank_owned(queries, k, self.exchange(self.approx_candidates(queries, k)))
+        # The probe is split across the ranks (each probes a slice of the
+        # batch against the replicated centroids) and exchanged.
+        probes = self.probe_table(self.exchange(self.probe_slice(queries)), queries.shape[0])
+        mine = self.rerank_owned(queries, k, self.exchange(self.approx_candidates(queries, k, probes)))
         gathered = self.exchange(mine)
         if self.rank != 0:
             return None, None

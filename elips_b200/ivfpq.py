@@ -31,6 +31,7 @@ class IvfPqIndex:
         if cent.shape[1] != self.dimension:
             raise DimensionMismatch("centroid dimension does not match index")
         self.n_lists, self.pq_dim, self.pq_bits = cent.shape[0], cb.shape[0], int(pq_bits)
+        self.nprobe = max(1, int(nprobe))
         h = ctypes.c_void_p()
         capi.check(capi.LIB.elips_b200_ivfpq_create(self.device, METRICS[metric], self.dimension, self.n_lists,
                                                     int(nprobe), self.pq_dim, int(pq_bits), _ptr(cent), _ptr(cb),
@@ -78,6 +79,7 @@ class IvfPqIndex:
 
     def set_nprobe(self, nprobe: int) -> None:
         capi.check(capi.LIB.elips_b200_ivfpq_set_nprobe(self._h, int(nprobe)), "elips_b200_ivfpq_set_nprobe")
+        self.nprobe = max(1, int(nprobe))
 
     def set_list_range(self, lo: int, hi: int) -> None:
         """Own only lists [lo, hi) (one GPU's share of a list-sharded index)."""
@@ -93,16 +95,35 @@ class IvfPqIndex:
         capi.check(capi.LIB.elips_b200_ivfpq_set_owned_lists(self._h, _ptr(words), words.size),
                    "elips_b200_ivfpq_set_owned_lists")
 
-    def search_candidates_device(self, queries, k: int, out=None, stream=None):
-        """The approximate stage: [nq, 4k, 2] int32 (distance bits, slot), ascending."""
+    def probe_device(self, queries, stream=None):
+        """The nprobe nearest lists of each query: [nq, nprobe] int32, ascending."""
+        import torch
+        nq = queries.shape[0]
+        nprobe = min(self.nprobe, self.n_lists)
+        out = torch.empty((nq, nprobe), dtype=torch.int32, device=queries.device)
+        s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_ivfpq_probe_device(self._h, queries.data_ptr(), nq, out.data_ptr(), s),
+                   "elips_b200_ivfpq_probe_device")
+        return out
+
+    def search_candidates_device(self, queries, k: int, out=None, stream=None, probes=None):
+        """The approximate stage: [nq, 4k, 2] int32 (distance bits, slot),
+        ascending; `probes` ([nq, nprobe] int32 CUDA tensor, probe_device's
+        output) skips the probe."""
         import torch
         nq = queries.shape[0]
         if out is None:
             out = torch.empty((nq, 4 * k, 2), dtype=torch.int32, device=queries.device)
         s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
-        capi.check(capi.LIB.elips_b200_ivfpq_search_candidates_device(self._h, queries.data_ptr(), nq, k,
-                                                                      out.data_ptr(), s),
-                   "elips_b200_ivfpq_search_candidates_device")
+        if probes is None:
+            capi.check(capi.LIB.elips_b200_ivfpq_search_candidates_device(self._h, queries.data_ptr(), nq, k,
+                                                                          out.data_ptr(), s),
+                       "elips_b200_ivfpq_search_candidates_device")
+        else:
+            probes = probes.contiguous()
+            capi.check(capi.LIB.elips_b200_ivfpq_search_candidates_probed_device(
+                self._h, queries.data_ptr(), nq, k, probes.data_ptr(), out.data_ptr(), s),
+                "elips_b200_ivfpq_search_candidates_probed_device")
         return out
 
     def rerank_device(self, queries, k: int, cand, out_dist=None, out_rows=None, stream=None):

@@ -329,6 +329,20 @@ ELIPS_B200_API int elips_b200_ivfpq_search_candidates_device(elips_b200_ivfpq* i
                                                              size_t k, uint32_t* out_cand,
                                                              void* stream);
 
+/* The probe alone (IvfIndexState::probe_lists, IvfIndexState.cpp:395-464):
+ * the min(nprobe, n_lists) nearest lists of each query, ascending, ties by
+ * list id; probes_out [nq][nprobe] DEVICE. With
+ * elips_b200_ivfpq_search_candidates_probed_device the probe of a large batch
+ * can be split across GPUs that hold the same centroids: each probes a slice,
+ * the slices are exchanged, every GPU scans its own lists with the full
+ * probe table (results equal elips_b200_ivfpq_search_candidates_device). */
+ELIPS_B200_API int elips_b200_ivfpq_probe_device(const elips_b200_ivfpq* index, const float* queries,
+                                                 size_t nq, uint32_t* probes_out, void* stream);
+ELIPS_B200_API int elips_b200_ivfpq_search_candidates_probed_device(elips_b200_ivfpq* index,
+                                                                    const float* queries, size_t nq,
+                                                                    size_t k, const uint32_t* probes,
+                                                                    uint32_t* out_cand, void* stream);
+
 /* The exact stage (exact_rank, GpuIVFPQIndex.cpp:37-71): for nq x R pairs
  * {any, slot} (slot 0xFFFFFFFF or past size = none), exact distances on this
  * index's raw rows, the k best ascending by (distance, slot). DEVICE. */

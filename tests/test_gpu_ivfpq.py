@@ -145,7 +145,11 @@ def test_list_sharded_search_equals_single_index(model, world, balanced, metric)
             ix.add_device(vd[r0:r0 + 25_000], ad[r0:r0 + 25_000], r0, cd[r0:r0 + 25_000])
     assert sum(ix.local.size() for ix in ranks) == len(base)
     qd = torch.from_numpy(q).cuda()
-    gathered = torch.stack([ix.approx_candidates(qd, k) for ix in ranks])
+    # the probe split across the ranks, then exchanged, as search_device does
+    probes = ShardedIvfPqIndex.probe_table(torch.stack([ix.probe_slice(qd) for ix in ranks]), qd.shape[0])
+    assert torch.equal(probes, single.probe_device(qd))
+    gathered = torch.stack([ix.approx_candidates(qd, k, probes) for ix in ranks])
+    assert torch.equal(gathered, torch.stack([ix.approx_candidates(qd, k) for ix in ranks]))
     mine = torch.stack([ix.rerank_owned(qd, k, gathered) for ix in ranks])
     d, r = ShardedIvfPqIndex.merge_final(mine, k)
     torch.cuda.synchronize()
