@@ -331,7 +331,9 @@ void dispatch_exact(OperandKind kind, int metric, const CUtensorMap& a, const CU
 // CTA pairs that can be resident at once (cluster occupancy of the pair
 // kernel: 1 CTA per SM, two SMs of one GPC per pair), cached per device.
 int pair_groups(int device) {
+    static std::mutex mu;
     static int cached[64] = {0};
+    std::lock_guard<std::mutex> lock(mu);
     if (device >= 0 && device < 64 && cached[device] > 0) return cached[device];
     const DeviceProps& props = device_props(device);
     cudaLaunchAttribute attr[1];

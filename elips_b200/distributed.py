@@ -195,13 +195,19 @@ class ShardedIvfPqIndex:
         held = (rows >= 0) & (self.global_rows[pos] == rows)
         return torch.where(held, pos, torch.full_like(pos, -1))
 
+    @staticmethod
+    def probe_rows(nq: int, rank: int, world: int) -> tuple[int, int, int]:
+        """(lo, hi, chunk): the queries [lo, hi) rank probes, every rank's block
+        padded to chunk = ceil(nq / world) rows (equal shapes for the exchange)."""
+        chunk = (nq + world - 1) // world
+        return min(nq, rank * chunk), min(nq, (rank + 1) * chunk), chunk
+
     def probe_slice(self, queries):
         """Phase 0: this rank's slice of the probe, padded to ceil(nq / world)
         rows so that every rank's block has the same shape: [chunk, nprobe] int32."""
         import torch
         nq = queries.shape[0]
-        chunk = (nq + self.world - 1) // self.world
-        lo, hi = min(nq, self.rank * chunk), min(nq, (self.rank + 1) * chunk)
+        lo, hi, chunk = self.probe_rows(nq, self.rank, self.world)
         out = torch.zeros((chunk, min(self.local.nprobe, self.nlist)), dtype=torch.int32, device=queries.device)
         if hi > lo:
             out[:hi - lo] = self.local.probe_device(queries[lo:hi].contiguous())

@@ -261,6 +261,17 @@ def train_pq_codebook(rows, m, ksub, iters):
     return cb
 
 
+def ivf_probe(metric, queries, centroids, nprobe):
+    """IvfIndexState::probe_lists restated: [nq][nprobe] nearest list ids, ties by id."""
+    queries, centroids = _f32(queries), _f32(centroids)
+    nq, d = queries.shape
+    out = np.empty((nq, nprobe), np.uint32)
+    for q in range(nq):
+        orc().orc_ivf_probe(METRIC[metric], _p(queries[q]), c_size_t(d), _p(centroids), c_size_t(centroids.shape[0]),
+                            c_size_t(nprobe), _p(out[q]), None)
+    return out
+
+
 def ivf_assign(metric, rows, centroids):
     rows, centroids = _f32(rows), _f32(centroids)
     out = np.empty(rows.shape[0], np.uint32)

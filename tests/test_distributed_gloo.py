@@ -136,3 +136,41 @@ def test_balanced_lists_partition():
         load = np.bincount(owner, weights=sizes.astype(float) ** 2, minlength=world)
         assert load.max() <= load.mean() + (sizes.astype(float) ** 2).max()
         assert np.array_equal(owner, balanced_lists(sizes, world))
+
+
+def _probe_worker(rank, world, port, out_dir):
+    """Each rank probes its slice of the batch (the oracle stands in for the
+    device probe), the padded slices go through the product's exchange, and
+    the product's probe_table reassembles the full table."""
+    import torch
+    import torch.distributed as dist
+    from elips_b200.distributed import ShardedIvfPqIndex
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        for nq in (1, 7, 50):
+            cents = H.gaussian(40, 12, seed=91)
+            q = H.gaussian(nq, 12, seed=92 + nq)
+            lo, hi, chunk = ShardedIvfPqIndex.probe_rows(nq, rank, world)
+            block = torch.zeros((chunk, 5), dtype=torch.int32)
+            if hi > lo:
+                block[:hi - lo] = torch.from_numpy(O.ivf_probe("euclidean", q[lo:hi], cents, 5).view(np.int32))
+            table = ShardedIvfPqIndex.probe_table(exchange_candidates(block, world), nq).numpy()
+            if rank == 0:
+                np.save(os.path.join(out_dir, f"probes{nq}.npy"), table)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_split_probe_exchange_equals_full_probe(tmp_path, world):
+    """The IVF-PQ probe split across ranks (ShardedIvfPqIndex.probe_rows /
+    probe_table over exchange_candidates) gives the full batch's probe table,
+    including batches smaller than the world (empty, padded slices)."""
+    mp.spawn(_probe_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for nq in (1, 7, 50):
+        cents = H.gaussian(40, 12, seed=91)
+        q = H.gaussian(nq, 12, seed=92 + nq)
+        got = np.load(tmp_path / f"probes{nq}.npy")
+        assert np.array_equal(got.view(np.uint32), O.ivf_probe("euclidean", q, cents, 5))
