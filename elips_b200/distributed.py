@@ -103,20 +103,23 @@ def list_range(nlist: int, rank: int, world: int) -> tuple[int, int]:
     return nlist * rank // world, nlist * (rank + 1) // world
 
 
-def balanced_lists(list_sizes, world: int) -> np.ndarray:
+def balanced_lists(list_sizes, world: int, probe_counts=None) -> np.ndarray:
     """Owner rank of every IVF list, balancing the scan work: a probed list
-    costs about its size times the queries that probe it, and queries probe
-    lists about in proportion to their size, so the weight is size^2. Greedy
-    longest-first: heaviest list to the least loaded rank (ties: lower list id,
-    lower rank). Deterministic, so every rank computes the same partition."""
+    costs its size times the queries that probe it. With `probe_counts` (how
+    often each list was probed by a sample of queries) the weight is
+    size x count; without it, queries are taken to probe lists about in
+    proportion to their size and the weight is size^2. Greedy longest-first:
+    heaviest list to the least loaded rank (ties: lower list id, lower rank).
+    Deterministic, so every rank computes the same partition."""
     sizes = np.asarray(list_sizes, np.float64)
-    order = np.lexsort((np.arange(sizes.size), -sizes * sizes))
+    weight = sizes * (sizes if probe_counts is None else np.asarray(probe_counts, np.float64))
+    order = np.lexsort((np.arange(sizes.size), -weight))
     load = np.zeros(world)
     owner = np.empty(sizes.size, np.int64)
     for l in order:
         r = int(np.argmin(load))
         owner[l] = r
-        load[r] += sizes[l] * sizes[l]
+        load[r] += weight[l]
     return owner
 
 
