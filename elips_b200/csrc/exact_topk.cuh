@@ -503,8 +503,20 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             __syncwarp();
             if (qvalid) {
                 uint2* out = p.partial + ((static_cast<size_t>(q) * p.splits + sp) * 2u + half) * p.k;
-                for (uint32_t i = 0; i < p.k; ++i) {
-                    out[i] = i < cnt ? my_list[i] : make_uint2(0x7f800000u, 0xFFFFFFFFu);
+                const uint2 none = make_uint2(0x7f800000u, 0xFFFFFFFFu);
+                if ((p.k & 1u) == 0u) {
+                    // k even: both the list (cap entries, cap a multiple of 32)
+                    // and this slot start on 16 bytes; two entries per access.
+                    const uint4* src = reinterpret_cast<const uint4*>(my_list);
+                    uint4* dst = reinterpret_cast<uint4*>(out);
+                    for (uint32_t i = 0; i < p.k / 2u; ++i) {
+                        uint4 e = src[i];
+                        if (2u * i >= cnt) e.x = none.x, e.y = none.y;
+                        if (2u * i + 1u >= cnt) e.z = none.x, e.w = none.y;
+                        dst[i] = e;
+                    }
+                } else {
+                    for (uint32_t i = 0; i < p.k; ++i) out[i] = i < cnt ? my_list[i] : none;
                 }
             }
             __syncwarp();
