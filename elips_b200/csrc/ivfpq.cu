@@ -36,7 +36,7 @@ class IvfLists {
 public:
     IvfLists(int device, int metric, uint32_t dim, uint32_t nlist, uint32_t nprobe, const float* centroids)
         : device_(device), metric_(metric), dim_(dim), nlist_(nlist), nprobe_(std::max<uint32_t>(1, nprobe)),
-          owned_host_(nlist, true) {
+          owned_host_(nlist, true), members_(nlist) {
         if (metric < 0 || metric > 2) fail(ELIPS_B200_UNSUPPORTED_METRIC, "unknown metric");
         if (dim == 0 || dim > 65535 || nlist == 0) fail(ELIPS_B200_INVALID_ARGUMENT, "bad dimension or list count");
         if (centroids == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "centroids are null");
@@ -78,6 +78,35 @@ public:
         set_owned_lists(words.data(), words.size());
     }
 
+    // IvfIndexState::remove (IvfIndexState.cpp:262-326) on the device: the
+    // slot leaves its list; unless it is the last slot, the last slot's row
+    // (vector, list, derived data) moves into it and keeps its place in its
+    // list under the new number; the store shrinks by one. No re-upload: one
+    // row copied on the device, the lists rebuilt from the member order at
+    // the next search. (The reference also retrains when fewer rows than
+    // lists remain; that case is the caller's: train again and re-add.)
+    void remove(size_t slot, cudaStream_t stream) {
+        if (slot >= n_) fail(ELIPS_B200_INVALID_ARGUMENT, "slot out of range");
+        DeviceGuard g(device_);
+        const size_t last = n_ - 1;
+        auto& mine = members_[assign_[slot]];
+        mine.erase(std::find(mine.begin(), mine.end(), static_cast<uint32_t>(slot)));
+        if (slot != last) {
+            float* v = static_cast<float*>(vectors_.get());
+            check_cuda(cudaMemcpyAsync(v + slot * dim_, v + last * dim_, static_cast<size_t>(dim_) * 4,
+                                       cudaMemcpyDeviceToDevice, stream),
+                       ELIPS_B200_TRANSFER_FAILED, "row move");
+            move_row(last, slot, stream);
+            assign_[slot] = assign_[last];
+            auto& moved = members_[assign_[slot]];
+            *std::find(moved.begin(), moved.end(), static_cast<uint32_t>(last)) = static_cast<uint32_t>(slot);
+        }
+        check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "remove");
+        assign_.pop_back();
+        --n_;
+        dirty_ = true;
+    }
+
 protected:
     // Validates the list ids (they must name a list), grows the row store and
     // appends the rows (DEVICE pointers). Returns the host copy of the ids;
@@ -111,6 +140,7 @@ protected:
 
     void commit_rows(const std::vector<uint32_t>& host_assign, cudaStream_t stream) {
         check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "ivf add");
+        for (size_t i = 0; i < host_assign.size(); ++i) members_[host_assign[i]].push_back(static_cast<uint32_t>(n_ + i));
         assign_.insert(assign_.end(), host_assign.begin(), host_assign.end());
         n_ += host_assign.size();
         dirty_ = true;
@@ -120,17 +150,19 @@ protected:
     virtual void grow(size_t rows) = 0;
     // Derived stores rebuild their list-major copies after the lists change.
     virtual void gather_lists(cudaStream_t stream) = 0;
+    // Derived stores move one row's data from slot `from` to slot `to`.
+    virtual void move_row(size_t from, size_t to, cudaStream_t stream) = 0;
 
-    // Lists in ascending slot order (IvfIndexState::rebuild_list_members,
-    // IvfIndexState.cpp:75-83), then the derived list-major copies.
+    // Lists in member order: ascending slots as rows are added
+    // (IvfIndexState::rebuild_list_members, IvfIndexState.cpp:75-83), a moved
+    // row keeping its place after a remove (IvfIndexState.cpp:285-301); then
+    // the derived list-major copies.
     void finalize(cudaStream_t stream) {
         if (!dirty_) return;
         std::vector<uint32_t> off(nlist_ + 1, 0);
-        for (uint32_t a : assign_) ++off[a + 1];
-        for (uint32_t l = 0; l < nlist_; ++l) off[l + 1] += off[l];
+        for (uint32_t l = 0; l < nlist_; ++l) off[l + 1] = off[l] + static_cast<uint32_t>(members_[l].size());
         std::vector<uint32_t> rows(n_);
-        std::vector<uint32_t> fill(off.begin(), off.end() - 1);
-        for (size_t s = 0; s < n_; ++s) rows[fill[assign_[s]]++] = static_cast<uint32_t>(s);
+        for (uint32_t l = 0; l < nlist_; ++l) std::copy(members_[l].begin(), members_[l].end(), rows.begin() + off[l]);
         list_off_ = DeviceBuffer(device_, off.size() * 4);
         list_rows_ = DeviceBuffer(device_, std::max<size_t>(n_, 1) * 4);
         check_cuda(cudaMemcpyAsync(list_off_.get(), off.data(), off.size() * 4, cudaMemcpyHostToDevice, stream),
@@ -336,6 +368,7 @@ protected:
     size_t n_ = 0, capacity_ = 0;
     bool dirty_ = false;
     std::vector<uint32_t> assign_;
+    std::vector<std::vector<uint32_t>> members_;  // slots of each list, in list order
     DeviceBuffer centroids_, vectors_, list_off_, list_rows_;
 };
 
@@ -360,6 +393,32 @@ public:
     }
 
     uint32_t pq_dim() const { return m_; }
+
+    // GpuIVFPQIndex::rebuild_codes (GpuIVFPQIndex.cpp:88-131), which the
+    // reference runs after every insert and remove: the PQ codebook trained
+    // again on every row's residual (10 rounds), then every row re-encoded,
+    // bit-identical to the CPU code.
+    void rebuild_codes(cudaStream_t stream) {
+        if (n_ == 0) return;
+        DeviceGuard g(device_);
+        StreamScratch s(a256(n_ * 4) + n_ * dim_ * 4, stream);
+        uint32_t* da = reinterpret_cast<uint32_t*>(s.get());
+        float* res = reinterpret_cast<float*>(s.get() + a256(n_ * 4));
+        check_cuda(cudaMemcpyAsync(da, assign_.data(), n_ * 4, cudaMemcpyHostToDevice, stream),
+                   ELIPS_B200_TRANSFER_FAILED, "assignment upload");
+        const uint64_t total = static_cast<uint64_t>(n_) * dim_;
+        {
+            Profiler::Scope prof("residuals", stream, n_);
+            residuals_kernel<<<static_cast<uint32_t>((total + 255) / 256), 256, 0, stream>>>(
+                static_cast<const float*>(vectors_.get()), da, static_cast<const float*>(centroids_.get()), n_, dim_, res);
+            launch_ok("residual kernel");
+        }
+        train_pq_codebook_device(device_, res, n_, dim_, m_, ksub_, 10, static_cast<float*>(codebook_.get()), stream);
+        pq_encode_device(res, n_, dim_, m_, ksub_, static_cast<const float*>(codebook_.get()),
+                         static_cast<uint8_t*>(codes_.get()), stream);
+        check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "rebuild codes");
+        dirty_ = true;
+    }
 
     // The PQ section of IndexSnapshot: codebook [pq_dim][ksub][dim/pq_dim] and
     // codes [n][pq_dim] in slot order, into host memory; either may be null.
@@ -498,6 +557,12 @@ private:
         if (queries == nullptr) fail(ELIPS_B200_INVALID_ARGUMENT, "queries is null");
     }
 
+    void move_row(size_t from, size_t to, cudaStream_t stream) override {
+        uint8_t* c = static_cast<uint8_t*>(codes_.get());
+        check_cuda(cudaMemcpyAsync(c + to * m_, c + from * m_, m_, cudaMemcpyDeviceToDevice, stream),
+                   ELIPS_B200_TRANSFER_FAILED, "code move");
+    }
+
     void grow(size_t rows) override {
         DeviceBuffer c(device_, rows * m_);
         if (n_ > 0)
@@ -597,6 +662,7 @@ public:
 
 private:
     void grow(size_t) override {}
+    void move_row(size_t, size_t, cudaStream_t) override {}
 
     void gather_lists(cudaStream_t stream) override {
         list_vecs_ = DeviceBuffer(device_, std::max<size_t>(n_, 1) * dim_ * 4);
@@ -783,6 +849,22 @@ int elips_b200_ivfpq_export(const elips_b200_ivfpq* index, float* centroids_out,
     });
 }
 
+int elips_b200_ivfpq_remove(elips_b200_ivfpq* index, size_t slot) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        OwnedStream st;
+        index->index.remove(slot, st.s);
+    });
+}
+
+int elips_b200_ivfpq_rebuild_codes(elips_b200_ivfpq* index) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        OwnedStream st;
+        index->index.rebuild_codes(st.s);
+    });
+}
+
 int elips_b200_ivfpq_codes_device(const elips_b200_ivfpq* index, uint8_t* codes_out, void* stream) {
     if (index == nullptr || codes_out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] { index->index.read_codes(codes_out, static_cast<cudaStream_t>(stream)); });
@@ -834,6 +916,14 @@ int elips_b200_ivfflat_export(const elips_b200_ivfflat* index, float* centroids_
                               float* vectors_out) {
     if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] { index->index.export_ivf(centroids_out, assignments_out, vectors_out); });
+}
+
+int elips_b200_ivfflat_remove(elips_b200_ivfflat* index, size_t slot) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        OwnedStream st;
+        index->index.remove(slot, st.s);
+    });
 }
 
 int elips_b200_ivfflat_size(const elips_b200_ivfflat* index, size_t* n_out) {

@@ -59,6 +59,14 @@ class IvfPqIndex:
                                                         codes.data_ptr() if codes is not None else None,
                                                         vectors.shape[0], s), "elips_b200_ivfpq_add_device")
 
+    def remove(self, slot: int) -> None:
+        """IvfIndexState::remove: the last slot's row moves into `slot`."""
+        capi.check(capi.LIB.elips_b200_ivfpq_remove(self._h, int(slot)), "elips_b200_ivfpq_remove")
+
+    def rebuild_codes(self) -> None:
+        """GpuIVFPQIndex::rebuild_codes: retrain the codebook on all residuals, re-encode."""
+        capi.check(capi.LIB.elips_b200_ivfpq_rebuild_codes(self._h), "elips_b200_ivfpq_rebuild_codes")
+
     def export_snapshot(self) -> dict:
         """IndexSnapshot's fields in slot order: centroids, assignments,
         vectors, codebook, codes (elips_b200_ivfpq_create + add rebuild it)."""
@@ -217,6 +225,10 @@ class IvfFlatIndex:
         s = stream if stream is not None else torch.cuda.current_stream(vectors.device).cuda_stream
         capi.check(capi.LIB.elips_b200_ivfflat_add_device(self._h, vectors.data_ptr(), assignments.data_ptr(),
                                                           vectors.shape[0], s), "elips_b200_ivfflat_add_device")
+
+    def remove(self, slot: int) -> None:
+        """IvfIndexState::remove: the last slot's row moves into `slot`."""
+        capi.check(capi.LIB.elips_b200_ivfflat_remove(self._h, int(slot)), "elips_b200_ivfflat_remove")
 
     def export_snapshot(self) -> dict:
         """centroids, assignments and vectors in slot order."""

@@ -360,6 +360,17 @@ ELIPS_B200_API int elips_b200_ivfpq_export(const elips_b200_ivfpq* index, float*
                                            uint32_t* assignments_out, float* vectors_out,
                                            float* codebook_out, uint8_t* codes_out);
 
+/* IvfIndexState::remove (src/gpu_engine/detail/IvfIndexState.cpp:262-326) on
+ * the device: the slot leaves its list and, unless it is the last slot, the
+ * last slot's row moves into it (keeping its place in its list); no
+ * re-upload. The reference then runs rebuild_codes
+ * (GpuIVFPQIndex.cpp:156-159): call elips_b200_ivfpq_rebuild_codes, which
+ * retrains the codebook on every residual (10 rounds) and re-encodes every
+ * row, bit-identical to the CPU code (also after an insert: assign with
+ * elips_b200_ivf_assign, add, rebuild). Not concurrent with searches. */
+ELIPS_B200_API int elips_b200_ivfpq_remove(elips_b200_ivfpq* index, size_t slot);
+ELIPS_B200_API int elips_b200_ivfpq_rebuild_codes(elips_b200_ivfpq* index);
+
 ELIPS_B200_API int elips_b200_ivfpq_destroy(elips_b200_ivfpq* index);
 
 /* -------------------------------------------------------------- IVF-Flat */
@@ -406,6 +417,9 @@ ELIPS_B200_API int elips_b200_ivfflat_search_device(elips_b200_ivfflat* index, c
 /* Snapshot readback: centroids, assignments and vectors in slot order (any may be NULL). */
 ELIPS_B200_API int elips_b200_ivfflat_export(const elips_b200_ivfflat* index, float* centroids_out,
                                              uint32_t* assignments_out, float* vectors_out);
+
+/* IvfIndexState::remove, as elips_b200_ivfpq_remove (IVF-Flat has no codes). */
+ELIPS_B200_API int elips_b200_ivfflat_remove(elips_b200_ivfflat* index, size_t slot);
 
 ELIPS_B200_API int elips_b200_ivfflat_destroy(elips_b200_ivfflat* index);
 

@@ -496,6 +496,23 @@ class RefIvfPqIndex:
                                c_int(_threads(nthreads)), _p(dist), _p(rows))
         return dist, rows
 
+    def remove(self, row):
+        """GpuIVFPQIndex::remove of the record added as `row` (rebuilds the codes)."""
+        self.lib.ref_ivfpq_remove(self.h, c_size_t(row))
+
+    def export(self, n, pq_dim, ksub):
+        """export_snapshot: (original rows, vectors, assignments, codebook, codes)."""
+        rows = np.empty(n, np.int64)
+        vec = np.empty((n, self.dim), np.float32)
+        asg = np.empty(n, np.uint32)
+        cb = np.empty((pq_dim, ksub, self.dim // pq_dim), np.float32)
+        codes = np.empty((n, pq_dim), np.uint8)
+        rc = self.lib.ref_ivfpq_export(self.h, c_size_t(n), c_uint32(self.dim), _p(rows), _p(vec), _p(asg), _p(cb),
+                                       c_size_t(cb.size), _p(codes), c_size_t(codes.size))
+        if rc != 0:
+            raise RuntimeError(f"reference export_snapshot failed ({rc})")
+        return rows, vec, asg, cb, codes
+
     def __del__(self):
         try:
             self.lib.ref_ivfpq_destroy(self.h)

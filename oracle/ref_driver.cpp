@@ -427,6 +427,28 @@ int ref_ivfpq_search(void* handle, uint32_t dim, const float* queries, size_t nq
     return 0;
 }
 
+// GpuIVFPQIndex::remove (state remove, then rebuild_codes), by original row.
+int ref_ivfpq_remove(void* handle, size_t row) {
+    static_cast<IvfPqHandle*>(handle)->index->remove(row_id(row));
+    return 0;
+}
+
+// export_snapshot: ids (as original rows), vectors, assignments, codebook, codes.
+int ref_ivfpq_export(void* handle, size_t n, uint32_t dim, std::int64_t* rows_out, float* vectors_out,
+                     uint32_t* assign_out, float* codebook_out, size_t codebook_len, std::uint8_t* codes_out,
+                     size_t codes_len) {
+    auto snap = static_cast<IvfPqHandle*>(handle)->index->export_snapshot();
+    if (!snap.has_value() || !snap->ivf.has_value() || !snap->pq.has_value()) return 1;
+    if (snap->ids.size() != n || snap->vectors.size() != n * dim || snap->ivf->assignments.size() != n) return 2;
+    if (snap->pq->codebook.size() != codebook_len || snap->pq->codes.size() != codes_len) return 3;
+    for (size_t i = 0; i < n; ++i) rows_out[i] = id_row(snap->ids[i]);
+    std::copy(snap->vectors.begin(), snap->vectors.end(), vectors_out);
+    std::copy(snap->ivf->assignments.begin(), snap->ivf->assignments.end(), assign_out);
+    std::copy(snap->pq->codebook.begin(), snap->pq->codebook.end(), codebook_out);
+    std::copy(snap->pq->codes.begin(), snap->pq->codes.end(), codes_out);
+    return 0;
+}
+
 void ref_ivfpq_destroy(void* handle) { delete static_cast<IvfPqHandle*>(handle); }
 
 // GpuIVFFlatIndex on the CPU port, loaded through import_snapshot
