@@ -488,17 +488,21 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
 def run_b200(args, cfg, world, rank, local):
     import torch
     from elips_b200 import ExactIndex, _capi
-    from elips_b200.distributed import ShardedExactIndex, shard_range
+    from elips_b200.distributed import ReplicatedIndex, ShardedExactIndex, query_range, shard_range
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     n, d, nq, k = cfg["n"], cfg["d"], cfg["q"], cfg["k"]
-    lo, hi = shard_range(n, rank, world)
+    replicate = args.distributed == "replicate" and world > 1
+    lo, hi = (0, n) if replicate else shard_range(n, rank, world)
     cents = _centroids(cfg, dev) if cfg["data"] == "mixture" else None
 
-    # ---- build: this rank's shard, generated on the device in chunks
+    # ---- build: this rank's shard (or whole replica), generated on the device in chunks
     t0 = time.perf_counter()
-    index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local)
+    if replicate:
+        index = ReplicatedIndex(ExactIndex(cfg["metric"], d, precision=cfg["precision"], device=local))
+    else:
+        index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local)
     host_base = [] if (world == 1 and not args.no_cpu_baseline) else None
     step_rows = 1 << 18
     for r0 in range(lo, hi, step_rows):
@@ -514,7 +518,7 @@ def run_b200(args, cfg, world, rank, local):
     mask_dev = None
     if cfg.get("mask_p"):
         words = gen_mask_words(cfg, n)
-        if world > 1:
+        if world > 1 and not replicate:
             # each rank's mask covers its own rows, starting at bit 0
             sub = np.zeros((hi - lo + 31) // 32, np.uint32)
             idx = np.arange(lo, hi)
@@ -589,28 +593,32 @@ def run_b200(args, cfg, world, rank, local):
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t, world)
     barrier(world)
-    in_bytes = queries.numel() * queries.element_size() * world
+    # sharded: every rank uploads the whole batch; replicas: each its own slice
+    in_bytes = queries.numel() * queries.element_size() * (1 if replicate else world)
     if mask_words is not None:
         in_bytes += mask_words.nbytes
     e2e = {"value": round(nq * args.steps / e2e_s, 2), "unit": "queries/s",
            "h2d_bytes_per_step": int(in_bytes), "d2h_bytes_per_step": int(nq * k * (4 + 8)),
            "api": "elips_b200_exact_search (host buffers)" if world == 1 else
-                  "ShardedExactIndex.search_batch (host buffers, NCCL all-gather, merge kernel)"}
+                  ("ReplicatedIndex.search_batch (host buffers, query slices, NCCL all-gather of the results)"
+                   if replicate else
+                   "ShardedExactIndex.search_batch (host buffers, NCCL all-gather, merge kernel)")}
 
     # ---- roofline of the dominant kernel (fused GEMM + top-k)
     peaks, peak_src = load_peaks()
     n_shard = hi - lo
-    d_pad = (d + 63) // 64 * 64
+    # queries one launch on this rank answers: the whole batch, or its slice
+    nq_rank = (lambda r: r[1] - r[0])(query_range(nq, rank, world)) if replicate else nq
     if cfg["precision"] == "int8":
-        flops = 2.0 * nq * n_shard * d
+        flops = 2.0 * nq_rank * n_shard * d
         peak = 2.0 * peaks["bf16_tflops"]
         peak_note = f"int8 dense = 2 x {peak_src} bf16 burst"
     elif cfg["precision"] == "fp32":
-        flops = 2.0 * nq * n_shard * d
+        flops = 2.0 * nq_rank * n_shard * d
         peak = peaks["bf16_tflops"] / 2.0
         peak_note = f"tf32 dense = {peak_src} bf16 burst / 2 (3xTF32 issues 3 MMAs per counted flop)"
     else:
-        flops = 2.0 * nq * n_shard * d
+        flops = 2.0 * nq_rank * n_shard * d
         # The sustained figure when the timed region is long or ran under the
         # power cap (the regime the sustained GEMM figure was measured in).
         capped = "sw_power_cap" in (sampler.summary().get("reasons") or [])
@@ -649,7 +657,9 @@ def run_b200(args, cfg, world, rank, local):
         "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes and distributions of the configuration)",
         "config": {"workload": cfg["workload"], "config": args.config, "base_rows": n, "dim": d,
                    "queries_per_step": nq, "k": k, "metric": cfg["metric"], "precision": cfg["precision"],
-                   "sharding": f"rows split {world} ways (contiguous ranges)" if world > 1 else "single GPU",
+                   "sharding": (f"replicas: whole base on each of {world} GPUs, query batch split {world} ways"
+                                if replicate else f"rows split {world} ways (contiguous ranges)")
+                               if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (base >= 2 GB); no flush"
                          if n * d * 2 > 126e6 else "L2-resident base; steps back to back"},
         "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "clocks": clocks,
@@ -1012,6 +1022,9 @@ def main():
     ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--distributed", default="shard", choices=["shard", "replicate"],
+                    help="exact configurations at N>1: rows split across the GPUs (shard) or the whole base on "
+                         "every GPU with the query batch split (replicate)")
     ap.add_argument("--base-rows", type=int, default=None,
                     help="smaller base of the same configuration (profiling captures)")
     ap.add_argument("--queries", type=int, default=None,
@@ -1033,6 +1046,8 @@ def main():
         return
     world, rank, local = dist_setup(args)
     try:
+        if args.distributed == "replicate" and world > 1 and args.config in ("ivfpq", "ivf_build", "batcher"):
+            raise SystemExit("--distributed replicate applies to the exact configurations")
         if args.config == "ivfpq":
             result = run_b200_ivfpq(args, cfg, world, rank, local)
         elif args.config in ("ivf_build", "batcher"):

@@ -97,6 +97,118 @@ class ShardedExactIndex:
         return out_dist, out_rows
 
 
+def query_range(nq: int, rank: int, world: int) -> tuple[int, int]:
+    """The slice of a query batch one replica answers: contiguous, split as
+    split_ids splits rows (GpuDistributedIndex.cpp:12-22)."""
+    return nq * rank // world, nq * (rank + 1) // world
+
+
+def gather_query_slices(dist_slice, rows_slice, nq: int, world: int, group=None):
+    """All-gather of every rank's results for its query_range slice into the
+    whole batch's (dist [nq, k] float32, rows [nq, k] int64), in query order,
+    on every rank. Slices are padded to ceil(nq / world) queries so the
+    collective moves equal blocks; (distance bits, row low, row high) travel
+    as one int32 block. Collective: every rank calls it with the same nq."""
+    import torch
+    import torch.distributed as dist
+    k = dist_slice.shape[1]
+    per = (nq + world - 1) // world
+    dev = dist_slice.device
+    if per == 0:
+        return (torch.empty((0, k), dtype=torch.float32, device=dev),
+                torch.empty((0, k), dtype=torch.int64, device=dev))
+    m = dist_slice.shape[0]
+    block = torch.empty((per, k, 3), dtype=torch.int32, device=dev)
+    block[:m, :, 0] = dist_slice.contiguous().view(torch.int32)
+    block[:m, :, 1:] = rows_slice.contiguous().view(torch.int32).view(m, k, 2)
+    flat = torch.empty((world * per, k, 3), dtype=torch.int32, device=dev)
+    dist.all_gather_into_tensor(flat, block, group=group)
+    take = torch.cat([torch.arange(r * per, r * per + (query_range(nq, r, world)[1] - query_range(nq, r, world)[0]))
+                      for r in range(world)]).to(dev)
+    g = flat.index_select(0, take)
+    return g[..., 0].contiguous().view(torch.float32), g[..., 1:].contiguous().view(torch.int64).view(nq, k)
+
+
+class ReplicatedIndex:
+    """GpuDistributedIndex in replicate mode (DistributedMode::replicate,
+    src/gpu_engine/GpuDistributedIndex.cpp): every rank holds a full copy of
+    the index. Inserts go to every replica (:50-55), removals too (:61-65),
+    and the size is one replica's (:110-112). For a batch the reference hands
+    the whole batch to one replica in turn (:173-177); here the batch is split
+    across the replicas by contiguous query ranges and the slices are
+    all-gathered, so one batch keeps every GPU busy and no base row crosses
+    NVLink. A query's results do not depend on which other queries share its
+    launch, so they equal one replica's answer for the whole batch.
+
+    `local` is this rank's index (ExactIndex, IvfPqIndex or IvfFlatIndex) on
+    its own GPU; every rank must build it from the same rows in the same order
+    and call search_device / search_batch with the same batch size."""
+
+    def __init__(self, local, group=None):
+        import torch.distributed as dist
+        self.local = local
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+
+    def type_name(self) -> str:
+        """GpuDistributedIndex::type_name (:116-118)."""
+        return "gpu_replicated"
+
+    def size(self) -> int:
+        return self.local.size()
+
+    def add_device(self, rows, *args) -> None:
+        """Appends the same rows to this replica (every rank does)."""
+        self.local.add_device(rows, *args)
+
+    def remove(self, slot: int):
+        return self.local.remove(slot)
+
+    def search_device(self, queries, k: int, **kwargs):
+        """queries: CUDA tensor [nq, d], the same batch on every rank. This rank
+        answers query_range(nq, rank, world); returns the whole batch's
+        (dist, rows) on every rank."""
+        import torch
+        nq = queries.shape[0]
+        lo, hi = query_range(nq, self.rank, self.world)
+        if hi > lo:
+            d, r = self.local.search_device(queries[lo:hi], k, **kwargs)
+        else:
+            d = torch.empty((0, k), dtype=torch.float32, device=queries.device)
+            r = torch.empty((0, k), dtype=torch.int64, device=queries.device)
+        if self.world == 1:
+            return d, r
+        return gather_query_slices(d, r, nq, self.world, self.group)
+
+    def search_batch(self, queries_host, k: int, out_dist=None, out_rows=None, device=None):
+        """End-to-end from host memory: every rank uploads only its own slice of
+        the batch, searches it, the slices are all-gathered, and the root copies
+        the whole batch's results to host memory (other ranks return None, None)."""
+        import torch
+        q = torch.as_tensor(queries_host)
+        nq = q.shape[0]
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        lo, hi = query_range(nq, self.rank, self.world)
+        per = (nq + self.world - 1) // self.world
+        if hi > lo:
+            d, r = self.local.search_device(q[lo:hi].to(dev, non_blocking=True), k)
+        else:
+            d = torch.empty((0, k), dtype=torch.float32, device=dev)
+            r = torch.empty((0, k), dtype=torch.int64, device=dev)
+        if self.world > 1 and per > 0:
+            d, r = gather_query_slices(d, r, nq, self.world, self.group)
+        if self.rank != 0:
+            return None, None
+        if out_dist is None:
+            out_dist = torch.empty((nq, k), dtype=torch.float32, pin_memory=True)
+            out_rows = torch.empty((nq, k), dtype=torch.int64, pin_memory=True)
+        out_dist.copy_(d, non_blocking=True)
+        out_rows.copy_(r, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return out_dist, out_rows
+
+
 def list_range(nlist: int, rank: int, world: int) -> tuple[int, int]:
     """The IVF lists a rank owns: contiguous list ids, split as split_ids splits
     rows (GpuDistributedIndex.cpp:12-22)."""

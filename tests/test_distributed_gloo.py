@@ -174,3 +174,67 @@ def test_split_probe_exchange_equals_full_probe(tmp_path, world):
         q = H.gaussian(nq, 12, seed=92 + nq)
         got = np.load(tmp_path / f"probes{nq}.npy")
         assert np.array_equal(got.view(np.uint32), O.ivf_probe("euclidean", q, cents, 5))
+
+
+class _OracleReplica:
+    """A replica whose per-slice search is the oracle's (CPU tensors in and
+    out); the split of the batch and the all-gather are the product's."""
+
+    def __init__(self, metric, base):
+        self.metric, self.base = metric, base
+
+    def size(self):
+        return self.base.shape[0]
+
+    def search_device(self, queries, k):
+        import torch
+        d, r = O.exact_search(self.metric, self.base, queries.numpy(), k, 1)
+        return torch.from_numpy(d), torch.from_numpy(r.astype(np.int64))
+
+
+def _replica_worker(rank, world, port, k, out_dir):
+    import torch
+    import torch.distributed as dist
+    from elips_b200.distributed import ReplicatedIndex
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        for c, (metric, n) in enumerate(CASES):
+            base, queries = _case_data(metric, n)
+            index = ReplicatedIndex(_OracleReplica(metric, base))
+            assert index.size() == n and index.type_name() == "gpu_replicated"
+            for nq in (7, 2, 1, 0):
+                d, r = index.search_device(torch.from_numpy(queries[:nq]), k)
+                np.save(os.path.join(out_dir, f"rep{c}_{nq}_r{rank}_d.npy"), d.numpy())
+                np.save(os.path.join(out_dir, f"rep{c}_{nq}_r{rank}_r.npy"), r.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_replicated_query_split_matches_one_replica(tmp_path, world):
+    """DistributedMode::replicate: every rank answers its query_range slice of
+    the batch against a full replica; after the all-gather every rank holds
+    the whole batch's results in query order, equal to one replica's answer
+    for the whole batch (batches smaller than the world leave ranks idle)."""
+    k = 4
+    mp.spawn(_replica_worker, args=(world, _free_port(), k, str(tmp_path)), nprocs=world, join=True)
+    for c, (metric, n) in enumerate(CASES):
+        base, queries = _case_data(metric, n)
+        for nq in (7, 2, 1, 0):
+            d_ref, r_ref = O.exact_search(metric, base, queries[:nq], k, 1)
+            for rank in range(world):
+                d = np.load(tmp_path / f"rep{c}_{nq}_r{rank}_d.npy")
+                r = np.load(tmp_path / f"rep{c}_{nq}_r{rank}_r.npy")
+                assert d.shape == (nq, k) and r.shape == (nq, k)
+                assert np.array_equal(r, r_ref) and np.array_equal(d.view(np.uint32), d_ref.view(np.uint32))
+
+
+def test_query_ranges_partition_the_batch():
+    from elips_b200.distributed import query_range
+    for nq in (0, 1, 5, 10_000):
+        for world in (1, 2, 3, 8):
+            spans = [query_range(nq, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == nq
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))

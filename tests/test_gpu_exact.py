@@ -204,6 +204,36 @@ def test_shard_candidates_merge_equals_single_index():
     np.testing.assert_allclose(d.cpu().numpy(), d_ref, rtol=1e-6)
 
 
+@pytest.mark.parametrize("precision,metric", [("fp16", "cosine"), ("int8", "dot_product"), ("fp32", "euclidean")])
+def test_replicated_query_slices_equal_whole_batch(precision, metric):
+    # Replicate mode (DistributedMode::replicate): each replica answers a
+    # query_range slice of the batch; ranks emulated on one GPU. Slices of a
+    # 300-query batch run the single-CTA kernel, the whole batch the CTA-pair
+    # kernel: every query's results are identical either way.
+    import torch
+    from elips_b200.distributed import ReplicatedIndex, query_range
+    rng = np.random.default_rng(23)
+    if precision == "int8":
+        base = rng.integers(-127, 128, size=(40_000, 96), dtype=np.int8)
+        queries = rng.integers(-127, 128, size=(300, 96), dtype=np.int8)
+    else:
+        base = H.gaussian(40_000, 96, seed=24)
+        queries = H.gaussian(300, 96, seed=25)
+        if metric == "cosine":
+            base, queries = H.normalize(base), H.normalize(queries)
+    ix = _index(metric, base, precision)
+    qd = torch.from_numpy(queries).cuda()
+    d_ref, r_ref = ix.search_device(qd, 50)
+    for world in (2, 3, 8):
+        parts = [ix.search_device(qd[lo:hi], 50) for lo, hi in (query_range(300, r, world) for r in range(world))]
+        assert torch.equal(torch.cat([p[1] for p in parts]), r_ref)
+        assert torch.equal(torch.cat([p[0] for p in parts]).view(torch.int32), d_ref.view(torch.int32))
+    one = ReplicatedIndex(ix)  # no process group: a single replica
+    d1, r1 = one.search_device(qd, 50)
+    assert one.world == 1 and one.size() == base.shape[0]
+    assert torch.equal(r1, r_ref) and torch.equal(d1.view(torch.int32), d_ref.view(torch.int32))
+
+
 def test_no_device_error_recorded():
     from elips_b200 import _capi
     assert _capi.device_error(0) == 0
