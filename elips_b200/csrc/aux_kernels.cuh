@@ -156,18 +156,96 @@ __device__ __forceinline__ void warp_bitonic_sort(unsigned long long* buf, uint3
     }
 }
 
+// One warp selects the `take` smallest of `count` composites read by get(j)
+// into buf[0, w) (unsorted); returns w (= take when at least take are real,
+// padding {+inf, 0xFFFFFFFF} included only to fill up otherwise). A first
+// pass finds the leading bits shared by all real candidates (the keys of one
+// query's candidates are close, so the top byte or two agree), the radix
+// select starts below them and stops once a bin is taken whole; the
+// survivors are then gathered.
+template <class Get>
+__device__ __forceinline__ uint32_t merge_select(Get get, uint32_t count, uint32_t take, uint32_t* hist,
+                                                 unsigned long long* buf) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t lt = lanemask_lt();
+    uint32_t w = 0;
+    // the real candidates: how many, and the high bits they all share
+    uint32_t real = 0;
+    unsigned long long first_c = 0, diff = 0;
+    bool have = false;
+    for (uint32_t j0 = 0; j0 < count; j0 += 128) {
+        unsigned long long c[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t j = j0 + u * 32 + lane;
+            c[u] = j < count ? get(j) : ~0ull;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const bool is_real = (c[u] & 0xFFFFFFFFull) != 0xFFFFFFFFull;
+            const uint32_t m = __ballot_sync(0xffffffffu, is_real);
+            real += __popc(m);
+            if (m != 0 && !have) {
+                first_c = __shfl_sync(0xffffffffu, c[u], __ffs(m) - 1);
+                have = true;
+            }
+            if (is_real) diff |= c[u] ^ first_c;
+        }
+    }
+    unsigned long long prefix = 0, pmask = 0;
+    uint32_t rank = take;
+    int first = 0;
+    if (real >= take) {
+        // select among the real ones only: start below their common bits
+        diff = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(diff >> 32)) * (1ull << 32) |
+               __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(diff));
+        const int top = diff == 0 ? 0 : 63 - __clzll(static_cast<long long>(diff));
+        first = (63 - top) / 8;
+        pmask = first == 0 ? 0ull : ~0ull << (64 - 8 * first);
+        prefix = first_c & pmask;
+    }
+    warp_radix_select(get, count, rank, prefix, pmask, first, hist);
+    // every composite below the selected group, then `rank` of the group
+    for (uint32_t j0 = 0; j0 < count; j0 += 32) {
+        const uint32_t j = j0 + lane;
+        const unsigned long long c = j < count ? get(j) : ~0ull;
+        const bool keep = j < count && (c & pmask) < prefix &&
+                          (real < take || (c & 0xFFFFFFFFull) != 0xFFFFFFFFull);
+        const uint32_t m = __ballot_sync(0xffffffffu, keep);
+        if (keep) buf[w + __popc(m & lt)] = c;
+        w += __popc(m);
+    }
+    const uint32_t target = w + rank;
+    for (uint32_t j0 = 0; j0 < count && w < target; j0 += 32) {
+        const uint32_t j = j0 + lane;
+        const unsigned long long c = j < count ? get(j) : ~0ull;
+        const bool eq = j < count && (c & pmask) == prefix;
+        const uint32_t m = __ballot_sync(0xffffffffu, eq);
+        const uint32_t pos = w + __popc(m & lt);
+        if (eq && pos < target) buf[pos] = c;
+        w = min(target, w + __popc(m));
+    }
+    return w;
+}
+
+__device__ __forceinline__ unsigned long long merge_composite(uint2 e) {
+    return (static_cast<unsigned long long>(ordered_key(__uint_as_float(e.x))) << 32) | e.y;
+}
+
 // Final top-k per query: one warp selects the k smallest (key, row) pairs
 // among `lists` candidate lists of length k and writes them sorted.
 // List l of query q starts at cand + q*stride_q + l*stride_l (entries).
 // Composite 64-bit keys (ordered key << 32 | row) are unique except the
-// padding {+inf, 0xFFFFFFFF}. A first pass finds the leading bits shared by
-// all real candidates (the keys of one query's candidates are close, so the
-// top byte or two agree), the radix select starts below them and stops once
-// a bin is taken whole; the survivors are then gathered and sorted.
-// Dynamic smem per warp: 256 words of histogram + kpow2 u64 sort buffer.
+// padding {+inf, 0xFFFFFFFF}. When a query has at most `cache_cap`
+// candidates they are read from global memory once (16-byte loads where the
+// lists are contiguous and aligned) into the warp's shared-memory cache, and
+// every selection pass reads them there; otherwise each pass reads them from
+// global memory.
+// Dynamic smem per warp: 256 words of histogram + kpow2 u64 sort buffer +
+// cache_cap u64 cache.
 __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, uint32_t lists,
                                   uint32_t k, uint64_t stride_q, uint64_t stride_l, uint32_t kpow2,
-                                  int metric, float* __restrict__ out_dist,
+                                  uint32_t cache_cap, int metric, float* __restrict__ out_dist,
                                   int64_t* __restrict__ out_rows, uint2* __restrict__ out_cand) {
     extern __shared__ uint8_t smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -175,73 +253,42 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
     uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + warp * 256u;
     unsigned long long* buf =
         reinterpret_cast<unsigned long long*>(smem + warps * 1024u) + static_cast<size_t>(warp) * kpow2;
+    unsigned long long* cache = reinterpret_cast<unsigned long long*>(smem + warps * 1024u) +
+                                static_cast<size_t>(warps) * kpow2 + static_cast<size_t>(warp) * cache_cap;
     const uint32_t q = blockIdx.x * warps + warp;
     if (q >= nq) return;
     const uint32_t count = lists * k;
-    const uint32_t lt = lanemask_lt();
-    auto composite = [&](uint32_t idx) -> unsigned long long {
-        const uint32_t l = idx / k, i = idx - l * k;
-        const uint2 e = cand[q * stride_q + l * stride_l + i];
-        return (static_cast<unsigned long long>(ordered_key(__uint_as_float(e.x))) << 32) | e.y;
-    };
     const uint32_t take = min(k, count);
     uint32_t w = 0;
     if (take > 0) {
-        // the real candidates: how many, and the high bits they all share
-        uint32_t real = 0;
-        unsigned long long first_c = 0, diff = 0;
-        bool have = false;
-        for (uint32_t j0 = 0; j0 < count; j0 += 128) {
-            unsigned long long c[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t j = j0 + u * 32 + lane;
-                c[u] = j < count ? composite(j) : ~0ull;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const bool is_real = (c[u] & 0xFFFFFFFFull) != 0xFFFFFFFFull;
-                const uint32_t m = __ballot_sync(0xffffffffu, is_real);
-                real += __popc(m);
-                if (m != 0 && !have) {
-                    first_c = __shfl_sync(0xffffffffu, c[u], __ffs(m) - 1);
-                    have = true;
+        if (count <= cache_cap) {
+            const uint2* base = cand + q * stride_q;
+            if (stride_l == k && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+                const uint4* src = reinterpret_cast<const uint4*>(base);
+                const uint32_t pairs = count / 2u;
+#pragma unroll 4
+                for (uint32_t i = lane; i < pairs; i += 32) {
+                    const uint4 v = src[i];
+                    cache[2u * i] = merge_composite(make_uint2(v.x, v.y));
+                    cache[2u * i + 1u] = merge_composite(make_uint2(v.z, v.w));
                 }
-                if (is_real) diff |= c[u] ^ first_c;
+                if ((count & 1u) && lane == 0) cache[count - 1u] = merge_composite(base[count - 1u]);
+            } else {
+#pragma unroll 4
+                for (uint32_t j = lane; j < count; j += 32) {
+                    const uint32_t l = j / k, i = j - l * k;
+                    cache[j] = merge_composite(base[l * stride_l + i]);
+                }
             }
-        }
-        unsigned long long prefix = 0, pmask = 0;
-        uint32_t rank = take;
-        int first = 0;
-        if (real >= take) {
-            // select among the real ones only: start below their common bits
-            diff = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(diff >> 32)) * (1ull << 32) |
-                   __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(diff));
-            const int top = diff == 0 ? 0 : 63 - __clzll(static_cast<long long>(diff));
-            first = (63 - top) / 8;
-            pmask = first == 0 ? 0ull : ~0ull << (64 - 8 * first);
-            prefix = first_c & pmask;
-        }
-        warp_radix_select(composite, count, rank, prefix, pmask, first, hist);
-        // every composite below the selected group, then `rank` of the group
-        for (uint32_t j0 = 0; j0 < count; j0 += 32) {
-            const uint32_t j = j0 + lane;
-            const unsigned long long c = j < count ? composite(j) : ~0ull;
-            const bool keep = j < count && (c & pmask) < prefix &&
-                              (real < take || (c & 0xFFFFFFFFull) != 0xFFFFFFFFull);
-            const uint32_t m = __ballot_sync(0xffffffffu, keep);
-            if (keep) buf[w + __popc(m & lt)] = c;
-            w += __popc(m);
-        }
-        const uint32_t target = w + rank;
-        for (uint32_t j0 = 0; j0 < count && w < target; j0 += 32) {
-            const uint32_t j = j0 + lane;
-            const unsigned long long c = j < count ? composite(j) : ~0ull;
-            const bool eq = j < count && (c & pmask) == prefix;
-            const uint32_t m = __ballot_sync(0xffffffffu, eq);
-            const uint32_t pos = w + __popc(m & lt);
-            if (eq && pos < target) buf[pos] = c;
-            w = min(target, w + __popc(m));
+            __syncwarp();
+            w = merge_select([&](uint32_t j) -> unsigned long long { return cache[j]; }, count, take, hist, buf);
+        } else {
+            w = merge_select(
+                [&](uint32_t idx) -> unsigned long long {
+                    const uint32_t l = idx / k, i = idx - l * k;
+                    return merge_composite(cand[q * stride_q + l * stride_l + i]);
+                },
+                count, take, hist, buf);
         }
     }
     for (uint32_t i = w + lane; i < kpow2; i += 32) buf[i] = ~0ull;

@@ -813,12 +813,17 @@ void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists
     uint32_t kpow2 = 1;
     while (kpow2 < k) kpow2 <<= 1;
     constexpr uint32_t warps = 4;
-    const size_t smem = warps * (1024 + static_cast<size_t>(kpow2) * 8);
+    // Up to 2048 candidates per query (16 KB) stay in shared memory for all
+    // selection passes; larger merges read global memory on every pass.
+    constexpr uint64_t kCacheMax = 2048;
+    const uint64_t count = static_cast<uint64_t>(lists) * k;
+    const uint32_t cache_cap = count <= kCacheMax ? static_cast<uint32_t>((count + 1) / 2 * 2) : 0u;
+    const size_t smem = warps * (1024 + static_cast<size_t>(kpow2) * 8 + static_cast<size_t>(cache_cap) * 8);
     allow_dynamic_smem(reinterpret_cast<const void*>(merge_topk_kernel), smem);
     const uint32_t blocks = (nq + warps - 1) / warps;
     Profiler::Scope prof("merge_topk", stream, static_cast<uint64_t>(nq) * lists * k);
     merge_topk_kernel<<<blocks, warps * 32, smem, stream>>>(cand, nq, lists, k, stride_q, stride_l, kpow2,
-                                                           metric, out_dist, out_rows, out_cand);
+                                                           cache_cap, metric, out_dist, out_rows, out_cand);
     check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "merge kernel launch");
 }
 
