@@ -235,6 +235,9 @@ __device__ __forceinline__ unsigned long long merge_composite(uint2 e) {
 // Final top-k per query: one warp selects the k smallest (key, row) pairs
 // among `lists` candidate lists of length k and writes them sorted.
 // List l of query q starts at cand + q*stride_q + l*stride_l (entries).
+// With sub > 1 each query's lists are cut into `sub` groups of `lists` lists
+// (the last group: `lists_last`), one warp per (query, group), and output row
+// q*sub + j holds group j's k best: the first stage of a two-stage merge.
 // Composite 64-bit keys (ordered key << 32 | row) are unique except the
 // padding {+inf, 0xFFFFFFFF}. When a query has at most `cache_cap`
 // candidates they are read from global memory once (16-byte loads where the
@@ -245,8 +248,9 @@ __device__ __forceinline__ unsigned long long merge_composite(uint2 e) {
 // cache_cap u64 cache.
 __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, uint32_t lists,
                                   uint32_t k, uint64_t stride_q, uint64_t stride_l, uint32_t kpow2,
-                                  uint32_t cache_cap, int metric, float* __restrict__ out_dist,
-                                  int64_t* __restrict__ out_rows, uint2* __restrict__ out_cand) {
+                                  uint32_t cache_cap, uint32_t sub, uint32_t lists_last, int metric,
+                                  float* __restrict__ out_dist, int64_t* __restrict__ out_rows,
+                                  uint2* __restrict__ out_cand) {
     extern __shared__ uint8_t smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t warps = blockDim.x >> 5;
@@ -255,14 +259,16 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
         reinterpret_cast<unsigned long long*>(smem + warps * 1024u) + static_cast<size_t>(warp) * kpow2;
     unsigned long long* cache = reinterpret_cast<unsigned long long*>(smem + warps * 1024u) +
                                 static_cast<size_t>(warps) * kpow2 + static_cast<size_t>(warp) * cache_cap;
-    const uint32_t q = blockIdx.x * warps + warp;
-    if (q >= nq) return;
-    const uint32_t count = lists * k;
+    const uint32_t q = blockIdx.x * warps + warp;  // output row: query, or (query, group)
+    if (q >= nq * sub) return;
+    const uint32_t qq = q / sub, grp = q - qq * sub;
+    const uint32_t my_lists = grp + 1u == sub ? lists_last : lists;
+    const uint2* base = cand + qq * stride_q + static_cast<uint64_t>(grp) * lists * stride_l;
+    const uint32_t count = my_lists * k;
     const uint32_t take = min(k, count);
     uint32_t w = 0;
     if (take > 0) {
         if (count <= cache_cap) {
-            const uint2* base = cand + q * stride_q;
             if (stride_l == k && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
                 const uint4* src = reinterpret_cast<const uint4*>(base);
                 const uint32_t pairs = count / 2u;
@@ -286,7 +292,7 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
             w = merge_select(
                 [&](uint32_t idx) -> unsigned long long {
                     const uint32_t l = idx / k, i = idx - l * k;
-                    return merge_composite(cand[q * stride_q + l * stride_l + i]);
+                    return merge_composite(base[l * stride_l + i]);
                 },
                 count, take, hist, buf);
         }

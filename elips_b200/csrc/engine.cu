@@ -278,15 +278,23 @@ void launch_exact_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUten
 
 uint32_t bn_of(OperandKind k) { return k == OperandKind::TF32X3 ? 128u : 256u; }
 
-// Lists merged per first-stage warp when a batch has too few queries to give
-// every SM work in a one-stage merge (one warp per query): the largest
-// divisor of `lists` in [4, 16], or 1 (one stage) when there is none or the
-// batch is large enough.
-uint32_t merge_group_size(uint32_t nq, uint32_t lists, int num_sms) {
-    if (nq >= 8u * static_cast<uint32_t>(num_sms) || lists < 8) return 1;
-    for (uint32_t g = 16; g >= 4; --g)
-        if (lists % g == 0 && lists / g >= 2) return g;
-    return 1;
+// Candidates per query that the merge kernel keeps in shared memory.
+constexpr uint64_t kMergeCacheMax = 2048;
+
+// Lists merged per first-stage warp of a two-stage merge, or `lists` (one
+// stage). Two stages when a batch has too few queries to give every SM work
+// with one warp per query, or when a query's candidates do not fit the merge
+// kernel's shared-memory cache. Groups hold up to 16 lists and, where k
+// allows, at most 2048 / k so each group is merged from the cache (at least
+// 8 lists for small batches, at least 2 otherwise); the last group takes the
+// remainder.
+uint32_t merge_group_size(uint32_t nq, uint32_t lists, uint32_t k, int num_sms) {
+    const bool few_queries = nq < 8u * static_cast<uint32_t>(num_sms) && lists >= 8;
+    const bool uncached = static_cast<uint64_t>(lists) * k > kMergeCacheMax && lists >= 4;
+    if (!few_queries && !uncached) return lists;
+    const uint32_t fit = static_cast<uint32_t>(kMergeCacheMax / std::max<uint32_t>(1u, k));
+    const uint32_t g = std::min<uint32_t>(16u, std::max<uint32_t>(few_queries ? 8u : 2u, fit));
+    return g < lists ? g : lists;
 }
 
 // Pipeline depth: the stages that fit 192 KB of shared memory.
@@ -667,8 +675,10 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     const size_t cand = align(static_cast<size_t>(plan.grid) * 2 * kTileM * plan.cap * sizeof(uint2));
     const size_t partial = align(nq * plan.splits * 2 * k * sizeof(uint2));
     const size_t qtau = align(nq * sizeof(uint32_t));
-    const uint32_t merge_group = merge_group_size(static_cast<uint32_t>(nq), plan.splits * 2, props.num_sms);
-    const uint32_t groups = merge_group > 1 ? plan.splits * 2 / merge_group : 0;
+    const uint32_t n_lists = plan.splits * 2;
+    const uint32_t merge_group = merge_group_size(static_cast<uint32_t>(nq), n_lists, static_cast<uint32_t>(k),
+                                                  props.num_sms);
+    const uint32_t groups = merge_group < n_lists ? (n_lists + merge_group - 1) / merge_group : 0;
     const size_t stage = align(static_cast<size_t>(nq) * groups * k * sizeof(uint2));
     StreamScratch scratch(q_ops + q_lo + q_norm + cand + partial + qtau + stage, stream);
     uint8_t* s = scratch.get();
@@ -711,14 +721,15 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     prm.metric = metric_;
     dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan, stream);
     if (groups > 0) {
-        // Few queries: one warp per query would walk all lists alone. First
-        // every group of merge_group lists is reduced to its k best (one warp
-        // per (query, group)), then the groups; the k smallest (key, row)
-        // of the k smallest of each group are the k smallest overall.
+        // Few queries (one warp per query would walk all lists alone) or
+        // more candidates per query than the merge cache holds: first every
+        // group of merge_group lists is reduced to its k best (one warp per
+        // (query, group)), then the groups; the k smallest (key, row) of the
+        // k smallest of each group are the k smallest overall.
         uint2* stage_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand + partial + qtau);
-        merge_candidates(device_, part_buf, static_cast<uint32_t>(nq) * groups, merge_group,
-                         static_cast<uint32_t>(k), static_cast<uint64_t>(merge_group) * k, k, metric_, nullptr,
-                         nullptr, stage_buf, stream);
+        merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), merge_group, static_cast<uint32_t>(k),
+                         static_cast<uint64_t>(n_lists) * k, k, metric_, nullptr, nullptr, stage_buf, stream,
+                         groups, n_lists - (groups - 1) * merge_group);
         merge_candidates(device_, stage_buf, static_cast<uint32_t>(nq), groups, static_cast<uint32_t>(k),
                          static_cast<uint64_t>(groups) * k, k, metric_, out_dist, out_rows, out_cand, stream);
         return;
@@ -807,23 +818,27 @@ void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t
 
 void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,
                       uint64_t stride_q, uint64_t stride_l, int metric, float* out_dist,
-                      int64_t* out_rows, uint2* out_cand, cudaStream_t stream) {
+                      int64_t* out_rows, uint2* out_cand, cudaStream_t stream, uint32_t sub,
+                      uint32_t lists_last) {
     if (nq == 0 || k == 0) return;
+    if (sub == 0) sub = 1;
+    if (sub == 1 || lists_last == 0) lists_last = lists;
     if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
     uint32_t kpow2 = 1;
     while (kpow2 < k) kpow2 <<= 1;
     constexpr uint32_t warps = 4;
     // Up to 2048 candidates per query (16 KB) stay in shared memory for all
     // selection passes; larger merges read global memory on every pass.
-    constexpr uint64_t kCacheMax = 2048;
-    const uint64_t count = static_cast<uint64_t>(lists) * k;
-    const uint32_t cache_cap = count <= kCacheMax ? static_cast<uint32_t>((count + 1) / 2 * 2) : 0u;
+    const uint64_t count = static_cast<uint64_t>(std::max(lists, lists_last)) * k;
+    const uint32_t cache_cap = count <= kMergeCacheMax ? static_cast<uint32_t>((count + 1) / 2 * 2) : 0u;
     const size_t smem = warps * (1024 + static_cast<size_t>(kpow2) * 8 + static_cast<size_t>(cache_cap) * 8);
     allow_dynamic_smem(reinterpret_cast<const void*>(merge_topk_kernel), smem);
-    const uint32_t blocks = (nq + warps - 1) / warps;
-    Profiler::Scope prof("merge_topk", stream, static_cast<uint64_t>(nq) * lists * k);
+    const uint64_t rows_out = static_cast<uint64_t>(nq) * sub;
+    const uint32_t blocks = static_cast<uint32_t>((rows_out + warps - 1) / warps);
+    Profiler::Scope prof("merge_topk", stream, static_cast<uint64_t>(nq) * ((sub - 1) * lists + lists_last) * k);
     merge_topk_kernel<<<blocks, warps * 32, smem, stream>>>(cand, nq, lists, k, stride_q, stride_l, kpow2,
-                                                           cache_cap, metric, out_dist, out_rows, out_cand);
+                                                           cache_cap, sub, lists_last, metric, out_dist,
+                                                           out_rows, out_cand);
     check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "merge kernel launch");
 }
 

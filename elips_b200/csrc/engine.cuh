@@ -165,10 +165,13 @@ private:
     void upload_live_words(size_t w0, size_t w1);
 };
 
-// Final merge over candidate lists (see merge_topk_kernel).
+// Final merge over candidate lists (see merge_topk_kernel). With sub > 1,
+// the first stage of a two-stage merge: each query's lists in `sub` groups of
+// `lists` (the last: lists_last), output row q*sub + j per group.
 void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,
                       uint64_t stride_q, uint64_t stride_l, int metric, float* out_dist,
-                      int64_t* out_rows, uint2* out_cand, cudaStream_t stream);
+                      int64_t* out_rows, uint2* out_cand, cudaStream_t stream, uint32_t sub = 1,
+                      uint32_t lists_last = 0);
 
 int read_and_clear_device_error(int device);
 

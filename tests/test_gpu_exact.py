@@ -234,6 +234,21 @@ def test_replicated_query_slices_equal_whole_batch(precision, metric):
     assert torch.equal(r1, r_ref) and torch.equal(d1.view(torch.int32), d_ref.view(torch.int32))
 
 
+@pytest.mark.parametrize("nq", [1300, 4000])
+def test_int8_many_lists_two_stage_merge(nq):
+    # Batches of a few thousand queries over a base cut into many splits give
+    # each query more candidates (2 x splits x k) than the merge cache holds;
+    # they are merged in two stages (groups of up to 16 lists, the last group
+    # ragged). int8 scores are exact, ties by row: bit-identical to the oracle.
+    rng = np.random.default_rng(29)
+    base = rng.integers(-127, 128, size=(60_000, 64), dtype=np.int8)
+    queries = rng.integers(-127, 128, size=(nq, 64), dtype=np.int8)
+    ix = _index("dot_product", base, "int8")
+    d, r = ix.search_batch(queries, 100)
+    d_ref, r_ref = O.int8_ip_search(base, queries, 100)
+    assert np.array_equal(r, r_ref) and np.array_equal(d, d_ref)
+
+
 def test_no_device_error_recorded():
     from elips_b200 import _capi
     assert _capi.device_error(0) == 0
