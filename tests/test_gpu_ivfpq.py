@@ -154,3 +154,26 @@ def test_list_sharded_search_equals_single_index(model, world, balanced, metric)
     d, r = ShardedIvfPqIndex.merge_final(mine, k)
     torch.cuda.synchronize()
     assert np.array_equal(r.cpu().numpy(), r_ref) and np.array_equal(d.cpu().numpy(), d_ref)
+
+
+@pytest.mark.parametrize("flat", [False, True])
+def test_replicated_query_slices_equal_whole_batch(model, flat):
+    """Replicate mode (DistributedMode::replicate) over an IVF index: each
+    replica answers a query_range slice of the batch (ranks emulated on one
+    GPU); every query's ids and distances equal the whole batch's, the
+    tie-heavy model included."""
+    import torch
+    from elips_b200.distributed import query_range
+    from elips_b200.ivfpq import IvfFlatIndex, IvfPqIndex
+    m = model
+    ix = (IvfFlatIndex("euclidean", 64, m["cent"], nprobe=8) if flat
+          else IvfPqIndex("euclidean", 64, m["cent"], m["cb"], nprobe=8))
+    ix.add(m["base"], m["asg"])
+    qd = torch.from_numpy(m["queries"]).cuda()
+    d_ref, r_ref = ix.search_device(qd, 10)
+    for world in (2, 3, 8):
+        parts = [ix.search_device(qd[lo:hi], 10) for lo, hi in (query_range(qd.shape[0], r, world)
+                                                                 for r in range(world))]
+        torch.cuda.synchronize()
+        assert torch.equal(torch.cat([p[1] for p in parts]), r_ref)
+        assert torch.equal(torch.cat([p[0] for p in parts]).view(torch.int32), d_ref.view(torch.int32))
