@@ -97,6 +97,47 @@ class ShardedExactIndex:
         return out_dist, out_rows
 
 
+def shard_candidates(dist, rows, row_begin: int):
+    """One shard's results (dist [nq, k] float32, local rows [nq, k] int64,
+    -1 = none) as [nq, k, 2] int32 candidate pairs (distance bits, global
+    row = row_begin + local row), the block exchange_candidates moves."""
+    import torch
+    glob = torch.where(rows >= 0, rows + row_begin, rows)
+    return _pairs(dist, glob)
+
+
+class ShardedRowsIndex:
+    """Row sharding (split_ids ranges, GpuDistributedIndex.cpp:12-22) over any
+    per-rank index whose search_device returns final distances and local
+    rows: the quantized ExactIndex (QuantizedIndex, sq8 / PQ / OPQ codes) is
+    the one that needs it, the exact index has the fused ShardedExactIndex.
+    Each rank searches the rows it holds, its k results become (distance,
+    global row) pairs, one all-gather moves them and the root's merge kernel
+    keeps the k smallest by (distance, row), the order one index over all
+    rows returns. The distances are final, so the merge applies no transform.
+    Every rank of the group must call search_device with the same batch."""
+
+    def __init__(self, local, total_rows: int, group=None):
+        import torch.distributed as dist
+        self.local = local
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.total_rows = total_rows
+        self.row_begin, self.row_end = shard_range(total_rows, self.rank, self.world)
+
+    def search_device(self, queries, k: int):
+        """queries: CUDA tensor, the same batch on every rank. Returns (dist,
+        global rows) CUDA tensors on the root rank, (None, None) elsewhere."""
+        d, r = self.local.search_device(queries, k)
+        if self.world == 1:
+            return d, r
+        gathered = exchange_candidates(shard_candidates(d, r, self.row_begin), self.world, self.group)
+        if self.rank != 0:
+            return None, None
+        return merge_candidates_device(gathered, self.world, k, "dot_product")
+
+
 def query_range(nq: int, rank: int, world: int) -> tuple[int, int]:
     """The slice of a query batch one replica answers: contiguous, split as
     split_ids splits rows (GpuDistributedIndex.cpp:12-22)."""

@@ -238,3 +238,14 @@ def test_query_ranges_partition_the_batch():
             spans = [query_range(nq, r, world) for r in range(world)]
             assert spans[0][0] == 0 and spans[-1][1] == nq
             assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+
+
+def test_shard_candidates_global_rows():
+    import torch
+    from elips_b200.distributed import shard_candidates
+    d = torch.tensor([[0.5, 1.25, float("inf")]], dtype=torch.float32)
+    r = torch.tensor([[3, 0, -1]], dtype=torch.int64)
+    c = shard_candidates(d, r, 1000)
+    assert c.dtype == torch.int32 and c.shape == (1, 3, 2)
+    assert c[0, :, 1].tolist() == [1003, 1000, -1]
+    assert torch.equal(c[..., 0], d.view(torch.int32))

@@ -159,3 +159,41 @@ def test_normalize_rows_bit_exact(n, d):
     x[0] = 0.0
     got = normalize_rows(x)
     assert np.array_equal(got.view(np.uint32), O.normalize_rows(x).view(np.uint32))
+
+
+@pytest.mark.parametrize("codec,metric", [("sq8", "euclidean"), ("pq", "cosine"), ("sq8", "dot_product")])
+def test_row_sharded_quantized_equals_single_index(codec, metric):
+    """Row sharding of the quantized ExactIndex (split_ids ranges,
+    GpuDistributedIndex.cpp:12-22), ranks emulated on one GPU: every shard's
+    k results become (distance, global row) pairs, the merge kernel keeps the
+    k smallest by (distance, row); ids and distances equal one index over all
+    rows bit for bit (duplicate rows make ties across shards)."""
+    import torch
+    from elips_b200 import merge_candidates_device
+    from elips_b200.distributed import shard_candidates, shard_range
+    from elips_b200.quant import QuantizedIndex
+    base = H.gaussian(9000, 64, seed=57)
+    base[4500:4600] = base[100:200]          # identical rows in different shards
+    q = H.gaussian(50, 64, seed=58)
+    if codec == "sq8":
+        mins, scales = O.sq8_train(base[:5000])
+        make = lambda: QuantizedIndex("sq8", metric, 64, mins=mins, scales=scales)
+    else:
+        cb = O.ref_train_pq_codebook(base[:4000], 16, 256, 4)
+        make = lambda: QuantizedIndex("pq", metric, 64, codebook=cb)
+    full = make()
+    full.add(base)
+    qd = torch.from_numpy(q).cuda()
+    d_ref, r_ref = full.search_device(qd, 30)
+    for world in (2, 3, 8):
+        blocks = []
+        for rank in range(world):
+            lo, hi = shard_range(base.shape[0], rank, world)
+            ix = make()
+            ix.add(base[lo:hi])
+            d, r = ix.search_device(qd, 30)
+            blocks.append(shard_candidates(d, r, lo))
+        d, r = merge_candidates_device(torch.stack(blocks), world, 30, "dot_product")
+        torch.cuda.synchronize()
+        assert torch.equal(r, r_ref), world
+        assert torch.equal(d.view(torch.int32), d_ref.view(torch.int32)), world
