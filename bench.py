@@ -488,7 +488,7 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
 def run_b200(args, cfg, world, rank, local):
     import torch
     from elips_b200 import ExactIndex, _capi
-    from elips_b200.distributed import ReplicatedIndex, ShardedExactIndex, query_range, shard_range
+    from elips_b200.distributed import ReplicatedIndex, ShardedExactIndex, query_range, shard_range, slice_mask
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -519,13 +519,7 @@ def run_b200(args, cfg, world, rank, local):
     if cfg.get("mask_p"):
         words = gen_mask_words(cfg, n)
         if world > 1 and not replicate:
-            # each rank's mask covers its own rows, starting at bit 0
-            sub = np.zeros((hi - lo + 31) // 32, np.uint32)
-            idx = np.arange(lo, hi)
-            bits = (words[idx >> 5] >> (idx & 31).astype(np.uint32)) & 1
-            on = np.nonzero(bits)[0]
-            np.bitwise_or.at(sub, on >> 5, (np.uint32(1) << (on & 31).astype(np.uint32)))
-            words = sub
+            words = slice_mask(words, lo, hi)  # this rank's rows, starting at bit 0
         mask_words = words
         mask_dev = torch.from_numpy(words.view(np.int32)).to(dev)
     torch.cuda.synchronize()

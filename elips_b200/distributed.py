@@ -26,6 +26,20 @@ def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
     return n * rank // world, n * (rank + 1) // world
 
 
+def slice_mask(words, lo: int, hi: int) -> np.ndarray:
+    """A global eligibility mask (uint32 words, bit i & 31 of word i >> 5 =
+    row i) cut to the rows [lo, hi) a rank holds, re-based so the rank's first
+    row is bit 0: the filter of a row-sharded filtered search."""
+    words = np.asarray(words, np.uint32)
+    out = np.zeros((hi - lo + 31) // 32, np.uint32)
+    if hi <= lo:
+        return out
+    idx = np.arange(lo, hi)
+    on = np.nonzero((words[idx >> 5] >> (idx & 31).astype(np.uint32)) & 1)[0]
+    np.bitwise_or.at(out, on >> 5, np.left_shift(np.uint32(1), (on & 31).astype(np.uint32)))
+    return out
+
+
 def exchange_candidates(cand, world: int, group=None):
     """All-gather of every rank's candidate block [nq, k, ...] into
     [world, nq, k, ...], rank-major (rank r's block at index r). The output is

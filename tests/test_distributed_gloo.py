@@ -249,3 +249,23 @@ def test_shard_candidates_global_rows():
     assert c.dtype == torch.int32 and c.shape == (1, 3, 2)
     assert c[0, :, 1].tolist() == [1003, 1000, -1]
     assert torch.equal(c[..., 0], d.view(torch.int32))
+
+
+def test_slice_mask_rebases_each_rank():
+    """The filter of a row-sharded filtered search: a rank's mask is the global
+    mask's bits for its rows, its first row at bit 0 (ragged ranges, ranges
+    not starting on a word boundary, empty ranges)."""
+    from elips_b200.distributed import slice_mask
+    rng = np.random.default_rng(7)
+    for n in (0, 1, 33, 1000, 4099):
+        bits = rng.random(n) < 0.3
+        words = np.zeros((n + 31) // 32, np.uint32)
+        for i in np.flatnonzero(bits):
+            words[i >> 5] |= np.uint32(1) << np.uint32(i & 31)
+        for world in (1, 2, 3, 8):
+            for rank in range(world):
+                lo, hi = shard_range(n, rank, world)
+                sub = slice_mask(words, lo, hi)
+                assert sub.shape == ((hi - lo + 31) // 32,)
+                got = [(int(sub[j >> 5]) >> (j & 31)) & 1 for j in range(hi - lo)]
+                assert got == bits[lo:hi].astype(int).tolist()

@@ -249,6 +249,38 @@ def test_int8_many_lists_two_stage_merge(nq):
     assert np.array_equal(r, r_ref) and np.array_equal(d, d_ref)
 
 
+@pytest.mark.parametrize("shards", [2, 3])
+def test_filtered_shards_merge_equals_single_index(shards):
+    # Row-sharded filtered search, ranks emulated on one GPU: each shard gets
+    # the global mask sliced to its rows (first row at bit 0); the merged
+    # results equal one filtered index over all rows.
+    import torch
+    from elips_b200 import merge_candidates_device
+    from elips_b200.distributed import shard_range, slice_mask
+    base = H.gaussian(20_000, 48, seed=33)
+    queries = H.gaussian(64, 48, seed=34)
+    rng = np.random.default_rng(35)
+    keep = rng.random(base.shape[0]) < 0.1
+    words = np.zeros((base.shape[0] + 31) // 32, np.uint32)
+    for i in np.flatnonzero(keep):
+        words[i >> 5] |= np.uint32(1) << np.uint32(i & 31)
+    k = 20
+    full = _index("euclidean", base, "bf16")
+    d_ref, r_ref = full.search_batch(queries, k, mask=words)
+    assert keep[r_ref[r_ref >= 0]].all()
+    qd = torch.from_numpy(queries).cuda()
+    cand = torch.empty((shards, 64, k, 2), dtype=torch.int32, device="cuda")
+    for s in range(shards):
+        lo, hi = shard_range(base.shape[0], s, shards)
+        ix = _index("euclidean", base[lo:hi], "bf16")
+        m = torch.from_numpy(slice_mask(words, lo, hi).view(np.int32)).cuda()
+        ix.search_candidates_device(qd, k, lo, cand[s], mask=m)
+    d, r = merge_candidates_device(cand, shards, k, "euclidean")
+    torch.cuda.synchronize()
+    assert np.array_equal(r.cpu().numpy(), r_ref)
+    np.testing.assert_allclose(d.cpu().numpy(), d_ref, rtol=1e-6)
+
+
 def test_no_device_error_recorded():
     from elips_b200 import _capi
     assert _capi.device_error(0) == 0
