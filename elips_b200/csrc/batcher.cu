@@ -55,6 +55,7 @@ public:
             running_ = false;
         }
         cv_.notify_all();
+        idle_cv_.notify_all();
         if (worker_.joinable()) worker_.join();
         // Destructors must not throw: plain calls, errors ignored.
         int prev = -1;
@@ -85,6 +86,17 @@ public:
         return done.get();
     }
 
+    // Dispatches what is pending without the window and waits until the
+    // worker has served everything (the queue is empty and no batch runs).
+    void flush() {
+        std::unique_lock<std::mutex> lock(mu_);
+        if (pending_.empty() && !busy_) return;
+        ++flushers_;
+        cv_.notify_all();
+        idle_cv_.wait(lock, [this] { return (pending_.empty() && !busy_) || !running_; });
+        --flushers_;
+    }
+
     void stats(uint64_t* launches, uint64_t* queries) const {
         if (launches != nullptr) *launches = launches_.load();
         if (queries != nullptr) *queries = queries_.load();
@@ -106,20 +118,27 @@ private:
                 std::unique_lock<std::mutex> lock(mu_);
                 cv_.wait(lock, [this] { return !pending_.empty() || !running_; });
                 if (pending_.empty() && !running_) return;
-                // The window opens with the first pending query.
+                // The window opens with the first pending query (a flush skips it).
                 cv_.wait_for(lock, std::chrono::microseconds(window_us_),
-                             [this] { return pending_.size() >= max_batch_ || !running_; });
+                             [this] { return pending_.size() >= max_batch_ || !running_ || flushers_ > 0; });
                 const size_t take = std::min(pending_.size(), max_batch_);
                 for (size_t i = 0; i < take; ++i) {
                     batch.push_back(std::move(pending_.front()));
                     pending_.pop_front();
                 }
+                busy_ = !batch.empty();
             }
-            if (batch.empty()) continue;
-            launches_++;
-            queries_ += batch.size();
-            const int st = guarded([&] { run(batch); });
-            for (auto& p : batch) p.status.set_value(st);
+            if (!batch.empty()) {
+                launches_++;
+                queries_ += batch.size();
+                const int st = guarded([&] { run(batch); });
+                for (auto& p : batch) p.status.set_value(st);
+            }
+            {
+                std::lock_guard<std::mutex> lock(mu_);
+                busy_ = false;
+                if (pending_.empty()) idle_cv_.notify_all();
+            }
         }
     }
 
@@ -184,8 +203,11 @@ private:
     size_t cap_ = 0;
     std::mutex mu_;
     std::condition_variable cv_;
+    std::condition_variable idle_cv_;  // the queue drained and no batch runs
     std::deque<Pending> pending_;
     bool running_ = false;
+    bool busy_ = false;     // the worker is serving a batch
+    int flushers_ = 0;      // callers waiting in flush()
     std::thread worker_;
     std::atomic<uint64_t> launches_{0}, queries_{0};
 };
@@ -221,6 +243,11 @@ int elips_b200_batcher_stats(const elips_b200_batcher* batcher, uint64_t* launch
     if (batcher == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
     batcher->b->stats(launches, queries);
     return ELIPS_B200_OK;
+}
+
+int elips_b200_batcher_flush(elips_b200_batcher* batcher) {
+    if (batcher == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return eb::guarded([&] { batcher->b->flush(); });
 }
 
 int elips_b200_batcher_destroy(elips_b200_batcher* batcher) {

@@ -230,6 +230,11 @@ class DynamicBatcher:
                    "elips_b200_batcher_search")
         return dist, rows
 
+    def flush(self) -> None:
+        """DynamicBatcher::flush: serve the pending queries now, without
+        waiting for the window; returns when they have been served."""
+        capi.check(capi.LIB.elips_b200_batcher_flush(self._h), "elips_b200_batcher_flush")
+
     def stats(self) -> dict:
         l, q = ctypes.c_uint64(0), ctypes.c_uint64(0)
         capi.check(capi.LIB.elips_b200_batcher_stats(self._h, ctypes.byref(l), ctypes.byref(q)),

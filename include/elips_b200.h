@@ -441,6 +441,10 @@ ELIPS_B200_API int elips_b200_batcher_search(elips_b200_batcher* batcher, const 
 /* Launches and queries so far (BatchStats::kernel_launches / queries_coalesced). */
 ELIPS_B200_API int elips_b200_batcher_stats(const elips_b200_batcher* batcher, uint64_t* launches,
                                             uint64_t* queries);
+/* DynamicBatcher::flush (DynamicBatcher.cpp:36-65): the queries pending now
+ * are dispatched without waiting for the window; returns once every query
+ * pending at the call (and any that arrived meanwhile) has been served. */
+ELIPS_B200_API int elips_b200_batcher_flush(elips_b200_batcher* batcher);
 ELIPS_B200_API int elips_b200_batcher_destroy(elips_b200_batcher* batcher);
 
 /* ----------------------------------------------------------- index build */

@@ -70,3 +70,41 @@ def test_batcher_sequential_caller_and_dimension_check():
         b.search(base[0, :10], 3)
     assert b.stats()["kernel_launches"] == 5
     b.close()
+
+
+def test_flush_serves_pending_without_the_window():
+    """DynamicBatcher::flush (DynamicBatcher.cpp:36-65): with a 20 s window
+    and a batch limit far above the callers, queries wait for the window
+    until flush() dispatches them; flush returns once they are served, and
+    flush on an idle batcher returns at once."""
+    import time
+    from elips_b200 import DynamicBatcher, ExactIndex
+    rng = np.random.default_rng(3)
+    base = rng.standard_normal((5000, 64)).astype(np.float32)
+    q = rng.standard_normal((6, 64)).astype(np.float32)
+    ix = ExactIndex("euclidean", 64, precision="fp32")
+    ix.add(base)
+    d_ref, r_ref = ix.search_batch(q, 10)
+    b = DynamicBatcher(ix, window_us=20_000_000, max_batch=1000)
+    t0 = time.perf_counter()
+    b.flush()
+    assert time.perf_counter() - t0 < 1.0
+    out = [None] * len(q)
+
+    def work(i):
+        out[i] = b.search(q[i], 10)
+
+    ts = [threading.Thread(target=work, args=(i,)) for i in range(len(q))]
+    for t in ts:
+        t.start()
+    time.sleep(0.2)
+    assert all(o is None for o in out)          # still inside the window
+    t0 = time.perf_counter()
+    b.flush()
+    assert time.perf_counter() - t0 < 5.0
+    for t in ts:
+        t.join(timeout=5.0)
+    assert all(o is not None for o in out)
+    for i, (d, r) in enumerate(out):
+        assert np.array_equal(r, r_ref[i]) and np.array_equal(d, d_ref[i])
+    b.close()
