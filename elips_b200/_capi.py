@@ -83,6 +83,7 @@ SIGNATURES = [
     ("elips_b200_batcher_search", c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     ("elips_b200_batcher_stats", c_int, [c_void_p, POINTER(c_uint64), POINTER(c_uint64)]),
     ("elips_b200_batcher_flush", c_int, [c_void_p]),
+    ("elips_b200_batcher_pending", c_int, [c_void_p, POINTER(c_uint64)]),
     ("elips_b200_batcher_destroy", c_int, [c_void_p]),
     ("elips_b200_ivfpq_probe_device", c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     ("elips_b200_ivfpq_search_candidates_probed_device", c_int,

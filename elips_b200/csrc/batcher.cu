@@ -79,6 +79,7 @@ public:
         {
             std::lock_guard<std::mutex> lock(mu_);
             if (!running_) return ELIPS_B200_BACKEND_UNAVAILABLE;
+            p.ticket = enqueued_++;
             pending_.push_back(std::move(p));
             if (pending_.size() >= max_batch_) cv_.notify_one();
         }
@@ -86,15 +87,22 @@ public:
         return done.get();
     }
 
-    // Dispatches what is pending without the window and waits until the
-    // worker has served everything (the queue is empty and no batch runs).
+    // Dispatches the queries pending at the call without the window and
+    // waits until the worker has served them (DynamicBatcher::flush,
+    // DynamicBatcher.cpp:36-65). Queries enqueued after the call neither
+    // extend the wait nor skip their window.
     void flush() {
         std::unique_lock<std::mutex> lock(mu_);
-        if (pending_.empty() && !busy_) return;
-        ++flushers_;
+        const uint64_t target = enqueued_;  // tickets below this were pending at the call
+        if (served_ >= target) return;
+        flush_upto_ = std::max(flush_upto_, target);
         cv_.notify_all();
-        idle_cv_.wait(lock, [this] { return (pending_.empty() && !busy_) || !running_; });
-        --flushers_;
+        idle_cv_.wait(lock, [&] { return served_ >= target || !running_; });
+    }
+
+    uint64_t pending() {
+        std::lock_guard<std::mutex> lock(mu_);
+        return pending_.size();
     }
 
     void stats(uint64_t* launches, uint64_t* queries) const {
@@ -109,6 +117,7 @@ private:
         float* dist = nullptr;
         int64_t* rows = nullptr;
         std::promise<int> status;
+        uint64_t ticket = 0;  // arrival order
     };
 
     void loop() {
@@ -118,15 +127,16 @@ private:
                 std::unique_lock<std::mutex> lock(mu_);
                 cv_.wait(lock, [this] { return !pending_.empty() || !running_; });
                 if (pending_.empty() && !running_) return;
-                // The window opens with the first pending query (a flush skips it).
-                cv_.wait_for(lock, std::chrono::microseconds(window_us_),
-                             [this] { return pending_.size() >= max_batch_ || !running_ || flushers_ > 0; });
+                // The window opens with the first pending query; a flush skips
+                // it while queries pending at the flush are still queued.
+                cv_.wait_for(lock, std::chrono::microseconds(window_us_), [this] {
+                    return pending_.size() >= max_batch_ || !running_ || pending_.front().ticket < flush_upto_;
+                });
                 const size_t take = std::min(pending_.size(), max_batch_);
                 for (size_t i = 0; i < take; ++i) {
                     batch.push_back(std::move(pending_.front()));
                     pending_.pop_front();
                 }
-                busy_ = !batch.empty();
             }
             if (!batch.empty()) {
                 launches_++;
@@ -134,10 +144,10 @@ private:
                 const int st = guarded([&] { run(batch); });
                 for (auto& p : batch) p.status.set_value(st);
             }
-            {
+            if (!batch.empty()) {
                 std::lock_guard<std::mutex> lock(mu_);
-                busy_ = false;
-                if (pending_.empty()) idle_cv_.notify_all();
+                served_ = batch.back().ticket + 1;  // FIFO: every earlier ticket is served too
+                idle_cv_.notify_all();
             }
         }
     }
@@ -206,8 +216,9 @@ private:
     std::condition_variable idle_cv_;  // the queue drained and no batch runs
     std::deque<Pending> pending_;
     bool running_ = false;
-    bool busy_ = false;     // the worker is serving a batch
-    int flushers_ = 0;      // callers waiting in flush()
+    uint64_t enqueued_ = 0;    // tickets handed out
+    uint64_t served_ = 0;      // every ticket below this has its results
+    uint64_t flush_upto_ = 0;  // queued tickets below this skip the window
     std::thread worker_;
     std::atomic<uint64_t> launches_{0}, queries_{0};
 };
@@ -242,6 +253,12 @@ int elips_b200_batcher_search(elips_b200_batcher* batcher, const void* query, si
 int elips_b200_batcher_stats(const elips_b200_batcher* batcher, uint64_t* launches, uint64_t* queries) {
     if (batcher == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
     batcher->b->stats(launches, queries);
+    return ELIPS_B200_OK;
+}
+
+int elips_b200_batcher_pending(const elips_b200_batcher* batcher, uint64_t* pending) {
+    if (batcher == nullptr || pending == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *pending = batcher->b->pending();
     return ELIPS_B200_OK;
 }
 

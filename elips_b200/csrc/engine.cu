@@ -297,6 +297,27 @@ uint32_t merge_group_size(uint32_t nq, uint32_t lists, uint32_t k, int num_sms) 
     return g < lists ? g : lists;
 }
 
+// The per-split candidate lists of every query merged into its k best. With
+// groups == 0 in one pass. Otherwise (few queries, where one warp per query
+// would walk all lists alone, or more candidates per query than the merge
+// cache holds) every group of merge_group lists is first reduced to its k
+// best, one warp per (query, group), into `stage`, then the groups are
+// merged: the k smallest (key, row) of the k smallest of each group are the k
+// smallest overall.
+void merge_split_lists(int device, const uint2* part, uint2* stage, uint32_t nq, uint32_t n_lists,
+                       uint32_t merge_group, uint32_t groups, uint32_t k, int metric, float* out_dist,
+                       int64_t* out_rows, uint2* out_cand, cudaStream_t stream) {
+    if (groups > 0) {
+        merge_candidates(device, part, nq, merge_group, k, static_cast<uint64_t>(n_lists) * k, k, metric, nullptr,
+                         nullptr, stage, stream, groups, n_lists - (groups - 1) * merge_group);
+        merge_candidates(device, stage, nq, groups, k, static_cast<uint64_t>(groups) * k, k, metric, out_dist,
+                         out_rows, out_cand, stream);
+        return;
+    }
+    merge_candidates(device, part, nq, n_lists, k, static_cast<uint64_t>(n_lists) * k, k, metric, out_dist, out_rows,
+                     out_cand, stream);
+}
+
 // Pipeline depth: the stages that fit 192 KB of shared memory.
 constexpr int stages_of(OperandKind k, int cg) {
     return k == OperandKind::TF32X3 ? (cg == 2 ? 4 : 3) : (cg == 2 ? 6 : 4);
@@ -720,23 +741,9 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
     prm.row_offset = row_offset;
     prm.metric = metric_;
     dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan, stream);
-    if (groups > 0) {
-        // Few queries (one warp per query would walk all lists alone) or
-        // more candidates per query than the merge cache holds: first every
-        // group of merge_group lists is reduced to its k best (one warp per
-        // (query, group)), then the groups; the k smallest (key, row) of the
-        // k smallest of each group are the k smallest overall.
-        uint2* stage_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand + partial + qtau);
-        merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), merge_group, static_cast<uint32_t>(k),
-                         static_cast<uint64_t>(n_lists) * k, k, metric_, nullptr, nullptr, stage_buf, stream,
-                         groups, n_lists - (groups - 1) * merge_group);
-        merge_candidates(device_, stage_buf, static_cast<uint32_t>(nq), groups, static_cast<uint32_t>(k),
-                         static_cast<uint64_t>(groups) * k, k, metric_, out_dist, out_rows, out_cand, stream);
-        return;
-    }
-    merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits * 2, static_cast<uint32_t>(k),
-                     static_cast<uint64_t>(plan.splits) * 2 * k, k, metric_, out_dist, out_rows, out_cand,
-                     stream);
+    uint2* stage_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand + partial + qtau);
+    merge_split_lists(device_, part_buf, stage_buf, static_cast<uint32_t>(nq), n_lists, merge_group, groups,
+                      static_cast<uint32_t>(k), metric_, out_dist, out_rows, out_cand, stream);
 }
 
 void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t k, const uint32_t* mask,
@@ -766,7 +773,12 @@ void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t
     const size_t cand = align(static_cast<size_t>(plan.grid) * 2 * kTileM * plan.cap * sizeof(uint2));
     const size_t partial = align(nq * plan.splits * 2 * k * sizeof(uint2));
     const size_t qtau = align(nq * sizeof(uint32_t));
-    const size_t need = q_ops + q_lo + q_norm + cand + partial + qtau;
+    const uint32_t n_lists = plan.splits * 2;
+    const uint32_t merge_group = merge_group_size(static_cast<uint32_t>(nq), n_lists, static_cast<uint32_t>(k),
+                                                  props.num_sms);
+    const uint32_t groups = merge_group < n_lists ? (n_lists + merge_group - 1) / merge_group : 0;
+    const size_t stage = align(static_cast<size_t>(nq) * groups * k * sizeof(uint2));
+    const size_t need = q_ops + q_lo + q_norm + cand + partial + qtau + stage;
     if (need > scratch_bytes)
         fail(ELIPS_B200_INVALID_ARGUMENT,
              "search needs " + std::to_string(need >> 20) + " MiB of scratch, above the " +
@@ -812,8 +824,9 @@ void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t
     prm.row_offset = 0;
     prm.metric = metric_;
     dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan, stream);
-    merge_candidates(device_, part_buf, static_cast<uint32_t>(nq), plan.splits * 2, static_cast<uint32_t>(k),
-                     static_cast<uint64_t>(plan.splits) * 2 * k, k, metric_, out_dist, out_rows, nullptr, stream);
+    uint2* stage_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand + partial + qtau);
+    merge_split_lists(device_, part_buf, stage_buf, static_cast<uint32_t>(nq), n_lists, merge_group, groups,
+                      static_cast<uint32_t>(k), metric_, out_dist, out_rows, nullptr, stream);
 }
 
 void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,

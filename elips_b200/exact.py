@@ -235,6 +235,12 @@ class DynamicBatcher:
         waiting for the window; returns when they have been served."""
         capi.check(capi.LIB.elips_b200_batcher_flush(self._h), "elips_b200_batcher_flush")
 
+    def pending(self) -> int:
+        """Queries queued and not yet taken into a batch."""
+        n = ctypes.c_uint64(0)
+        capi.check(capi.LIB.elips_b200_batcher_pending(self._h, ctypes.byref(n)), "elips_b200_batcher_pending")
+        return n.value
+
     def stats(self) -> dict:
         l, q = ctypes.c_uint64(0), ctypes.c_uint64(0)
         capi.check(capi.LIB.elips_b200_batcher_stats(self._h, ctypes.byref(l), ctypes.byref(q)),

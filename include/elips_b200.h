@@ -155,8 +155,13 @@ ELIPS_B200_API int elips_b200_exact_search_device(const elips_b200_exact* index,
  * from one fixed 64 MiB device array inside this library, which every GPU that
  * loads the library holds until the process exits; a call needing more (large
  * query batches) fails with ELIPS_B200_INVALID_ARGUMENT, and at most 32 SMs
- * are used. The first call on a device looks up the array's address (no
- * allocation); make that first call before any stream capture. All calls
+ * are used. The first call on a device looks up the array's address; under
+ * CUDA's default lazy module loading that lookup is also what loads this
+ * library's module on the device and so reserves the 64 MiB (a call with
+ * nq = 0 does only this). Make that first call at set-up, while device memory
+ * is still free and before any stream capture, or run the process with
+ * CUDA_MODULE_LOADING=EAGER so the array is reserved when the library loads.
+ * All calls
  * share the array and it keeps the last call's contents: calls that overlap
  * on the GPU (different streams, or unordered host threads) race, so the
  * caller must serialise them. */
@@ -443,8 +448,13 @@ ELIPS_B200_API int elips_b200_batcher_stats(const elips_b200_batcher* batcher, u
                                             uint64_t* queries);
 /* DynamicBatcher::flush (DynamicBatcher.cpp:36-65): the queries pending now
  * are dispatched without waiting for the window; returns once every query
- * pending at the call (and any that arrived meanwhile) has been served. */
+ * pending at the call has been served. Queries that arrive after the call
+ * do not extend the wait. */
 ELIPS_B200_API int elips_b200_batcher_flush(elips_b200_batcher* batcher);
+/* Queries waiting for a batch (queued, not yet taken by the worker). The
+ * reference's BatchStats (include/elips/gpu_engine/DynamicBatcher.hpp:32-37)
+ * has no queue depth; this lets a caller see that its queries are queued. */
+ELIPS_B200_API int elips_b200_batcher_pending(const elips_b200_batcher* batcher, uint64_t* pending);
 ELIPS_B200_API int elips_b200_batcher_destroy(elips_b200_batcher* batcher);
 
 /* ----------------------------------------------------------- index build */

@@ -30,7 +30,9 @@ ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libelips_ref.so"
 REF_B200_SO = HERE / "_ref" / "libelips_ref_b200.so"
 PRODUCT_SO = HERE.parent / "elips_b200" / "libelips_b200.so"
-REF_ROOT = Path(os.environ.get("ELIPS_REF_ROOT", "/root/reference"))
+# The reference tree: ELIPS_REF_ROOT, else a checkout named `reference` beside
+# this repository.
+REF_ROOT = Path(os.environ.get("ELIPS_REF_ROOT", str(HERE.parent.parent / "reference")))
 
 METRIC = {"cosine": 0, "euclidean": 1, "dot_product": 2}
 

@@ -97,7 +97,10 @@ def test_flush_serves_pending_without_the_window():
     ts = [threading.Thread(target=work, args=(i,)) for i in range(len(q))]
     for t in ts:
         t.start()
-    time.sleep(0.2)
+    deadline = time.perf_counter() + 10.0
+    while b.pending() < len(q) and time.perf_counter() < deadline:
+        time.sleep(0.01)
+    assert b.pending() == len(q)                # every caller is queued
     assert all(o is None for o in out)          # still inside the window
     t0 = time.perf_counter()
     b.flush()
