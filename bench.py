@@ -47,9 +47,10 @@ CONFIGS = {
         n=5_000_000, d=1024, q=4096, k=50, metric="dot_product", precision="int8", data="int8",
         dtype="s8 (int32 accumulate)"),
     "filtered_bf16_l2": dict(
-        workload="filtered exact L2 bf16, N=1,000,000 x d=384 N(0,1), Bernoulli(0.1) mask, Q=64, k=20",
+        workload="filtered exact L2 bf16, N=1,000,000 x d=384 N(0,1), Bernoulli(0.1) row filter, query batches "
+                 "of 1, 8 and 64, k=20",
         n=1_000_000, d=384, q=64, k=20, metric="euclidean", precision="bf16", data="gaussian",
-        mask_p=0.1, dtype="bf16 (fp32 accumulate)"),
+        mask_p=0.1, batches=[1, 8, 64], dtype="bf16 (fp32 accumulate)"),
     "ivfpq": dict(
         workload="IVF-PQ, N=10,000,000 x d=128 Gaussian mixture (4,096 centroids, sigma=0.2, fp32), nlist=4,096 "
                  "(k-means), PQ 16 x 8 bits on residuals, nprobe=32, Q=10,000, k=10",
@@ -69,7 +70,17 @@ CONFIGS = {
         n=1_000_000, d=384, q=4096, k=20, metric="euclidean", precision="bf16", data="gaussian",
         callers=64, window_us=200, max_batch=256, dtype="bf16 (fp32 accumulate)"),
 }
+for _name, _c in CONFIGS.items():
+    _c["name"] = _name
 DEFAULT_CONFIG = "exact_fp16_cosine"
+# The other configurations the default run also times, each reported under
+# `workloads` in the same JSON line (with its own roofline, e2e, clocks, CPU
+# baseline and parity), the headline staying the top-level value.
+DEFAULT_WORKLOADS = ["exact_fp32_l2", "ivfpq", "int8_ip", "filtered_bf16_l2"]
+# Queries checked against the oracle per configuration (seeded, the first of
+# the batch): at least 1,000 for the large ones, every query for the small.
+PARITY_QUERIES = {"exact_fp16_cosine": 1000, "ivfpq": 1000, "int8_ip": 1000, "exact_fp32_l2": 1000,
+                  "filtered_bf16_l2": 64}
 METRIC_NAME = "k-NN queries/sec (exact d=768 N=2M k=100; IVF-PQ) at 1/2/4/8 B200, % roofline"
 CHUNK = 1 << 16
 SEED = 20261201
@@ -210,7 +221,7 @@ def dist_setup(args):
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -317,7 +328,7 @@ def scanned_bytes(cfg, centroids, queries, assign, lists=None):
 
 # ------------------------------------------------------------ b200 arm
 
-def run_b200_ivfpq(args, cfg, world, rank, local):
+def run_b200_ivfpq(args, cfg, world, rank, local, parity_q=None):
     """IVF-PQ on one GPU, or list-sharded over N (ShardedIvfPqIndex: rank 0
     trains the model and broadcasts it with the assignments; every rank keeps
     the rows of its own lists)."""
@@ -330,7 +341,8 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
     dev = torch.device("cuda", local)
     n, d, nq, k = cfg["n"], cfg["d"], cfg["q"], cfg["k"]
     t0 = time.perf_counter()
-    base, q_dev, centroids, assign, codebook, _, model_s = ivfpq_inputs(cfg, dev, train=(rank == 0))
+    base, q_dev, centroids, assign, codebook, all_codes, model_s = ivfpq_inputs(cfg, dev, train=(rank == 0))
+    parity_q = 0 if args.no_parity else min(nq, parity_q if parity_q is not None else nq)
     if world > 1:
         import torch.distributed as dist
         if rank != 0:
@@ -365,12 +377,14 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
     build_s = time.perf_counter() - t0
     out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
     out_r = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    last = [None]
 
     def step():
         if world == 1:
             index.search_device(q_dev, k, out_dist=out_d, out_rows=out_r)
+            last[0] = (out_d, out_r)
         else:
-            index.search_device(q_dev, k)
+            last[0] = index.search_device(q_dev, k)
 
     for _ in range(args.warmup):
         step()
@@ -401,6 +415,9 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
     per_kernel = {name: round(_capi.profiler_stats(name)["total_ms"] / args.steps, 4)
                   for name in ("distances", "topk_rows", "ivfpq_plan", "ivfpq_scan", "merge_topk", "ivfpq_rerank")}
     value = nq * args.steps / (ms / 1e3)
+    timed = None
+    if rank == 0 and parity_q and last[0] is not None and last[0][0] is not None:
+        timed = (last[0][0][:parity_q].cpu().numpy(), last[0][1][:parity_q].cpu().numpy())
 
     q_pin = q_dev.cpu().pin_memory()
     q_np = q_pin.numpy()
@@ -436,7 +453,7 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
     achieved = alg_bytes / (scan_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(peaks["hbm_gbs"], 1), "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "traffic": load_traffic(args.config, n if world == 1 else index.local.size()),
+                "traffic": load_traffic(cfg["name"], n if world == 1 else index.local.size()),
                 "kernel": "ivfpq_scan_kernel", "kernel_ms_avg": round(scan_ms, 4),
                 "kernel_ms_max_over_ranks": round(scan_ms_max, 4),
                 "kernel_share_of_step": round(scan["total_ms"] / max(1e-9, allk["total_ms"]), 4),
@@ -447,7 +464,7 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": cfg["dtype"],
         "data": "synthetic (seeded; shapes and distributions of the configuration)",
-        "config": {"workload": cfg["workload"], "config": args.config, "base_rows": n, "dim": d,
+        "config": {"workload": cfg["workload"], "config": cfg["name"], "base_rows": n, "dim": d,
                    "queries_per_step": nq, "k": k, "nlist": cfg["nlist"], "nprobe": cfg["nprobe"],
                    "pq": f"{cfg['pq_dim']}x{cfg['pq_bits']}",
                    "l2": "inputs larger than L2 (codes 160 MB, vectors 5.1 GB); no flush"},
@@ -458,34 +475,123 @@ def run_b200_ivfpq(args, cfg, world, rank, local):
                         "api": "elips_b200_ivfpq_train (bit-identical to GpuIVFPQIndex::build_from_batch)"}}
     if world > 1:
         result["config"]["parallelism"] = f"lists sharded over {world} GPUs (balanced by size^2)"
-    if not args.no_cpu_baseline and world == 1:
+    if rank == 0 and ((not args.no_cpu_baseline and world == 1) or timed is not None):
         import oracle
+        from oracle import parity
         host_base = base.cpu().numpy()
-        codes = index.codes()
+        codes = all_codes.cpu().numpy()
         a_np = assign.cpu().numpy().view(np.uint32)
         cent_np, cb_np = centroids.cpu().numpy(), codebook.cpu().numpy()
         threads = os.cpu_count() or 1
-        try:
-            ref = oracle.RefIvfPqIndex(cfg["metric"], cent_np, a_np, cb_np, codes, host_base, cfg["nprobe"],
-                                       pq_bits=cfg["pq_bits"])
-            kind, what = "reference", "reference GpuIVFPQIndex::search on a CPU GpuPort (import_snapshot of this model)"
-            search = lambda qq, kk, tt: ref.search(qq, kk, tt)
-        except Exception:
-            kind, what = "port", "C restatement of GpuIVFPQIndex::search"
-            search = lambda qq, kk, tt: oracle.ivfpq_search(cfg["metric"], cent_np, cb_np, codes, host_base, a_np,
-                                                            qq, cfg["nprobe"], kk, tt)
         qh = q_dev.cpu().numpy()
-        sample = _calibrated_sample(search, cfg, qh, threads, target_s=10.0)
-        t = time.perf_counter()
-        search(qh[:sample], k, threads)
-        dt = time.perf_counter() - t
-        result["cpu_baseline"] = {"value": round(sample / dt, 3), "unit": "queries/s", "cores": min(threads, sample),
-                                  "kind": kind, "sample": f"{sample} of the {nq} queries over the full {n}-row "
-                                  f"index ({what}), {dt:.2f} s wall"}
+        del index, base
+        torch.cuda.empty_cache()
+        ref_answers, sample, ref_kind = None, 0, None
+        if not args.no_cpu_baseline and world == 1:
+            try:
+                ref = oracle.RefIvfPqIndex(cfg["metric"], cent_np, a_np, cb_np, codes, host_base, cfg["nprobe"],
+                                           pq_bits=cfg["pq_bits"])
+                ref_kind, what = "reference", \
+                    "reference GpuIVFPQIndex::search on a CPU GpuPort (import_snapshot of this model)"
+                search = lambda qq, kk, tt: ref.search(qq, kk, tt)
+            except Exception:
+                ref_kind, what = "port", "C restatement of GpuIVFPQIndex::search"
+                search = lambda qq, kk, tt: oracle.ivfpq_search(cfg["metric"], cent_np, cb_np, codes, host_base,
+                                                                a_np, qq, cfg["nprobe"], kk, tt)
+            sample = _calibrated_sample(search, cfg, qh, threads, target_s=10.0)
+            t = time.perf_counter()
+            ref_answers = search(qh[:sample], k, threads)
+            dt = time.perf_counter() - t
+            result["cpu_baseline"] = {"value": round(sample / dt, 3), "unit": "queries/s",
+                                      "cores": min(threads, sample), "kind": ref_kind,
+                                      "sample": f"{sample} of the {nq} queries over the full {n}-row "
+                                      f"index ({what}), {dt:.2f} s wall"}
+        if timed is not None:
+            t = time.perf_counter()
+            od_, or_ = oracle.ivfpq_search(cfg["metric"], cent_np, cb_np, codes, host_base, a_np, qh[:parity_q],
+                                           cfg["nprobe"], k, threads, order="device")
+            par = parity.bit_exact(timed[0], timed[1], od_, or_)
+            par["oracle"] = ("oracle.c GpuIVFPQIndex::search restatement in the device's documented order "
+                             "(approximate terms grouped per subspace, rerank-set ties by slot)")
+            par["oracle_s"] = round(time.perf_counter() - t, 2)
+            if ref_answers is not None and ref_kind == "reference":
+                m = min(sample, parity_q)
+                _, _, gap = oracle.ivfpq_search(cfg["metric"], cent_np, cb_np, codes, host_base, a_np, qh[:m],
+                                                cfg["nprobe"], k, threads, order="reference", with_gap=True)
+                par["vs_reference_sample"] = parity.against_reference_with_ties(
+                    timed[0][:m], timed[1][:m], ref_answers[0][:m], ref_answers[1][:m], gap)
+                par["pass"] = bool(par["pass"] and par["vs_reference_sample"]["pass"])
+            par["what"] = "the last timed step's answers for the first queries of the batch"
+            result["parity"] = par
+    barrier(world)
     return result
 
 
-def run_b200(args, cfg, world, rank, local):
+def _peak_for(cfg, peaks, peak_src, capped, long_timed):
+    """Tensor peak for this configuration's operand type: the measured bf16
+    burst figure for a kernel timed alone in a short region (the regime it was
+    measured in), with the sustained figure reported beside it."""
+    if cfg["precision"] == "int8":
+        return 2.0 * peaks["bf16_tflops"], 2.0 * peaks["bf16_tflops_sustained"], \
+            f"int8 dense = 2 x {peak_src} bf16 burst"
+    if cfg["precision"] == "fp32":
+        return peaks["bf16_tflops"] / 2.0, peaks["bf16_tflops_sustained"] / 2.0, \
+            f"tf32 dense = {peak_src} bf16 burst / 2 (3xTF32 issues 3 MMAs per counted flop)"
+    note = f"{peak_src} bf16 burst" + (" (sw_power_cap was active in the timed region; the sustained "
+                                        "fraction is given beside it)" if capped else "")
+    return peaks["bf16_tflops"], peaks["bf16_tflops_sustained"], note
+
+
+def _full_base_host(cfg, dev, cents):
+    """The whole seeded base on the host (float32, int8 for the int8 codec),
+    generated on `dev` in chunks: what the oracle searches."""
+    n = cfg["n"]
+    out = np.empty((n, cfg["d"]), np.int8 if cfg["precision"] == "int8" else np.float32)
+    for r0 in range(0, n, 1 << 18):
+        cnt = min(1 << 18, n - r0)
+        out[r0:r0 + cnt] = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev).cpu().numpy()
+    return out
+
+
+def exact_parity(cfg, base, queries, dist, rows, mask_words, ref_answers=None, ref_sample=0):
+    """Parity of an exact search's results (dist, rows: host arrays of the
+    first len(dist) queries) with the oracle (oracle.c's arithmetic, pinned to
+    the reference's ExactIndex::search), plus, when given, with the
+    reference's own answers for the first ref_sample queries (the CPU
+    baseline's sample)."""
+    import oracle
+    from oracle import parity
+    nq = dist.shape[0]
+    q = queries[:nq]
+    threads = os.cpu_count() or 1
+    t = time.perf_counter()
+    if cfg["precision"] == "int8":
+        rd, rr = oracle.int8_ip_search_fast(base, q, cfg["k"], threads)
+        out = parity.bit_exact(dist, rows, rd, rr)
+        out["oracle"] = "integer restatement of the int8 inner-product codec (oracle_fast.c)"
+    else:
+        rd, rr = oracle.exact_search_fast(cfg["metric"], base, q, cfg["k"], threads, mask=mask_words)
+        if cfg["precision"] == "fp32":
+            atol = 1e-5 if cfg["metric"] == "cosine" else 0.0
+            out = parity.fp32_exact(dist, rows, rd, rr,
+                                    lambda qi, r: oracle.distance(cfg["metric"], q[qi], base[r]), atol=atol)
+        else:
+            out = parity.low_precision(dist, rows, rd, rr)
+        out["oracle"] = "oracle.c ExactIndex::search arithmetic (blocked form, oracle_fast.c) on the stored " \
+                        "(rounded) values"
+    out["oracle_s"] = round(time.perf_counter() - t, 2)
+    if ref_answers is not None and ref_sample:
+        d_ref, r_ref, kind = ref_answers
+        m = min(ref_sample, nq)
+        out["vs_cpu_baseline_sample"] = {
+            "queries": m, "recall": round(parity.recall(rows[:m], r_ref[:m]), 6),
+            "max_abs_dist_err": parity._dist_err(dist[:m], d_ref[:m])[0],
+            "source": ("the reference's own answers (oracle/_ref)" if kind == "reference" else
+                       "the CPU restatement's answers") + " for the cpu_baseline sample"}
+    return out
+
+
+def run_b200(args, cfg, world, rank, local, parity_q=None):
     import torch
     from elips_b200 import ExactIndex, _capi
     from elips_b200.distributed import ReplicatedIndex, ShardedExactIndex, query_range, shard_range, slice_mask
@@ -496,6 +602,8 @@ def run_b200(args, cfg, world, rank, local):
     replicate = args.distributed == "replicate" and world > 1
     lo, hi = (0, n) if replicate else shard_range(n, rank, world)
     cents = _centroids(cfg, dev) if cfg["data"] == "mixture" else None
+    parity_q = 0 if args.no_parity else min(nq, parity_q if parity_q is not None else nq)
+    want_cpu = world == 1 and not args.no_cpu_baseline
 
     # ---- build: this rank's shard (or whole replica), generated on the device in chunks
     t0 = time.perf_counter()
@@ -503,21 +611,24 @@ def run_b200(args, cfg, world, rank, local):
         index = ReplicatedIndex(ExactIndex(cfg["metric"], d, precision=cfg["precision"], device=local))
     else:
         index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local)
-    host_base = [] if (world == 1 and not args.no_cpu_baseline) else None
+    host_base = np.empty((hi - lo, d), np.int8 if cfg["precision"] == "int8" else np.float32) \
+        if (world == 1 and (want_cpu or parity_q)) else None
     step_rows = 1 << 18
     for r0 in range(lo, hi, step_rows):
         cnt = min(step_rows, hi - r0)
         rows = gen_rows(cfg, r0, cnt, SEED + 1, n, cents, device=dev)
         if host_base is not None:
-            host_base.append(rows.cpu().numpy())
+            host_base[r0 - lo:r0 - lo + cnt] = rows.cpu().numpy()
         index.add_device(rows)
         del rows
     q_dev = gen_rows(cfg, 0, nq, SEED + 2, nq, cents, device=dev)
     queries = q_dev.cpu()
     mask_words = None
     mask_dev = None
+    global_mask = None
     if cfg.get("mask_p"):
-        words = gen_mask_words(cfg, n)
+        global_mask = gen_mask_words(cfg, n)
+        words = global_mask
         if world > 1 and not replicate:
             words = slice_mask(words, lo, hi)  # this rank's rows, starting at bit 0
         mask_words = words
@@ -527,12 +638,14 @@ def run_b200(args, cfg, world, rank, local):
 
     out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
     out_r = torch.empty((nq, k), dtype=torch.int64, device=dev)
+    last = [None]
 
     def step():
         if world == 1:
             index.local.search_device(q_dev, k, mask=mask_dev, out_dist=out_d, out_rows=out_r)
+            last[0] = (out_d, out_r)
         else:
-            index.search_device(q_dev, k, mask=mask_dev)
+            last[0] = index.search_device(q_dev, k, mask=mask_dev)
 
     # ---- device-resident throughput (value), with the kernel profiler live
     for _ in range(args.warmup):
@@ -564,6 +677,10 @@ def run_b200(args, cfg, world, rank, local):
     allstats = _capi.profiler_stats(None)
     ms_per_step = ms_max / args.steps
     value = nq * args.steps / (ms_max / 1e3)
+    # the last timed step's answers (root rank): what the parity leg checks
+    timed = None
+    if last[0] is not None and last[0][0] is not None and parity_q:
+        timed = (last[0][0][:parity_q].cpu().numpy(), last[0][1][:parity_q].cpu().numpy())
 
     # ---- end to end through the public API, host (pinned) buffers
     q_pin = queries.pin_memory()
@@ -603,23 +720,10 @@ def run_b200(args, cfg, world, rank, local):
     n_shard = hi - lo
     # queries one launch on this rank answers: the whole batch, or its slice
     nq_rank = (lambda r: r[1] - r[0])(query_range(nq, rank, world)) if replicate else nq
-    if cfg["precision"] == "int8":
-        flops = 2.0 * nq_rank * n_shard * d
-        peak = 2.0 * peaks["bf16_tflops"]
-        peak_note = f"int8 dense = 2 x {peak_src} bf16 burst"
-    elif cfg["precision"] == "fp32":
-        flops = 2.0 * nq_rank * n_shard * d
-        peak = peaks["bf16_tflops"] / 2.0
-        peak_note = f"tf32 dense = {peak_src} bf16 burst / 2 (3xTF32 issues 3 MMAs per counted flop)"
-    else:
-        flops = 2.0 * nq_rank * n_shard * d
-        # The sustained figure when the timed region is long or ran under the
-        # power cap (the regime the sustained GEMM figure was measured in).
-        capped = "sw_power_cap" in (sampler.summary().get("reasons") or [])
-        long_run = ms_max > 2000 or capped
-        peak = peaks["bf16_tflops_sustained"] if long_run else peaks["bf16_tflops"]
-        peak_note = f"{peak_src} bf16 {'sustained' if long_run else 'burst'}" + \
-            (" (sw_power_cap active in the timed region)" if capped else "")
+    clocks = sampler.summary()
+    capped = "sw_power_cap" in (clocks.get("reasons") or [])
+    flops = 2.0 * nq_rank * n_shard * d
+    peak, peak_sus, peak_note = _peak_for(cfg, peaks, peak_src, capped, ms_max > 2000)
     avg_kernel_ms = kstats["total_ms"] / max(1, kstats["launches"])
     achieved = flops / (avg_kernel_ms / 1e3) / 1e12
     bytes_alg = n_shard * d * (2 if cfg["precision"] in ("fp16", "bf16") else (1 if cfg["precision"] == "int8" else 4))
@@ -630,11 +734,13 @@ def run_b200(args, cfg, world, rank, local):
     if t_hbm > t_tensor:
         bound, ach, pk, unit = "hbm", bytes_alg / (avg_kernel_ms / 1e3) / 1e9, peaks["hbm_gbs"], "GB/s"
         peak_note = f"{peak_src} HBM copy bandwidth (base bytes / HBM exceeds FLOPs / tensor peak here)"
+        frac_sus = None
     else:
         bound, ach, pk, unit = "tensor", achieved, peak, "TFLOP/s"
+        frac_sus = round(achieved / peak_sus, 4)
     roofline = {
         "bound": bound, "achieved": round(ach, 1), "peak": round(pk, 1), "unit": unit,
-        "frac": round(ach / pk, 4), "traffic": load_traffic(args.config, n_shard),
+        "frac": round(ach / pk, 4), "traffic": load_traffic(cfg["name"], n_shard),
         "kernel": "exact_topk_kernel", "kernel_ms_avg": round(avg_kernel_ms, 4),
         "kernel_share_of_step": round(kstats["total_ms"] / max(1e-9, allstats["total_ms"]), 4),
         "per_kernel_ms_per_step": {name: round(_capi.profiler_stats(name)["total_ms"] / args.steps, 4)
@@ -642,14 +748,24 @@ def run_b200(args, cfg, world, rank, local):
         "algorithmic_flops_per_launch": flops, "algorithmic_bytes_per_launch": bytes_alg,
         "hbm_time_ms_at_peak": round(bytes_alg / (peaks["hbm_gbs"] * 1e9) * 1e3, 4),
         "peak_source": peak_note}
+    if frac_sus is not None:
+        roofline["frac_of_sustained"] = frac_sus
+        roofline["peak_sustained"] = round(peak_sus, 1)
+    if world > 1:
+        # where a step goes on this rank: the fused kernel, the merges, and
+        # the rest (NCCL exchange, waiting for the slowest rank, glue)
+        kern = kstats["total_ms"] / args.steps
+        merge = _capi.profiler_stats("merge_topk")["total_ms"] / args.steps
+        roofline["step_breakdown_ms"] = {
+            "kernel": round(kern, 4), "kernel_max_over_ranks": round(max_over_ranks(kern, world), 4),
+            "merges": round(merge, 4), "exchange_and_skew": round(ms_per_step - kern - merge, 4)}
 
-    clocks = sampler.summary()
     result = {
         "metric": METRIC_NAME, "value": round(value, 2), "unit": "queries/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes and distributions of the configuration)",
-        "config": {"workload": cfg["workload"], "config": args.config, "base_rows": n, "dim": d,
+        "config": {"workload": cfg["workload"], "config": cfg["name"], "base_rows": n, "dim": d,
                    "queries_per_step": nq, "k": k, "metric": cfg["metric"], "precision": cfg["precision"],
                    "sharding": (f"replicas: whole base on each of {world} GPUs, query batch split {world} ways"
                                 if replicate else f"rows split {world} ways (contiguous ranges)")
@@ -659,9 +775,164 @@ def run_b200(args, cfg, world, rank, local):
         "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "clocks": clocks,
         "build_s": round(build_s, 2),
     }
-    if world == 1 and not args.no_cpu_baseline and rank == 0:
-        result["cpu_baseline"] = cpu_baseline(cfg, np.concatenate(host_base) if host_base else None,
-                                              queries.numpy(), mask_words)
+    if rank == 0 and (want_cpu or parity_q):
+        del index
+        torch.cuda.empty_cache()
+        base_np = host_base if host_base is not None else _full_base_host(cfg, dev, cents)
+        ref_answers, ref_sample = None, 0
+        if want_cpu:
+            result["cpu_baseline"], ref_answers, ref_sample = cpu_baseline(cfg, base_np, queries.numpy(),
+                                                                           global_mask)
+        if timed is not None:
+            result["parity"] = exact_parity(cfg, base_np, queries.numpy(), timed[0], timed[1], global_mask,
+                                            ref_answers, ref_sample)
+            result["parity"]["what"] = "the last timed step's answers for the first queries of the batch"
+    barrier(world)
+    return result
+
+
+def run_b200_filtered(args, cfg, world, rank, local, parity_q=None):
+    """Filtered exact search at small batches (1, 8 and 64 queries): per-call
+    latency (p50 / p99, CUDA events on the launching stream) and queries/s
+    for each batch, on device-resident queries, and end to end from host
+    buffers (queries and the row filter copied in, results copied out)."""
+    import torch
+    from elips_b200 import ExactIndex, _capi
+    from elips_b200.distributed import ShardedExactIndex, shard_range, slice_mask
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n, d, k = cfg["n"], cfg["d"], cfg["k"]
+    pool = max(cfg["batches"])
+    lo, hi = shard_range(n, rank, world)
+    t0 = time.perf_counter()
+    index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local)
+    host_base = [] if rank == 0 and world == 1 else None
+    for r0 in range(lo, hi, 1 << 18):
+        rows = gen_rows(cfg, r0, min(1 << 18, hi - r0), SEED + 1, n, None, device=dev)
+        if host_base is not None:
+            host_base.append(rows.cpu().numpy())
+        index.add_device(rows)
+    q_dev = gen_rows(cfg, 0, pool, SEED + 2, pool, None, device=dev)
+    queries = q_dev.cpu().numpy()
+    global_mask = gen_mask_words(cfg, n)
+    words = slice_mask(global_mask, lo, hi) if world > 1 else global_mask
+    mask_dev = torch.from_numpy(words.view(np.int32)).to(dev)
+    sel_local = int(np.unpackbits(words.view(np.uint8)).sum())
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    stream = torch.cuda.current_stream(dev)
+    iters = max(50, 10 * args.steps)
+    per_batch = {}
+    answers = {}
+    sampler = ClockSampler(local)
+    peaks, peak_src = load_peaks()
+    launches = 0
+    with sampler:
+        for b in cfg["batches"]:
+            nbat = pool // b
+            qs = [q_dev[i * b:(i + 1) * b] for i in range(nbat)]
+            outs = []
+            for i in range(nbat):   # warm-up, and every query of the pool answered once
+                outs.append(index.search_device(qs[i], k, mask=mask_dev))
+            torch.cuda.synchronize()
+            if rank == 0:
+                answers[b] = (torch.cat([o[0] for o in outs]).cpu().numpy(),
+                              torch.cat([o[1] for o in outs]).cpu().numpy())
+            barrier(world)
+            _capi.profiler_reset()
+            _capi.profiler_enable(True)
+            l0 = _capi.launch_count()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(iters)]
+            sampler.active = True
+            for i in range(iters):
+                evs[i][0].record(stream)
+                index.search_device(qs[i % nbat], k, mask=mask_dev)
+                evs[i][1].record(stream)
+            torch.cuda.synchronize()
+            sampler.active = False
+            launches += _capi.launch_count() - l0
+            _capi.profiler_enable(False)
+            lat = np.array([a.elapsed_time(z) for a, z in evs])   # ms, this rank
+            tot_ms = max_over_ranks(float(evs[0][0].elapsed_time(evs[-1][1])), world)
+            kst = _capi.profiler_stats("exact_topk")
+            kms = kst["total_ms"] / max(1, kst["launches"])
+            # end to end from host buffers: the queries and the filter in, the results out
+            qh = np.ascontiguousarray(queries[:b])
+            if world == 1:
+                od = torch.empty((b, k), dtype=torch.float32).pin_memory().numpy()
+                orr = torch.empty((b, k), dtype=torch.int64).pin_memory().numpy()
+            e2e_lat = []
+            barrier(world)
+            for i in range(iters):
+                qh = np.ascontiguousarray(queries[(i % nbat) * b:(i % nbat + 1) * b])
+                t = time.perf_counter()
+                if world == 1:
+                    index.local.search_batch(qh, k, mask=words, out_dist=od, out_rows=orr)
+                else:
+                    index.search_batch(torch.from_numpy(qh).pin_memory(), k, mask=words)
+                e2e_lat.append((time.perf_counter() - t) * 1e3)
+            e2e_lat = np.array(e2e_lat)
+            sel_bytes = sel_local * d * 2 + words.nbytes
+            full_bytes = (hi - lo) * d * 2
+            per_batch[str(b)] = {
+                "queries_per_s": round(b * iters / (tot_ms / 1e3), 1),
+                "latency_us_p50": round(float(np.percentile(lat, 50)) * 1e3, 1),
+                "latency_us_p99": round(float(np.percentile(lat, 99)) * 1e3, 1),
+                "e2e_latency_us_p50": round(float(np.percentile(e2e_lat, 50)) * 1e3, 1),
+                "e2e_latency_us_p99": round(float(np.percentile(e2e_lat, 99)) * 1e3, 1),
+                "e2e_queries_per_s": round(b * iters / (max_over_ranks(float(e2e_lat.sum()), world) / 1e3), 1),
+                "kernel_us_avg": round(kms * 1e3, 2),
+                "hbm_frac_selected_rows": round(sel_bytes / (kms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                "hbm_frac_full_scan": round(full_bytes / (kms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                "calls": iters}
+    top = per_batch[str(max(cfg["batches"]))]
+    sel_rows = int(_mask_rows(global_mask, n).shape[0])
+    kms_top = top["kernel_us_avg"] / 1e3
+    full_b = (hi - lo) * d * 2
+    result = {
+        "metric": "filtered k-NN queries/sec and latency at batches 1/8/64", "value": top["queries_per_s"],
+        "unit": "queries/s", "n_gpus": world, "steps": iters, "warmup": 1,
+        "ms_per_step": round(1e3 * max(cfg["batches"]) / top["queries_per_s"], 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic (seeded; shapes and distributions of the configuration)",
+        "config": {"workload": cfg["workload"], "config": cfg["name"], "base_rows": n, "dim": d, "k": k,
+                   "batches": cfg["batches"], "selected_rows": sel_rows,
+                   "sharding": f"rows split {world} ways, filter sliced per range" if world > 1 else "single GPU",
+                   "l2": "base 768 MB > L2, read by every call; no flush"},
+        "per_batch": per_batch,
+        "e2e": {"value": per_batch[str(max(cfg["batches"]))]["e2e_queries_per_s"], "unit": "queries/s",
+                "h2d_bytes_per_step": int(max(cfg["batches"]) * d * 4 + words.nbytes),
+                "d2h_bytes_per_step": int(max(cfg["batches"]) * k * 12),
+                "api": "elips_b200_exact_search (host buffers, row filter passed per call)" if world == 1 else
+                       "ShardedExactIndex.search_batch (host buffers)"},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(full_b / kms_top / 1e6, 1), "peak": round(peaks["hbm_gbs"], 1),
+                     "unit": "GB/s", "frac": round(full_b / kms_top / 1e6 / peaks["hbm_gbs"], 4), "traffic": None,
+                     "kernel": "exact_topk_kernel", "kernel_ms_avg": round(kms_top, 4),
+                     "algorithmic_bytes_per_launch": full_b,
+                     "selected_row_bytes_per_launch": int(sel_local * d * 2 + words.nbytes),
+                     "frac_vs_selected_row_bytes": top["hbm_frac_selected_rows"],
+                     "peak_source": f"{peak_src} HBM copy bandwidth; batch {max(cfg['batches'])}"},
+        "clocks": sampler.summary(), "build_s": round(build_s, 2)}
+    if rank == 0:
+        del index
+        torch.cuda.empty_cache()
+        base_np = np.concatenate(host_base) if host_base is not None else _full_base_host(cfg, dev, None)
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"], _, _ = cpu_baseline(cfg, base_np, queries, global_mask, target_s=5.0)
+        if not args.no_parity:
+            par = {}
+            ok = True
+            for b, (dd, rr) in answers.items():
+                par[str(b)] = exact_parity(cfg, base_np, queries, dd, rr, global_mask)
+                bits_ok = bool(((global_mask[rr[rr >= 0] >> 5] >> (rr[rr >= 0] & 31).astype(np.uint32)) & 1).all())
+                par[str(b)]["masked_rows_returned"] = not bits_ok
+                ok = ok and par[str(b)]["pass"] and bits_ok
+            result["parity"] = {"per_batch": par, "queries": pool, "pass": ok,
+                                "what": "every query of the pool answered at each batch size"}
+    barrier(world)
     return result
 
 
@@ -866,7 +1137,7 @@ def run_b200_batcher(args, cfg):
     if not args.no_cpu_baseline:
         base = np.concatenate([gen_rows(cfg, r0, min(1 << 18, n - r0), SEED + 1, n, None, device=dev).cpu().numpy()
                                for r0 in range(0, n, 1 << 18)])
-        result["cpu_baseline"] = cpu_baseline(cfg, base, queries, None)
+        result["cpu_baseline"], _, _ = cpu_baseline(cfg, base, queries, None)
     return result
 
 
@@ -876,22 +1147,13 @@ def _cpu_searcher(cfg, base, mask_words):
     oracle, kind = _ref_or_port()
     metric = cfg["metric"]
     if cfg["precision"] == "int8":
-        # No reference int8 codec: time its sq8 ExactIndex path (dot_product) on
-        # the same rows, the nearest codec the reference ships.
-        b = base.astype(np.float32)
-        if kind == "reference":
-            mins, scales = oracle.ref_sq8_train(metric, b)
-            idx = oracle.RefExactIndex(metric, b, codec="sq8", mins=mins, scales=scales)
-            return (lambda q, k, t: idx.search(q.astype(np.float32), k, t)), kind, \
-                "reference ExactIndex + ScalarQuantizer(sq8, dot_product)"
-        mins, scales = oracle.sq8_train(b)
-        codes = oracle.sq8_encode(mins, scales, b)
-        return (lambda q, k, t: oracle.sq8_search(metric, mins, scales, codes, q.astype(np.float32), k, t)), \
-            kind, "C restatement of ExactIndex + sq8"
+        # The reference ships no int8 x int8 codec: its CPU counterpart is the
+        # C restatement of the codec's definition (scalar loops, exact int32).
+        return (lambda q, k, t: oracle.int8_ip_search(base, q, k, t)), "port", \
+            "C restatement of the symmetric int8 inner-product codec (no reference counterpart), scalar loops"
     if mask_words is not None:
         if kind == "reference":
-            bits = ((mask_words[np.arange(base.shape[0]) >> 5] >> (np.arange(base.shape[0]) & 31).astype(np.uint32)) & 1)
-            sel = np.nonzero(bits)[0]
+            sel = _mask_rows(mask_words, base.shape[0])
             idx = oracle.RefExactIndex(metric, base[sel])
             return (lambda q, k, t: idx.search(q, k, t)), kind, \
                 "reference ExactIndex over the MetadataIndex::exact_candidates subset"
@@ -914,16 +1176,30 @@ def _calibrated_sample(search, cfg, queries, threads, target_s):
     return min(queries.shape[0], first * rounds)
 
 
-def cpu_baseline(cfg, base, queries, mask_words):
+def cpu_baseline(cfg, base, queries, mask_words, target_s=10.0):
+    """The reference's CPU path timed on this host over a calibrated sample of
+    the queries. Returns (cpu_baseline object, (dist, rows) of the sample,
+    sample size, answers comparable with the device's); the answers are in
+    the base's row numbering."""
     threads = os.cpu_count() or 1
     search, kind, what = _cpu_searcher(cfg, base, mask_words)
-    sample = _calibrated_sample(search, cfg, queries, threads, target_s=10.0)
+    sample = _calibrated_sample(search, cfg, queries, threads, target_s=target_s)
     t = time.perf_counter()
-    search(queries[:sample], cfg["k"], threads)
+    dist, rows = search(queries[:sample], cfg["k"], threads)
     dt = time.perf_counter() - t
-    return {"value": round(sample / dt, 3), "unit": "queries/s", "cores": min(threads, sample), "kind": kind,
-            "sample": f"{sample} of the {queries.shape[0]} queries over the full {base.shape[0]}-row base "
-                      f"({what}), {dt:.2f} s wall"}
+    if mask_words is not None and kind == "reference":
+        sel = _mask_rows(mask_words, base.shape[0])
+        rows = np.where(rows >= 0, sel[np.maximum(rows, 0)], -1)
+    obj = {"value": round(sample / dt, 3), "unit": "queries/s", "cores": min(threads, sample), "kind": kind,
+           "sample": f"{sample} of the {queries.shape[0]} queries over the full {base.shape[0]}-row base "
+                     f"({what}), {dt:.2f} s wall"}
+    obj_kind = kind
+    return obj, (dist, rows, obj_kind), sample
+
+
+def _mask_rows(mask_words, n):
+    idx = np.arange(n)
+    return np.nonzero((mask_words[idx >> 5] >> (idx & 31).astype(np.uint32)) & 1)[0].astype(np.int64)
 
 
 def _reference_ivfpq(cfg):
@@ -1008,14 +1284,48 @@ def _time_reference(args, cfg, search, kind, what, base, queries, threads):
     }
 
 
+def _trim(r: dict) -> dict:
+    """A workload's result without the keys the enclosing line already holds."""
+    drop = ("metric", "n_gpus", "steps", "warmup", "higher_is_better", "vs_baseline", "data")
+    out = {"metric": r.get("metric")} if r.get("metric") != METRIC_NAME else {}
+    out.update({key: v for key, v in r.items() if key not in drop})
+    return out
+
+
+def run_config(args, name, cfg, world, rank, local):
+    if world > 1 and args.distributed == "replicate" and name in ("ivfpq", "ivf_build", "batcher",
+                                                                   "filtered_bf16_l2"):
+        raise SystemExit("--distributed replicate applies to the exact configurations")
+    pq = args.parity_queries if args.parity_queries is not None else PARITY_QUERIES.get(name, 256)
+    if world > 1:
+        pq = min(pq, 256)   # rank 0 checks a smaller sample while the other ranks wait
+    if name == "ivfpq":
+        return run_b200_ivfpq(args, cfg, world, rank, local, pq)
+    if name == "filtered_bf16_l2":
+        return run_b200_filtered(args, cfg, world, rank, local, pq)
+    if name in ("ivf_build", "batcher"):
+        if world > 1:
+            raise SystemExit(f"--config {name} runs on one GPU")
+        return (run_b200_build if name == "ivf_build" else run_b200_batcher)(args, cfg)
+    return run_b200(args, cfg, world, rank, local, pq)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(CONFIGS))
+    ap.add_argument("--config", default=None, choices=sorted(CONFIGS),
+                    help="time one configuration alone (default: the headline configuration, "
+                         f"{DEFAULT_CONFIG}, then the workloads)")
+    ap.add_argument("--workloads", default="all",
+                    help="default run only: 'all', 'none', or a comma-separated list of configurations timed "
+                         "after the headline and reported under `workloads`")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle comparison of the timed answers")
+    ap.add_argument("--parity-queries", type=int, default=None,
+                    help="queries of each timed batch checked against the oracle (default per configuration)")
     ap.add_argument("--distributed", default="shard", choices=["shard", "replicate"],
                     help="exact configurations at N>1: rows split across the GPUs (shard) or the whole base on "
                          "every GPU with the query batch split (replicate)")
@@ -1025,31 +1335,52 @@ def main():
                     help="smaller query batch of the same configuration (profiling captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    cfg = dict(CONFIGS[args.config])
+    explicit = args.config is not None
+    name = args.config or DEFAULT_CONFIG
+    cfg = dict(CONFIGS[name])
     if args.base_rows:
         cfg["n"] = args.base_rows
         cfg["workload"] += f" [reduced: N={args.base_rows:,}]"
     if args.queries:
         cfg["q"] = args.queries
         cfg["workload"] += f" [reduced: Q={args.queries:,}]"
+    args.config = name
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
         print(json.dumps(run_reference(args, cfg)), flush=True)
         return
+    if explicit:
+        workloads = []
+    elif args.workloads == "all":
+        workloads = list(DEFAULT_WORKLOADS)
+    elif args.workloads == "none":
+        workloads = []
+    else:
+        workloads = [w for w in args.workloads.split(",") if w]
+        for w in workloads:
+            if w not in CONFIGS:
+                raise SystemExit(f"unknown workload {w!r}")
     world, rank, local = dist_setup(args)
     try:
-        if args.distributed == "replicate" and world > 1 and args.config in ("ivfpq", "ivf_build", "batcher"):
-            raise SystemExit("--distributed replicate applies to the exact configurations")
-        if args.config == "ivfpq":
-            result = run_b200_ivfpq(args, cfg, world, rank, local)
-        elif args.config in ("ivf_build", "batcher"):
-            if world > 1:
-                raise SystemExit(f"--config {args.config} runs on one GPU")
-            result = (run_b200_build if args.config == "ivf_build" else run_b200_batcher)(args, cfg)
-        else:
-            result = run_b200(args, cfg, world, rank, local)
+        result = run_config(args, name, cfg, world, rank, local)
+        if workloads:
+            import gc
+            import torch
+            result["workloads"] = {}
+            for w in workloads:
+                gc.collect()
+                torch.cuda.empty_cache()
+                t = time.perf_counter()
+                try:
+                    r = _trim(run_config(args, w, dict(CONFIGS[w]), world, rank, local))
+                except Exception as e:  # one GPU: report it and go on; N GPUs: every rank fails alike
+                    if world > 1:
+                        raise
+                    r = {"error": f"{type(e).__name__}: {e}"}
+                r["wall_s"] = round(time.perf_counter() - t, 1)
+                result["workloads"][w] = r
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:

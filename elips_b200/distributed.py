@@ -92,14 +92,20 @@ class ShardedExactIndex:
             return None, None
         return merge_candidates_device(gathered, self.world, k, self.metric)
 
-    def search_batch(self, queries_host, k: int, out_dist=None, out_rows=None):
+    def search_batch(self, queries_host, k: int, out_dist=None, out_rows=None, mask=None):
         """End-to-end search from host memory: uploads the queries on every rank,
         searches, gathers, merges, and copies the k results back to host memory on
-        the root rank. queries_host: pinned CPU torch tensor (or numpy array)."""
+        the root rank. queries_host: pinned CPU torch tensor (or numpy array).
+        mask: this rank's row filter as host uint32 words (slice_mask of the
+        global filter), uploaded with the queries."""
         import torch
         q = torch.as_tensor(queries_host)
         qd = q.to(f"cuda:{self.device}", non_blocking=True)
-        d, r = self.search_device(qd, k)
+        md = None
+        if mask is not None:
+            md = torch.from_numpy(np.ascontiguousarray(mask, np.uint32).view(np.int32)).to(
+                f"cuda:{self.device}", non_blocking=True)
+        d, r = self.search_device(qd, k, mask=md)
         if d is None:
             return None, None
         if out_dist is None:

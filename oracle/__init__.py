@@ -156,6 +156,35 @@ def int8_ip_search(base, queries, k, nthreads=None):
     return dist, rows
 
 
+def exact_search_fast(metric, base, queries, k, nthreads=None, mask=None):
+    """exact_search's results (bit for bit) from the blocked, vectorised scan
+    of oracle_fast.c: each pair's sum is still the sequential single-precision
+    loop, 16 queries share a vector. For large bases (2M x 768)."""
+    base, queries = _f32(base), _f32(queries)
+    n, d = base.shape
+    nq = queries.shape[0]
+    dist = np.empty((nq, k), np.float32)
+    rows = np.empty((nq, k), np.int64)
+    m = None if mask is None else np.ascontiguousarray(mask, np.uint32)
+    orc().orc_exact_search_fast(METRIC[metric], _p(base), c_size_t(n), c_size_t(d),
+                                None if m is None else _p(m), _p(queries), c_size_t(nq), c_size_t(k),
+                                c_int(_threads(nthreads)), _p(dist), _p(rows))
+    return dist, rows
+
+
+def int8_ip_search_fast(base, queries, k, nthreads=None):
+    """int8_ip_search's results (bit for bit) from oracle_fast.c's blocked scan."""
+    base = np.ascontiguousarray(base, np.int8)
+    queries = np.ascontiguousarray(queries, np.int8)
+    n, d = base.shape
+    nq = queries.shape[0]
+    dist = np.empty((nq, k), np.float32)
+    rows = np.empty((nq, k), np.int64)
+    orc().orc_int8_ip_search_fast(_p(base), c_size_t(n), c_size_t(d), _p(queries), c_size_t(nq), c_size_t(k),
+                                  c_int(_threads(nthreads)), _p(dist), _p(rows))
+    return dist, rows
+
+
 def sq8_train(rows):
     rows = _f32(rows)
     n, d = rows.shape
