@@ -72,6 +72,7 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
     ("elips_b200_quant_destroy", c_int, [c_void_p]),
     ("elips_b200_exact_live", c_int, [c_void_p, POINTER(c_size_t)]),
+    ("elips_b200_exact_device_bytes", c_int, [c_void_p, POINTER(c_size_t)]),
     ("elips_b200_exact_remove", c_int, [c_void_p, c_size_t, POINTER(c_int)]),
     ("elips_b200_exact_compact", c_int, [c_void_p, c_void_p, c_size_t]),
     ("elips_b200_exact_snapshot_bytes", c_int, [c_void_p, POINTER(c_size_t)]),

@@ -90,6 +90,12 @@ int elips_b200_exact_live(const elips_b200_exact* index, size_t* n_out) {
     return ELIPS_B200_OK;
 }
 
+int elips_b200_exact_device_bytes(const elips_b200_exact* index, size_t* bytes_out) {
+    if (index == nullptr || bytes_out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *bytes_out = index->index.device_bytes();
+    return ELIPS_B200_OK;
+}
+
 int elips_b200_exact_remove(elips_b200_exact* index, size_t row, int* removed_out) {
     if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
     return guarded([&] {

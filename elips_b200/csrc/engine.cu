@@ -524,6 +524,12 @@ void ExactIndex::compact(uint32_t* new_to_old) {
     live_host_.clear();
 }
 
+size_t ExactIndex::device_bytes() const {
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    return capacity_ * row_bytes * (ops_lo_.get() ? 2 : 1) + (norms_.get() ? capacity_ * 4 : 0) +
+           (live_.get() ? live_host_.size() * 4 : 0);
+}
+
 size_t ExactIndex::blob_bytes() const {
     const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
     return sizeof(BlobHeader) + n_ * row_bytes * (ops_lo_.get() ? 2 : 1) + (norms_.get() ? n_ * 4 : 0) +

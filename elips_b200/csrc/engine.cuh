@@ -126,6 +126,9 @@ public:
     // index of the same metric, precision and dimension without converting
     // the rows again.
     size_t blob_bytes() const;
+    // Device memory this index holds: operand rows at capacity (both 3xTF32
+    // planes), norms, removal bits.
+    size_t device_bytes() const;
     void export_blob(void* out, size_t bytes) const;
     void import_blob(const void* blob, size_t bytes);
     int device() const { return device_; }

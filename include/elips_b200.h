@@ -107,6 +107,10 @@ ELIPS_B200_API int elips_b200_exact_size(const elips_b200_exact* index, size_t* 
  * row-number space results are reported in). */
 ELIPS_B200_API int elips_b200_exact_live(const elips_b200_exact* index, size_t* n_out);
 
+/* GpuIndexPort::device_bytes_used (GpuIndexPort.hpp:42): device memory the
+ * index holds (operand rows at capacity, norms, removal bits). */
+ELIPS_B200_API int elips_b200_exact_device_bytes(const elips_b200_exact* index, size_t* bytes_out);
+
 /* Incremental removal on the device, in place of GpuBruteForceIndex::remove's
  * full re-upload (src/gpu_engine/GpuBruteForceIndex.cpp:84-99): the row keeps
  * its number but no search returns it again (a removal bit folded into the

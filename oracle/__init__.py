@@ -404,18 +404,33 @@ class RefExactIndex:
             raise ValueError(codec)
         self.h = c_void_p(self.h)
 
+    def _l(self):
+        return getattr(self, "_lib", None) or ref()
+
     def search(self, queries, k, nthreads=None):
         queries = _f32(queries)
         nq = queries.shape[0]
         dist = np.empty((nq, k), np.float32)
         rows = np.empty((nq, k), np.int64)
-        ref().ref_exact_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
-                               c_int(_threads(nthreads)), _p(dist), _p(rows))
+        self._l().ref_exact_search(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+                                   c_int(_threads(nthreads)), _p(dist), _p(rows))
         return dist, rows
+
+    def insert(self, rows, first):
+        """ExactIndex::insert of rows with ids row_id(first + i)."""
+        rows = _f32(rows)
+        self._l().ref_exact_insert(self.h, _p(rows), c_size_t(rows.shape[0]), c_uint32(self.dim), c_size_t(first))
+
+    def remove(self, row):
+        self._l().ref_exact_remove(self.h, c_size_t(row))
+
+    def size(self):
+        self._l().ref_exact_size.restype = c_size_t
+        return int(self._l().ref_exact_size(self.h))
 
     def __del__(self):
         try:
-            ref().ref_exact_destroy(self.h)
+            self._l().ref_exact_destroy(self.h)
         except Exception:
             pass
 
@@ -459,6 +474,131 @@ class RefBruteForceIndex:
             pass
 
 
+class B200PortIndex:
+    """One of the B200 index adapters (elips_b200/integration/B200Indexes.cpp),
+    selected by make_b200_index from an elips::Config and driven through the
+    reference's own IndexPort / GpuIndexPort / IndexTransferPort calls (GPU
+    only). Row i has RecordID row_id(i); results come back as rows.
+
+    kind "brute_force" (precision "fp32" / "fp16" / "bf16"), "ivf_pq", or
+    "quantized" (codec "sq8" with params = mins ++ scales, "pq" / "opq" with
+    params = codebook)."""
+
+    ALGO = {"brute_force": 4, "ivf_pq": 3}
+    PRECISION = {"fp32": 0, "fp16": 1, "int8": 2, "auto": 3, "bf16": 4}
+    CODEC = {"pq": 1, "opq": 2, "sq8": 3}
+
+    def __init__(self, kind, metric, dim, precision="fp32", n_lists=1024, nprobe=64, pq_dim=0, pq_bits=8,
+                 kmeans_iters=20, codec=None, params=None, rotation=None):
+        self.lib = ref_b200()
+        self.dim = int(dim)
+        if kind == "quantized":
+            params = _f32(params)
+            rot = None if rotation is None else _f32(rotation)
+            h = self.lib.ref_b200_quant_index_create(METRIC[metric], c_uint32(dim), c_int(self.CODEC[codec]),
+                                                     c_uint32(pq_dim), c_uint32(pq_bits), _p(params),
+                                                     None if rot is None else _p(rot))
+        else:
+            h = self.lib.ref_b200_index_create(METRIC[metric], c_uint32(dim), c_int(self.ALGO[kind]),
+                                               c_int(self.PRECISION[precision]), c_size_t(n_lists),
+                                               c_size_t(nprobe), c_uint32(pq_dim), c_uint32(pq_bits),
+                                               c_size_t(kmeans_iters))
+        if not h:
+            raise RuntimeError("make_b200_index returned no index")
+        self.h = c_void_p(h)
+
+    def insert(self, rows, first=0):
+        """IndexPort::insert of every row; returns False when it threw DimensionMismatch."""
+        rows = _f32(rows)
+        return self.lib.ref_b200_index_insert(self.h, _p(rows), c_size_t(rows.shape[0]), c_size_t(rows.shape[1]),
+                                              c_size_t(first)) == 0
+
+    def remove(self, row):
+        self.lib.ref_b200_index_remove(self.h, c_size_t(row))
+
+    def build(self, rows):
+        rows = _f32(rows)
+        return self.lib.ref_b200_index_build(self.h, _p(rows), c_size_t(rows.shape[0]), c_uint32(rows.shape[1]))
+
+    def search(self, queries, k, nthreads=4):
+        """IndexPort::search per query; (dist, rows, threw DimensionMismatch)."""
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        dist = np.zeros((nq, k), np.float32)
+        rows = np.full((nq, k), -1, np.int64)
+        rc = self.lib.ref_b200_index_search(self.h, c_uint32(queries.shape[1]), _p(queries), c_size_t(nq),
+                                            c_size_t(k), c_int(nthreads), _p(dist), _p(rows))
+        return dist, rows, rc == 1
+
+    def search_batch(self, queries, k, candidates=None):
+        """GpuIndexPort::search_batch (or the filtered form over candidate rows):
+        (status 0 or 1 + GpuError, dist, rows)."""
+        queries = _f32(queries)
+        nq = queries.shape[0]
+        dist = np.zeros((nq, k), np.float32)
+        rows = np.full((nq, k), -1, np.int64)
+        cand = None if candidates is None else np.ascontiguousarray(candidates, np.int64)
+        rc = self.lib.ref_b200_index_search_batch(self.h, c_uint32(self.dim), _p(queries), c_size_t(nq), c_size_t(k),
+                                                  None if cand is None else _p(cand),
+                                                  c_size_t(0 if cand is None else cand.size), _p(dist), _p(rows))
+        return rc, dist, rows
+
+    def size(self):
+        self.lib.ref_b200_index_size.restype = c_size_t
+        return int(self.lib.ref_b200_index_size(self.h))
+
+    def type_name(self):
+        buf = ctypes.create_string_buffer(64)
+        self.lib.ref_b200_index_type_name(self.h, buf, c_size_t(64))
+        return buf.value.decode()
+
+    def device_bytes(self):
+        self.lib.ref_b200_index_device_bytes.restype = c_size_t
+        return int(self.lib.ref_b200_index_device_bytes(self.h))
+
+    def copy_snapshot_to(self, other):
+        """export_snapshot of this index imported into `other`; 0 on success."""
+        return self.lib.ref_b200_index_snapshot_copy(self.h, other.h)
+
+    def export_to_cpu(self, metric):
+        """export_to_cpu_index into a new CPU ExactIndex (a RefExactIndex)."""
+        self.lib.ref_b200_index_export_to_cpu.restype = c_void_p
+        h = self.lib.ref_b200_index_export_to_cpu(self.h, METRIC[metric], c_uint32(self.dim))
+        if not h:
+            raise RuntimeError("export_to_cpu_index failed")
+        out = RefExactIndex.__new__(RefExactIndex)
+        out.dim, out.h, out._lib = self.dim, c_void_p(h), self.lib
+        return out
+
+    def import_from_cpu(self, exact):
+        return self.lib.ref_b200_index_import_from_cpu(self.h, exact.h)
+
+    def centroids(self, n_lists):
+        out = np.zeros((n_lists, self.dim), np.float32)
+        self.lib.ref_b200_index_centroids.restype = c_size_t
+        got = self.lib.ref_b200_index_centroids(self.h, _p(out), c_size_t(out.size))
+        return out[:got]
+
+    def export(self, n, pq_dim, ksub):
+        """An IVF-PQ index's export_snapshot: (rows, vectors, assignments, codebook, codes)."""
+        rows = np.empty(n, np.int64)
+        vec = np.empty((n, self.dim), np.float32)
+        asg = np.empty(n, np.uint32)
+        cb = np.empty((pq_dim, ksub, self.dim // pq_dim), np.float32)
+        codes = np.empty((n, pq_dim), np.uint8)
+        rc = self.lib.ref_b200_index_export(self.h, c_size_t(n), c_uint32(self.dim), _p(rows), _p(vec), _p(asg),
+                                            _p(cb), c_size_t(cb.size), _p(codes), c_size_t(codes.size))
+        if rc != 0:
+            raise RuntimeError(f"export_snapshot failed ({rc})")
+        return rows, vec, asg, cb, codes
+
+    def __del__(self):
+        try:
+            self.lib.ref_b200_index_destroy(self.h)
+        except Exception:
+            pass
+
+
 class RefIvfFlatIndex:
     """The reference's GpuIVFFlatIndex on a CPU GpuPort, loaded via import_snapshot."""
 
@@ -497,6 +637,48 @@ class RefIvfFlatIndex:
     def __del__(self):
         try:
             self.lib.ref_ivfflat_destroy(self.h)
+        except Exception:
+            pass
+
+
+class RefIvfPqEmpty:
+    """The reference's GpuIVFPQIndex on the CPU port, created empty (its own
+    config: n_lists, nprobe, pq_dim, pq_bits, kmeans rounds), filled by
+    insert or build_from_batch; search / remove / export as RefIvfPqIndex."""
+
+    def __init__(self, metric, dim, n_lists, nprobe, pq_dim, pq_bits=8, kmeans_iters=20):
+        self.lib = ref()
+        self.dim = int(dim)
+        self.lib.ref_ivfpq_create_empty.restype = c_void_p
+        self.h = c_void_p(self.lib.ref_ivfpq_create_empty(METRIC[metric], c_uint32(dim), c_size_t(n_lists),
+                                                          c_size_t(nprobe), c_uint32(pq_dim), c_uint32(pq_bits),
+                                                          c_size_t(kmeans_iters)))
+
+    def insert(self, rows, first=0):
+        rows = _f32(rows)
+        self.lib.ref_ivfpq_insert(self.h, _p(rows), c_size_t(rows.shape[0]), c_uint32(self.dim), c_size_t(first))
+
+    def build(self, rows):
+        rows = _f32(rows)
+        return self.lib.ref_ivfpq_build(self.h, _p(rows), c_size_t(rows.shape[0]), c_uint32(self.dim))
+
+    def size(self):
+        self.lib.ref_ivfpq_size.restype = c_size_t
+        return int(self.lib.ref_ivfpq_size(self.h))
+
+    def centroids(self, n_lists):
+        out = np.zeros((n_lists, self.dim), np.float32)
+        self.lib.ref_ivfpq_centroids.restype = c_size_t
+        got = self.lib.ref_ivfpq_centroids(self.h, _p(out), c_size_t(out.size))
+        return out[:got]
+
+    search = lambda self, *a, **kw: RefIvfPqIndex.search(self, *a, **kw)
+    remove = lambda self, row: RefIvfPqIndex.remove(self, row)
+    export = lambda self, *a: RefIvfPqIndex.export(self, *a)
+
+    def __del__(self):
+        try:
+            self.lib.ref_ivfpq_destroy(self.h)
         except Exception:
             pass
 

@@ -37,7 +37,9 @@
 #include "elips/quant_engine/detail/KMeans.hpp"
 #include "elips/vector_engine/Metrics.hpp"
 #ifdef REF_WITH_B200
+#include "B200Indexes.hpp"
 #include "backends/cuda/CudaBackend.hpp"
+#include "elips/domain/Errors.hpp"
 #endif
 
 namespace {
@@ -449,6 +451,14 @@ int ref_ivfpq_export(void* handle, size_t n, uint32_t dim, std::int64_t* rows_ou
     return 0;
 }
 
+// export_snapshot's IVF centroids [n_lists][dim]; returns the list count, 0 when untrained.
+size_t ref_ivfpq_centroids(void* handle, float* out, size_t cap) {
+    auto snap = static_cast<IvfPqHandle*>(handle)->index->export_snapshot();
+    if (!snap.has_value() || !snap->ivf.has_value()) return 0;
+    std::copy_n(snap->ivf->centroids.begin(), std::min(cap, snap->ivf->centroids.size()), out);
+    return snap->ivf->n_lists;
+}
+
 void ref_ivfpq_destroy(void* handle) { delete static_cast<IvfPqHandle*>(handle); }
 
 // GpuIVFFlatIndex on the CPU port, loaded through import_snapshot
@@ -568,6 +578,281 @@ int ref_brute_search_batch(void* handle, uint32_t dim, const float* queries, siz
 }
 
 void ref_brute_destroy(void* handle) { delete static_cast<BruteHandle*>(handle); }
+
+#ifdef REF_WITH_B200
+// ---- the B200 index adapters (elips_b200/integration/B200Indexes.cpp) driven
+// through the reference's own interfaces: IndexPort, GpuIndexPort,
+// IndexTransferPort, selected by make_b200_index with an elips::Config.
+
+}  // extern "C"
+
+namespace {
+
+struct B200Handle {
+    std::unique_ptr<elips::IndexPort> index;
+};
+
+elips::gpu::GpuIndexPort* as_gpu(void* h) {
+    return dynamic_cast<elips::gpu::GpuIndexPort*>(static_cast<B200Handle*>(h)->index.get());
+}
+
+void* wrap(std::unique_ptr<elips::IndexPort> index) {
+    if (!index) return nullptr;
+    auto* h = new B200Handle;
+    h->index = std::move(index);
+    return h;
+}
+
+}  // namespace
+
+extern "C" {
+
+// make_index's selection (IndexFactory.cpp:40-50) with the B200 classes:
+// algorithm 4 = BruteForce, 3 = IvfPq (GpuIndexAlgorithm order); precision
+// as GpuPrecision with BF16 = 4.
+void* ref_b200_index_create(int metric, uint32_t dim, int algorithm, int precision, size_t n_lists,
+                            size_t nprobe, uint32_t pq_dim, uint32_t pq_bits, size_t kmeans_iters) {
+    elips::gpu::GpuConfig g;
+    g.policy = elips::gpu::GpuPolicy::RequireGpu;
+    g.index_build_mode = elips::gpu::IndexBuildMode::GpuBuild_GpuServe;
+    g.algorithm = static_cast<elips::gpu::GpuIndexAlgorithm>(algorithm);
+    g.search_precision = static_cast<elips::gpu::GpuPrecision>(precision);
+    g.default_ef_search_gpu = nprobe;
+    g.ivf_pq_params.n_lists = n_lists;
+    g.ivf_pq_params.pq_dim = pq_dim;
+    g.ivf_pq_params.pq_bits = pq_bits;
+    g.ivf_pq_params.kmeans_n_iters = kmeans_iters;
+    g.device_index = 0;
+    elips::Config config;
+    config.metric(static_cast<Metric>(metric)).index(elips::IndexType::exact).gpu(g);
+    return wrap(elips::gpu::b200::make_b200_index(config, static_cast<std::uint16_t>(dim)));
+}
+
+// A quantized vault's index: make_b200_index with the reference's trained
+// quantizer attached (codec 3 = sq8 from mins/scales, 1 = PQ from a codebook,
+// 2 = OPQ with a rotation), the CPU twin of ref_sq8/pq/opq_exact_create.
+void* ref_b200_quant_index_create(int metric, uint32_t dim, int codec, uint32_t pq_dim, uint32_t pq_bits,
+                                  const float* params, const float* rotation) {
+    elips::quant::QuantizerPtr q;
+    if (codec == 3) {
+        q = std::make_shared<elips::quant::ScalarQuantizer>(static_cast<Metric>(metric), static_cast<std::uint16_t>(dim),
+                                                            std::vector<float>(params, params + dim),
+                                                            std::vector<float>(params + dim, params + 2 * dim));
+    } else {
+        const size_t cb = static_cast<size_t>(pq_dim) * (size_t{1} << pq_bits) * (dim / pq_dim);
+        q = std::make_shared<elips::quant::ProductQuantizer>(
+            static_cast<Metric>(metric), static_cast<std::uint16_t>(dim), pq_dim, pq_bits,
+            std::vector<float>(params, params + cb),
+            codec == 2 ? std::vector<float>(rotation, rotation + static_cast<size_t>(dim) * dim) : std::vector<float>{});
+    }
+    elips::gpu::GpuConfig g;
+    g.policy = elips::gpu::GpuPolicy::RequireGpu;
+    g.algorithm = elips::gpu::GpuIndexAlgorithm::BruteForce;
+    elips::Config config;
+    config.metric(static_cast<Metric>(metric)).index(elips::IndexType::exact).gpu(g);
+    config.attach_quantizer(q);
+    return wrap(elips::gpu::b200::make_b200_index(config, static_cast<std::uint16_t>(dim)));
+}
+
+// IndexPort::insert of rows [first, first + n) with ids row_id(first + i).
+// Returns 1 when insert threw DimensionMismatch (width != dim).
+int ref_b200_index_insert(void* h, const float* rows, size_t n, size_t width, size_t first) {
+    try {
+        for (size_t i = 0; i < n; ++i)
+            static_cast<B200Handle*>(h)->index->insert(row_id(first + i), std::span<const float>{rows + i * width, width});
+    } catch (const elips::DimensionMismatch&) {
+        return 1;
+    }
+    return 0;
+}
+
+int ref_b200_index_remove(void* h, size_t row) {
+    static_cast<B200Handle*>(h)->index->remove(row_id(row));
+    return 0;
+}
+
+// GpuIndexPort::build_from_batch with ids row_id(i); 1 + GpuError on failure.
+int ref_b200_index_build(void* h, const float* rows, size_t n, uint32_t dim) {
+    auto* g = as_gpu(h);
+    if (g == nullptr) return -1;
+    std::vector<RecordID> ids;
+    ids.reserve(n);
+    for (size_t i = 0; i < n; ++i) ids.push_back(row_id(i));
+    auto r = g->build_from_batch(std::span<const float>{rows, n * dim}, ids, {});
+    return r.has_value() ? 0 : 1 + static_cast<int>(r.error());
+}
+
+// IndexPort::search per query on nthreads threads (Vault::seek's readers).
+// Returns 1 when a query threw DimensionMismatch (width != index dimension).
+int ref_b200_index_search(void* h, uint32_t width, const float* queries, size_t nq, size_t k, int nthreads,
+                          float* out_dist, std::int64_t* out_rows) {
+    std::atomic<int> mismatch{0};
+    parallel_queries(nq, nthreads, [&](size_t q) {
+        try {
+            const auto hits = static_cast<B200Handle*>(h)->index->search(
+                std::span<const float>{queries + q * width, width}, k);
+            write_hits(hits, k, out_dist + q * k, out_rows + q * k);
+        } catch (const elips::DimensionMismatch&) {
+            mismatch = 1;
+        }
+    });
+    return mismatch.load();
+}
+
+// GpuIndexPort::search_batch; 1 + GpuError on failure. With candidates
+// (n_cand > 0 or candidates != NULL) the brute-force index's filtered search
+// over ids row_id(candidates[i]).
+int ref_b200_index_search_batch(void* h, uint32_t dim, const float* queries, size_t nq, size_t k,
+                                const std::int64_t* candidates, size_t n_cand, float* out_dist,
+                                std::int64_t* out_rows) {
+    auto* g = as_gpu(h);
+    if (g == nullptr) return -1;
+    std::expected<std::vector<std::vector<elips::SearchResult>>, elips::gpu::GpuError> res;
+    if (candidates != nullptr) {
+        auto* bf = dynamic_cast<elips::gpu::b200::B200BruteForceIndex*>(g);
+        if (bf == nullptr) return -2;
+        std::vector<RecordID> ids;
+        for (size_t i = 0; i < n_cand; ++i) ids.push_back(row_id(static_cast<std::uint64_t>(candidates[i])));
+        res = bf->search_batch_filtered(std::span<const float>{queries, nq * dim}, k, ids);
+    } else {
+        res = g->search_batch(std::span<const float>{queries, nq * dim}, k, 0);
+    }
+    if (!res.has_value()) return 1 + static_cast<int>(res.error());
+    for (size_t q = 0; q < nq; ++q) {
+        const auto& row = (*res)[q];
+        for (size_t i = 0; i < k; ++i) {
+            out_dist[q * k + i] = i < row.size() ? row[i].distance : 0.0f;
+            out_rows[q * k + i] = i < row.size() ? id_row(row[i].id) : -1;
+        }
+    }
+    return 0;
+}
+
+size_t ref_b200_index_size(void* h) { return static_cast<B200Handle*>(h)->index->size(); }
+
+// type_name() into buf (NUL-terminated, truncated to cap).
+void ref_b200_index_type_name(void* h, char* buf, size_t cap) {
+    const auto name = static_cast<B200Handle*>(h)->index->type_name();
+    const size_t n = std::min(cap - 1, name.size());
+    std::memcpy(buf, name.data(), n);
+    buf[n] = 0;
+}
+
+size_t ref_b200_index_device_bytes(void* h) {
+    auto* g = as_gpu(h);
+    return g != nullptr ? g->device_bytes_used() : 0;
+}
+
+// export_snapshot of src imported into dst (IndexTransferPort); 0 on success.
+int ref_b200_index_snapshot_copy(void* src, void* dst) {
+    auto* s = dynamic_cast<elips::IndexTransferPort*>(static_cast<B200Handle*>(src)->index.get());
+    auto* d = dynamic_cast<elips::IndexTransferPort*>(static_cast<B200Handle*>(dst)->index.get());
+    if (s == nullptr || d == nullptr) return 1;
+    auto snap = s->export_snapshot();
+    if (!snap.has_value()) return 2;
+    return d->import_snapshot(*snap).has_value() ? 0 : 3;
+}
+
+// GpuIndexPort::export_to_cpu_index into a new CPU ExactIndex (an ExactHandle
+// searched with ref_exact_search), or import_from_cpu_index from one (dir = 1).
+void* ref_b200_index_export_to_cpu(void* h, int metric, uint32_t dim) {
+    auto* g = as_gpu(h);
+    if (g == nullptr) return nullptr;
+    auto* e = new ExactHandle;
+    e->index = std::make_unique<elips::ExactIndex>(static_cast<Metric>(metric), static_cast<std::uint16_t>(dim));
+    if (!g->export_to_cpu_index(*e->index).has_value()) {
+        delete e;
+        return nullptr;
+    }
+    return e;
+}
+
+int ref_b200_index_import_from_cpu(void* h, void* exact_handle) {
+    auto* g = as_gpu(h);
+    if (g == nullptr) return -1;
+    auto r = g->import_from_cpu_index(*static_cast<ExactHandle*>(exact_handle)->index);
+    return r.has_value() ? 0 : 1 + static_cast<int>(r.error());
+}
+
+// export_snapshot's IVF-PQ fields (as ref_ivfpq_export): ids as rows, vectors,
+// assignments, codebook, codes. 1..3 when a section is missing or mis-sized.
+int ref_b200_index_export(void* h, size_t n, uint32_t dim, std::int64_t* rows_out, float* vectors_out,
+                          uint32_t* assign_out, float* codebook_out, size_t codebook_len, std::uint8_t* codes_out,
+                          size_t codes_len) {
+    auto* t = dynamic_cast<elips::IndexTransferPort*>(static_cast<B200Handle*>(h)->index.get());
+    if (t == nullptr) return 4;
+    auto snap = t->export_snapshot();
+    if (!snap.has_value() || !snap->ivf.has_value() || !snap->pq.has_value()) return 1;
+    if (snap->ids.size() != n || snap->vectors.size() != n * dim || snap->ivf->assignments.size() != n) return 2;
+    if (snap->pq->codebook.size() != codebook_len || snap->pq->codes.size() != codes_len) return 3;
+    for (size_t i = 0; i < n; ++i) rows_out[i] = id_row(snap->ids[i]);
+    std::copy(snap->vectors.begin(), snap->vectors.end(), vectors_out);
+    std::copy(snap->ivf->assignments.begin(), snap->ivf->assignments.end(), assign_out);
+    std::copy(snap->pq->codebook.begin(), snap->pq->codebook.end(), codebook_out);
+    std::copy(snap->pq->codes.begin(), snap->pq->codes.end(), codes_out);
+    return 0;
+}
+
+size_t ref_b200_index_centroids(void* h, float* out, size_t cap) {
+    auto* t = dynamic_cast<elips::IndexTransferPort*>(static_cast<B200Handle*>(h)->index.get());
+    if (t == nullptr) return 0;
+    auto snap = t->export_snapshot();
+    if (!snap.has_value() || !snap->ivf.has_value()) return 0;
+    std::copy_n(snap->ivf->centroids.begin(), std::min(cap, snap->ivf->centroids.size()), out);
+    return snap->ivf->n_lists;
+}
+
+void ref_b200_index_destroy(void* h) { delete static_cast<B200Handle*>(h); }
+#endif  // REF_WITH_B200
+
+// CPU counterparts for the insert / remove sequences: ExactIndex::insert /
+// remove, and GpuIVFPQIndex built empty then filled by insert or
+// build_from_batch (on the CPU port).
+int ref_exact_insert(void* handle, const float* rows, size_t n, uint32_t dim, size_t first) {
+    auto* h = static_cast<ExactHandle*>(handle);
+    for (size_t i = 0; i < n; ++i) h->index->insert(row_id(first + i), std::span<const float>{rows + i * dim, dim});
+    return 0;
+}
+
+int ref_exact_remove(void* handle, size_t row) {
+    static_cast<ExactHandle*>(handle)->index->remove(row_id(row));
+    return 0;
+}
+
+size_t ref_exact_size(void* handle) { return static_cast<ExactHandle*>(handle)->index->size(); }
+
+void* ref_ivfpq_create_empty(int metric, uint32_t dim, size_t n_lists, size_t nprobe, uint32_t pq_dim,
+                             uint32_t pq_bits, size_t kmeans_iters) {
+    auto* h = new IvfPqHandle;
+    if (!h->port) {
+        delete h;
+        return nullptr;
+    }
+    elips::gpu::GpuConfig config;
+    config.default_ef_search_gpu = nprobe;
+    config.ivf_pq_params.n_lists = n_lists;
+    config.ivf_pq_params.pq_dim = pq_dim;
+    config.ivf_pq_params.pq_bits = pq_bits;
+    config.ivf_pq_params.kmeans_n_iters = kmeans_iters;
+    h->index = std::make_unique<elips::gpu::GpuIVFPQIndex>(*h->port, static_cast<Metric>(metric),
+                                                           static_cast<std::uint16_t>(dim), config);
+    return h;
+}
+
+int ref_ivfpq_insert(void* handle, const float* rows, size_t n, uint32_t dim, size_t first) {
+    auto* h = static_cast<IvfPqHandle*>(handle);
+    for (size_t i = 0; i < n; ++i) h->index->insert(row_id(first + i), std::span<const float>{rows + i * dim, dim});
+    return 0;
+}
+
+int ref_ivfpq_build(void* handle, const float* rows, size_t n, uint32_t dim) {
+    auto* h = static_cast<IvfPqHandle*>(handle);
+    std::vector<RecordID> ids;
+    for (size_t i = 0; i < n; ++i) ids.push_back(row_id(i));
+    return h->index->build_from_batch(std::span<const float>{rows, n * dim}, ids, {}).has_value() ? 0 : 1;
+}
+
+size_t ref_ivfpq_size(void* handle) { return static_cast<IvfPqHandle*>(handle)->index->size(); }
 
 // Selects the GpuPort of the handles created next: 1 = the B200 CudaBackend
 // (REF_WITH_B200 build only), 0 = the CPU port. Returns the selection made.
