@@ -43,6 +43,7 @@ SIGNATURES = [
     ("elips_b200_status_string", c_char_p, [c_int]),
     ("elips_b200_device_count", c_int, [POINTER(c_int)]),
     ("elips_b200_device_error", c_int, [c_int, POINTER(c_int)]),
+    ("elips_b200_wait_selftest", c_int, [c_int, c_uint64]),
     ("elips_b200_exact_create", c_int, [c_int, c_int, c_int, c_uint32, POINTER(c_void_p)]),
     ("elips_b200_exact_add", c_int, [c_void_p, c_void_p, c_size_t]),
     ("elips_b200_exact_add_device", c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -59,6 +59,13 @@ int elips_b200_device_error(int device, int* code_out) {
     return guarded([&] { *code_out = eb::read_and_clear_device_error(device); });
 }
 
+int elips_b200_wait_selftest(int device, uint64_t cycles) {
+    int code = 0;
+    const int st = guarded([&] { code = eb::wait_selftest(device, static_cast<long long>(cycles)); });
+    if (st != ELIPS_B200_OK) return st;
+    return code != 0 ? ELIPS_B200_DEVICE_TIMEOUT : ELIPS_B200_OK;
+}
+
 int elips_b200_exact_create(int device, int metric, int precision, uint32_t dimension,
                             elips_b200_exact** out) {
     if (out == nullptr) return ELIPS_B200_INVALID_ARGUMENT;

@@ -861,6 +861,36 @@ void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists
     check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "merge kernel launch");
 }
 
+namespace {
+
+// One thread waits on an mbarrier that nothing arrives on, for `budget`
+// cycles: the bounded wait expires, records the device error word and raises
+// the CTA's abort flag, the path every pipeline wait takes when a producer or
+// consumer is lost. Nothing asynchronous is in flight, so returning with the
+// barrier pending is safe.
+__global__ void wait_selftest_kernel(long long budget) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x != 0) return;
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+    mbar_wait_for(smem_u32(&bar), 0, &abort_flag, budget);
+}
+
+}  // namespace
+
+int wait_selftest(int device, long long budget) {
+    if (budget < 1 || budget > kWaitTimeoutCycles)
+        fail(ELIPS_B200_INVALID_ARGUMENT, "wait budget must be in [1, 2^31] cycles");
+    DeviceGuard g(device);
+    // start from a clear error word so the result is this launch's
+    read_and_clear_device_error(device);
+    wait_selftest_kernel<<<1, 32>>>(budget);
+    check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "wait self-test launch");
+    return read_and_clear_device_error(device);
+}
+
 int read_and_clear_device_error(int device) {
     DeviceGuard g(device);
     check_cuda(cudaDeviceSynchronize(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "cudaDeviceSynchronize");

@@ -177,5 +177,8 @@ void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists
                       uint32_t lists_last = 0);
 
 int read_and_clear_device_error(int device);
+// Launches a bounded wait that must expire after `budget` cycles and returns
+// the device error word it leaves (cleared again).
+int wait_selftest(int device, long long budget);
 
 }  // namespace eb

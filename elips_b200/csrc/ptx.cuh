@@ -72,20 +72,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete. Returns false (and
-// raises *abort) if the wait expired or another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// Waits for the phase with the given parity to complete, for at most `budget`
+// cycles. Returns false (and raises *abort) if the wait expired or another
+// role already aborted.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, volatile int* abort,
+                                              long long budget) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long start = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (*abort) return false;
-        if (clock64() - start > kWaitTimeoutCycles) {
+        if (clock64() - start > budget) {
             record_device_error(kDevErrWaitTimeout);
             *abort = 1;
             return false;
         }
     }
     return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+    return mbar_wait_for(bar, parity, abort, kWaitTimeoutCycles);
 }
 
 // ---------------------------------------------------------------------- TMA

@@ -78,6 +78,15 @@ ELIPS_B200_API int elips_b200_device_count(int* count_out);
  * write on timeout (0 = none). Synchronises the device. */
 ELIPS_B200_API int elips_b200_device_error(int device, int* code_out);
 
+/* Self-test of the bounded device waits; no counterpart in the reference.
+ * One thread waits on an mbarrier that nothing arrives on, for `cycles`
+ * clock cycles (1 .. 2^31); the wait expires, records the device error word
+ * and raises its abort flag, as any pipeline wait does when a producer or
+ * consumer is lost. Returns ELIPS_B200_DEVICE_TIMEOUT when the expiry was
+ * reported (the expected outcome; the error word is cleared again and the
+ * context stays usable), ELIPS_B200_OK if the wait completed. */
+ELIPS_B200_API int elips_b200_wait_selftest(int device, uint64_t cycles);
+
 /* ------------------------------------------------ exact brute-force index */
 /* Replaces ExactIndex (include/elips/index_engine/ExactIndex.hpp:26-66) and
  * GpuBruteForceIndex (src/gpu_engine/GpuBruteForceIndex.cpp:77-170): a
