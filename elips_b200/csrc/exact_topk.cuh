@@ -45,6 +45,9 @@ enum MetricId : int { kCosine = 0, kEuclidean = 1, kDot = 2 };  // elips::Metric
 constexpr int kTileM = 128;           // queries per tile = TMEM lanes
 constexpr int kKBlockBytes = 128;     // K bytes per pipeline stage (one swizzle atom)
 constexpr int kEpilogueWarps = 8;
+// Admission staging: a lane's 16 accumulator words of one half-chunk, padded
+// to 20 words so the 16-byte stores of 8 consecutive lanes hit distinct banks.
+constexpr uint32_t kStageStride = 20;
 constexpr int kExactThreads = 32 * (2 + kEpilogueWarps);
 
 struct ExactParams {
@@ -100,8 +103,11 @@ struct ExactConfig {
     // barriers: full[S], empty[S], tfull[2], tempty[2], mma_done
     static constexpr uint32_t kBarBytes = 8 * (2 * STAGES + 5);
     static constexpr uint32_t kMiscOffset = STAGES * kStageBytes;
+    // Per epilogue warp: the compaction histogram (256 words) and, never at
+    // the same time, the admission staging rows (32 lanes x kStageStride words).
+    static constexpr uint32_t kWarpScratchBytes = 32u * kStageStride * 4u > 1024u ? 32u * kStageStride * 4u : 1024u;
     static constexpr uint32_t kHistOffset = kMiscOffset + 256;
-    static constexpr uint32_t kNormOffset = kHistOffset + kEpilogueWarps * 1024;  // per-warp norms
+    static constexpr uint32_t kNormOffset = kHistOffset + kEpilogueWarps * kWarpScratchBytes;  // per-warp norms
     static constexpr uint32_t kSmemBytes = 1024 /* alignment slack */ + kNormOffset + kEpilogueWarps * (BN / 2) * 4;
     static_assert(kBarBytes + 16 <= 256, "barrier area");
     static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
@@ -158,36 +164,41 @@ __device__ __forceinline__ float key_of(uint32_t v, float xn, float qn) {
     }
 }
 
-// Smallest key of a 32-column chunk, computed with one min/max per value.
-// Every key_of above is a monotone function of one running extreme, so this
-// equals the minimum of key_of over the chunk exactly.
+// Admission test in the accumulator domain, one compare per column. Every
+// column whose key is below `thr` passes (the converse need not hold: the
+// exact key is tested again before an append):
+//  * cosine: fl(1 - v) < thr implies v > 1 - thr (real), so v > c with c one
+//    ulp below fl(1 - thr);
+//  * dot: -v < thr  <=>  v > -thr (negation is exact);
+//  * int8: -(float)iv < thr  <=>  iv > floor(-thr) (|iv| < 2^24 converts exactly);
+//  * euclidean: fl(fma(-2, v, xn) + qn) < thr implies fma(-2, v, xn) < thr - qn
+//    (real), so compare with fl(thr - qn) rounded one ulp up.
 template <OperandKind KIND, int METRIC>
-__device__ __forceinline__ float chunk_min_key(const uint32_t (&v)[32], const float* xn, float qn) {
-    // Four independent running extremes, then combined: short dependency chains.
-    if constexpr (KindTraits<KIND>::integer) {
-        int32_t m[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) m[j] = static_cast<int32_t>(v[j]);
-#pragma unroll
-        for (int i = 4; i < 32; ++i) m[i & 3] = max(m[i & 3], static_cast<int32_t>(v[i]));
-        return -static_cast<float>(max(max(m[0], m[1]), max(m[2], m[3])));
-    } else if constexpr (METRIC == kEuclidean) {
-        float m[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) m[j] = fmaf(-2.0f, __uint_as_float(v[j]), xn[j]);
-#pragma unroll
-        for (int i = 4; i < 32; ++i) m[i & 3] = fminf(m[i & 3], fmaf(-2.0f, __uint_as_float(v[i]), xn[i]));
-        return fminf(fminf(m[0], m[1]), fminf(m[2], m[3])) + qn;
-    } else {
-        float m[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) m[j] = __uint_as_float(v[j]);
-#pragma unroll
-        for (int i = 4; i < 32; ++i) m[i & 3] = fmaxf(m[i & 3], __uint_as_float(v[i]));
-        const float mx = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
-        return METRIC == kCosine ? 1.0f - mx : -mx;
+struct Admission {
+    float c;     // float cutoff (cosine / dot: v > c; euclidean: fma(-2, v, xn) < c)
+    int32_t ic;  // int8: iv > ic
+    __device__ __forceinline__ Admission(float thr, float qn) {
+        if constexpr (KindTraits<KIND>::integer) {
+            const float t = -thr;
+            ic = t < -2147483520.0f ? INT32_MIN : (t >= 2147483520.0f ? INT32_MAX : static_cast<int32_t>(floorf(t)));
+            c = 0.0f;
+        } else if constexpr (METRIC == kCosine) {
+            c = nextafterf(1.0f - thr, -__int_as_float(0x7f800000));
+            ic = 0;
+        } else if constexpr (METRIC == kDot) {
+            c = -thr;
+            ic = 0;
+        } else {
+            c = nextafterf(thr - qn, __int_as_float(0x7f800000));
+            ic = 0;
+        }
     }
-}
+    __device__ __forceinline__ bool pass(uint32_t v, float xn) const {
+        if constexpr (KindTraits<KIND>::integer) return static_cast<int32_t>(v) > ic;
+        else if constexpr (METRIC == kEuclidean) return fmaf(-2.0f, __uint_as_float(v), xn) < c;
+        else return __uint_as_float(v) > c;
+    }
+};
 
 template <OperandKind KIND, int BN, int STAGES, int METRIC, int CG = 1>
 __global__ void __launch_bounds__(kExactThreads, 1)
@@ -391,7 +402,8 @@ __global__ void __launch_bounds__(kExactThreads, 1)
         const uint32_t lane_row = quad * 32u + lane;  // query row within the tile
         constexpr uint32_t kHalfCols = BN / 2;
         constexpr uint32_t kChunks = kHalfCols / 32;
-        uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Cfg::kHistOffset) + ew * 256u;
+        uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Cfg::kHistOffset + ew * Cfg::kWarpScratchBytes);
+        uint32_t* const stage_row = hist + lane * kStageStride;
         float* xs = reinterpret_cast<float*>(smem + Cfg::kNormOffset) + ew * kHalfCols;
         uint2* const lists = p.cand + (static_cast<size_t>(blockIdx.x) * 2u + half) * kTileM * p.cap;
         uint2* const my_list = lists + static_cast<size_t>(lane_row) * p.cap;
@@ -416,7 +428,8 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             for (uint32_t bt = bt0; bt < bt1; ++bt, ++tile_iter) {
                 const uint32_t acc = tile_iter & 1u;
                 const uint32_t acc_phase = (tile_iter >> 1) & 1u;
-                const float thr = admission_threshold(tau, qvalid ? __ldcg(p.qtau + q) : 0xFFFFFFFFu);
+                float thr = admission_threshold(tau, qvalid ? __ldcg(p.qtau + q) : 0xFFFFFFFFu);
+                const Admission<KIND, METRIC> adm_test(thr, qn);
                 const uint32_t col0 = half * kHalfCols;
                 const uint32_t row_half = bt * BN + col0;
                 if constexpr (METRIC == kEuclidean) {
@@ -454,17 +467,52 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                     if (p.live != nullptr) mword &= __ldg(p.live + (row0 >> 5));
                     if (!qvalid) mword = 0;
                     const float* xn = xs + c * 32u;
-                    // Fast reject: most chunks hold nothing below the threshold.
-                    const bool slow = mword != 0u && chunk_min_key<KIND, METRIC>(v, xn, qn) < thr;
-                    if (__any_sync(0xffffffffu, slow)) {
-                        // Predicated appends (a predicated store instruction,
-                        // not a branch around a store: lanes disagree often).
+                    // Admission mask, one compare per column; admitted columns
+                    // are few, so only they are visited: a lane with any
+                    // stages its half-chunk in shared memory and walks the set
+                    // bits with the exact key test.
+                    uint32_t am[4] = {0u, 0u, 0u, 0u};  // four independent chains
 #pragma unroll
-                        for (uint32_t i = 0; i < 32; ++i) {
-                            const float key = key_of<KIND, METRIC>(v[i], xn[i], qn);
-                            const bool take = slow && ((mword >> i) & 1u) && key < thr;
-                            st_global_pred(my_list + cnt, __float_as_uint(key), p.row_offset + row0 + i, take);
-                            cnt += take ? 1u : 0u;
+                    for (uint32_t i = 0; i < 32; ++i) am[i & 3u] |= adm_test.pass(v[i], xn[i]) ? (1u << i) : 0u;
+                    const uint32_t adm = ((am[0] | am[1]) | (am[2] | am[3])) & mword;
+                    if (__any_sync(0xffffffffu, adm != 0u)) {
+#pragma unroll
+                        for (uint32_t h = 0; h < 2; ++h) {
+                            uint32_t hm = (adm >> (16u * h)) & 0xFFFFu;
+                            if (__any_sync(0xffffffffu, __popc(hm) > 4)) {
+                                // Many admissions (no tight bound yet): predicated
+                                // appends over the half-chunk's 16 registers.
+#pragma unroll
+                                for (uint32_t j = 0; j < 16; ++j) {
+                                    const uint32_t col = 16u * h + j;
+                                    const float key = key_of<KIND, METRIC>(v[col], xn[col], qn);
+                                    const bool take = ((hm >> j) & 1u) && key < thr;
+                                    st_global_pred(my_list + cnt, __float_as_uint(key), p.row_offset + row0 + col, take);
+                                    cnt += take ? 1u : 0u;
+                                }
+                            } else if (hm != 0u) {
+                                // Few admissions: stage the half-chunk in shared
+                                // memory and visit only the set bits, two per step.
+#pragma unroll
+                                for (uint32_t j = 0; j < 4; ++j)
+                                    *reinterpret_cast<uint4*>(stage_row + 4u * j) =
+                                        make_uint4(v[16u * h + 4u * j], v[16u * h + 4u * j + 1u],
+                                                   v[16u * h + 4u * j + 2u], v[16u * h + 4u * j + 3u]);
+                                do {
+                                    const uint32_t i0 = __ffs(hm) - 1u;
+                                    hm &= hm - 1u;
+                                    const bool two = hm != 0u;
+                                    const uint32_t i1 = two ? __ffs(hm) - 1u : i0;
+                                    hm &= hm - 1u;
+                                    const float k0 = key_of<KIND, METRIC>(stage_row[i0], xn[16u * h + i0], qn);
+                                    const float k1 = key_of<KIND, METRIC>(stage_row[i1], xn[16u * h + i1], qn);
+                                    const bool t0 = k0 < thr, t1 = two && k1 < thr;
+                                    if (t0) my_list[cnt] = make_uint2(__float_as_uint(k0), p.row_offset + row0 + 16u * h + i0);
+                                    cnt += t0 ? 1u : 0u;
+                                    if (t1) my_list[cnt] = make_uint2(__float_as_uint(k1), p.row_offset + row0 + 16u * h + i1);
+                                    cnt += t1 ? 1u : 0u;
+                                } while (hm != 0u);
+                            }
                         }
                     }
                 }
