@@ -858,6 +858,8 @@ def run_b200_filtered(args, cfg, world, rank, local, parity_q=None):
             tot_ms = max_over_ranks(float(evs[0][0].elapsed_time(evs[-1][1])), world)
             kst = _capi.profiler_stats("exact_topk")
             kms = kst["total_ms"] / max(1, kst["launches"])
+            breakdown = {name: round(_capi.profiler_stats(name)["total_ms"] / iters * 1e3, 2)
+                         for name in ("mask_select", "mask_gather", "prep_rows", "exact_topk", "merge_topk")}
             # end to end from host buffers: the queries and the filter in, the results out
             qh = np.ascontiguousarray(queries[:b])
             if world == 1:
@@ -883,7 +885,7 @@ def run_b200_filtered(args, cfg, world, rank, local, parity_q=None):
                 "e2e_latency_us_p50": round(float(np.percentile(e2e_lat, 50)) * 1e3, 1),
                 "e2e_latency_us_p99": round(float(np.percentile(e2e_lat, 99)) * 1e3, 1),
                 "e2e_queries_per_s": round(b * iters / (max_over_ranks(float(e2e_lat.sum()), world) / 1e3), 1),
-                "kernel_us_avg": round(kms * 1e3, 2),
+                "kernel_us_avg": round(kms * 1e3, 2), "device_us_per_call": breakdown,
                 "hbm_frac_selected_rows": round(sel_bytes / (kms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
                 "hbm_frac_full_scan": round(full_bytes / (kms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
                 "calls": iters}

@@ -318,4 +318,120 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
     }
 }
 
+// ------------------------------------------------- filtered-subset gathering
+// A row filter selecting a small share of the rows (Vault's equality
+// candidates, MetadataIndex::exact_candidates) is searched by gathering the
+// selected rows into a contiguous buffer first: the fused kernel then reads
+// only those rows instead of streaming the whole base and discarding most
+// of it in the epilogue.
+
+// Word w of the selection: filter bits ANDed with the live bits, cut at n.
+__device__ __forceinline__ uint32_t selected_word(const uint32_t* __restrict__ mask,
+                                                  const uint32_t* __restrict__ live, uint32_t n, uint32_t w) {
+    uint32_t m = mask[w];
+    if (live != nullptr) m &= live[w];
+    const uint32_t left = n - w * 32u;
+    if (left < 32u) m &= (1u << left) - 1u;
+    return m;
+}
+
+// Selected-row listing in two launches over blocks of kSelectThreads words.
+constexpr uint32_t kSelectThreads = 256;
+
+// Block-wide exclusive scan of one value per thread (kSelectThreads threads);
+// *block_total receives the sum.
+__device__ __forceinline__ uint32_t select_block_scan(uint32_t v, uint32_t* warp_sums, uint32_t* block_total) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    uint32_t incl = v;
+#pragma unroll
+    for (uint32_t off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        constexpr uint32_t kWarps = kSelectThreads / 32;
+        const uint32_t x = lane < kWarps ? warp_sums[lane] : 0u;
+        uint32_t xi = x;
+#pragma unroll
+        for (uint32_t off = 1; off < 32; off <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, xi, off);
+            if (lane >= off) xi += t;
+        }
+        if (lane < kWarps) warp_sums[lane] = xi - x;
+        if (lane == 31) *block_total = xi;
+    }
+    __syncthreads();
+    return warp_sums[warp] + incl - v;
+}
+
+// Launch 1: selected rows per block of kSelectThreads words.
+__global__ void __launch_bounds__(kSelectThreads) select_count_kernel(const uint32_t* __restrict__ mask,
+                                                                      const uint32_t* __restrict__ live, uint32_t n,
+                                                                      uint32_t nwords, uint32_t* __restrict__ block_counts) {
+    __shared__ uint32_t warp_sums[32];
+    __shared__ uint32_t total;
+    const uint32_t w = blockIdx.x * kSelectThreads + threadIdx.x;
+    const uint32_t c = w < nwords ? __popc(selected_word(mask, live, n, w)) : 0u;
+    select_block_scan(c, warp_sums, &total);
+    if (threadIdx.x == 0) block_counts[blockIdx.x] = total;
+}
+
+// Launch 2: each block offsets its rows by the counts of the blocks before
+// it, then writes its selected rows in ascending order (at most `cap` rows in
+// all); the last block writes the total to *total_out.
+__global__ void __launch_bounds__(kSelectThreads) select_rows_kernel(const uint32_t* __restrict__ mask,
+                                                                     const uint32_t* __restrict__ live, uint32_t n,
+                                                                     uint32_t nwords,
+                                                                     const uint32_t* __restrict__ block_counts,
+                                                                     uint32_t* __restrict__ rows_out, uint32_t cap,
+                                                                     uint32_t* __restrict__ total_out) {
+    __shared__ uint32_t warp_sums[32];
+    __shared__ uint32_t total, before;
+    // rows selected by the earlier blocks (a block-wide sum over block_counts)
+    uint32_t part = 0;
+    for (uint32_t b = threadIdx.x; b < blockIdx.x; b += kSelectThreads) part += block_counts[b];
+    select_block_scan(part, warp_sums, &before);
+    const uint32_t w = blockIdx.x * kSelectThreads + threadIdx.x;
+    uint32_t m = w < nwords ? selected_word(mask, live, n, w) : 0u;
+    uint32_t o = before + select_block_scan(__popc(m), warp_sums, &total);
+    if (blockIdx.x + 1 == gridDim.x && threadIdx.x == 0) *total_out = before + total;
+    while (m != 0u && o < cap) {
+        rows_out[o++] = w * 32u + (__ffs(m) - 1u);
+        m &= m - 1u;
+    }
+}
+
+// One warp per selected row: copies its operand row (row_bytes, a multiple
+// of 16) and, when norms is given, its squared norm.
+__global__ void gather_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                   const uint32_t* __restrict__ rows, uint32_t m, uint32_t row_bytes,
+                                   const float* __restrict__ norms, float* __restrict__ norms_out) {
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t lane = threadIdx.x & 31u;
+    if (warp >= m) return;
+    const uint32_t r = rows[warp];
+    const uint4* s = reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * row_bytes);
+    uint4* d = reinterpret_cast<uint4*>(dst + static_cast<size_t>(warp) * row_bytes);
+    for (uint32_t i = lane; i < row_bytes / 16u; i += 32u) d[i] = __ldg(s + i);
+    if (norms != nullptr && lane == 0) norms_out[warp] = norms[r];
+}
+
+// Rows of a search over the gathered subset back to index slots (+ offset):
+// out_rows (int64, -1 = none) and/or candidate pairs (row word, all ones = none).
+__global__ void remap_rows_kernel(int64_t* __restrict__ out_rows, uint2* __restrict__ out_cand, size_t count,
+                                  const uint32_t* __restrict__ rows, uint32_t row_offset) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    if (out_rows != nullptr) {
+        const int64_t r = out_rows[i];
+        if (r >= 0) out_rows[i] = static_cast<int64_t>(rows[r]) + row_offset;
+    }
+    if (out_cand != nullptr) {
+        const uint32_t r = out_cand[i].y;
+        if (r != 0xFFFFFFFFu) out_cand[i].y = rows[r] + row_offset;
+    }
+}
+
 }  // namespace eb

@@ -201,6 +201,8 @@ ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int group
 namespace {
 
 constexpr uint32_t kMaxK = 1024;
+// Bases smaller than this are searched whole even when a row filter is given.
+constexpr size_t kGatherMinRows = 65536;
 
 uint32_t elem_bytes_of(OperandKind k) {
     switch (k) {
@@ -689,7 +691,80 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
                          metric_, out_dist, out_rows, out_cand, stream);
         return;
     }
+    if (mask != nullptr && n_ >= kGatherMinRows &&
+        search_gathered(queries, nq, k, mask, row_offset, out_dist, out_rows, out_cand, stream))
+        return;
+    const RowView own{ops_.get(), ops_lo_.get(), static_cast<const float*>(norms_.get()),
+                      static_cast<const uint32_t*>(live_.get()), static_cast<uint32_t>(n_)};
+    search_rows(own, queries, nq, k, mask, row_offset, out_dist, out_rows, out_cand, stream);
+}
+
+bool ExactIndex::search_gathered(const void* queries, size_t nq, size_t k, const uint32_t* mask,
+                                 uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
+                                 cudaStream_t stream) const {
     const uint32_t n = static_cast<uint32_t>(n_);
+    const uint32_t nwords = (n + 31u) / 32u;
+    const uint32_t* live = static_cast<const uint32_t*>(live_.get());
+    auto align = [](size_t x) { return (x + 255) / 256 * 256; };
+    // The selected rows (at most n / 2 are kept; more and the whole base is
+    // searched) and their count, read back to size the subset and its plan.
+    const uint32_t cap = n / 2u + 1u;
+    const uint32_t blocks = (nwords + kSelectThreads - 1) / kSelectThreads;
+    const size_t rows_b = align(static_cast<size_t>(cap) * sizeof(uint32_t));
+    StreamScratch sel(rows_b + align(static_cast<size_t>(blocks) * sizeof(uint32_t)) + 256, stream);
+    uint32_t* rows = reinterpret_cast<uint32_t*>(sel.get());
+    uint32_t* block_counts = reinterpret_cast<uint32_t*>(sel.get() + rows_b);
+    uint32_t* total = block_counts + align(static_cast<size_t>(blocks) * sizeof(uint32_t)) / sizeof(uint32_t);
+    {
+        Profiler::Scope prof("mask_select", stream, nwords);
+        select_count_kernel<<<blocks, kSelectThreads, 0, stream>>>(mask, live, n, nwords, block_counts);
+        select_rows_kernel<<<blocks, kSelectThreads, 0, stream>>>(mask, live, n, nwords, block_counts, rows, cap,
+                                                                  total);
+        check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "row selection launch");
+    }
+    uint32_t m = 0;
+    check_cuda(cudaMemcpyAsync(&m, total, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
+               ELIPS_B200_TRANSFER_FAILED, "selected count");
+    check_cuda(cudaStreamSynchronize(stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "selected count");
+    if (static_cast<uint64_t>(m) * 2 > n) return false;
+    if (m == 0) {
+        merge_candidates(device_, nullptr, static_cast<uint32_t>(nq), 0, static_cast<uint32_t>(k), 0, 0, metric_,
+                         out_dist, out_rows, out_cand, stream);
+        return true;
+    }
+    const size_t row_bytes = static_cast<size_t>(d_pad_) * elem_bytes_;
+    const size_t ops_b = align(static_cast<size_t>(m) * row_bytes);
+    const size_t lo_b = ops_lo_.get() ? ops_b : 0;
+    const size_t norms_b = norms_.get() ? align(static_cast<size_t>(m) * sizeof(float)) : 0;
+    StreamScratch sub(ops_b + lo_b + norms_b, stream);
+    uint8_t* g_ops = sub.get();
+    uint8_t* g_lo = lo_b ? g_ops + ops_b : nullptr;
+    float* g_norms = norms_b ? reinterpret_cast<float*>(g_ops + ops_b + lo_b) : nullptr;
+    {
+        Profiler::Scope prof("mask_gather", stream, static_cast<uint64_t>(m) * row_bytes);
+        const uint32_t blocks = static_cast<uint32_t>((static_cast<uint64_t>(m) * 32 + 255) / 256);
+        gather_rows_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(ops_.get()), g_ops, rows, m,
+                                                       static_cast<uint32_t>(row_bytes),
+                                                       static_cast<const float*>(norms_.get()), g_norms);
+        if (g_lo != nullptr)
+            gather_rows_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(ops_lo_.get()), g_lo, rows,
+                                                           m, static_cast<uint32_t>(row_bytes), nullptr, nullptr);
+        check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "gather launch");
+    }
+    const RowView subset{g_ops, g_lo, g_norms, nullptr, m};
+    search_rows(subset, queries, nq, k, nullptr, 0, out_dist, out_rows, out_cand, stream);
+    const size_t count = nq * k;
+    remap_rows_kernel<<<static_cast<uint32_t>((count + 255) / 256), 256, 0, stream>>>(out_rows, out_cand, count,
+                                                                                       rows, row_offset);
+    check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "remap launch");
+    return true;
+}
+
+void ExactIndex::search_rows(const RowView& rv, const void* queries, size_t nq, size_t k, const uint32_t* mask,
+                             uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
+                             cudaStream_t stream) const {
+    const DeviceProps& props = device_props(device_);
+    const uint32_t n = rv.n;
     // More than one 128-query tile: CTA pairs (M = 256 per MMA).
     const bool pair = nq > kTileM;
     const ExactPlan plan = plan_exact(static_cast<uint32_t>(nq), n, static_cast<uint32_t>(k), bn_of(kind_),
@@ -721,17 +796,17 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
 
     const CUtensorMapDataType dt = tma_dtype_of(kind_);
     const CUtensorMap ma = make_operand_map(qa, dt, elem_bytes_, d_pad_, nq, kTileM);
-    const CUtensorMap mb = make_operand_map(ops_.get(), dt, elem_bytes_, d_pad_, n, plan.bn / plan.cg);
+    const CUtensorMap mb = make_operand_map(rv.ops, dt, elem_bytes_, d_pad_, n, plan.bn / plan.cg);
     CUtensorMap malo = ma, mblo = mb;
     if (kind_ == OperandKind::TF32X3) {
         malo = make_operand_map(qlo, dt, elem_bytes_, d_pad_, nq, kTileM);
-        mblo = make_operand_map(ops_lo_.get(), dt, elem_bytes_, d_pad_, n, plan.bn / plan.cg);
+        mblo = make_operand_map(rv.ops_lo, dt, elem_bytes_, d_pad_, n, plan.bn / plan.cg);
     }
     ExactParams prm{};
-    prm.base_norms = static_cast<const float*>(norms_.get());
+    prm.base_norms = rv.norms;
     prm.query_norms = qn;
     prm.mask = mask;
-    prm.live = static_cast<const uint32_t*>(live_.get());
+    prm.live = rv.live;
     prm.cand = cand_buf;
     prm.partial = part_buf;
     prm.qtau = qtau_buf;

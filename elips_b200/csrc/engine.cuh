@@ -146,12 +146,28 @@ public:
     // buffer of `scratch_bytes` and at most `max_grid` CTAs; performs no
     // device allocation. Fails with INVALID_ARGUMENT when the call needs more
     // scratch than the buffer holds.
+    // Rows one search scans: the index's own storage, or a gathered subset.
+    struct RowView {
+        const void* ops;
+        const void* ops_lo;
+        const float* norms;
+        const uint32_t* live;
+        uint32_t n;
+    };
+
     void search_device_in_scratch(const void* queries, size_t nq, size_t k, const uint32_t* mask,
                                   float* out_dist, int64_t* out_rows, uint8_t* scratch,
                                   size_t scratch_bytes, uint32_t max_grid, cudaStream_t stream) const;
 
 private:
     void reserve(size_t rows);
+    void search_rows(const RowView& rv, const void* queries, size_t nq, size_t k, const uint32_t* mask,
+                     uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
+                     cudaStream_t stream) const;
+    // A row filter that selects at most half of the rows: gathers them and
+    // searches the subset; false (nothing launched beyond the count) otherwise.
+    bool search_gathered(const void* queries, size_t nq, size_t k, const uint32_t* mask, uint32_t row_offset,
+                         float* out_dist, int64_t* out_rows, uint2* out_cand, cudaStream_t stream) const;
 
     int device_;
     int metric_;

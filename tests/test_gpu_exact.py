@@ -284,3 +284,28 @@ def test_filtered_shards_merge_equals_single_index(shards):
 def test_no_device_error_recorded():
     from elips_b200 import _capi
     assert _capi.device_error(0) == 0
+
+
+@pytest.mark.parametrize("p,k", [(0.2, 10), (0.02, 50), (0.0, 5)])
+def test_filtered_subset_gather_with_removals(p, k, nthreads):
+    """A row filter selecting at most half of a large base is searched by
+    gathering the selected live rows first; results (slots, distances) equal
+    the oracle's scan restricted to filter AND live rows, ties by slot."""
+    base = H.gaussian(100_000, 64, seed=41)
+    base[50_000:50_100] = base[:100]                      # exact ties across the base
+    queries = H.gaussian(150, 64, seed=42)
+    words, bits = H.bernoulli_mask(base.shape[0], p, seed=43)
+    ix = _index("euclidean", base, "fp32")
+    removed = np.arange(7, 100_000, 997)
+    for r in removed:
+        ix.remove(int(r))
+    live = np.ones(base.shape[0], bool)
+    live[removed] = False
+    dist, rows = ix.search_batch(queries, k, mask=words)
+    sel = bits & live
+    sel_words = np.zeros_like(words)
+    idx = np.nonzero(sel)[0]
+    np.bitwise_or.at(sel_words, idx >> 5, (np.uint32(1) << (idx & 31).astype(np.uint32)))
+    dr, rr = O.exact_search("euclidean", base, queries, k, nthreads=nthreads, mask=sel_words)
+    assert sel[rows[rows >= 0]].all()
+    H.assert_ranked_match(dist, rows, dr, rr, _true("euclidean", base, queries), rtol=1e-5)
