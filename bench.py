@@ -610,7 +610,8 @@ def run_b200(args, cfg, world, rank, local, parity_q=None):
     if replicate:
         index = ReplicatedIndex(ExactIndex(cfg["metric"], d, precision=cfg["precision"], device=local))
     else:
-        index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local)
+        index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local,
+                                  exchange=args.exchange)
     host_base = np.empty((hi - lo, d), np.int8 if cfg["precision"] == "int8" else np.float32) \
         if (world == 1 and (want_cpu or parity_q)) else None
     step_rows = 1 << 18
@@ -704,6 +705,8 @@ def run_b200(args, cfg, world, rank, local, parity_q=None):
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t, world)
     barrier(world)
+    if getattr(index, "peer", None) is not None:
+        index.peer.close()  # collective: unmap, then the root frees its exchange buffers
     # sharded: every rank uploads the whole batch; replicas: each its own slice
     in_bytes = queries.numel() * queries.element_size() * (1 if replicate else world)
     if mask_words is not None:
@@ -713,7 +716,9 @@ def run_b200(args, cfg, world, rank, local, parity_q=None):
            "api": "elips_b200_exact_search (host buffers)" if world == 1 else
                   ("ReplicatedIndex.search_batch (host buffers, query slices, NCCL all-gather of the results)"
                    if replicate else
-                   "ShardedExactIndex.search_batch (host buffers, NCCL all-gather, merge kernel)")}
+                   ("ShardedExactIndex.search_batch (host buffers; bounds shared and candidates handed to the "
+                    "root over NVLink peer memory, merge kernel)" if getattr(index, "exchange", "") == "peer" else
+                    "ShardedExactIndex.search_batch (host buffers, NCCL all-gather, merge kernel)"))}
 
     # ---- roofline of the dominant kernel (fused GEMM + top-k)
     peaks, peak_src = load_peaks()
@@ -806,7 +811,7 @@ def run_b200_filtered(args, cfg, world, rank, local, parity_q=None):
     pool = max(cfg["batches"])
     lo, hi = shard_range(n, rank, world)
     t0 = time.perf_counter()
-    index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local)
+    index = ShardedExactIndex(cfg["metric"], d, n, precision=cfg["precision"], device=local, exchange=args.exchange)
     host_base = [] if rank == 0 and world == 1 else None
     for r0 in range(lo, hi, 1 << 18):
         rows = gen_rows(cfg, r0, min(1 << 18, hi - r0), SEED + 1, n, None, device=dev)
@@ -889,6 +894,8 @@ def run_b200_filtered(args, cfg, world, rank, local, parity_q=None):
                 "hbm_frac_selected_rows": round(sel_bytes / (kms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
                 "hbm_frac_full_scan": round(full_bytes / (kms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
                 "calls": iters}
+    if getattr(index, "peer", None) is not None:
+        index.peer.close()
     top = per_batch[str(max(cfg["batches"]))]
     sel_rows = int(_mask_rows(global_mask, n).shape[0])
     kms_top = top["kernel_us_avg"] / 1e3
@@ -1331,6 +1338,9 @@ def main():
     ap.add_argument("--distributed", default="shard", choices=["shard", "replicate"],
                     help="exact configurations at N>1: rows split across the GPUs (shard) or the whole base on "
                          "every GPU with the query batch split (replicate)")
+    ap.add_argument("--exchange", default=None, choices=["peer", "allgather"],
+                    help="row-sharded exact search at N>1: shared bounds and candidates over NVLink peer memory "
+                         "(peer, the default with NCCL) or private bounds and an NCCL all-gather (allgather)")
     ap.add_argument("--base-rows", type=int, default=None,
                     help="smaller base of the same configuration (profiling captures)")
     ap.add_argument("--queries", type=int, default=None,

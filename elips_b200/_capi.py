@@ -59,6 +59,13 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_uint32, c_void_p, c_void_p]),
     ("elips_b200_merge_candidates_device", c_int,
      [c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_exact_search_candidates_shared_device", c_int, [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_uint32, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_peer_alloc", c_int, [c_int, c_size_t, POINTER(c_void_p), c_void_p]),
+    ("elips_b200_peer_open", c_int, [c_int, c_void_p, POINTER(c_void_p)]),
+    ("elips_b200_peer_close", c_int, [c_int, c_void_p]),
+    ("elips_b200_peer_free", c_int, [c_int, c_void_p]),
+    ("elips_b200_copy_device", c_int, [c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("elips_b200_fill_device", c_int, [c_int, c_void_p, c_int, c_size_t, c_void_p]),
     ("elips_b200_compute_distances_batch", c_int,
      [c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_int, c_void_p]),
     ("elips_b200_top_k", c_int,

@@ -1,6 +1,8 @@
 // extern "C" surface declared in include/elips_b200.h. Each function catches
 // every C++ exception and returns a status code; nothing throws across it.
 #include <cstdio>
+#include <cstring>
+#include <string>
 #include <new>
 
 #include "../../include/elips_b200.h"
@@ -207,6 +209,85 @@ int elips_b200_exact_search_candidates_device(const elips_b200_exact* index,
             eb::fail(ELIPS_B200_INVALID_ARGUMENT, "row_offset + size exceeds the 32-bit row space");
         index->index.search_device(queries, nq, k, mask, row_offset, nullptr, nullptr,
                                    reinterpret_cast<uint2*>(out_cand), as_stream(stream));
+    });
+}
+
+int elips_b200_exact_search_candidates_shared_device(const elips_b200_exact* index, const void* queries,
+                                                     size_t nq, size_t k, const uint32_t* mask, uint32_t row_offset,
+                                                     uint32_t* out_cand, uint32_t* shared_bound, void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (out_cand == nullptr || shared_bound == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        if (static_cast<uint64_t>(row_offset) + index->index.size() >= 0xFFFFFFFFull)
+            eb::fail(ELIPS_B200_INVALID_ARGUMENT, "row_offset + size exceeds the 32-bit row space");
+        index->index.search_device(queries, nq, k, mask, row_offset, nullptr, nullptr,
+                                   reinterpret_cast<uint2*>(out_cand), as_stream(stream), shared_bound);
+    });
+}
+
+int elips_b200_peer_alloc(int device, size_t bytes, void** ptr_out, void* ipc_handle_out) {
+    if (ptr_out == nullptr || ipc_handle_out == nullptr || bytes == 0) return ELIPS_B200_INVALID_ARGUMENT;
+    *ptr_out = nullptr;
+    return guarded([&] {
+        eb::DeviceGuard g(device);
+        void* p = nullptr;
+        eb::check_cuda(cudaMalloc(&p, bytes), ELIPS_B200_INSUFFICIENT_MEMORY, "peer buffer");
+        cudaIpcMemHandle_t h;
+        const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+        if (e != cudaSuccess) {
+            cudaFree(p);
+            eb::fail(ELIPS_B200_INITIALIZATION_FAILED, std::string("cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+        }
+        std::memcpy(ipc_handle_out, &h, sizeof(h));
+        *ptr_out = p;
+    });
+}
+
+int elips_b200_peer_open(int device, const void* ipc_handle, void** ptr_out) {
+    if (ptr_out == nullptr || ipc_handle == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    *ptr_out = nullptr;
+    return guarded([&] {
+        eb::DeviceGuard g(device);
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, ipc_handle, sizeof(h));
+        eb::check_cuda(cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess),
+                       ELIPS_B200_INITIALIZATION_FAILED, "cudaIpcOpenMemHandle");
+    });
+}
+
+int elips_b200_peer_close(int device, void* ptr) {
+    if (ptr == nullptr) return ELIPS_B200_OK;
+    return guarded([&] {
+        eb::DeviceGuard g(device);
+        eb::check_cuda(cudaIpcCloseMemHandle(ptr), ELIPS_B200_INITIALIZATION_FAILED, "cudaIpcCloseMemHandle");
+    });
+}
+
+int elips_b200_peer_free(int device, void* ptr) {
+    if (ptr == nullptr) return ELIPS_B200_OK;
+    return guarded([&] {
+        eb::DeviceGuard g(device);
+        eb::check_cuda(cudaFree(ptr), ELIPS_B200_INVALID_ARGUMENT, "peer buffer free");
+    });
+}
+
+int elips_b200_copy_device(int device, void* dst, const void* src, size_t bytes, void* stream) {
+    if (bytes == 0) return ELIPS_B200_OK;
+    if (dst == nullptr || src == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        eb::DeviceGuard g(device);
+        eb::check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, as_stream(stream)),
+                       ELIPS_B200_TRANSFER_FAILED, "device copy");
+    });
+}
+
+int elips_b200_fill_device(int device, void* dst, int byte_value, size_t bytes, void* stream) {
+    if (bytes == 0) return ELIPS_B200_OK;
+    if (dst == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        eb::DeviceGuard g(device);
+        eb::check_cuda(cudaMemsetAsync(dst, byte_value, bytes, as_stream(stream)), ELIPS_B200_KERNEL_LAUNCH_FAILED,
+                       "device fill");
     });
 }
 

@@ -678,7 +678,7 @@ void ExactIndex::add_device(const void* rows, size_t n, cudaStream_t stream) {
 
 void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const uint32_t* mask,
                                uint32_t row_offset, float* out_dist, int64_t* out_rows,
-                               uint2* out_cand, cudaStream_t stream) const {
+                               uint2* out_cand, cudaStream_t stream, uint32_t* shared_bound) const {
     if (nq == 0 || k == 0) return;
     if (k > kMaxK) fail(ELIPS_B200_INVALID_ARGUMENT, "k above 1024 is not supported");
     if (nq > 0x7FFFFFFFull) fail(ELIPS_B200_INVALID_ARGUMENT, "too many queries in one call");
@@ -692,16 +692,16 @@ void ExactIndex::search_device(const void* queries, size_t nq, size_t k, const u
         return;
     }
     if (mask != nullptr && n_ >= kGatherMinRows &&
-        search_gathered(queries, nq, k, mask, row_offset, out_dist, out_rows, out_cand, stream))
+        search_gathered(queries, nq, k, mask, row_offset, out_dist, out_rows, out_cand, stream, shared_bound))
         return;
     const RowView own{ops_.get(), ops_lo_.get(), static_cast<const float*>(norms_.get()),
                       static_cast<const uint32_t*>(live_.get()), static_cast<uint32_t>(n_)};
-    search_rows(own, queries, nq, k, mask, row_offset, out_dist, out_rows, out_cand, stream);
+    search_rows(own, queries, nq, k, mask, row_offset, out_dist, out_rows, out_cand, stream, shared_bound);
 }
 
 bool ExactIndex::search_gathered(const void* queries, size_t nq, size_t k, const uint32_t* mask,
                                  uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
-                                 cudaStream_t stream) const {
+                                 cudaStream_t stream, uint32_t* shared_bound) const {
     const uint32_t n = static_cast<uint32_t>(n_);
     const uint32_t nwords = (n + 31u) / 32u;
     const uint32_t* live = static_cast<const uint32_t*>(live_.get());
@@ -752,7 +752,7 @@ bool ExactIndex::search_gathered(const void* queries, size_t nq, size_t k, const
         check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "gather launch");
     }
     const RowView subset{g_ops, g_lo, g_norms, nullptr, m};
-    search_rows(subset, queries, nq, k, nullptr, 0, out_dist, out_rows, out_cand, stream);
+    search_rows(subset, queries, nq, k, nullptr, 0, out_dist, out_rows, out_cand, stream, shared_bound);
     const size_t count = nq * k;
     remap_rows_kernel<<<static_cast<uint32_t>((count + 255) / 256), 256, 0, stream>>>(out_rows, out_cand, count,
                                                                                        rows, row_offset);
@@ -762,7 +762,7 @@ bool ExactIndex::search_gathered(const void* queries, size_t nq, size_t k, const
 
 void ExactIndex::search_rows(const RowView& rv, const void* queries, size_t nq, size_t k, const uint32_t* mask,
                              uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
-                             cudaStream_t stream) const {
+                             cudaStream_t stream, uint32_t* shared_bound) const {
     const DeviceProps& props = device_props(device_);
     const uint32_t n = rv.n;
     // More than one 128-query tile: CTA pairs (M = 256 per MMA).
@@ -790,8 +790,10 @@ void ExactIndex::search_rows(const RowView& rv, const void* queries, size_t nq, 
     uint2* cand_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm);
     uint2* part_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand);
     uint32_t* qtau_buf = reinterpret_cast<uint32_t*>(s + q_ops + q_lo + q_norm + cand + partial);
-    check_cuda(cudaMemsetAsync(qtau_buf, 0xFF, nq * sizeof(uint32_t), stream), ELIPS_B200_KERNEL_LAUNCH_FAILED,
-               "threshold init");
+    if (shared_bound != nullptr) qtau_buf = shared_bound;
+    else
+        check_cuda(cudaMemsetAsync(qtau_buf, 0xFF, nq * sizeof(uint32_t), stream), ELIPS_B200_KERNEL_LAUNCH_FAILED,
+                   "threshold init");
     prep_operands(kind_, queries, nq, dim_, d_pad_, qa, qlo, qn, stream);
 
     const CUtensorMapDataType dt = tma_dtype_of(kind_);

@@ -138,9 +138,13 @@ public:
 
     // queries: device, nq x dim (fp32, int8 for INT8). Exactly one of
     // (out_dist, out_rows) or out_cand is used.
+    // shared_bound (optional, DEVICE, may be another GPU's memory): nq
+    // per-query admission bounds (ordered keys, all ones = none) shared by
+    // every shard searching the same queries; the kernel reads and tightens
+    // them (atomicMin) instead of private ones. The caller initialises them.
     void search_device(const void* queries, size_t nq, size_t k, const uint32_t* mask,
                        uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
-                       cudaStream_t stream) const;
+                       cudaStream_t stream, uint32_t* shared_bound = nullptr) const;
 
     // The same search with all scratch carved from a caller-provided device
     // buffer of `scratch_bytes` and at most `max_grid` CTAs; performs no
@@ -163,11 +167,12 @@ private:
     void reserve(size_t rows);
     void search_rows(const RowView& rv, const void* queries, size_t nq, size_t k, const uint32_t* mask,
                      uint32_t row_offset, float* out_dist, int64_t* out_rows, uint2* out_cand,
-                     cudaStream_t stream) const;
+                     cudaStream_t stream, uint32_t* shared_bound) const;
     // A row filter that selects at most half of the rows: gathers them and
     // searches the subset; false (nothing launched beyond the count) otherwise.
     bool search_gathered(const void* queries, size_t nq, size_t k, const uint32_t* mask, uint32_t row_offset,
-                         float* out_dist, int64_t* out_rows, uint2* out_cand, cudaStream_t stream) const;
+                         float* out_dist, int64_t* out_rows, uint2* out_cand, cudaStream_t stream,
+                         uint32_t* shared_bound) const;
 
     int device_;
     int metric_;

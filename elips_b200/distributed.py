@@ -18,6 +18,7 @@ from typing import Optional
 
 import numpy as np
 
+from .exact import METRICS as METRICS_CODE
 from .exact import ExactIndex, merge_candidates_device
 
 
@@ -54,12 +55,111 @@ def exchange_candidates(cand, world: int, group=None):
     return flat.view((world,) + tuple(cand.shape))
 
 
+class PeerExchange:
+    """The shard exchange over NVLink peer memory (one process per GPU of one
+    node): the root owns, twice over (alternating steps), a receive buffer for
+    every rank's [nq, k] candidate block and nq shared per-query admission
+    bounds; every rank maps them (CUDA interprocess handles) and
+      * passes the bounds to its fused kernel, which reads and tightens them
+        while it runs, so a shard admits only candidates that can still reach
+        the global top-k;
+      * copies its k candidates per query straight into its slot of the
+        root's buffer (a device-to-peer copy), where the root's merge kernel
+        reads them after one tiny all-reduce orders the ranks.
+    Collective: every rank calls ensure() and step() in the same order."""
+
+    def __init__(self, rank: int, world: int, device: int, group=None):
+        import torch
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.rank, self.world, self.device = rank, world, device
+        self.cap_q = self.k = 0
+        self.base = None         # this process's mapping of the root's buffer
+        self.owned = None        # the root's own allocation
+        self.step_no = 0
+        self.flag = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
+
+    def _sizes(self, nq, k):
+        recv = self.world * nq * k * 8
+        return recv, recv + nq * 4  # one set: candidate blocks, then bounds
+
+    def ensure(self, nq: int, k: int) -> None:
+        """(Re)creates the buffers for batches of up to nq queries at this k."""
+        import ctypes
+        from . import _capi as capi
+        if nq <= self.cap_q and k == self.k:
+            return
+        self.close()
+        cap_q = max(nq, self.cap_q)
+        _, set_bytes = self._sizes(cap_q, k)
+        handle = (ctypes.c_uint8 * 64)()
+        if self.rank == 0:
+            ptr = ctypes.c_void_p()
+            capi.check(capi.LIB.elips_b200_peer_alloc(self.device, 2 * set_bytes, ctypes.byref(ptr), handle),
+                       "elips_b200_peer_alloc")
+            self.owned = self.base = ptr.value
+            capi.check(capi.LIB.elips_b200_fill_device(self.device, self.base, 0xFF, 2 * set_bytes, None),
+                       "elips_b200_fill_device")
+            import torch
+            torch.cuda.synchronize(self.device)
+        obj = [bytes(handle)]
+        self.dist.broadcast_object_list(obj, src=0, group=self.group)
+        if self.rank != 0:
+            ctypes.memmove(handle, obj[0], 64)
+            ptr = ctypes.c_void_p()
+            capi.check(capi.LIB.elips_b200_peer_open(self.device, handle, ctypes.byref(ptr)), "elips_b200_peer_open")
+            self.base = ptr.value
+        self.cap_q, self.k = cap_q, k
+        self.dist.barrier(group=self.group)
+
+    def slots(self, nq: int):
+        """(this rank's candidate slot, the bounds, the root's candidate
+        blocks) of the current step's buffer set, as device addresses."""
+        _, set_bytes = self._sizes(self.cap_q, self.k)
+        recv_bytes, _ = self._sizes(self.cap_q, self.k)
+        s = self.base + (self.step_no & 1) * set_bytes
+        return s + self.rank * nq * self.k * 8, s + recv_bytes, s
+
+    def finish_step(self, nq: int, stream) -> None:
+        """Root: resets the other set's bounds for the next step; all: one
+        all-reduce that orders every rank's copy before the root's merge."""
+        from . import _capi as capi
+        if self.rank == 0:
+            _, set_bytes = self._sizes(self.cap_q, self.k)
+            recv_bytes, _ = self._sizes(self.cap_q, self.k)
+            other = self.base + ((self.step_no + 1) & 1) * set_bytes + recv_bytes
+            capi.check(capi.LIB.elips_b200_fill_device(self.device, other, 0xFF, nq * 4, stream),
+                       "elips_b200_fill_device")
+        self.dist.all_reduce(self.flag, group=self.group)
+        self.step_no += 1
+
+    def close(self) -> None:
+        """Collective: the other ranks unmap the root's buffer, then the root frees it."""
+        import torch
+        from . import _capi as capi
+        if self.base is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.rank != 0:
+            capi.LIB.elips_b200_peer_close(self.device, self.base)
+        self.dist.barrier(group=self.group)
+        if self.owned is not None:
+            capi.LIB.elips_b200_peer_free(self.device, self.owned)
+        self.base = self.owned = None
+        self.cap_q = self.k = 0
+
+
 class ShardedExactIndex:
     """One rank's share of a row-sharded index. Every rank of the process group
-    must call each method with the same arguments (collective semantics)."""
+    must call each method with the same arguments (collective semantics).
+
+    exchange="peer" (default with NCCL): the ranks share their admission
+    bounds while their kernels run and hand their candidates to the root over
+    NVLink peer memory (PeerExchange); "allgather": private bounds and an NCCL
+    all-gather of the candidate blocks (any backend)."""
 
     def __init__(self, metric: str, dimension: int, total_rows: int, precision: str = "fp16",
-                 device: Optional[int] = None, group=None):
+                 device: Optional[int] = None, group=None, exchange: Optional[str] = None):
         import torch
         import torch.distributed as dist
         self.dist = dist
@@ -72,6 +172,10 @@ class ShardedExactIndex:
         self.total_rows = total_rows
         self.row_begin, self.row_end = shard_range(total_rows, self.rank, self.world)
         self.local = ExactIndex(metric, dimension, precision=precision, device=self.device)
+        if exchange is None:
+            exchange = "peer" if (self.world > 1 and dist.get_backend(group) == "nccl") else "allgather"
+        self.exchange = exchange
+        self.peer = PeerExchange(self.rank, self.world, self.device, group) if exchange == "peer" else None
 
     def add_device(self, rows) -> None:
         """Appends this rank's rows (a CUDA tensor); rows must arrive in global order."""
@@ -86,11 +190,35 @@ class ShardedExactIndex:
         if self.world == 1:
             return self.local.search_device(queries, k, mask=mask)
         cand = torch.empty((nq, k, 2), dtype=torch.int32, device=dev)
+        if self.peer is not None:
+            return self._search_peer(queries, k, mask, cand)
         self.local.search_candidates_device(queries, k, self.row_begin, cand, mask=mask)
         gathered = exchange_candidates(cand, self.world, self.group)
         if self.rank != 0:
             return None, None
         return merge_candidates_device(gathered, self.world, k, self.metric)
+
+    def _search_peer(self, queries, k, mask, cand):
+        import torch
+        from . import _capi as capi
+        nq = queries.shape[0]
+        self.peer.ensure(nq, k)
+        my_slot, bounds, blocks = self.peer.slots(nq)
+        stream = torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_exact_search_candidates_shared_device(
+            self.local._h, queries.data_ptr(), nq, k, mask.data_ptr() if mask is not None else None,
+            self.row_begin, cand.data_ptr(), bounds, stream), "elips_b200_exact_search_candidates_shared_device")
+        capi.check(capi.LIB.elips_b200_copy_device(self.device, my_slot, cand.data_ptr(), nq * k * 8, stream),
+                   "elips_b200_copy_device")
+        self.peer.finish_step(nq, stream)
+        if self.rank != 0:
+            return None, None
+        out_dist = torch.empty((nq, k), dtype=torch.float32, device=queries.device)
+        out_rows = torch.empty((nq, k), dtype=torch.int64, device=queries.device)
+        capi.check(capi.LIB.elips_b200_merge_candidates_device(
+            self.device, blocks, nq, self.world, k, METRICS_CODE[self.metric], out_dist.data_ptr(),
+            out_rows.data_ptr(), stream), "elips_b200_merge_candidates_device")
+        return out_dist, out_rows
 
     def search_batch(self, queries_host, k: int, out_dist=None, out_rows=None, mask=None):
         """End-to-end search from host memory: uploads the queries on every rank,

@@ -178,6 +178,19 @@ class ExactIndex:
             "elips_b200_exact_search_candidates_device")
         return out_cand
 
+    def search_candidates_shared_device(self, queries, k: int, row_offset: int, out_cand, shared_bound, mask=None,
+                                        stream=None):
+        """Shard-level search whose per-query admission bounds (shared_bound:
+        an int32 CUDA tensor [nq] of ordered keys, all ones = none) are shared
+        with the other shards searching the same queries."""
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_exact_search_candidates_shared_device(
+            self._h, queries.data_ptr(), queries.shape[0], k, mask.data_ptr() if mask is not None else None,
+            row_offset, out_cand.data_ptr(), shared_bound.data_ptr(), s),
+            "elips_b200_exact_search_candidates_shared_device")
+        return out_cand
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             capi.LIB.elips_b200_exact_destroy(self._h)

@@ -193,6 +193,35 @@ ELIPS_B200_API int elips_b200_exact_search_candidates_device(const elips_b200_ex
                                               const uint32_t* mask, uint32_t row_offset,
                                               uint32_t* out_cand, void* stream);
 
+/* The shard-level search above with the per-query admission bounds shared
+ * by every shard searching the same queries: shared_bound (DEVICE, nq
+ * uint32 ordered keys, may be another GPU's memory mapped with
+ * elips_b200_peer_open) is read and tightened (atomicMin) by the kernel while
+ * it runs, so each shard admits only candidates that can still reach the
+ * global top-k. The caller sets it to all ones (0xFF bytes) before the
+ * shards' searches and not again until all of them have finished. The merged
+ * result over all shards equals the one with private bounds. */
+ELIPS_B200_API int elips_b200_exact_search_candidates_shared_device(const elips_b200_exact* index,
+                                                                    const void* queries, size_t nq, size_t k,
+                                                                    const uint32_t* mask, uint32_t row_offset,
+                                                                    uint32_t* out_cand, uint32_t* shared_bound,
+                                                                    void* stream);
+
+/* Device buffers shared between the processes of one node (one per GPU) for
+ * the shard exchange: elips_b200_peer_alloc allocates `bytes` on `device` and
+ * writes its 64-byte interprocess handle; another process maps it into its
+ * own device's address space with elips_b200_peer_open (reads, writes and
+ * atomics then travel over NVLink) and unmaps it with elips_b200_peer_close;
+ * the owner frees it with elips_b200_peer_free. */
+ELIPS_B200_API int elips_b200_peer_alloc(int device, size_t bytes, void** ptr_out, void* ipc_handle_out);
+ELIPS_B200_API int elips_b200_peer_open(int device, const void* ipc_handle, void** ptr_out);
+ELIPS_B200_API int elips_b200_peer_close(int device, void* ptr);
+ELIPS_B200_API int elips_b200_peer_free(int device, void* ptr);
+/* Stream-ordered copy between device buffers (this GPU's or a mapped peer's)
+ * and byte fill of a device buffer. */
+ELIPS_B200_API int elips_b200_copy_device(int device, void* dst, const void* src, size_t bytes, void* stream);
+ELIPS_B200_API int elips_b200_fill_device(int device, void* dst, int byte_value, size_t bytes, void* stream);
+
 /* Final top-k over candidate lists (GpuDistributedIndex::merge_hits,
  * src/gpu_engine/GpuDistributedIndex.cpp:68-83): cand holds `lists` blocks of
  * nq x k pairs as written above, block-major (block l = one shard's output for
