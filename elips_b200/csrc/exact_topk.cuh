@@ -425,10 +425,15 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             }
             float tau = __int_as_float(0x7f800000);  // +inf: this list's own k-th key
             uint32_t cnt = 0;
+            // The shared bound is read one tile ahead: the bound array may sit
+            // in another GPU's memory, and a stale bound is still a valid one.
+            uint32_t next_bound = qvalid ? __ldcg(p.qtau + q) : 0xFFFFFFFFu;
             for (uint32_t bt = bt0; bt < bt1; ++bt, ++tile_iter) {
                 const uint32_t acc = tile_iter & 1u;
                 const uint32_t acc_phase = (tile_iter >> 1) & 1u;
-                float thr = admission_threshold(tau, qvalid ? __ldcg(p.qtau + q) : 0xFFFFFFFFu);
+                const uint32_t bound = next_bound;
+                if (qvalid && bt + 1 < bt1) next_bound = __ldcg(p.qtau + q);
+                float thr = admission_threshold(tau, bound);
                 const Admission<KIND, METRIC> adm_test(thr, qn);
                 const uint32_t col0 = half * kHalfCols;
                 const uint32_t row_half = bt * BN + col0;
