@@ -70,6 +70,8 @@ SIGNATURES = [
      [c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_int, c_void_p]),
     ("elips_b200_top_k", c_int,
      [c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_void_p]),
+    ("elips_b200_gemm_fp32", c_int,
+     [c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_int, c_int, c_void_p]),
     ("elips_b200_quant_create", c_int,
      [c_int, c_int, c_int, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, POINTER(c_void_p)]),
     ("elips_b200_quant_add", c_int, [c_void_p, c_void_p, c_size_t]),

@@ -411,6 +411,95 @@ int elips_b200_compute_distances_batch(int device, const float* queries, const f
     });
 }
 
+namespace {
+
+// Row-major C[m][n] = op(A) op(B) in fp32, 64 x 64 output tile per block of
+// 256 threads (4 x 4 per thread), k staged 16 at a time in shared memory.
+// op(A)[i][p] = trans_a ? A[p][i] : A[i][p] (A is m x kk, or kk x m);
+// op(B)[p][j] = trans_b ? B[j][p] : B[p][j].
+__global__ void __launch_bounds__(256) gemm_fp32_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                        float* __restrict__ C, uint32_t m, uint32_t n, uint32_t kk,
+                                                        int trans_a, int trans_b) {
+    __shared__ float As[16][64 + 4];
+    __shared__ float Bs[16][64 + 4];
+    const uint32_t tx = threadIdx.x & 15u, ty = threadIdx.x >> 4;
+    const uint32_t i0 = blockIdx.y * 64u, j0 = blockIdx.x * 64u;
+    float acc[4][4] = {};
+    for (uint32_t p0 = 0; p0 < kk; p0 += 16) {
+        for (uint32_t e = threadIdx.x; e < 16u * 64u; e += 256u) {
+            const uint32_t pp = e / 64u, ii = e % 64u;
+            const uint32_t i = i0 + ii, j = j0 + ii, p = p0 + pp;
+            float av = 0.0f, bv = 0.0f;
+            if (i < m && p < kk) av = trans_a ? A[static_cast<size_t>(p) * m + i] : A[static_cast<size_t>(i) * kk + p];
+            if (j < n && p < kk) bv = trans_b ? B[static_cast<size_t>(j) * kk + p] : B[static_cast<size_t>(p) * n + j];
+            As[pp][ii] = av;
+            Bs[pp][ii] = bv;
+        }
+        __syncthreads();
+#pragma unroll
+        for (uint32_t pp = 0; pp < 16; ++pp) {
+            float a[4], b[4];
+#pragma unroll
+            for (uint32_t r = 0; r < 4; ++r) a[r] = As[pp][ty * 4u + r];
+#pragma unroll
+            for (uint32_t c = 0; c < 4; ++c) b[c] = Bs[pp][tx * 4u + c];
+#pragma unroll
+            for (uint32_t r = 0; r < 4; ++r)
+#pragma unroll
+                for (uint32_t c = 0; c < 4; ++c) acc[r][c] = fmaf(a[r], b[c], acc[r][c]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (uint32_t r = 0; r < 4; ++r)
+#pragma unroll
+        for (uint32_t c = 0; c < 4; ++c) {
+            const uint32_t i = i0 + ty * 4u + r, j = j0 + tx * 4u + c;
+            if (i < m && j < n) C[static_cast<size_t>(i) * n + j] = acc[r][c];
+        }
+}
+
+void gemm_fp32_device(const float* a, const float* b, float* c, size_t m, size_t n, size_t kk, int trans_a,
+                      int trans_b, cudaStream_t stream) {
+    if (m == 0 || n == 0) return;
+    if (m > 0x7FFFFFFFull || n > 0x7FFFFFFFull || kk > 0x7FFFFFFFull)
+        eb::fail(ELIPS_B200_INVALID_ARGUMENT, "GEMM dimensions above 2^31");
+    const dim3 grid(static_cast<uint32_t>((n + 63) / 64), static_cast<uint32_t>((m + 63) / 64));
+    gemm_fp32_kernel<<<grid, 256, 0, stream>>>(a, b, c, static_cast<uint32_t>(m), static_cast<uint32_t>(n),
+                                               static_cast<uint32_t>(kk), trans_a, trans_b);
+    eb::check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "gemm launch");
+}
+
+}  // namespace
+
+int elips_b200_gemm_fp32(int device, const float* a, const float* b, float* c, size_t m, size_t n, size_t k_inner,
+                         int trans_a, int trans_b, int pointers_on_device, void* stream) {
+    if (m > 0 && n > 0 && (a == nullptr || b == nullptr || c == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        eb::DeviceGuard g(device);
+        if (pointers_on_device) {
+            gemm_fp32_device(a, b, c, m, n, k_inner, trans_a, trans_b, static_cast<cudaStream_t>(stream));
+            return;
+        }
+        if (m == 0 || n == 0) return;
+        OwnedStream st;
+        {
+            eb::StreamScratch s((m * k_inner + k_inner * n + m * n) * 4 + 512, st.s);
+            float* da = reinterpret_cast<float*>(s.get());
+            float* db = da + m * k_inner;
+            float* dc = db + k_inner * n;
+            eb::check_cuda(cudaMemcpyAsync(da, a, m * k_inner * 4, cudaMemcpyHostToDevice, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "gemm upload");
+            eb::check_cuda(cudaMemcpyAsync(db, b, k_inner * n * 4, cudaMemcpyHostToDevice, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "gemm upload");
+            gemm_fp32_device(da, db, dc, m, n, k_inner, trans_a, trans_b, st.s);
+            eb::check_cuda(cudaMemcpyAsync(c, dc, m * n * 4, cudaMemcpyDeviceToHost, st.s),
+                           ELIPS_B200_TRANSFER_FAILED, "gemm download");
+        }
+        eb::check_cuda(cudaStreamSynchronize(st.s), ELIPS_B200_KERNEL_LAUNCH_FAILED, "gemm");
+    });
+}
+
 int elips_b200_top_k(int device, const float* distances, uint32_t* indices_out, float* values_out, size_t nq,
                      size_t nb, size_t k, int pointers_on_device, void* stream) {
     if (nq > 0 && k > 0 && (indices_out == nullptr || values_out == nullptr)) return ELIPS_B200_INVALID_ARGUMENT;

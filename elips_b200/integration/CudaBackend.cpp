@@ -9,7 +9,7 @@
 //
 // Build (inside an ELIPS tree, or against one with -I): compile with
 // -std=c++23 -DELIPS_CUDA_ENABLED -I<elips>/include -I<elips>/src/gpu_engine
-// -I<this repo>/include, link libelips_b200.so, libcudart and libcublas.
+// -I<this repo>/include, link libelips_b200.so and libcudart.
 //
 // Semantics kept from the port contract:
 //  * compute_distances_batch / top_k take HOST spans (the callers in
@@ -21,8 +21,6 @@
 //    (elips::distance sequential fp32, top_k ascending, ties by index);
 //  * errors come back as std::expected, never as exceptions.
 #include "backends/cuda/CudaBackend.hpp"
-
-#include <cublas_v2.h>
 
 #include <string>
 
@@ -160,46 +158,15 @@ std::expected<void, GpuError> CudaBackend::top_k(std::span<const float> distance
 }
 
 // Row-major C[m][n] = op(A) op(B), op(A) is m x k_inner, op(B) k_inner x n
-// (HOST spans): a plain library GEMM, cuBLAS in full fp32.
+// (HOST spans), in fp32 through the library's GEMM kernel.
 std::expected<void, GpuError> CudaBackend::gemm_fp32(std::span<const float> a, std::span<const float> b,
                                                      std::span<float> c, size_t m, size_t n, size_t k_inner,
                                                      bool trans_a, bool trans_b) {
     if (!initialized_) return std::unexpected(GpuError::BackendUnavailable);
     if (a.size() < m * k_inner || b.size() < k_inner * n || c.size() < m * n)
         return std::unexpected(GpuError::KernelLaunchFailed);
-    if (m == 0 || n == 0) return {};
-    cudaSetDevice(device_index_);
-    float *da = nullptr, *db = nullptr, *dc = nullptr;
-    auto release = [&] {
-        cudaFree(da);
-        cudaFree(db);
-        cudaFree(dc);
-    };
-    if (cudaMalloc(&da, a.size() * 4) != cudaSuccess || cudaMalloc(&db, b.size() * 4) != cudaSuccess ||
-        cudaMalloc(&dc, m * n * 4) != cudaSuccess) {
-        release();
-        return std::unexpected(GpuError::InsufficientMemory);
-    }
-    cublasHandle_t h = nullptr;
-    bool ok = cudaMemcpyAsync(da, a.data(), a.size() * 4, cudaMemcpyHostToDevice, stream_) == cudaSuccess &&
-              cudaMemcpyAsync(db, b.data(), b.size() * 4, cudaMemcpyHostToDevice, stream_) == cudaSuccess &&
-              cublasCreate(&h) == CUBLAS_STATUS_SUCCESS && cublasSetStream(h, stream_) == CUBLAS_STATUS_SUCCESS &&
-              cublasSetMathMode(h, CUBLAS_PEDANTIC_MATH) == CUBLAS_STATUS_SUCCESS;
-    if (ok) {
-        // Row-major C = op(A) op(B) is column-major C^T = op(B)^T op(A)^T.
-        const float one = 1.0f, zero = 0.0f;
-        const int lda = static_cast<int>(trans_a ? m : k_inner);
-        const int ldb = static_cast<int>(trans_b ? k_inner : n);
-        ok = cublasSgemm(h, trans_b ? CUBLAS_OP_T : CUBLAS_OP_N, trans_a ? CUBLAS_OP_T : CUBLAS_OP_N,
-                         static_cast<int>(n), static_cast<int>(m), static_cast<int>(k_inner), &one, db, ldb, da, lda,
-                         &zero, dc, static_cast<int>(n)) == CUBLAS_STATUS_SUCCESS &&
-             cudaMemcpyAsync(c.data(), dc, m * n * 4, cudaMemcpyDeviceToHost, stream_) == cudaSuccess &&
-             cudaStreamSynchronize(stream_) == cudaSuccess;
-    }
-    if (h != nullptr) cublasDestroy(h);
-    release();
-    if (!ok) return std::unexpected(GpuError::KernelLaunchFailed);
-    return {};
+    return to_expected(elips_b200_gemm_fp32(device_index_, a.data(), b.data(), c.data(), m, n, k_inner,
+                                            trans_a ? 1 : 0, trans_b ? 1 : 0, 0, nullptr));
 }
 
 void CudaBackend::synchronize() {

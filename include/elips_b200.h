@@ -245,6 +245,15 @@ ELIPS_B200_API int elips_b200_compute_distances_batch(int device, const float* q
                                                       size_t nq, size_t nb, size_t dim, int metric,
                                                       int pointers_on_device, void* stream);
 
+/* CudaBackend::gemm_fp32 (src/gpu_engine/backends/cuda/CudaBackend.hpp:42):
+ * row-major C[m][n] = op(A) op(B), op(A) m x k_inner (A stored k_inner x m
+ * when trans_a), op(B) k_inner x n (B stored n x k_inner when trans_b), fp32
+ * with fused multiply-add. Not on the search path (no reference class calls
+ * it); a plain SIMT kernel. Pointers as elips_b200_compute_distances_batch. */
+ELIPS_B200_API int elips_b200_gemm_fp32(int device, const float* a, const float* b, float* c, size_t m, size_t n,
+                                        size_t k_inner, int trans_a, int trans_b, int pointers_on_device,
+                                        void* stream);
+
 /* GpuPort::top_k (GpuPort.hpp:75-82): per row of an nq x nb distance matrix,
  * the k smallest values ascending with their column indexes (ties by index);
  * slots past nb hold index 0xFFFFFFFF and +inf. Pointer modes as above. */

@@ -60,3 +60,19 @@ def test_ivf_pq_index_on_the_b200_port(model):
     d1, r1 = cpu.search(q, 10, 4)
     d2, r2 = b200.search(q, 10, 4)
     assert np.array_equal(r1, r2) and np.array_equal(d1, d2)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_gemm_fp32_matches_float64(ta, tb):
+    """CudaBackend::gemm_fp32 runs on the library's fp32 kernel: row-major
+    C = op(A) op(B) within fp32 rounding of a float64 product."""
+    from elips_b200 import _capi
+    rng = np.random.default_rng(7 + 2 * ta + tb)
+    m, n, kk = 70, 131, 45
+    a = rng.standard_normal((kk, m) if ta else (m, kk)).astype(np.float32)
+    b = rng.standard_normal((n, kk) if tb else (kk, n)).astype(np.float32)
+    c = np.empty((m, n), np.float32)
+    assert _capi.LIB.elips_b200_gemm_fp32(0, a.ctypes.data, b.ctypes.data, c.ctypes.data, m, n, kk, ta, tb, 0,
+                                          None) == 0
+    ref = (a.T if ta else a).astype(np.float64) @ (b.T if tb else b).astype(np.float64)
+    np.testing.assert_allclose(c, ref, rtol=1e-5, atol=1e-4)
