@@ -233,7 +233,8 @@ __device__ __forceinline__ unsigned long long merge_composite(uint2 e) {
 }
 
 // Final top-k per query: one warp selects the k smallest (key, row) pairs
-// among `lists` candidate lists of length k and writes them sorted.
+// among `lists` candidate lists of `len` (>= k) entries each and writes
+// them sorted.
 // List l of query q starts at cand + q*stride_q + l*stride_l (entries).
 // With sub > 1 each query's lists are cut into `sub` groups of `lists` lists
 // (the last group: `lists_last`), one warp per (query, group), and output row
@@ -247,7 +248,7 @@ __device__ __forceinline__ unsigned long long merge_composite(uint2 e) {
 // Dynamic smem per warp: 256 words of histogram + kpow2 u64 sort buffer +
 // cache_cap u64 cache.
 __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, uint32_t lists,
-                                  uint32_t k, uint64_t stride_q, uint64_t stride_l, uint32_t kpow2,
+                                  uint32_t k, uint32_t len, uint64_t stride_q, uint64_t stride_l, uint32_t kpow2,
                                   uint32_t cache_cap, uint32_t sub, uint32_t lists_last, int metric,
                                   float* __restrict__ out_dist, int64_t* __restrict__ out_rows,
                                   uint2* __restrict__ out_cand) {
@@ -264,12 +265,12 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
     const uint32_t qq = q / sub, grp = q - qq * sub;
     const uint32_t my_lists = grp + 1u == sub ? lists_last : lists;
     const uint2* base = cand + qq * stride_q + static_cast<uint64_t>(grp) * lists * stride_l;
-    const uint32_t count = my_lists * k;
+    const uint32_t count = my_lists * len;
     const uint32_t take = min(k, count);
     uint32_t w = 0;
     if (take > 0) {
         if (count <= cache_cap) {
-            if (stride_l == k && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+            if (stride_l == len && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
                 const uint4* src = reinterpret_cast<const uint4*>(base);
                 const uint32_t pairs = count / 2u;
 #pragma unroll 4
@@ -282,7 +283,7 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
             } else {
 #pragma unroll 4
                 for (uint32_t j = lane; j < count; j += 32) {
-                    const uint32_t l = j / k, i = j - l * k;
+                    const uint32_t l = j / len, i = j - l * len;
                     cache[j] = merge_composite(base[l * stride_l + i]);
                 }
             }
@@ -291,7 +292,7 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
         } else {
             w = merge_select(
                 [&](uint32_t idx) -> unsigned long long {
-                    const uint32_t l = idx / k, i = idx - l * k;
+                    const uint32_t l = idx / len, i = idx - l * len;
                     return merge_composite(base[l * stride_l + i]);
                 },
                 count, take, hist, buf);

@@ -198,6 +198,21 @@ ExactPlan plan_exact(uint32_t nq, uint32_t n, uint32_t k, uint32_t bn, int group
     return p;
 }
 
+// Entries each (query, split, column half) list publishes. In a batch of
+// one query tile (8 to 128 queries) whose splits are at most 8 base tiles
+// long, compacting every list to k at the end of its unit (one list at a
+// time per warp) costs more than the unit's distances; there a list of up
+// to 2k entries (rounded up to 32) is published as it is and the merge,
+// which reads every list anyway, selects the k best. Otherwise k: longer
+// units compact rarely at their end, and the merge would read padding.
+// Measured on 100,000 x 384 bf16 L2, k = 20, per call: 64 queries 293 ->
+// 208 us, 8 queries 112 -> 102 us; at 1,000,000 rows (26 tiles per split)
+// 2k slots were 2-8 us slower, at one query 5 us slower.
+uint32_t publish_slot(const ExactPlan& p, uint32_t nq, uint32_t k) {
+    if (p.n_qt != 1 || p.cg != 1 || nq < 8 || p.n_bt > 8u * p.splits) return k;
+    return std::min<uint32_t>(p.cap, (2u * k + 31u) / 32u * 32u);
+}
+
 namespace {
 
 constexpr uint32_t kMaxK = 1024;
@@ -286,15 +301,15 @@ constexpr uint64_t kMergeCacheMax = 2048;
 // Lists merged per first-stage warp of a two-stage merge, or `lists` (one
 // stage). Two stages when a batch has too few queries to give every SM work
 // with one warp per query, or when a query's candidates do not fit the merge
-// kernel's shared-memory cache. Groups hold up to 16 lists and, where k
-// allows, at most 2048 / k so each group is merged from the cache (at least
+// kernel's shared-memory cache. Groups hold up to 16 lists and, where the
+// list length allows, at most 2048 / len so each group is merged from the cache (at least
 // 8 lists for small batches, at least 2 otherwise); the last group takes the
 // remainder.
-uint32_t merge_group_size(uint32_t nq, uint32_t lists, uint32_t k, int num_sms) {
+uint32_t merge_group_size(uint32_t nq, uint32_t lists, uint32_t len, int num_sms) {
     const bool few_queries = nq < 8u * static_cast<uint32_t>(num_sms) && lists >= 8;
-    const bool uncached = static_cast<uint64_t>(lists) * k > kMergeCacheMax && lists >= 4;
+    const bool uncached = static_cast<uint64_t>(lists) * len > kMergeCacheMax && lists >= 4;
     if (!few_queries && !uncached) return lists;
-    const uint32_t fit = static_cast<uint32_t>(kMergeCacheMax / std::max<uint32_t>(1u, k));
+    const uint32_t fit = static_cast<uint32_t>(kMergeCacheMax / std::max<uint32_t>(1u, len));
     const uint32_t g = std::min<uint32_t>(16u, std::max<uint32_t>(few_queries ? 8u : 2u, fit));
     return g < lists ? g : lists;
 }
@@ -308,16 +323,16 @@ uint32_t merge_group_size(uint32_t nq, uint32_t lists, uint32_t k, int num_sms) 
 // smallest overall.
 void merge_split_lists(int device, const uint2* part, uint2* stage, uint32_t nq, uint32_t n_lists,
                        uint32_t merge_group, uint32_t groups, uint32_t k, int metric, float* out_dist,
-                       int64_t* out_rows, uint2* out_cand, cudaStream_t stream) {
+                       int64_t* out_rows, uint2* out_cand, cudaStream_t stream, uint32_t len) {
     if (groups > 0) {
-        merge_candidates(device, part, nq, merge_group, k, static_cast<uint64_t>(n_lists) * k, k, metric, nullptr,
-                         nullptr, stage, stream, groups, n_lists - (groups - 1) * merge_group);
+        merge_candidates(device, part, nq, merge_group, k, static_cast<uint64_t>(n_lists) * len, len, metric, nullptr,
+                         nullptr, stage, stream, groups, n_lists - (groups - 1) * merge_group, len);
         merge_candidates(device, stage, nq, groups, k, static_cast<uint64_t>(groups) * k, k, metric, out_dist,
                          out_rows, out_cand, stream);
         return;
     }
-    merge_candidates(device, part, nq, n_lists, k, static_cast<uint64_t>(n_lists) * k, k, metric, out_dist, out_rows,
-                     out_cand, stream);
+    merge_candidates(device, part, nq, n_lists, k, static_cast<uint64_t>(n_lists) * len, len, metric, out_dist,
+                     out_rows, out_cand, stream, 1, 0, len);
 }
 
 // Pipeline depth: the stages that fit 192 KB of shared memory.
@@ -775,11 +790,11 @@ void ExactIndex::search_rows(const RowView& rv, const void* queries, size_t nq, 
     const size_t q_lo = kind_ == OperandKind::TF32X3 ? q_ops : 0;
     const size_t q_norm = metric_ == kEuclidean ? align(nq * sizeof(float)) : 0;
     const size_t cand = align(static_cast<size_t>(plan.grid) * 2 * kTileM * plan.cap * sizeof(uint2));
-    const size_t partial = align(nq * plan.splits * 2 * k * sizeof(uint2));
+    const uint32_t slot = publish_slot(plan, static_cast<uint32_t>(nq), static_cast<uint32_t>(k));
+    const size_t partial = align(nq * plan.splits * 2 * slot * sizeof(uint2));
     const size_t qtau = align(nq * sizeof(uint32_t));
     const uint32_t n_lists = plan.splits * 2;
-    const uint32_t merge_group = merge_group_size(static_cast<uint32_t>(nq), n_lists, static_cast<uint32_t>(k),
-                                                  props.num_sms);
+    const uint32_t merge_group = merge_group_size(static_cast<uint32_t>(nq), n_lists, slot, props.num_sms);
     const uint32_t groups = merge_group < n_lists ? (n_lists + merge_group - 1) / merge_group : 0;
     const size_t stage = align(static_cast<size_t>(nq) * groups * k * sizeof(uint2));
     StreamScratch scratch(q_ops + q_lo + q_norm + cand + partial + qtau + stage, stream);
@@ -821,12 +836,13 @@ void ExactIndex::search_rows(const RowView& rv, const void* queries, size_t nq, 
     prm.n_bt = plan.n_bt;
     prm.num_units = plan.n_qt * plan.splits;
     prm.kblocks = d_pad_ * elem_bytes_ / kKBlockBytes;
+    prm.slot = slot;
     prm.row_offset = row_offset;
     prm.metric = metric_;
     dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan, stream);
     uint2* stage_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand + partial + qtau);
     merge_split_lists(device_, part_buf, stage_buf, static_cast<uint32_t>(nq), n_lists, merge_group, groups,
-                      static_cast<uint32_t>(k), metric_, out_dist, out_rows, out_cand, stream);
+                      static_cast<uint32_t>(k), metric_, out_dist, out_rows, out_cand, stream, slot);
 }
 
 void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t k, const uint32_t* mask,
@@ -905,17 +921,20 @@ void ExactIndex::search_device_in_scratch(const void* queries, size_t nq, size_t
     prm.num_units = plan.n_qt * plan.splits;
     prm.kblocks = d_pad_ * elem_bytes_ / kKBlockBytes;
     prm.row_offset = 0;
+    prm.slot = prm.k;
     prm.metric = metric_;
     dispatch_exact(kind_, metric_, ma, mb, malo, mblo, prm, plan, stream);
     uint2* stage_buf = reinterpret_cast<uint2*>(s + q_ops + q_lo + q_norm + cand + partial + qtau);
     merge_split_lists(device_, part_buf, stage_buf, static_cast<uint32_t>(nq), n_lists, merge_group, groups,
-                      static_cast<uint32_t>(k), metric_, out_dist, out_rows, nullptr, stream);
+                      static_cast<uint32_t>(k), metric_, out_dist, out_rows, nullptr, stream,
+                      static_cast<uint32_t>(k));
 }
 
 void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,
                       uint64_t stride_q, uint64_t stride_l, int metric, float* out_dist,
                       int64_t* out_rows, uint2* out_cand, cudaStream_t stream, uint32_t sub,
-                      uint32_t lists_last) {
+                      uint32_t lists_last, uint32_t len) {
+    if (len == 0) len = k;
     if (nq == 0 || k == 0) return;
     if (sub == 0) sub = 1;
     if (sub == 1 || lists_last == 0) lists_last = lists;
@@ -925,14 +944,14 @@ void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists
     constexpr uint32_t warps = 4;
     // Up to 2048 candidates per query (16 KB) stay in shared memory for all
     // selection passes; larger merges read global memory on every pass.
-    const uint64_t count = static_cast<uint64_t>(std::max(lists, lists_last)) * k;
+    const uint64_t count = static_cast<uint64_t>(std::max(lists, lists_last)) * len;
     const uint32_t cache_cap = count <= kMergeCacheMax ? static_cast<uint32_t>((count + 1) / 2 * 2) : 0u;
     const size_t smem = warps * (1024 + static_cast<size_t>(kpow2) * 8 + static_cast<size_t>(cache_cap) * 8);
     allow_dynamic_smem(reinterpret_cast<const void*>(merge_topk_kernel), smem);
     const uint64_t rows_out = static_cast<uint64_t>(nq) * sub;
     const uint32_t blocks = static_cast<uint32_t>((rows_out + warps - 1) / warps);
-    Profiler::Scope prof("merge_topk", stream, static_cast<uint64_t>(nq) * ((sub - 1) * lists + lists_last) * k);
-    merge_topk_kernel<<<blocks, warps * 32, smem, stream>>>(cand, nq, lists, k, stride_q, stride_l, kpow2,
+    Profiler::Scope prof("merge_topk", stream, static_cast<uint64_t>(nq) * ((sub - 1) * lists + lists_last) * len);
+    merge_topk_kernel<<<blocks, warps * 32, smem, stream>>>(cand, nq, lists, k, len, stride_q, stride_l, kpow2,
                                                            cache_cap, sub, lists_last, metric, out_dist,
                                                            out_rows, out_cand);
     check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "merge kernel launch");

@@ -192,10 +192,11 @@ private:
 // Final merge over candidate lists (see merge_topk_kernel). With sub > 1,
 // the first stage of a two-stage merge: each query's lists in `sub` groups of
 // `lists` (the last: lists_last), output row q*sub + j per group.
+// len: entries per candidate list (0 = k).
 void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,
                       uint64_t stride_q, uint64_t stride_l, int metric, float* out_dist,
                       int64_t* out_rows, uint2* out_cand, cudaStream_t stream, uint32_t sub = 1,
-                      uint32_t lists_last = 0);
+                      uint32_t lists_last = 0, uint32_t len = 0);
 
 int read_and_clear_device_error(int device);
 // Launches a bounded wait that must expire after `budget` cycles and returns

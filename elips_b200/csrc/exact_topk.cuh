@@ -10,8 +10,10 @@
 //
 // Work decomposition. Queries are tiled by 128 (one TMEM lane each), base rows
 // by BN. The base is cut into S contiguous splits; a work unit is one
-// (query tile, split) pair and writes that split's k best candidates per
-// query to `partial[q][s][0..k)`. Units are ordered split-major so the CTAs
+// (query tile, split) pair and writes that split's candidates per query and
+// column half to `partial[q][s][h][0..slot)`: its k best, or, when a list
+// holds at most `slot` >= k entries, all of them, padded. Units are ordered
+// split-major so the CTAs
 // resident at any time share the same base region, which then streams from
 // HBM once and is re-read from L2 by every query tile.
 //
@@ -56,9 +58,10 @@ struct ExactParams {
     const uint32_t* mask;      // [ceil(n/32)] eligibility bits, or null
     const uint32_t* live;      // [ceil(n/32)] 0 bits = removed rows, or null (none removed)
     uint2* cand;               // [gridDim.x][2][128][cap] candidate lists per (column half, query)
-    uint2* partial;            // [nq][splits][2][k]
+    uint2* partial;            // [nq][splits][2][slot]
     uint32_t* qtau;            // [nq] shared admission bound per query (ordered key)
     uint32_t n, nq, k, cap, splits, n_qt, n_bt, num_units, kblocks;
+    uint32_t slot;             // entries per published list, k <= slot <= cap
     uint32_t row_offset;       // added to every emitted row (shard base)
     int metric;
 };
@@ -539,9 +542,10 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                 if constexpr (METRIC == kEuclidean) __syncwarp();
             }
             if (!ok) break;
-            // End of unit: reduce every list to its k best, then publish.
+            // End of unit: reduce every list longer than its slot to its k
+            // best, then publish (slot > k leaves short lists to the merge).
             __syncwarp();
-            uint32_t need = __ballot_sync(0xffffffffu, cnt > p.k);
+            uint32_t need = __ballot_sync(0xffffffffu, cnt > p.slot);
             while (need) {
                 const uint32_t L = __ffs(need) - 1;
                 const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
@@ -555,21 +559,21 @@ __global__ void __launch_bounds__(kExactThreads, 1)
             }
             __syncwarp();
             if (qvalid) {
-                uint2* out = p.partial + ((static_cast<size_t>(q) * p.splits + sp) * 2u + half) * p.k;
+                uint2* out = p.partial + ((static_cast<size_t>(q) * p.splits + sp) * 2u + half) * p.slot;
                 const uint2 none = make_uint2(0x7f800000u, 0xFFFFFFFFu);
-                if ((p.k & 1u) == 0u) {
-                    // k even: both the list (cap entries, cap a multiple of 32)
-                    // and this slot start on 16 bytes; two entries per access.
+                if ((p.slot & 1u) == 0u) {
+                    // slot even: both the list (cap entries, cap a multiple of
+                    // 32) and this slot start on 16 bytes; two entries per access.
                     const uint4* src = reinterpret_cast<const uint4*>(my_list);
                     uint4* dst = reinterpret_cast<uint4*>(out);
-                    for (uint32_t i = 0; i < p.k / 2u; ++i) {
+                    for (uint32_t i = 0; i < p.slot / 2u; ++i) {
                         uint4 e = src[i];
                         if (2u * i >= cnt) e.x = none.x, e.y = none.y;
                         if (2u * i + 1u >= cnt) e.z = none.x, e.w = none.y;
                         dst[i] = e;
                     }
                 } else {
-                    for (uint32_t i = 0; i < p.k; ++i) out[i] = i < cnt ? my_list[i] : none;
+                    for (uint32_t i = 0; i < p.slot; ++i) out[i] = i < cnt ? my_list[i] : none;
                 }
             }
             __syncwarp();
