@@ -368,7 +368,8 @@ def run_b200_ivfpq(args, cfg, world, rank, local, parity_q=None):
         owner = balanced_lists(torch.bincount(assign.long(), minlength=cfg["nlist"]).cpu().numpy(), world,
                                counts.cpu().numpy())
         index = ShardedIvfPqIndex(cfg["metric"], d, cent_np, cb_np, cfg["nprobe"], pq_bits=cfg["pq_bits"],
-                                  rank=rank, world=world, device=local, owner=owner)
+                                  rank=rank, world=world, device=local, owner=owner,
+                                  peer=False if args.exchange == "allgather" else None)
         for r0 in range(0, n, 1 << 21):
             index.add_device(base[r0:r0 + (1 << 21)], assign[r0:r0 + (1 << 21)], r0)
         lists = owner == rank
@@ -446,7 +447,9 @@ def run_b200_ivfpq(args, cfg, world, rank, local, parity_q=None):
     e2e = {"value": round(nq * args.steps / e2e_s, 2), "unit": "queries/s",
            "h2d_bytes_per_step": int(q_np.nbytes) * world, "d2h_bytes_per_step": int(nq * k * 12),
            "api": "elips_b200_ivfpq_search (host buffers)" if world == 1 else
-                  "ShardedIvfPqIndex.search_device from pinned host queries (NCCL all-gathers, merge kernels)"}
+                  "ShardedIvfPqIndex.search_device from pinned host queries (probe and candidate all-gathers, "
+                  + ("peer-memory bounds and hand-off to the root" if index.peer is not None else
+                     "NCCL all-gather of the k best") + ", merge kernels)"}
 
     peaks, peak_src = load_peaks()
     scan_ms = scan["total_ms"] / max(1, scan["launches"])
@@ -474,7 +477,9 @@ def run_b200_ivfpq(args, cfg, world, rank, local, parity_q=None):
                         "kmeans_rounds": cfg["kmeans_iters"], "pq_rounds": 10,
                         "api": "elips_b200_ivfpq_train (bit-identical to GpuIVFPQIndex::build_from_batch)"}}
     if world > 1:
-        result["config"]["parallelism"] = f"lists sharded over {world} GPUs (balanced by size^2)"
+        result["config"]["parallelism"] = (f"lists sharded over {world} GPUs (balanced by size x sampled probe "
+                                           f"count), exchange: {'peer' if index.peer is not None else 'allgather'}")
+        index.close()  # collective: unmap, then the root frees its exchange buffers
     if rank == 0 and ((not args.no_cpu_baseline and world == 1) or timed is not None):
         import oracle
         from oracle import parity

@@ -99,6 +99,8 @@ SIGNATURES = [
     ("elips_b200_ivfpq_probe_device", c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     ("elips_b200_ivfpq_search_candidates_probed_device", c_int,
      [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p]),
+    ("elips_b200_ivfpq_search_candidates_shared_device", c_int,
+     [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("elips_b200_ivfpq_remove", c_int, [c_void_p, c_size_t]),
     ("elips_b200_ivfpq_rebuild_codes", c_int, [c_void_p]),
     ("elips_b200_ivfflat_remove", c_int, [c_void_p, c_size_t]),

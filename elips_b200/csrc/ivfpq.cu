@@ -224,8 +224,12 @@ protected:
 
     // probes_in (optional, DEVICE [nq][nprobe]): probe lists computed
     // elsewhere (another rank's slice of the batch), used instead of probing.
+    // shared_bound (optional, DEVICE [nq], possibly another GPU's memory):
+    // per-query admission bounds shared with other shards searching the same
+    // batch, used instead of this search's own (and not reset here).
     Plan probe_and_plan(const float* queries, size_t nq, uint32_t r, uint32_t G, bool flat, uint8_t*& w,
-                        cudaStream_t stream, const uint32_t* probes_in = nullptr) {
+                        cudaStream_t stream, const uint32_t* probes_in = nullptr,
+                        uint32_t* shared_bound = nullptr) {
         Plan pl;
         pl.nprobe = std::min(nprobe_, nlist_);
         pl.npairs = nq * pl.nprobe;
@@ -256,7 +260,10 @@ protected:
         }
         check_cuda(cudaMemsetAsync(pl.counts, 0, static_cast<size_t>(nlist_) * 4, stream),
                    ELIPS_B200_KERNEL_LAUNCH_FAILED, "pair counts");
-        check_cuda(cudaMemsetAsync(pl.qbound, 0xFF, nq * 4, stream), ELIPS_B200_KERNEL_LAUNCH_FAILED, "query bounds");
+        if (shared_bound != nullptr) pl.qbound = shared_bound;
+        else
+            check_cuda(cudaMemsetAsync(pl.qbound, 0xFF, nq * 4, stream), ELIPS_B200_KERNEL_LAUNCH_FAILED,
+                       "query bounds");
         const uint32_t pblocks = static_cast<uint32_t>((pl.npairs + 255) / 256);
         const uint32_t* loff = static_cast<const uint32_t*>(list_off_.get());
         {
@@ -489,7 +496,7 @@ public:
     // over the probed lists this index owns, ascending, padded with
     // {+inf, 0xFFFFFFFF}. out_cand: [nq][R] DEVICE.
     void candidates(const float* queries, size_t nq, size_t k, uint2* out_cand, cudaStream_t stream,
-                    const uint32_t* probes_in = nullptr) {
+                    const uint32_t* probes_in = nullptr, uint32_t* shared_bound = nullptr) {
         if (nq == 0 || k == 0) return;
         check_search(queries, nq, k);
         DeviceGuard g(device_);
@@ -507,7 +514,7 @@ public:
         StreamScratch s(plan_bytes(nq, r, false), stream);
         uint8_t* w = s.get();
         // 1-2. probe and plan
-        const Plan pl = probe_and_plan(queries, nq, r, G, false, w, stream, probes_in);
+        const Plan pl = probe_and_plan(queries, nq, r, G, false, w, stream, probes_in, shared_bound);
         // 3. per (list, query group) approximate scan, R best per (query, list)
         IvfGroupParams p = group_params(queries, pl, r, capq, lut_stride);
         p.codebook = static_cast<const float*>(codebook_.get());
@@ -826,6 +833,18 @@ int elips_b200_ivfpq_search_candidates_probed_device(elips_b200_ivfpq* index, co
     return guarded([&] {
         index->index.candidates(queries, nq, k, reinterpret_cast<uint2*>(out_cand), static_cast<cudaStream_t>(stream),
                                 probes);
+    });
+}
+
+int elips_b200_ivfpq_search_candidates_shared_device(elips_b200_ivfpq* index, const float* queries, size_t nq,
+                                                     size_t k, const uint32_t* probes, uint32_t* out_cand,
+                                                     uint32_t* shared_bound, void* stream) {
+    if (index == nullptr) return ELIPS_B200_INVALID_ARGUMENT;
+    if (nq > 0 && k > 0 && (queries == nullptr || out_cand == nullptr || shared_bound == nullptr))
+        return ELIPS_B200_INVALID_ARGUMENT;
+    return guarded([&] {
+        index->index.candidates(queries, nq, k, reinterpret_cast<uint2*>(out_cand), static_cast<cudaStream_t>(stream),
+                                probes, shared_bound);
     });
 }
 

@@ -657,11 +657,14 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
             if constexpr (FLAT) s_pairoff[tid] = tid < ng ? p.pair_off[p.pairs[first + tid]] : 0u;
         }
         __syncthreads();
-        if (warp < ng) refresh_bound(warp, p.qbound[s_bound[G + warp]]);
+        // The query's bound (possibly another GPU's memory) is loaded before
+        // the lookup tables are built and applied after.
+        const uint32_t qb0 = warp < ng ? p.qbound[s_bound[G + warp]] : 0u;
         if constexpr (!FLAT) {
             build_group_lut<G>(lut, p.lut_stride, qv, cv, p.codebook, p.d, p.m, p.pq_bits, ng, p.metric);
-            __syncthreads();
         }
+        if (warp < ng) refresh_bound(warp, qb0);
+        if constexpr (!FLAT) __syncthreads();
 
         const uint32_t b0 = p.list_off[list], b1 = p.list_off[list + 1];
         bool qvalid[QP];

@@ -128,7 +128,8 @@ class PeerExchange:
             _, set_bytes = self._sizes(self.cap_q, self.k)
             recv_bytes, _ = self._sizes(self.cap_q, self.k)
             other = self.base + ((self.step_no + 1) & 1) * set_bytes + recv_bytes
-            capi.check(capi.LIB.elips_b200_fill_device(self.device, other, 0xFF, nq * 4, stream),
+            # every bound of the set: the next step may carry more queries
+            capi.check(capi.LIB.elips_b200_fill_device(self.device, other, 0xFF, self.cap_q * 4, stream),
                        "elips_b200_fill_device")
         self.dist.all_reduce(self.flag, group=self.group)
         self.step_no += 1
@@ -451,10 +452,18 @@ class ShardedIvfPqIndex:
     Before step 1 the probe itself is split: each rank probes a slice of the
     batch and the slices are exchanged (probe_slice, probe_table).
     The phases are methods, so a test can drive several ranks in one process;
-    `exchange` defaults to exchange_candidates over the process group."""
+    `exchange` defaults to exchange_candidates over the process group.
+
+    With a PeerExchange (`peer`; made by default for NCCL process groups
+    when `exchange` is not given) the ranks' scans share their per-query
+    admission bounds through the root's memory while they run (a bound any
+    rank publishes is the R-th key of R of its candidates, so no candidate of
+    the global R best is dropped), and step 4 becomes a copy of each rank's
+    k best into its slot of the root's buffer plus one 4-byte all-reduce."""
 
     def __init__(self, metric: str, dimension: int, centroids, codebook, nprobe: int, pq_bits: int = 8,
-                 rank: int = 0, world: int = 1, device: int = 0, group=None, exchange=None, owner=None):
+                 rank: int = 0, world: int = 1, device: int = 0, group=None, exchange=None, owner=None,
+                 peer=None):
         import torch
         from .ivfpq import IvfPqIndex
         self.metric, self.rank, self.world, self.group = metric, rank, world, group
@@ -470,8 +479,18 @@ class ShardedIvfPqIndex:
         self.local.set_owned_lists(owned)
         self.owned = torch.from_numpy(owned).to(f"cuda:{device}")
         self.global_rows = None  # int64 device tensor, ascending: local slot -> global slot
+        if peer is None and exchange is None and world > 1:
+            import torch.distributed as dist
+            if dist.is_initialized() and dist.get_backend(group) == "nccl":
+                peer = PeerExchange(rank, world, device, group)
+        self.peer = peer or None   # peer=False: NCCL all-gathers only
         self.exchange = exchange if exchange is not None else (
             lambda t: exchange_candidates(t, self.world, self.group))
+
+    def close(self) -> None:
+        """Collective: releases the peer buffers (every rank calls it)."""
+        if self.peer is not None:
+            self.peer.close()
 
     def add_device(self, vectors, assignments, first_row: int, codes=None) -> None:
         """Offers rows [first_row, first_row + n) in global order (CUDA tensors;
@@ -522,12 +541,13 @@ class ShardedIvfPqIndex:
         """The full probe table from the gathered slices [world, chunk, nprobe]."""
         return gathered.reshape(-1, gathered.shape[-1])[:nq].contiguous()
 
-    def approx_candidates(self, queries, k: int, probes=None):
+    def approx_candidates(self, queries, k: int, probes=None, shared_bound=None):
         """Phase 1: [nq, 4k, 2] int32 (distance bits, global slot). `probes`
         (the full [nq, nprobe] table, e.g. from probe_slice + exchange) skips
-        this rank's own probe of the whole batch."""
+        this rank's own probe of the whole batch; `shared_bound` (device
+        address of nq bounds shared by the ranks) replaces the scan's own."""
         import torch
-        cand = self.local.search_candidates_device(queries, k, probes=probes)
+        cand = self.local.search_candidates_device(queries, k, probes=probes, shared_bound=shared_bound)
         return _pairs(cand[..., 0].contiguous().view(torch.float32), self._to_global(cand[..., 1].long()))
 
     def rerank_owned(self, queries, k: int, gathered):
@@ -553,8 +573,31 @@ class ShardedIvfPqIndex:
         # The probe is split across the ranks (each probes a slice of the
         # batch against the replicated centroids) and exchanged.
         probes = self.probe_table(self.exchange(self.probe_slice(queries)), queries.shape[0])
+        if self.peer is not None:
+            return self._search_peer(queries, k, probes)
         mine = self.rerank_owned(queries, k, self.exchange(self.approx_candidates(queries, k, probes)))
         gathered = self.exchange(mine)
         if self.rank != 0:
             return None, None
         return self.merge_final(gathered, k)
+
+    def _search_peer(self, queries, k, probes):
+        import torch
+        from . import _capi as capi
+        nq = queries.shape[0]
+        self.peer.ensure(nq, k)
+        my_slot, bounds, blocks = self.peer.slots(nq)
+        approx = self.approx_candidates(queries, k, probes, shared_bound=bounds)
+        mine = self.rerank_owned(queries, k, self.exchange(approx)).contiguous()
+        stream = torch.cuda.current_stream(queries.device).cuda_stream
+        capi.check(capi.LIB.elips_b200_copy_device(self.local.device, my_slot, mine.data_ptr(), nq * k * 8, stream),
+                   "elips_b200_copy_device")
+        self.peer.finish_step(nq, stream)
+        if self.rank != 0:
+            return None, None
+        out_dist = torch.empty((nq, k), dtype=torch.float32, device=queries.device)
+        out_rows = torch.empty((nq, k), dtype=torch.int64, device=queries.device)
+        capi.check(capi.LIB.elips_b200_merge_candidates_device(
+            self.local.device, blocks, nq, self.world, k, METRICS_CODE["dot_product"], out_dist.data_ptr(),
+            out_rows.data_ptr(), stream), "elips_b200_merge_candidates_device")
+        return out_dist, out_rows

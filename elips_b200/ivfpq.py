@@ -114,16 +114,24 @@ class IvfPqIndex:
                    "elips_b200_ivfpq_probe_device")
         return out
 
-    def search_candidates_device(self, queries, k: int, out=None, stream=None, probes=None):
+    def search_candidates_device(self, queries, k: int, out=None, stream=None, probes=None, shared_bound=None):
         """The approximate stage: [nq, 4k, 2] int32 (distance bits, slot),
         ascending; `probes` ([nq, nprobe] int32 CUDA tensor, probe_device's
-        output) skips the probe."""
+        output) skips the probe. `shared_bound` (device address of nq uint32
+        admission bounds, possibly a peer GPU's, shared by the shards of one
+        list-sharded index searching this batch) replaces the search's own."""
         import torch
         nq = queries.shape[0]
         if out is None:
             out = torch.empty((nq, 4 * k, 2), dtype=torch.int32, device=queries.device)
         s = stream if stream is not None else torch.cuda.current_stream(queries.device).cuda_stream
-        if probes is None:
+        if shared_bound is not None:
+            if probes is not None:
+                probes = probes.contiguous()
+            capi.check(capi.LIB.elips_b200_ivfpq_search_candidates_shared_device(
+                self._h, queries.data_ptr(), nq, k, None if probes is None else probes.data_ptr(), out.data_ptr(),
+                shared_bound, s), "elips_b200_ivfpq_search_candidates_shared_device")
+        elif probes is None:
             capi.check(capi.LIB.elips_b200_ivfpq_search_candidates_device(self._h, queries.data_ptr(), nq, k,
                                                                           out.data_ptr(), s),
                        "elips_b200_ivfpq_search_candidates_device")

@@ -399,6 +399,23 @@ ELIPS_B200_API int elips_b200_ivfpq_search_candidates_probed_device(elips_b200_i
                                                                     size_t k, const uint32_t* probes,
                                                                     uint32_t* out_cand, void* stream);
 
+/* elips_b200_ivfpq_search_candidates_probed_device (probes may be NULL: this
+ * index probes) with the per-query admission bounds in `shared_bound`
+ * ([nq] uint32 ordered keys, all 0xFF before the first shard of a batch
+ * starts; DEVICE memory of this GPU or of a peer GPU mapped here) instead of
+ * the search's own: shards of one list-sharded index searching the same
+ * batch at the same time tighten each other's bounds with atomicMin. A bound
+ * any shard publishes is the R-th key of R of its candidates, so it is at or
+ * above the R-th key of the whole index and admission keeps keys equal to
+ * it: every shard's candidates among the index's R best are kept, and the
+ * merged result is the one an unshared search gives. The buffer is not
+ * reset here. */
+ELIPS_B200_API int elips_b200_ivfpq_search_candidates_shared_device(elips_b200_ivfpq* index,
+                                                                     const float* queries, size_t nq,
+                                                                     size_t k, const uint32_t* probes,
+                                                                     uint32_t* out_cand,
+                                                                     uint32_t* shared_bound, void* stream);
+
 /* The exact stage (exact_rank, GpuIVFPQIndex.cpp:37-71): for nq x R pairs
  * {any, slot} (slot 0xFFFFFFFF or past size = none), exact distances on this
  * index's raw rows, the k best ascending by (distance, slot). DEVICE. */

@@ -154,6 +154,21 @@ def test_list_sharded_search_equals_single_index(model, world, balanced, metric)
     d, r = ShardedIvfPqIndex.merge_final(mine, k)
     torch.cuda.synchronize()
     assert np.array_equal(r.cpu().numpy(), r_ref) and np.array_equal(d.cpu().numpy(), d_ref)
+    # Bounds shared by the ranks' scans (one after another here, so later
+    # ranks start from the earlier ones' tight bounds): the merged R best and
+    # the final result are unchanged.
+    from elips_b200.exact import merge_candidates_device
+    bound = torch.full((qd.shape[0],), -1, dtype=torch.int32, device="cuda")
+    shared = torch.stack([ix.approx_candidates(qd, k, probes, shared_bound=bound.data_ptr()) for ix in ranks])
+    rk = 4 * k
+    ua, ub = merge_candidates_device(gathered, world, rk, "dot_product")
+    sa, sb = merge_candidates_device(shared, world, rk, "dot_product")
+    assert torch.equal(ub, sb) and torch.equal(ua.view(torch.int32), sa.view(torch.int32))
+    assert int((bound != -1).sum()) == qd.shape[0]        # every query's bound was tightened
+    mine = torch.stack([ix.rerank_owned(qd, k, shared) for ix in ranks])
+    d, r = ShardedIvfPqIndex.merge_final(mine, k)
+    torch.cuda.synchronize()
+    assert np.array_equal(r.cpu().numpy(), r_ref) and np.array_equal(d.cpu().numpy(), d_ref)
 
 
 @pytest.mark.parametrize("flat", [False, True])

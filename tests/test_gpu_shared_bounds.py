@@ -84,3 +84,27 @@ def test_peer_exchange_two_processes_equals_single_index(tmp_path):
         d_ref, r_ref = whole.search_batch(queries, k)
         assert np.array_equal(got[f"rows{k}"], r_ref)
         assert np.array_equal(got[f"dist{k}"].view(np.uint32), d_ref.view(np.uint32))
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_ivfpq_peer_exchange_two_processes_equals_single_index(tmp_path):
+    """Two ranks (NCCL, one GPU each) of a list-sharded IVF-PQ index on the
+    tie-heavy model: their scans share the per-query bounds in rank 0's
+    memory and their k best reach rank 0 over peer memory; rank 0's result
+    equals one index over all lists, ids and distances."""
+    script = os.path.join(os.path.dirname(__file__), "ivfpq_peer_worker.py")
+    out = tmp_path / "result.npz"
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT="29534", NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr", "127.0.0.1", "--master-port", "29534", script, str(out)],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    got = np.load(out)
+    from elips_b200.ivfpq import IvfPqIndex
+    m = H.ivfpq_tie_model()
+    single = IvfPqIndex("euclidean", 64, m["cent"], m["cb"], nprobe=8)
+    single.add(m["base"], m["asg"], m["codes"])
+    for k in (10, 20):
+        d_ref, r_ref = single.search_batch(m["queries"], k)
+        assert np.array_equal(got[f"rows{k}"], r_ref)
+        assert np.array_equal(got[f"dist{k}"].view(np.uint32), d_ref.view(np.uint32))
