@@ -31,6 +31,7 @@
 #include <cstdint>
 #include <type_traits>
 
+#include "ptx.cuh"
 #include "scan_kernels.cuh"
 
 namespace eb {
@@ -599,6 +600,12 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
     uint32_t* s_bound = reinterpret_cast<uint32_t*>(smem + L.bound);  // [G] z bound, [G] query ids
     uint32_t* s_item = reinterpret_cast<uint32_t*>(smem + L.item);    // next item: live, list, first, ng
     __shared__ uint32_t s_pairoff[G];                                 // flat: gather offset of each pair
+    // Round barrier, split in two: a warp arrives when its appends of round g
+    // are done and waits for the others only before appending in round g + 1,
+    // so its lookups of round g + 1 overlap the slower warps' round g.
+    __shared__ __align__(8) uint64_t s_rbar;
+    __shared__ uint32_t s_need[2];   // [g & 1] = g: an append of round g left a buffer short of a round's room
+    __shared__ int s_abort;
 
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t pq = lane % P, j = lane / P;  // this lane: quad pq of candidate j
@@ -638,8 +645,15 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
         s_item[3] = ng;
     };
 
-    if (tid == 0) fetch_item();
+    const uint32_t rbar = smem_u32(&s_rbar);
+    if (tid == 0) {
+        mbar_init(rbar, kGroupWarps);
+        s_need[0] = s_need[1] = 0xFFFFFFFFu;
+        s_abort = 0;
+        fetch_item();
+    }
     __syncthreads();
+    uint32_t g = 0;  // rounds so far (the same count in every warp)
     for (;;) {
         if (s_item[0] == 0) break;
         const uint32_t list = s_item[1], first = s_item[2], ng = s_item[3];
@@ -757,6 +771,31 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
                         if (pass && pos < b1 && qvalid[qi]) amask |= 1u << (st * QP + qi);
                     }
                 }
+                // Every warp's appends of the previous round are done (it
+                // arrived after them); a warp that saw a buffer left with less
+                // than a round of room stamped s_need with that round, so all
+                // warps take the same decision: the short buffers are compacted
+                // (one warp each) before anyone appends again. The stamp of
+                // round g - 1 cannot be overwritten before every warp read it:
+                // round g + 1's appends wait for every warp's round g arrival.
+                ++g;
+                if (g > 1) {
+                    if (!mbar_wait_for(rbar, g & 1u, &s_abort, kWaitTimeoutCycles)) amask = 0;
+                    if (s_need[(g - 1u) & 1u] == g - 1u) {
+                        if (warp < ng && s_cnt[warp] + kRound > p.capq) {
+                            const uint32_t t =
+                                warp_select_compact(buf + warp * p.capq, s_cnt[warp], p.r, hist + warp * 256u);
+                            if (lane == 0) {
+                                s_cnt[warp] = p.r;
+                                s_thr[warp] = t;
+                                atomicMin(&p.qbound[s_bound[G + warp]], t);
+                            }
+                            __syncwarp();
+                        }
+                        __syncthreads();
+                    }
+                    if (warp < ng) refresh_bound(warp, qb);
+                }
                 const bool appended = __any_sync(0xffffffffu, amask != 0);
                 bool need = false;  // some count this warp saw leaves less than a round of room
                 if (appended) {
@@ -784,23 +823,11 @@ __global__ void __launch_bounds__(kGroupThreads, 1) ivfpq_group_scan_kernel(cons
                     }
                 }
                 // Counts only grow within a round, so the last appender to a
-                // buffer sees its final count: the OR over the block is exactly
-                // "some buffer has less than a round of room left". Otherwise
-                // no compaction and no second barrier.
-                if (__syncthreads_or(need)) {
-                    if (warp < ng && s_cnt[warp] + kRound > p.capq) {
-                        const uint32_t t =
-                            warp_select_compact(buf + warp * p.capq, s_cnt[warp], p.r, hist + warp * 256u);
-                        if (lane == 0) {
-                            s_cnt[warp] = p.r;
-                            s_thr[warp] = t;
-                            atomicMin(&p.qbound[s_bound[G + warp]], t);
-                        }
-                        __syncwarp();
-                    }
-                    __syncthreads();
-                }
-                if (warp < ng) refresh_bound(warp, qb);
+                // buffer sees its final count: the stamps of a round say
+                // exactly "some buffer has less than a round of room left".
+                if (need) s_need[g & 1u] = g;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(rbar);
             }
         };
         if (p.metric == kMetricL2)
