@@ -405,16 +405,26 @@ def list_range(nlist: int, rank: int, world: int) -> tuple[int, int]:
     return nlist * rank // world, nlist * (rank + 1) // world
 
 
-def balanced_lists(list_sizes, world: int, probe_counts=None) -> np.ndarray:
+def balanced_lists(list_sizes, world: int, probe_counts=None, queries_per_item: int = 0,
+                   item_rows: int = 1024) -> np.ndarray:
     """Owner rank of every IVF list, balancing the scan work: a probed list
     costs its size times the queries that probe it. With `probe_counts` (how
     often each list was probed by a sample of queries) the weight is
     size x count; without it, queries are taken to probe lists about in
-    proportion to their size and the weight is size^2. Greedy longest-first:
-    heaviest list to the least loaded rank (ties: lower list id, lower rank).
-    Deterministic, so every rank computes the same partition."""
+    proportion to their size and the weight is size^2. With
+    `queries_per_item` (the scan's group size G: a scan item streams a list
+    once for up to G of its queries, and costs the same for fewer) the weight
+    is ceil(count / G) x (size + item_rows), item_rows standing for an item's
+    fixed cost (its lookup tables, start and write-out) in list rows.
+    Greedy longest-first: heaviest list to the least loaded rank (ties: lower
+    list id, lower rank). Deterministic, so every rank computes the same
+    partition."""
     sizes = np.asarray(list_sizes, np.float64)
-    weight = sizes * (sizes if probe_counts is None else np.asarray(probe_counts, np.float64))
+    if probe_counts is not None and queries_per_item > 0:
+        items = np.ceil(np.asarray(probe_counts, np.float64) / queries_per_item)
+        weight = items * np.where(sizes > 0, sizes + item_rows, 0.0)
+    else:
+        weight = sizes * (sizes if probe_counts is None else np.asarray(probe_counts, np.float64))
     order = np.lexsort((np.arange(sizes.size), -weight))
     load = np.zeros(world)
     owner = np.empty(sizes.size, np.int64)
@@ -479,6 +489,7 @@ class ShardedIvfPqIndex:
         self.local.set_owned_lists(owned)
         self.owned = torch.from_numpy(owned).to(f"cuda:{device}")
         self.global_rows = None  # int64 device tensor, ascending: local slot -> global slot
+        self._local_of = None    # int32 device tensor: global slot -> local slot or -1
         if peer is None and exchange is None and world > 1:
             import torch.distributed as dist
             if dist.is_initialized() and dist.get_backend(group) == "nccl":
@@ -503,6 +514,7 @@ class ShardedIvfPqIndex:
                               None if codes is None else codes[idx].contiguous())
         g = idx + first_row
         self.global_rows = g if self.global_rows is None else torch.cat((self.global_rows, g))
+        self._local_of = None
 
     def _to_global(self, rows):
         import torch
@@ -511,12 +523,19 @@ class ShardedIvfPqIndex:
         return torch.where(rows >= 0, self.global_rows[rows.clamp(min=0)], rows)
 
     def _to_local(self, rows):
+        """Global slots -> this rank's slots (-1: none, or held by another
+        rank), through a dense map over the global slots built once per
+        change of the rows."""
         import torch
         if self.global_rows is None:
             return torch.full_like(rows, -1)
-        pos = torch.searchsorted(self.global_rows, rows.clamp(min=0)).clamp(max=self.global_rows.numel() - 1)
-        held = (rows >= 0) & (self.global_rows[pos] == rows)
-        return torch.where(held, pos, torch.full_like(pos, -1))
+        if self._local_of is None:
+            top = int(self.global_rows.max().item()) + 1
+            self._local_of = torch.full((top + 1,), -1, dtype=torch.int32, device=self.global_rows.device)
+            self._local_of[self.global_rows] = torch.arange(self.global_rows.numel(), dtype=torch.int32,
+                                                            device=self.global_rows.device)
+        top = self._local_of.numel() - 1           # the last entry stays -1: rows past this rank's last
+        return self._local_of[rows.clamp(min=0, max=top)].long().masked_fill_(rows < 0, -1)
 
     @staticmethod
     def probe_rows(nq: int, rank: int, world: int) -> tuple[int, int, int]:

@@ -136,6 +136,12 @@ def test_balanced_lists_partition():
         load = np.bincount(owner, weights=sizes.astype(float) ** 2, minlength=world)
         assert load.max() <= load.mean() + (sizes.astype(float) ** 2).max()
         assert np.array_equal(owner, balanced_lists(sizes, world))
+        # item-aware weights: ceil(count / G) items, each costing size + item_rows
+        counts = rng.integers(0, 200, sizes.size)
+        owner = balanced_lists(sizes, world, counts, queries_per_item=8, item_rows=1024)
+        w = np.ceil(counts / 8) * np.where(sizes > 0, sizes + 1024.0, 0.0)
+        load = np.bincount(owner, weights=w, minlength=world)
+        assert load.max() <= load.mean() + w.max()
 
 
 def _probe_worker(rank, world, port, out_dir):
