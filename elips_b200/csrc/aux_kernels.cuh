@@ -404,19 +404,44 @@ __global__ void __launch_bounds__(kSelectThreads) select_rows_kernel(const uint3
     }
 }
 
-// One warp per selected row: copies its operand row (row_bytes, a multiple
-// of 16) and, when norms is given, its squared norm.
+// Selected rows per warp of gather_rows_kernel, and 16-byte loads a lane
+// keeps in flight before its stores.
+constexpr uint32_t kGatherRowsPerWarp = 4;
+constexpr uint32_t kGatherLoadsPerLane = 8;
+
+// One warp per kGatherRowsPerWarp selected rows: copies their operand rows
+// (row_bytes, a multiple of 16) and, when norms is given, their squared
+// norms. The warp's rows are one flat run of 16-byte chunks; every lane
+// issues up to kGatherLoadsPerLane loads before storing them, so a warp has
+// whole rows in flight rather than one load per lane.
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                    const uint32_t* __restrict__ rows, uint32_t m, uint32_t row_bytes,
                                    const float* __restrict__ norms, float* __restrict__ norms_out) {
     const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t lane = threadIdx.x & 31u;
-    if (warp >= m) return;
-    const uint32_t r = rows[warp];
-    const uint4* s = reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * row_bytes);
-    uint4* d = reinterpret_cast<uint4*>(dst + static_cast<size_t>(warp) * row_bytes);
-    for (uint32_t i = lane; i < row_bytes / 16u; i += 32u) d[i] = __ldg(s + i);
-    if (norms != nullptr && lane == 0) norms_out[warp] = norms[r];
+    const uint32_t r0 = warp * kGatherRowsPerWarp;
+    if (r0 >= m) return;
+    const uint32_t nr = min(kGatherRowsPerWarp, m - r0);
+    const uint32_t my_src = lane < nr ? rows[r0 + lane] : 0u;
+    if (norms != nullptr && lane < nr) norms_out[r0 + lane] = norms[my_src];
+    const uint32_t chunks = row_bytes / 16u, total = nr * chunks;
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst) + static_cast<size_t>(r0) * chunks;
+    for (uint32_t base = 0; base < total; base += 32u * kGatherLoadsPerLane) {
+        uint4 v[kGatherLoadsPerLane];
+#pragma unroll
+        for (uint32_t u = 0; u < kGatherLoadsPerLane; ++u) {
+            const uint32_t f = base + u * 32u + lane;
+            const uint32_t rr = f / chunks;
+            const uint32_t sr = __shfl_sync(0xffffffffu, my_src, rr & 31u);
+            if (f < total) v[u] = __ldg(s + static_cast<size_t>(sr) * chunks + (f - rr * chunks));
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kGatherLoadsPerLane; ++u) {
+            const uint32_t f = base + u * 32u + lane;
+            if (f < total) d[f] = v[u];
+        }
+    }
 }
 
 // Rows of a search over the gathered subset back to index slots (+ offset):

@@ -757,7 +757,8 @@ bool ExactIndex::search_gathered(const void* queries, size_t nq, size_t k, const
     float* g_norms = norms_b ? reinterpret_cast<float*>(g_ops + ops_b + lo_b) : nullptr;
     {
         Profiler::Scope prof("mask_gather", stream, static_cast<uint64_t>(m) * row_bytes);
-        const uint32_t blocks = static_cast<uint32_t>((static_cast<uint64_t>(m) * 32 + 255) / 256);
+        const uint64_t warps = (static_cast<uint64_t>(m) + kGatherRowsPerWarp - 1) / kGatherRowsPerWarp;
+        const uint32_t blocks = static_cast<uint32_t>((warps * 32 + 255) / 256);
         gather_rows_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint8_t*>(ops_.get()), g_ops, rows, m,
                                                        static_cast<uint32_t>(row_bytes),
                                                        static_cast<const float*>(norms_.get()), g_norms);
