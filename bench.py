@@ -393,18 +393,20 @@ def run_b200_ivfpq(args, cfg, world, rank, local, parity_q=None):
         else:
             last[0] = index.search_device(q_dev, k)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    _capi.profiler_reset()
-    _capi.profiler_enable(True)
-    launches0 = _capi.launch_count()
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
     with sampler:
+        # the clock sampler's first reading, then the warm-up steps, then the
+        # ranks enter the timed steps together (barrier right before them)
         time.sleep(0.25)
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        _capi.profiler_reset()
+        _capi.profiler_enable(True)
+        launches0 = _capi.launch_count()
         sampler.active = True
         ev0.record(stream)
         for _ in range(args.steps):
@@ -676,19 +678,21 @@ def run_b200(args, cfg, world, rank, local, parity_q=None):
             last[0] = index.search_device(q_dev, k, mask=mask_dev)
 
     # ---- device-resident throughput (value), with the kernel profiler live
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    _capi.profiler_reset()
-    _capi.profiler_enable(True)
-    launches0 = _capi.launch_count()
     stream = torch.cuda.current_stream(dev)
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
     with sampler:
+        # the clock sampler's first reading, then the warm-up steps, then the
+        # ranks enter the timed steps together (barrier right before them)
         time.sleep(0.25)
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        _capi.profiler_reset()
+        _capi.profiler_enable(True)
+        launches0 = _capi.launch_count()
         sampler.active = True
         ev0.record(stream)
         for _ in range(args.steps):
