@@ -62,6 +62,7 @@ struct ExactParams {
     uint32_t* qtau;            // [nq] shared admission bound per query (ordered key)
     uint32_t n, nq, k, cap, splits, n_qt, n_bt, num_units, kblocks;
     uint32_t slot;             // entries per published list, k <= slot <= cap
+    uint32_t early;            // first compaction of a list in a unit once it holds more (0: none early)
     uint32_t row_offset;       // added to every emitted row (shard base)
     int metric;
 };
@@ -524,9 +525,13 @@ __global__ void __launch_bounds__(kExactThreads, 1)
                         }
                     }
                 }
-                // Keep room for one more half-tile: compact any list that could overflow.
+                // Keep room for one more half-tile: compact any list that could
+                // overflow, and a list not yet compacted in this unit once it
+                // holds more than `early` entries, which gives it a threshold
+                // (its k-th key) long before it would otherwise fill.
                 __syncwarp();
-                uint32_t need = __ballot_sync(0xffffffffu, cnt + kHalfCols > p.cap);
+                const bool first = p.early != 0u && cnt > p.early && tau == __int_as_float(0x7f800000);
+                uint32_t need = __ballot_sync(0xffffffffu, cnt + kHalfCols > p.cap || first);
                 while (need) {
                     const uint32_t L = __ffs(need) - 1;
                     const uint32_t cnt_l = __shfl_sync(0xffffffffu, cnt, L);
