@@ -242,7 +242,8 @@ __device__ __forceinline__ unsigned long long merge_composite(uint2 e) {
 // Composite 64-bit keys (ordered key << 32 | row) are unique except the
 // padding {+inf, 0xFFFFFFFF}. When a query has at most `cache_cap`
 // candidates they are read from global memory once (16-byte loads where the
-// lists are contiguous and aligned) into the warp's shared-memory cache, and
+// lists are contiguous and aligned) into the warp's shared-memory cache,
+// padding dropped (all of them are kept when no more than k are real), and
 // every selection pass reads them there; otherwise each pass reads them from
 // global memory.
 // Dynamic smem per warp: 256 words of histogram + kpow2 u64 sort buffer +
@@ -270,25 +271,56 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
     uint32_t w = 0;
     if (take > 0) {
         if (count <= cache_cap) {
+            // Only real candidates enter the cache (padding, row all ones,
+            // is dropped here), so the selection passes walk the real ones:
+            // lists from shards that own few of a query's probes, or
+            // published shorter than their slot, are mostly padding.
+            const uint32_t lt = lanemask_lt();
+            uint32_t fill = 0;
+            auto put = [&](uint2 e) {
+                const bool real = e.y != 0xFFFFFFFFu;
+                const uint32_t m = __ballot_sync(0xffffffffu, real);
+                if (real) cache[fill + __popc(m & lt)] = merge_composite(e);
+                fill += __popc(m);
+            };
+            const uint2 none = make_uint2(0x7f800000u, 0xFFFFFFFFu);
             if (stride_l == len && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
                 const uint4* src = reinterpret_cast<const uint4*>(base);
                 const uint32_t pairs = count / 2u;
-#pragma unroll 4
-                for (uint32_t i = lane; i < pairs; i += 32) {
-                    const uint4 v = src[i];
-                    cache[2u * i] = merge_composite(make_uint2(v.x, v.y));
-                    cache[2u * i + 1u] = merge_composite(make_uint2(v.z, v.w));
+                for (uint32_t i0 = 0; i0 < pairs; i0 += 128) {
+                    uint4 v[4];
+#pragma unroll
+                    for (uint32_t u = 0; u < 4; ++u) {
+                        const uint32_t i = i0 + u * 32u + lane;
+                        v[u] = i < pairs ? src[i] : make_uint4(none.x, none.y, none.x, none.y);
+                    }
+#pragma unroll
+                    for (uint32_t u = 0; u < 4; ++u) {
+                        put(make_uint2(v[u].x, v[u].y));
+                        put(make_uint2(v[u].z, v[u].w));
+                    }
                 }
-                if ((count & 1u) && lane == 0) cache[count - 1u] = merge_composite(base[count - 1u]);
+                if (count & 1u) put(lane == 0 ? base[count - 1u] : none);
             } else {
-#pragma unroll 4
-                for (uint32_t j = lane; j < count; j += 32) {
-                    const uint32_t l = j / len, i = j - l * len;
-                    cache[j] = merge_composite(base[l * stride_l + i]);
+                for (uint32_t j0 = 0; j0 < count; j0 += 128) {
+                    uint2 v[4];
+#pragma unroll
+                    for (uint32_t u = 0; u < 4; ++u) {
+                        const uint32_t j = j0 + u * 32u + lane;
+                        const uint32_t l = j / len, i = j - l * len;
+                        v[u] = j < count ? base[l * stride_l + i] : none;
+                    }
+#pragma unroll
+                    for (uint32_t u = 0; u < 4; ++u) put(v[u]);
                 }
             }
             __syncwarp();
-            w = merge_select([&](uint32_t j) -> unsigned long long { return cache[j]; }, count, take, hist, buf);
+            if (fill <= take) {  // every real candidate is kept
+                for (uint32_t j = lane; j < fill; j += 32) buf[j] = cache[j];
+                w = fill;
+            } else {
+                w = merge_select([&](uint32_t j) -> unsigned long long { return cache[j]; }, fill, take, hist, buf);
+            }
         } else {
             w = merge_select(
                 [&](uint32_t idx) -> unsigned long long {
