@@ -55,6 +55,18 @@ def exchange_candidates(cand, world: int, group=None):
     return flat.view((world,) + tuple(cand.shape))
 
 
+def peer_set_layout(world: int, nq: int, k: int) -> tuple[int, int]:
+    """(bytes before the bounds, bytes of one buffer set) of PeerExchange's
+    root buffer: the candidate blocks (world x nq x k pairs of 8 bytes), then
+    nq 4-byte bounds, each part rounded up to 256 bytes so that the second
+    set, the bounds and every block start aligned whatever nq is (the merge
+    kernel reads the blocks with 8- and 16-byte loads)."""
+    def up(x):
+        return (x + 255) // 256 * 256
+    recv = up(world * nq * k * 8)
+    return recv, up(recv + nq * 4)
+
+
 class PeerExchange:
     """The shard exchange over NVLink peer memory (one process per GPU of one
     node): the root owns, twice over (alternating steps), a receive buffer for
@@ -80,8 +92,7 @@ class PeerExchange:
         self.flag = torch.zeros(1, dtype=torch.int32, device=f"cuda:{device}")
 
     def _sizes(self, nq, k):
-        recv = self.world * nq * k * 8
-        return recv, recv + nq * 4  # one set: candidate blocks, then bounds
+        return peer_set_layout(self.world, nq, k)
 
     def ensure(self, nq: int, k: int) -> None:
         """(Re)creates the buffers for batches of up to nq queries at this k."""

@@ -26,6 +26,14 @@ def main(out_path):
         assert ix.exchange == "peer"
         ix.add_device(torch.from_numpy(base[ix.row_begin:ix.row_end]).cuda())
         res = {}
+        # a single-query batch first: the buffers are sized for one query, so
+        # both sets' layout has to stay aligned for an odd batch size
+        d1, r1 = ix.search_device(queries[:1], 20)
+        d1b, r1b = ix.search_device(queries[:1], 20)
+        torch.cuda.synchronize()
+        if dist.get_rank() == 0:
+            res["dist1"], res["rows1"] = d1b.cpu().numpy(), r1b.cpu().numpy()
+            assert np.array_equal(d1.cpu().numpy(), res["dist1"])
         for k in (10, 100):
             for _ in range(3):          # several steps: both buffer sets, bounds reset between steps
                 dd, rr = ix.search_device(queries, k)

@@ -275,3 +275,17 @@ def test_slice_mask_rebases_each_rank():
                 assert sub.shape == ((hi - lo + 31) // 32,)
                 got = [(int(sub[j >> 5]) >> (j & 31)) & 1 for j in range(hi - lo)]
                 assert got == bits[lo:hi].astype(int).tolist()
+
+
+def test_peer_set_layout_keeps_every_part_aligned():
+    """The root's exchange buffer holds two sets of (candidate blocks, bounds);
+    with odd batch sizes (a single query) the second set and the bounds must
+    still start on 256 bytes, or the merge kernel's 8-byte loads of the second
+    set fault."""
+    from elips_b200.distributed import peer_set_layout
+    for world in (2, 3, 8):
+        for nq in (1, 3, 7, 8, 63, 64, 500, 10_000):
+            for k in (1, 10, 20, 100):
+                recv, set_bytes = peer_set_layout(world, nq, k)
+                assert recv % 256 == 0 and set_bytes % 256 == 0
+                assert recv >= world * nq * k * 8 and set_bytes >= recv + nq * 4

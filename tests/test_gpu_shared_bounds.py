@@ -84,6 +84,9 @@ def test_peer_exchange_two_processes_equals_single_index(tmp_path):
         d_ref, r_ref = whole.search_batch(queries, k)
         assert np.array_equal(got[f"rows{k}"], r_ref)
         assert np.array_equal(got[f"dist{k}"].view(np.uint32), d_ref.view(np.uint32))
+    d_ref, r_ref = whole.search_batch(queries[:1], 20)
+    assert np.array_equal(got["rows1"], r_ref)
+    assert np.array_equal(got["dist1"].view(np.uint32), d_ref.view(np.uint32))
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
