@@ -313,7 +313,7 @@ def ivfpq_inputs(cfg, dev, train=True):
     return (base, queries) + train_ivfpq_model(cfg, base)
 
 
-def _capi_num_sms(device):
+def _num_sms(device):
     import torch
     return torch.cuda.get_device_properties(device).multi_processor_count
 
@@ -470,7 +470,7 @@ def run_b200_ivfpq(args, cfg, world, rank, local, parity_q=None):
     pairs = alg_bytes // (cfg["pq_dim"] + 4)
     lookups = pairs * cfg["pq_dim"]
     sm_hz = (clk["sm_mhz"] or 1965) * 1e6
-    floor_ms = lookups * 0.0655 / (_capi_num_sms(local) * sm_hz) * 1e3
+    floor_ms = lookups * 0.0655 / (_num_sms(local) * sm_hz) * 1e3
     probed_pairs = nq * min(cfg["nprobe"], cfg["nlist"])
     lookup_floor = {"lookups": int(lookups), "wavefronts_per_lookup": 0.0655, "sm_mhz": clk["sm_mhz"],
                     "floor_ms": round(floor_ms, 3), "frac": round(floor_ms / scan_ms, 4),
