@@ -351,6 +351,48 @@ __global__ void merge_topk_kernel(const uint2* __restrict__ cand, uint32_t nq, u
     }
 }
 
+// One warp per row of a distance matrix: the k smallest (value, index) of
+// dist[q][0..nb), sorted, padded with {index 0xFFFFFFFF, +inf}. Values of
+// +inf and NaN are never taken, as the block top-k's strict "< threshold"
+// offer never takes them, so both kernels return the same rows. The row is
+// read from global memory (L2) by every selection pass. Dynamic smem per
+// warp: 256 words of histogram + kpow2 u64 sort buffer.
+__global__ void topk_rows_warp_kernel(const float* __restrict__ dist, uint32_t nq, uint32_t nb, uint32_t k,
+                                      uint32_t kpow2, uint32_t* __restrict__ idx_out,
+                                      float* __restrict__ val_out) {
+    extern __shared__ uint8_t smem[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t warps = blockDim.x >> 5;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem) + warp * 256u;
+    unsigned long long* buf =
+        reinterpret_cast<unsigned long long*>(smem + warps * 1024u) + static_cast<size_t>(warp) * kpow2;
+    const uint32_t q = blockIdx.x * warps + warp;
+    if (q >= nq) return;
+    const float* row = dist + static_cast<size_t>(q) * nb;
+    uint32_t w = 0;
+    if (nb > 0) {
+        w = merge_select(
+            [&](uint32_t j) -> unsigned long long {
+                const float v = __ldg(row + j);
+                return v < __int_as_float(0x7f800000)
+                           ? (static_cast<unsigned long long>(ordered_key(v)) << 32) | j
+                           : ~0ull;
+            },
+            nb, min(k, nb), hist, buf);
+    }
+    for (uint32_t i = w + lane; i < kpow2; i += 32) buf[i] = ~0ull;
+    __syncwarp();
+    warp_bitonic_sort(buf, kpow2);
+    for (uint32_t i = lane; i < k; i += 32) {
+        const unsigned long long c = i < w ? buf[i] : ~0ull;
+        const uint32_t r = static_cast<uint32_t>(c & 0xFFFFFFFFull);
+        const bool valid = r != 0xFFFFFFFFu;
+        idx_out[static_cast<size_t>(q) * k + i] = valid ? r : 0xFFFFFFFFu;
+        val_out[static_cast<size_t>(q) * k + i] =
+            valid ? key_to_float(static_cast<uint32_t>(c >> 32)) : __int_as_float(0x7f800000);
+    }
+}
+
 // ------------------------------------------------- filtered-subset gathering
 // A row filter selecting a small share of the rows (Vault's equality
 // candidates, MetadataIndex::exact_candidates) is searched by gathering the

@@ -412,6 +412,24 @@ int pair_groups(int device) {
 
 }  // namespace
 
+// The k <= 256 smallest (value, index) of every row of a distance matrix,
+// one warp per row (topk_rows_warp_kernel).
+void top_k_rows_warp(int device, const float* dist, uint32_t* idx, float* val, size_t nq, size_t nb, size_t k,
+                     cudaStream_t stream) {
+    constexpr uint32_t kWarps = 8;
+    uint32_t kpow2 = 32;
+    while (kpow2 < k) kpow2 <<= 1;
+    const size_t smem = kWarps * (1024 + static_cast<size_t>(kpow2) * 8);
+    allow_dynamic_smem(reinterpret_cast<const void*>(topk_rows_warp_kernel), smem);
+    Profiler::Scope prof("topk_rows", stream, static_cast<uint64_t>(nq) * nb);
+    const uint32_t blocks = static_cast<uint32_t>((nq + kWarps - 1) / kWarps);
+    topk_rows_warp_kernel<<<blocks, kWarps * 32, smem, stream>>>(dist, static_cast<uint32_t>(nq),
+                                                                  static_cast<uint32_t>(nb), static_cast<uint32_t>(k),
+                                                                  kpow2, idx, val);
+    check_cuda(cudaGetLastError(), ELIPS_B200_KERNEL_LAUNCH_FAILED, "top-k rows launch");
+    (void)device;
+}
+
 ExactIndex::ExactIndex(int device, int metric, int precision, uint32_t dim)
     : device_(device), metric_(metric), precision_(precision), dim_(dim) {
     if (dim == 0 || dim > 65535) fail(ELIPS_B200_INVALID_ARGUMENT, "dimension must be in [1, 65535]");

@@ -192,6 +192,12 @@ private:
 // Final merge over candidate lists (see merge_topk_kernel). With sub > 1,
 // the first stage of a two-stage merge: each query's lists in `sub` groups of
 // `lists` (the last: lists_last), output row q*sub + j per group.
+// The k (<= 256) smallest (value, index) of each of nq rows of nb distances,
+// one warp per row; same results as the block top-k (values +inf and NaN
+// never taken, ties by index). DEVICE pointers on `stream`.
+void top_k_rows_warp(int device, const float* dist, uint32_t* idx, float* val, size_t nq, size_t nb, size_t k,
+                     cudaStream_t stream);
+
 // len: entries per candidate list (0 = k).
 void merge_candidates(int device, const uint2* cand, uint32_t nq, uint32_t lists, uint32_t k,
                       uint64_t stride_q, uint64_t stride_l, int metric, float* out_dist,

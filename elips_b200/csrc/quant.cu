@@ -129,6 +129,10 @@ void top_k_device(int device, const float* dist, uint32_t* idx, float* val, size
         top_k_sorted(dist, idx, val, nq, nb, k, stream);
         return;
     }
+    if (k <= 256) {  // one warp per row
+        top_k_rows_warp(device, dist, idx, val, nq, nb, k, stream);
+        return;
+    }
     const uint32_t cap = btk_cap(static_cast<uint32_t>(k));
     const uint32_t kp = pow2_at_least(static_cast<uint32_t>(k));
     const size_t smem = btk_bytes(cap) + static_cast<size_t>(kp) * 8;

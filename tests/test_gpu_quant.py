@@ -58,6 +58,27 @@ def test_top_k_matches_stable_sort(nb, k):
         assert (idx[:, nb:] == 0xFFFFFFFF).all() and np.isinf(val[:, nb:]).all()
 
 
+@pytest.mark.parametrize("k", [20, 100, 400])
+def test_top_k_never_takes_inf_or_nan(k):
+    """Values of +inf and NaN are never among the k best (the warp-per-row
+    kernel for k <= 256 and the block kernel above it agree): the finite
+    values in stable order, then {0xFFFFFFFF, +inf} padding."""
+    from elips_b200.quant import top_k
+    rng = np.random.default_rng(46)
+    d = rng.integers(0, 30, size=(9, 500)).astype(np.float32)
+    d[rng.random(d.shape) < 0.6] = np.inf
+    d[rng.random(d.shape) < 0.05] = np.nan
+    d[:, :3] = -np.inf
+    idx, val = top_k(d, k)
+    for r in range(d.shape[0]):
+        fin = np.flatnonzero(d[r] < np.inf)
+        order = fin[np.argsort(d[r, fin], kind="stable")][:k]
+        t = order.size
+        assert np.array_equal(idx[r, :t], order.astype(np.uint32))
+        assert np.array_equal(val[r, :t], d[r, order])
+        assert (idx[r, t:] == 0xFFFFFFFF).all() and np.isposinf(val[r, t:]).all()
+
+
 @pytest.fixture(scope="module")
 def pq_data():
     base = H.gaussian(20_000, 64, seed=46)
